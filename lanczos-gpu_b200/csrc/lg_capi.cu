@@ -1,0 +1,160 @@
+// lg_capi.cu — extern "C" entry points of liblanczos_b200.so (declared in
+// include/lanczos_b200.h).
+#include "lg_solver.h"
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <string>
+
+struct lg_eigsh_plan {
+  lg::Solver solver;
+};
+
+extern "C" {
+
+int lg_eigsh_opts_default(lg_eigsh_opts* o) {
+  if (!o) return LG_ERR_INVALID;
+  std::memset(o, 0, sizeof(*o));
+  o->k = 6;
+  o->ncv = 0;
+  o->maxiter = 0;
+  o->max_steps = 0;
+  o->tol = 0.0;
+  o->which = LG_WHICH_LM;
+  o->use_sigma = 0;
+  o->sigma = 0.0;
+  o->cg_max_iters = 0;
+  o->cg_tol = 1e-12;
+  o->mixed = 0;
+  o->seed = 42;
+  o->return_vectors = 1;
+  o->evecs_rowmajor = 0;
+  return LG_OK;
+}
+
+int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr, const int* col_idx,
+                         const double* vals, int device_ptrs, int max_ncv, int mixed) {
+  if (!plan) return LG_ERR_INVALID;
+  *plan = nullptr;
+  lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();
+  if (!p) return LG_ERR_NOMEM;
+  const int rc = p->solver.create(n, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv, mixed);
+  if (rc != LG_OK) {
+    delete p;
+    return rc;
+  }
+  *plan = p;
+  return LG_OK;
+}
+
+int lg_eigsh_plan_run(lg_eigsh_plan* plan, const lg_eigsh_opts* opts, const double* v0, double* evals,
+                      double* evecs, int io_on_device, lg_eigsh_info* info) {
+  if (!plan || !opts || !evals) {
+    lg::g_last_error = "null plan, opts or evals";
+    return LG_ERR_INVALID;
+  }
+  return plan->solver.run(*opts, v0, evals, evecs, io_on_device, info);
+}
+
+int lg_eigsh_plan_destroy(lg_eigsh_plan* plan) {
+  delete plan;
+  return LG_OK;
+}
+
+int lg_eigsh_plan_matvec(lg_eigsh_plan* plan, const double* x, double* y) {
+  if (!plan || !x || !y) return LG_ERR_INVALID;
+  return plan->solver.matvec(x, y);
+}
+
+int lg_eigsh_plan_factorize(lg_eigsh_plan* plan, const double* v0, int m, double* alpha, double* beta) {
+  if (!plan || !v0 || !alpha || !beta) return LG_ERR_INVALID;
+  return plan->solver.factorize(v0, m, alpha, beta);
+}
+
+int lg_eigsh(int n, long long nnz, const int* row_ptr, const int* col_idx, const double* vals,
+             const lg_eigsh_opts* opts, const double* v0, double* evals, double* evecs, lg_eigsh_info* info) {
+  if (!opts) return LG_ERR_INVALID;
+  int ncv = opts->ncv > 0 ? opts->ncv : std::min(n, std::max(2 * opts->k + 1, 20));
+  lg_eigsh_plan* p = nullptr;
+  int rc = lg_eigsh_plan_create(&p, n, nnz, row_ptr, col_idx, vals, 0, ncv, opts->mixed);
+  if (rc != LG_OK) return rc;
+  rc = lg_eigsh_plan_run(p, opts, v0, evals, evecs, 0, info);
+  lg_eigsh_plan_destroy(p);
+  return rc;
+}
+
+const char* lg_status_string(int status) {
+  switch (status) {
+    case LG_OK: return "ok";
+    case LG_NOCONV: return "iteration limit reached before all Ritz pairs converged";
+    case LG_ERR_INVALID: return "invalid argument";
+    case LG_ERR_CUDA: return "CUDA error";
+    case LG_ERR_NOMEM: return "device memory allocation failed";
+    case LG_ERR_TIMEOUT: return "bounded device wait timed out";
+    case LG_ERR_NUMERIC: return "numerical failure";
+    case LG_ERR_CG_NOCONV: return "inner CG did not converge";
+    default: return "unknown status";
+  }
+}
+
+int lg_last_error(char* buf, int len) {
+  const std::string& s = lg::g_last_error;
+  if (buf && len > 0) {
+    const int c = std::min<int>(len - 1, (int)s.size());
+    std::memcpy(buf, s.data(), c);
+    buf[c] = '\0';
+  }
+  return (int)s.size();
+}
+
+// ---- reference-compatible ABI ---------------------------------------------
+
+// Reference behaviour kept: k smallest-algebraic pairs, ncv = 0 means
+// min(max(3k, 40), n), max_iters is a Lanczos-step budget, the return value
+// is min(k, ncv), eigenvectors are column-major.
+int compute_eigsh(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals, int k, int ncv,
+                  int max_iters, double tol, double* out_eigenvalues, double* out_eigenvectors) {
+  if (n < 2 || k < 1 || k >= n || !out_eigenvalues) return LG_ERR_INVALID;
+  lg_eigsh_opts o;
+  lg_eigsh_opts_default(&o);
+  o.k = k;
+  o.ncv = ncv > 0 ? std::min(ncv, n) : std::min(std::max(3 * k, 40), n);
+  if (o.ncv <= k) o.ncv = std::min(n, k + 1);
+  o.which = LG_WHICH_SA;
+  o.tol = tol;
+  o.max_steps = max_iters > 0 ? max_iters : 0;
+  o.maxiter = 2147483647;
+  o.return_vectors = out_eigenvectors != nullptr;
+  o.evecs_rowmajor = 0;
+  lg_eigsh_info info;
+  const int rc = lg_eigsh(n, nnz, row_ptr, col_idx, vals, &o, nullptr, out_eigenvalues, out_eigenvectors, &info);
+  if (rc < 0) return rc;
+  return std::min(k, o.ncv);
+}
+
+int compute_eigsh_sigma(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals, int k,
+                        int ncv, int max_iters, double tol, double sigma, int cg_max_iters, double cg_tol,
+                        double* out_eigenvalues, double* out_eigenvectors) {
+  if (n < 2 || k < 1 || k >= n || !out_eigenvalues) return LG_ERR_INVALID;
+  lg_eigsh_opts o;
+  lg_eigsh_opts_default(&o);
+  o.k = k;
+  o.ncv = ncv > 0 ? std::min(ncv, n) : std::min(std::max(3 * k, 40), n);
+  if (o.ncv <= k) o.ncv = std::min(n, k + 1);
+  o.which = LG_WHICH_LM;   // largest |mu| of (A - sigma I)^-1 = nearest sigma
+  o.tol = tol;
+  o.max_steps = max_iters > 0 ? max_iters : 0;
+  o.maxiter = 2147483647;
+  o.use_sigma = 1;
+  o.sigma = sigma;
+  o.cg_max_iters = cg_max_iters;
+  o.cg_tol = cg_tol;
+  o.return_vectors = out_eigenvectors != nullptr;
+  lg_eigsh_info info;
+  const int rc = lg_eigsh(n, nnz, row_ptr, col_idx, vals, &o, nullptr, out_eigenvalues, out_eigenvectors, &info);
+  if (rc < 0 && rc != LG_ERR_CG_NOCONV) return rc;
+  return std::min(k, o.ncv);
+}
+
+}  // extern "C"

@@ -1,0 +1,179 @@
+// lg_common.cuh — shared constants, error handling and sm_100a device helpers
+// for the B200 Lanczos engine.
+//
+// Numerical constants restate the reference's choices
+// (src/lanczos_types.cuh:63-75): DGKS threshold 1/sqrt(2), SAFE_MIN = DBL_MIN,
+// MACH_EPS = DBL_EPSILON, at most two refinement passes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cfloat>
+
+namespace lg {
+
+// ---------------------------------------------------------------------------
+// Limits and layout constants
+// ---------------------------------------------------------------------------
+constexpr int kMaxCols = 128;          // basis columns held in one tile (ncv+1 <= 128)
+constexpr int kPartStride = 136;       // doubles per partial-sum row: 128 columns + scalars
+constexpr int kPartScalar = 128;       // slot of the first scalar in a partial row
+constexpr int kRowAlign = 256;         // leading dimension of V is a multiple of this
+constexpr int kGsThreads = 512;        // threads of the Gram-Schmidt pass kernels
+constexpr int kMaxStages = 8;          // deepest TMA ring
+
+constexpr double kDgks = 0.7071067811865476;      // 1/sqrt(2)
+constexpr double kSafeMin = DBL_MIN;
+constexpr double kEps = DBL_EPSILON;
+
+// Device-side state words (int32 array in device memory).
+enum StateWord {
+  ST_STATUS = 0,      // 0 = running; otherwise one of Status
+  ST_STEP = 1,        // step index the status refers to
+  ST_NCONV = 2,
+  ST_NEV_USE = 3,
+  ST_DONE = 4,        // restart kernel decided to stop (converged or out of iterations)
+  ST_KSEL = 5,        // number of selected Ritz pairs written to zsel
+  ST_ERRINFO = 6,     // extra error detail (e.g. tridiagonal QR failure, timeout site)
+  ST_WORDS = 16
+};
+
+enum Status {
+  STATUS_RUNNING = 0,
+  STATUS_PASS3 = 1,       // DGKS wants a third Gram-Schmidt pass at step ST_STEP
+  STATUS_BREAKDOWN = 2,   // invariant subspace found after step ST_STEP
+  STATUS_TRIDIAG_FAIL = 3,
+  STATUS_TIMEOUT = 4,     // a bounded wait on a TMA barrier gave up
+};
+
+// Device-side double scalars.
+enum ScalarWord {
+  SC_WN2 = 0,        // ||w||^2 of the current step
+  SC_R1N2 = 1,       // ||r1||^2 after the first Gram-Schmidt pass
+  SC_HJ = 2,         // first-pass coefficient h_j (diagonal part of alpha_j)
+  SC_RCOEF = 3,      // restart: coefficient on the old residual
+  SC_TAU = 4,        // restart: coefficient on V_new[:, nev_use]
+  SC_BN = 5,         // residual norm at the last restart check
+  SC_BETA_NEXT = 6,  // norm of the residual that will become the next basis vector
+  SC_WORDS = 16
+};
+
+__host__ __device__ inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions (fixed order, so every run is bitwise repeatable)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_sumf(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum one double over the block; result valid in every thread.
+// `scratch` needs blockDim.x/32 doubles.
+__device__ inline double block_sum(double v, double* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < nw; ++w) t += scratch[w];
+  __syncthreads();
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// Safe scaling (two-step when the norm is below SAFE_MIN; the reference does
+// the same with two Dscal calls, src/lanczos_ops.cuh:204-216).
+// x * s1 * s2 where s2 == 1 in the normal case.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void safe_inv(double nrm, double& s1, double& s2) {
+  if (nrm >= kSafeMin) { s1 = 1.0 / nrm; s2 = 1.0; }
+  else if (nrm > 0.0) { s1 = kSafeMin / nrm; s2 = 1.0 / kSafeMin; }
+  else { s1 = 1.0; s2 = 1.0; }
+}
+
+// ---------------------------------------------------------------------------
+// Counter-based uniform RNG (splitmix64 finaliser).  Used for the default
+// starting vector and for restart vectors after an invariant subspace.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+// uniform in [-0.5, 0.5)
+__host__ __device__ __forceinline__ double uniform_centered(uint64_t seed, uint64_t i) {
+  uint64_t r = mix64(seed * 0x100000001B3ull + mix64(i));
+  return (double)(r >> 11) * (1.0 / 9007199254740992.0) - 0.5;
+}
+
+// ---------------------------------------------------------------------------
+// TMA bulk copies (cp.async.bulk, global -> shared, completion on an
+// mbarrier).  No multicast anywhere: every copy reads this GPU's own memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// dst and src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~`limit_cycles` SM clock cycles and returns
+// false.  A TMA read of resident memory completes in microseconds, so the
+// limit (about a second) is only reached when something is badly wrong.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit_cycles = 2000000000ll) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit_cycles) return false;
+  }
+  return true;
+}
+
+}  // namespace lg

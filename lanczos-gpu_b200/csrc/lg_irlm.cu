@@ -1,0 +1,591 @@
+// lg_irlm.cu — host driver of the implicitly restarted Lanczos method.
+//
+// Reference: src/irlm_lanczos.cu:153-394 (irlm_lanczos), :110-148
+// (lanczos_extend) and the C ABI wrappers python/gpu_eigsh/_cuda_eigsh.cu.
+//
+// Differences in structure (same mathematics):
+//  * all vectors, alpha/beta, the restart logic and the convergence test stay
+//    on the device; the host enqueues a whole Lanczos extension
+//    (4 kernels per step) without waiting and synchronises once per
+//    restart to read a 16-word state record;
+//  * rare events (a third DGKS pass, an invariant subspace) are detected on
+//    the device, which then turns the rest of the queued work into no-ops;
+//    the host handles the event at the next sync and resumes at the next step;
+//  * workspace lives in a plan that can be reused across solves; nothing is
+//    allocated inside the iteration.
+#include "lg_common.cuh"
+#include "lg_kernels.cuh"
+#include "lg_solver.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace lg {
+
+thread_local std::string g_last_error;
+
+void set_error(const char* fmt, const char* a, int line) {
+  char buf[512];
+  snprintf(buf, sizeof(buf), fmt, a, line);
+  g_last_error = buf;
+}
+
+#define LG_TRY(expr)                                                     \
+  do {                                                                   \
+    cudaError_t _e = (expr);                                             \
+    if (_e != cudaSuccess) {                                             \
+      set_error("CUDA error %s at lg_irlm.cu:%d", cudaGetErrorString(_e), __LINE__); \
+      return (_e == cudaErrorMemoryAllocation) ? LG_ERR_NOMEM : LG_ERR_CUDA; \
+    }                                                                    \
+  } while (0)
+
+static int pick_lanes(double mean) {
+  if (mean < 3.0) return 2;
+  if (mean < 6.0) return 4;
+  if (mean < 12.0) return 8;
+  if (mean < 24.0) return 16;
+  return 32;
+}
+
+__global__ void cast_f64_f32_kernel(const double* __restrict__ a, float* __restrict__ b, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    b[i] = (float)a[i];
+}
+
+__global__ void scale_kernel(double* x, int n, double s) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] *= s;
+}
+
+Solver::~Solver() { release(); }
+
+void Solver::release() {
+  void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, V, W, R, partA, partB, partC, alpha, beta, scal,
+                  ritz, bounds, zsel, Q, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  d_rowptr = d_col = nullptr;
+  d_val64 = nullptr;
+  d_val32 = nullptr;
+  V = W = R = partA = partB = partC = alpha = beta = scal = ritz = bounds = zsel = Q = Ytmp = cg_ws = nullptr;
+  cg_part = cg_scal = nullptr;
+  cg_counter = nullptr;
+  conv = state = cg_flags = nullptr;
+  if (h_state) cudaFreeHost(h_state);
+  if (h_cg_flags) cudaFreeHost(h_cg_flags);
+  h_state = h_cg_flags = nullptr;
+  for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+  ev_pool.clear();
+  if (ev0) cudaEventDestroy(ev0);
+  if (ev1) cudaEventDestroy(ev1);
+  ev0 = ev1 = nullptr;
+  if (stream) cudaStreamDestroy(stream);
+  stream = nullptr;
+}
+
+int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, const double* vals, int device_ptrs,
+                   int max_ncv_, int mixed_) {
+  if (n_ < 1 || nnz_ < 0 || !rowptr || (nnz_ > 0 && (!col || !vals))) {
+    g_last_error = "invalid CSR arguments";
+    return LG_ERR_INVALID;
+  }
+  if (nnz_ > 2147483647ll) {
+    g_last_error = "nnz exceeds int32 indexing";
+    return LG_ERR_INVALID;
+  }
+  if (!device_ptrs) {
+    // Host-side structural checks (the reference performs none).
+    if (rowptr[0] != 0 || (long long)rowptr[n_] != nnz_) {
+      g_last_error = "row_ptr must start at 0 and end at nnz";
+      return LG_ERR_INVALID;
+    }
+    for (int i = 0; i < n_; ++i)
+      if (rowptr[i + 1] < rowptr[i]) {
+        g_last_error = "row_ptr is not monotone";
+        return LG_ERR_INVALID;
+      }
+    for (long long k = 0; k < nnz_; ++k)
+      if (col[k] < 0 || col[k] >= n_) {
+        g_last_error = "column index out of range";
+        return LG_ERR_INVALID;
+      }
+  }
+  n = n_;
+  nnz = nnz_;
+  mixed = mixed_;
+  max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
+  ld = round_up(n, kRowAlign);
+
+  LG_TRY(cudaGetDevice(&device));
+  LG_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, device));
+  int smem_optin = 0;
+  LG_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  smem_budget = (size_t)std::min(smem_optin, 200 * 1024);
+  LG_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  LG_TRY(cudaEventCreate(&ev0));
+  LG_TRY(cudaEventCreate(&ev1));
+
+  grid_gs = num_sm;
+  grid_spmv = num_sm * 8;
+  grid_basis = num_sm;
+
+  LG_TRY(cudaMalloc(&d_rowptr, sizeof(int) * (size_t)(n + 1)));
+  LG_TRY(cudaMalloc(&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
+  LG_TRY(cudaMalloc(&d_val64, sizeof(double) * (size_t)std::max<long long>(nnz, 1)));
+  const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  LG_TRY(cudaMemcpyAsync(d_rowptr, rowptr, sizeof(int) * (size_t)(n + 1), kind, stream));
+  if (nnz > 0) {
+    LG_TRY(cudaMemcpyAsync(d_col, col, sizeof(int) * (size_t)nnz, kind, stream));
+    LG_TRY(cudaMemcpyAsync(d_val64, vals, sizeof(double) * (size_t)nnz, kind, stream));
+  }
+  if (mixed) {
+    LG_TRY(cudaMalloc(&d_val32, sizeof(float) * (size_t)std::max<long long>(nnz, 1)));
+    cast_f64_f32_kernel<<<num_sm * 4, 256, 0, stream>>>(d_val64, d_val32, nnz);
+    LG_TRY(cudaGetLastError());
+  }
+
+  const size_t cols = (size_t)max_ncv + 1;
+  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)ld * cols));
+  LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
+  LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * cols, stream));
+  LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
+  LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+  const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
+  for (double** p : {&partA, &partB, &partC}) {
+    LG_TRY(cudaMalloc(p, sizeof(double) * (size_t)prow * kPartStride));
+    LG_TRY(cudaMemsetAsync(*p, 0, sizeof(double) * (size_t)prow * kPartStride, stream));
+  }
+  LG_TRY(cudaMalloc(&alpha, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(cudaMalloc(&beta, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(cudaMalloc(&scal, sizeof(double) * SC_WORDS));
+  LG_TRY(cudaMalloc(&ritz, sizeof(double) * kMaxCols));
+  LG_TRY(cudaMalloc(&bounds, sizeof(double) * kMaxCols));
+  LG_TRY(cudaMalloc(&zsel, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(cudaMalloc(&Q, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(cudaMalloc(&conv, sizeof(int) * kMaxCols));
+  LG_TRY(cudaMalloc(&state, sizeof(int) * ST_WORDS));
+  LG_TRY(cudaMallocHost(&h_state, sizeof(int) * ST_WORDS));
+
+  A.n = n;
+  A.nnz = nnz;
+  A.rowptr = d_rowptr;
+  A.col = d_col;
+  A.val64 = d_val64;
+  A.val32 = mixed ? d_val32 : nullptr;
+  A.lanes = pick_lanes(nnz / (double)n);
+
+  LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+int Solver::sync_state() {
+  LG_TRY(cudaMemcpyAsync(h_state, state, sizeof(int) * ST_WORDS, cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+int Solver::clear_status() {
+  LG_TRY(cudaMemsetAsync(state, 0, sizeof(int) * 2, stream));
+  return LG_OK;
+}
+
+// w = OP(v_j) preceded by the normalisation of R into V[:, j].
+int Solver::apply_step(int j, int beta_mode) {
+  double* Vj = V + (size_t)j * ld;
+  if (!opts.use_sigma) {
+    // CSR stream + x gather (counted once) + v_j and w written
+    const double vb = mixed ? 4.0 : 8.0;
+    const double bytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 16.0 * n;
+    LG_TRY(timed(LG_K_SPMV, bytes, 1, [&] {
+      return spmv_step(A, stream, grid_spmv, R, W, Vj, partC, nrowsC, j, beta_mode, alpha, beta, scal, state);
+    }));
+    return LG_OK;
+  }
+  return apply_shift_invert(j, beta_mode);
+}
+
+int Solver::extend(int j0, int j1, int first_mode) {
+  for (int j = j0; j < j1; ++j) {
+    int rc = apply_step(j, j == j0 ? first_mode : BETA_STEP);
+    if (rc != LG_OK) return rc;
+    const int ncols = j + 1;
+    const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+    const double vbytes = 8.0 * (double)n * ncols;
+    LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
+                 [&] { return gs_project(p, stream, V, ld, ncols, W, partA, state); }));
+    LG_TRY(timed(LG_K_CORRPROJ, vbytes + 16.0 * n, 1, [&] {
+      return gs_correct_project(p, stream, V, ld, ncols, W, R, partA, p.grid, partB, scal, state);
+    }));
+    LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
+      return gs_correct(p, stream, V, ld, ncols, R, partB, p.grid, partC, scal, alpha, j, 1, state);
+    }));
+    nrowsC = p.grid;
+  }
+  return LG_OK;
+}
+
+cudaEvent_t Solver::next_event() {
+  if (ev_used == ev_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    ev_pool.push_back(e);
+  }
+  return ev_pool[ev_used++];
+}
+
+void Solver::collect_profile(lg_eigsh_info* info) {
+  for (const KTime& kt : ktimes) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, kt.a, kt.b) == cudaSuccess && kt.cls >= 0 && kt.cls < LG_K_CLASSES) {
+      info->kernel_ms[kt.cls] += ms;
+      info->kernel_calls[kt.cls] += 1;
+      info->kernel_bytes[kt.cls] += kt.bytes;
+    }
+  }
+  ktimes.clear();
+  ev_used = 0;
+}
+
+// Third DGKS pass on the residual of step s (reference: the second
+// refinement pass of dgks_reorth, src/lanczos_ops.cuh:158-191).
+int Solver::pass3(int s) {
+  const int ncols = s + 1;
+  const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+  launches += 2;
+  LG_TRY(gs_project(p, stream, V, ld, ncols, R, partA, state));
+  LG_TRY(gs_correct(p, stream, V, ld, ncols, R, partA, p.grid, partC, scal, alpha, s, 2, state));
+  nrowsC = p.grid;
+  return LG_OK;
+}
+
+// Invariant subspace after step s: a random vector made orthogonal to
+// V[:, 0..s] by two Gram-Schmidt passes (reference: inject_random_restart,
+// src/lanczos_ops.cuh:229-253; ARPACK dgetv0).  The coupling beta_{s+1} is
+// set to zero (as ARPACK does), so T decouples.
+int Solver::random_restart(int s) {
+  const int ncols = s + 1;
+  ++breakdowns;
+  LG_TRY(fill_random(stream, R, n, ld, mix64(opts.seed + 0x5bd1e995ull * (uint64_t)(breakdowns + 1) + (uint64_t)s)));
+  const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+  launches += 5;
+  for (int pass = 0; pass < 2; ++pass) {
+    LG_TRY(gs_project(p, stream, V, ld, ncols, R, partA, state));
+    LG_TRY(gs_correct(p, stream, V, ld, ncols, R, partA, p.grid, partC, scal, alpha, s, 0, state));
+  }
+  nrowsC = p.grid;
+  return LG_OK;
+}
+
+int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double* evecs, int io_on_device,
+                lg_eigsh_info* info) {
+  opts = o;
+  const int k = o.k;
+  if (k < 1 || k >= n) {
+    g_last_error = "k must satisfy 1 <= k < n";
+    return LG_ERR_INVALID;
+  }
+  int m = o.ncv > 0 ? o.ncv : std::min(n, std::max(2 * k + 1, 20));
+  if (m > n) m = n;
+  if (m <= k || m > max_ncv) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "ncv must satisfy k < ncv <= min(n, %d); got ncv=%d k=%d", max_ncv, m, k);
+    g_last_error = buf;
+    return LG_ERR_INVALID;
+  }
+  if (o.which < 0 || o.which > 4) {
+    g_last_error = "unknown which";
+    return LG_ERR_INVALID;
+  }
+  const int maxiter = o.maxiter > 0 ? o.maxiter : (n > 214748364 ? 2147483647 : 10 * n);
+  breakdowns = 0;
+  int pass3_count = 0;
+  cg_iters = 0;
+  cg_failures = 0;
+  skip_checks_next = 0;
+  launches = 0;
+  ktimes.clear();
+  ev_used = 0;
+
+  if (o.use_sigma) {
+    int rc = prepare_shift_invert();
+    if (rc != LG_OK) return rc;
+  }
+
+  LG_TRY(cudaEventRecord(ev0, stream));
+  LG_TRY(cudaMemsetAsync(state, 0, sizeof(int) * ST_WORDS, stream));
+  LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
+  LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
+  LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * (m + 1), stream));
+
+  // Starting vector into R.
+  if (v0) {
+    LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+    LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n,
+                           io_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream));
+  } else {
+    LG_TRY(fill_random(stream, R, n, ld, o.seed));
+    ++launches;
+  }
+  LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
+  ++launches;
+  nrowsC = grid_gs;
+
+  long long steps = 0;
+  int rc = extend(0, m, BETA_INIT);
+  if (rc != LG_OK) return rc;
+  steps += m;
+
+  int iter = 1;
+  int last_pass3_step = -1;
+  for (;;) {
+    RestartArgs ra;
+    ra.m = m;
+    ra.nev0 = k;
+    ra.which = o.which;
+    ra.tol = o.tol;
+    ra.iter = iter;
+    ra.maxiter = maxiter;
+    ra.force_done = (o.max_steps > 0 && steps >= o.max_steps) ? 1 : 0;
+    ra.skip_checks = skip_checks_next;
+    skip_checks_next = 0;
+    ra.part_in = partC;
+    ra.nrows_in = nrowsC;
+    ra.alpha = alpha;
+    ra.beta = beta;
+    ra.scal = scal;
+    ra.ritz_out = ritz;
+    ra.bounds_out = bounds;
+    ra.conv_out = conv;
+    ra.zsel = zsel;
+    ra.Q = Q;
+    ra.state = state;
+    LG_TRY(timed(LG_K_RESTART, 0.0, 1, [&] { return restart_step(ra, stream); }));
+    rc = sync_state();
+    if (rc != LG_OK) return rc;
+
+    const int status = h_state[ST_STATUS];
+    if (status == STATUS_TIMEOUT) {
+      g_last_error = "bounded device wait timed out";
+      return LG_ERR_TIMEOUT;
+    }
+    if (status == STATUS_TRIDIAG_FAIL) {
+      g_last_error = "tridiagonal QR iteration did not converge (non-finite values?)";
+      return LG_ERR_NUMERIC;
+    }
+    if (status == STATUS_PASS3 || status == STATUS_BREAKDOWN) {
+      const int s = h_state[ST_STEP];
+      if (s < 0 || s >= m) {
+        g_last_error = "internal: bad step index in device state";
+        return LG_ERR_NUMERIC;
+      }
+      rc = clear_status();
+      if (rc != LG_OK) return rc;
+      int next_mode = BETA_STEP;
+      if (status == STATUS_PASS3 && s != last_pass3_step) {
+        rc = pass3(s);
+        ++pass3_count;
+        last_pass3_step = s;
+      } else {
+        // breakdown, or a third pass that did not restore the norm
+        rc = random_restart(s);
+        next_mode = BETA_ZERO;
+        last_pass3_step = -1;
+      }
+      if (rc != LG_OK) return rc;
+      if (s + 1 < m) {
+        rc = extend(s + 1, m, next_mode);
+        if (rc != LG_OK) return rc;
+        steps += m - (s + 1);
+      } else if (next_mode == BETA_ZERO) {
+        // invariant subspace at the last step: the residual is exactly zero
+        LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+        LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
+        ++launches;
+        nrowsC = grid_gs;
+        skip_checks_next = 1;
+      }
+      continue;  // re-run the Ritz computation for this restart
+    }
+    last_pass3_step = -1;
+
+    if (h_state[ST_DONE]) break;
+    const int nev_use = h_state[ST_NEV_USE];
+    if (nev_use < 1 || nev_use >= m) {
+      g_last_error = "internal: bad nev in device state";
+      return LG_ERR_NUMERIC;
+    }
+    BasisArgs ba;
+    ba.V = V;
+    ba.ld = ld;
+    ba.nrows = n;
+    ba.m = m;
+    ba.kq = nev_use + 1;
+    ba.Q = Q;
+    ba.ldq = m;
+    ba.restart = 1;
+    ba.R = R;
+    ba.scal = scal;
+    ba.part_out = partC;
+    ba.state = state;
+    const BasisPlan bp = basis_plan(ld, m, ba.kq, grid_basis, smem_budget);
+    LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + nev_use) + 16.0 * n, 1, [&] { return basis_update(bp, ba, stream); }));
+    nrowsC = bp.grid;
+    rc = extend(nev_use, m, BETA_RESTART);
+    if (rc != LG_OK) return rc;
+    steps += m - nev_use;
+    ++iter;
+  }
+
+  const int ksel = h_state[ST_KSEL];
+  const int nconv = h_state[ST_NCONV];
+  std::vector<double> hr(ksel);
+  std::vector<int> hconv(ksel);
+  LG_TRY(cudaMemcpyAsync(hr.data(), ritz, sizeof(double) * ksel, cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaMemcpyAsync(hconv.data(), conv, sizeof(int) * ksel, cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaStreamSynchronize(stream));
+
+  // Final eigenvalues, ascending.  Shift-invert: lambda = sigma + 1/mu
+  // (reference _cuda_eigsh.cu:121-152), which reorders the pairs.
+  std::vector<double> lam(ksel);
+  std::vector<int> order(ksel);
+  for (int i = 0; i < ksel; ++i) {
+    order[i] = i;
+    lam[i] = hr[i];
+    if (o.use_sigma) lam[i] = (fabs(hr[i]) > kSafeMin) ? o.sigma + 1.0 / hr[i] : o.sigma;
+  }
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lam[a] < lam[b]; });
+  bool identity = true;
+  for (int i = 0; i < ksel; ++i) identity = identity && order[i] == i;
+  if (!identity && o.return_vectors && evecs) {
+    std::vector<double> zs((size_t)m * ksel), zp((size_t)m * ksel);
+    LG_TRY(cudaMemcpyAsync(zs.data(), zsel, sizeof(double) * zs.size(), cudaMemcpyDeviceToHost, stream));
+    LG_TRY(cudaStreamSynchronize(stream));
+    for (int c = 0; c < ksel; ++c)
+      std::copy(zs.begin() + (size_t)order[c] * m, zs.begin() + (size_t)(order[c] + 1) * m, zp.begin() + (size_t)c * m);
+    LG_TRY(cudaMemcpyAsync(zsel, zp.data(), sizeof(double) * zp.size(), cudaMemcpyHostToDevice, stream));
+  }
+
+  if (o.return_vectors && evecs) {
+    double* Y = evecs;
+    if (!io_on_device) {
+      if (!Ytmp || ytmp_elems < (size_t)n * ksel) {
+        if (Ytmp) cudaFree(Ytmp);
+        Ytmp = nullptr;
+        LG_TRY(cudaMalloc(&Ytmp, sizeof(double) * (size_t)n * ksel));
+        ytmp_elems = (size_t)n * ksel;
+      }
+      Y = Ytmp;
+    }
+    BasisArgs ba;
+    ba.V = V;
+    ba.ld = ld;
+    ba.nrows = n;
+    ba.m = m;
+    ba.kq = ksel;
+    ba.Q = zsel;
+    ba.ldq = m;
+    ba.restart = 0;
+    ba.Y = Y;
+    ba.ldy = n;
+    ba.rowmajor = o.evecs_rowmajor;
+    ba.state = state;
+    const BasisPlan bp = basis_plan(ld, m, ksel, grid_basis, smem_budget);
+    LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + ksel), 1, [&] { return basis_update(bp, ba, stream); }));
+    if (!io_on_device)
+      LG_TRY(cudaMemcpyAsync(evecs, Ytmp, sizeof(double) * (size_t)n * ksel, cudaMemcpyDeviceToHost, stream));
+  }
+  LG_TRY(cudaEventRecord(ev1, stream));
+  LG_TRY(cudaStreamSynchronize(stream));
+  rc = sync_state();
+  if (rc != LG_OK) return rc;
+  if (h_state[ST_STATUS] == STATUS_TIMEOUT) {
+    g_last_error = "bounded device wait timed out";
+    return LG_ERR_TIMEOUT;
+  }
+  for (int i = 0; i < ksel; ++i) evals[i] = lam[order[i]];
+
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, ev0, ev1);
+  if (info) {
+    info->nconv = nconv;
+    info->restarts = iter - 1;
+    info->steps = steps;
+    info->pass3 = pass3_count;
+    info->breakdowns = breakdowns;
+    info->cg_iters = cg_iters;
+    info->cg_failures = cg_failures;
+    info->ms = ms;
+    info->launches = launches;
+    for (int c = 0; c < LG_K_CLASSES; ++c) {
+      info->kernel_ms[c] = 0.0;
+      info->kernel_calls[c] = 0;
+      info->kernel_bytes[c] = 0.0;
+    }
+    collect_profile(info);
+  }
+  ktimes.clear();
+  ev_used = 0;
+  for (int i = 0; i < ksel; ++i)
+    if (!std::isfinite(hr[i])) {
+      g_last_error = "non-finite Ritz value";
+      return LG_ERR_NUMERIC;
+    }
+  if (o.use_sigma && cg_failures > 0) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "%d inner CG solves stopped before cg_tol (cg_max_iters=%d)", cg_failures,
+             o.cg_max_iters);
+    g_last_error = buf;
+    return LG_ERR_CG_NOCONV;
+  }
+  return nconv >= k ? LG_OK : LG_NOCONV;
+}
+
+// m Lanczos steps from v0 (host vector) without restarts; returns the
+// tridiagonal (alpha[0..m), beta[0..m], beta[m] = final residual norm).
+int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_out) {
+  if (m < 1 || m > max_ncv || m > n || !v0) {
+    g_last_error = "factorize: need 1 <= m <= min(n, max_ncv) and a starting vector";
+    return LG_ERR_INVALID;
+  }
+  lg_eigsh_opts o;
+  std::memset(&o, 0, sizeof(o));
+  opts = o;
+  LG_TRY(cudaMemsetAsync(state, 0, sizeof(int) * ST_WORDS, stream));
+  LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
+  LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
+  LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * (m + 1), stream));
+  LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+  LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
+  LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
+  nrowsC = grid_gs;
+  int rc = extend(0, m, BETA_INIT);
+  if (rc != LG_OK) return rc;
+  std::vector<double> part((size_t)nrowsC * kPartStride);
+  LG_TRY(cudaMemcpyAsync(alpha_out, alpha, sizeof(double) * m, cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaMemcpyAsync(beta_out, beta, sizeof(double) * m, cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaMemcpyAsync(part.data(), partC, sizeof(double) * part.size(), cudaMemcpyDeviceToHost, stream));
+  rc = sync_state();
+  if (rc != LG_OK) return rc;
+  if (h_state[ST_STATUS] != STATUS_RUNNING) {
+    g_last_error = "factorize: invariant subspace or DGKS third pass met (not handled in this entry point)";
+    return LG_ERR_NUMERIC;
+  }
+  double s = 0.0;
+  for (int r = 0; r < nrowsC; ++r) s += part[(size_t)r * kPartStride + kPartScalar];
+  beta_out[m] = std::sqrt(s);
+  return LG_OK;
+}
+
+int Solver::matvec(const double* x, double* y) {
+  LG_TRY(spmv_plain(A, stream, grid_spmv, x, y, 0.0));
+  LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+}  // namespace lg

@@ -1,0 +1,122 @@
+// lg_kernels.cuh — launch interfaces of the eigsh kernels (host side).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace lg {
+
+// Launch geometry of the Gram-Schmidt pass kernels (lg_gs.cu).
+struct GsPlan {
+  int T = 64;        // rows per tile
+  int S = 2;         // TMA ring depth
+  int ntiles = 0;    // ld / T
+  int grid = 0;      // CTAs (each owns a contiguous range of tiles)
+  size_t smem = 0;   // dynamic shared memory bytes
+};
+
+GsPlan gs_plan(int ld, int ncols, int grid, size_t smem_budget);
+size_t gs_smem_bytes(int S, int T, int ncols);
+
+__device__ void reduce_partials(const double* part, int nrows, int nc, double* out, double* scal_out,
+                                double* red);
+
+cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+                       const double* vec, double* part_out, int* state);
+cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+                               const double* W, double* R, const double* part_in, int nrows_in,
+                               double* part_out, double* scal, int* state);
+cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols, double* R,
+                       const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
+                       int j, int alpha_mode, int* state);
+
+// SpMV step (lg_spmv.cu).  beta_mode says what the norm of R means.
+enum BetaMode {
+  BETA_INIT = 0,      // starting vector: normalise only
+  BETA_STEP = 1,      // residual of step j-1: store beta[j], run the DGKS / breakdown checks
+  BETA_RESTART = 2,   // residual after an implicit restart: store beta[j], breakdown check only
+  BETA_ZERO = 3,      // fresh vector after an invariant subspace: beta[j] = 0
+};
+
+struct CsrDev {
+  int n = 0;
+  long long nnz = 0;
+  const int* rowptr = nullptr;
+  const int* col = nullptr;
+  const double* val64 = nullptr;   // fp64 values (or null)
+  const float* val32 = nullptr;    // fp32 values (mixed mode) (or null)
+  int lanes = 8;                   // lanes per row of the vector kernel
+};
+
+cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
+                      const double* part_in, int nrows_in, int j, int beta_mode, double* alpha, double* beta,
+                      double* scal, int* state);
+
+// Normalise R into V[:, j] (same checks as spmv_step) without applying A.
+cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, const double* part_in,
+                           int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
+                           int* state);
+
+// y = A x (+ shift * x) for plain vectors, used by CG and checks.
+cudaError_t spmv_plain(const CsrDev& A, cudaStream_t st, int grid, const double* x, double* y,
+                       double shift);
+
+// Misc vector kernels (lg_spmv.cu).
+cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed);
+cudaError_t norm_partials(cudaStream_t st, int grid, const double* x, int ld, double* part_out);
+
+// Restart (lg_restart.cu).
+struct RestartArgs {
+  int m = 0;            // ncv
+  int nev0 = 0;         // requested eigenpairs
+  int which = 0;        // Which enum
+  double tol = 0.0;
+  int iter = 0;         // restart counter (1-based, ARPACK convention)
+  int maxiter = 0;
+  int force_done = 0;   // stop after this Ritz computation (e.g. step budget exhausted)
+  int skip_checks = 0;  // residual known to be exactly zero (invariant subspace at the last step)
+  const double* part_in = nullptr;
+  int nrows_in = 0;
+  double* alpha = nullptr;
+  double* beta = nullptr;
+  double* scal = nullptr;
+  double* ritz_out = nullptr;   // m: selected Ritz values (ascending) when done
+  double* bounds_out = nullptr; // m
+  int* conv_out = nullptr;      // m: converged flag of each selected value
+  double* zsel = nullptr;       // m x m col-major: eigenvectors of T for the selection
+  double* Q = nullptr;          // m x m col-major: accumulated shift rotations
+  int* state = nullptr;
+};
+enum Which { WHICH_LM = 0, WHICH_SM = 1, WHICH_LA = 2, WHICH_SA = 3, WHICH_BE = 4 };
+cudaError_t restart_step(const RestartArgs& a, cudaStream_t st);
+
+// Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq].
+//  restart mode: V[:, 0:kq-1] <- out[:, 0:kq-1] in place;
+//                R <- rcoef * R + tau * out[:, kq-1];  norm partials of R.
+//  ritz mode   : Y[:, 0:kq] = out (column-major ldy, or row-major when rowmajor).
+struct BasisArgs {
+  double* V = nullptr;
+  int ld = 0;
+  int nrows = 0;        // rows actually written in ritz mode (n)
+  int m = 0;            // columns of V used
+  int kq = 0;           // columns of Q used
+  const double* Q = nullptr;   // m x kq col-major, leading dim ldq
+  int ldq = 0;
+  int restart = 0;
+  double* R = nullptr;
+  const double* scal = nullptr;  // SC_RCOEF, SC_TAU
+  double* part_out = nullptr;
+  double* Y = nullptr;
+  long long ldy = 0;
+  int rowmajor = 0;
+  int* state = nullptr;
+};
+struct BasisPlan {
+  int T = 64, S = 2, ntiles = 0, grid = 0;
+  size_t smem = 0;
+};
+BasisPlan basis_plan(int ld, int m, int kq, int grid, size_t smem_budget);
+cudaError_t basis_update(const BasisPlan& p, const BasisArgs& a, cudaStream_t st);
+
+}  // namespace lg

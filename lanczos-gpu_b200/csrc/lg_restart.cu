@@ -1,0 +1,381 @@
+// lg_restart.cu — the implicit-restart step of IRLM, on the device, in one CTA.
+//
+// Reference: src/irlm_lanczos.cu:225-363 (host loop: LAPACK dstev, convergence
+// test, NEV adjustment, exact shifts, bulge chase, H2D of Q) and
+// src/tridiag.cuh:33-124 (givens, apply_shifts_tridiag).  Here everything runs
+// in one CTA so the host never touches the tridiagonal:
+//
+//   1. beta_m = ||r|| from the partial sums of the last Gram-Schmidt pass,
+//      DGKS / breakdown checks for the last step;
+//   2. eigen-decomposition of T (m x m) by implicit symmetric QR with the
+//      Wilkinson shift (Golub & Van Loan, Alg. 8.3.2/8.3.3).  Thread 0 runs
+//      the scalar recurrence on (d, e) one sweep at a time and logs the
+//      Givens rotations; all threads then apply the sweep to their own row
+//      of Z (rows are independent), so Z costs no serial time;
+//   3. Ritz estimates |beta_m * Z(m-1, i)|, ARPACK-style ordering of the
+//      wanted end of the spectrum for which = LM/SM/LA/SA/BE, convergence
+//      test |bound| <= tol * max(eps^(2/3), |theta|), locking of zero
+//      bounds and the NEV adjustment of ARPACK's dsaup2;
+//   4. either the selection of the wanted Ritz pairs (finished), or the np
+//      exact shifts applied by bulge chases with deflation splitting
+//      (ARPACK dsapps), accumulating Q the same row-parallel way.
+#include "lg_common.cuh"
+#include "lg_kernels.cuh"
+
+#include <cmath>
+
+namespace lg {
+
+namespace {
+
+constexpr int kRsThreads = 128;
+constexpr double kUnit = 1.1102230246251565e-16;      // 2^-53
+constexpr double kEps23Arpack = 2.3112508282095347e-11; // (2^-53)^(2/3)
+
+// [c -s; s c] [a; b] = [r; 0]
+__device__ __forceinline__ void givens(double a, double b, double& c, double& s) {
+  if (b == 0.0) {
+    c = 1.0;
+    s = 0.0;
+  } else if (fabs(b) > fabs(a)) {
+    const double tau = -a / b;
+    s = 1.0 / sqrt(1.0 + tau * tau);
+    c = s * tau;
+  } else {
+    const double tau = -b / a;
+    c = 1.0 / sqrt(1.0 + tau * tau);
+    s = c * tau;
+  }
+}
+
+// One implicit QR sweep with shift sigma on the unreduced block [l, mm] of the
+// symmetric tridiagonal (d, e) (e[i] couples i and i+1).  Logs the rotations
+// (rotation i acts on columns l+i, l+i+1).  Single thread.
+__device__ void chase(double* d, double* e, int l, int mm, double sigma, double* lc, double* ls) {
+  double bulge = 0.0;
+  for (int k = l; k < mm; ++k) {
+    double c, s;
+    if (k == l) {
+      givens(d[l] - sigma, e[l], c, s);
+    } else {
+      givens(e[k - 1], bulge, c, s);
+      e[k - 1] = c * e[k - 1] - s * bulge;
+    }
+    const double dk = d[k], dk1 = d[k + 1], ek = e[k];
+    const double cc = c * c, ss = s * s, cs = c * s;
+    d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
+    d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
+    e[k] = cs * (dk - dk1) + (cc - ss) * ek;
+    if (k + 1 < mm) {
+      bulge = -s * e[k + 1];
+      e[k + 1] = c * e[k + 1];
+    }
+    lc[k - l] = c;
+    ls[k - l] = s;
+  }
+}
+
+// Apply logged rotations (columns k0.., consecutive) to row `row` of the
+// column-major m x m matrix M: M <- M * G_0 * G_1 * ...
+__device__ __forceinline__ void apply_log(double* M, int m, int row, int k0, int nrot, const double* lc,
+                                          const double* ls) {
+  double a = M[row + (size_t)k0 * m];
+  for (int i = 0; i < nrot; ++i) {
+    const int k = k0 + i;
+    const double b = M[row + (size_t)(k + 1) * m];
+    const double c = lc[i], s = ls[i];
+    M[row + (size_t)k * m] = c * a - s * b;
+    a = s * a + c * b;
+  }
+  M[row + (size_t)(k0 + nrot) * m] = a;
+}
+
+__device__ __forceinline__ bool negligible(double e, double da, double db) {
+  return e * e <= (kUnit * kUnit) * fabs(da) * fabs(db) + kSafeMin;
+}
+
+// Order (rz, bd, id) so that the nev wanted values are at the end
+// (ARPACK dsgets restated: LA ascending, SA descending, LM ascending |x|,
+// SM descending |x|, BE ascending then the low end swapped in front of the
+// high end).  Input arrays are in ascending value order.
+__device__ void order_wanted(int which, int m, int nev, double* rz, double* bd, int* id) {
+  auto swap3 = [&](int i, int k) {
+    double t = rz[i]; rz[i] = rz[k]; rz[k] = t;
+    t = bd[i]; bd[i] = bd[k]; bd[k] = t;
+    int u = id[i]; id[i] = id[k]; id[k] = u;
+  };
+  if (which == WHICH_SA) {
+    for (int i = 0; i < m / 2; ++i) swap3(i, m - 1 - i);
+  } else if (which == WHICH_LM || which == WHICH_SM) {
+    // insertion sort on |rz| (ascending for LM, descending for SM)
+    for (int i = 1; i < m; ++i) {
+      for (int k = i; k > 0; --k) {
+        const double a = fabs(rz[k - 1]), b = fabs(rz[k]);
+        const bool out = (which == WHICH_LM) ? (a > b) : (a < b);
+        if (!out) break;
+        swap3(k - 1, k);
+      }
+    }
+  } else if (which == WHICH_BE) {
+    const int np = m - nev, kevd2 = nev / 2;
+    if (nev > 1) {
+      const int cnt = kevd2 < np ? kevd2 : np;
+      const int off = kevd2 > np ? kevd2 : np;
+      for (int i = 0; i < cnt; ++i) swap3(i, off + i);
+    }
+  }
+  // WHICH_LA: already ascending
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
+  int* state = a.state;
+  if (state[ST_STATUS] != STATUS_RUNNING) return;
+  extern __shared__ __align__(16) double M[];   // m x m, column-major
+  __shared__ double d[kMaxCols], e[kMaxCols], lc[kMaxCols], ls[kMaxCols];
+  __shared__ double rz[kMaxCols], bd[kMaxCols], shifts[kMaxCols];
+  __shared__ int id[kMaxCols];
+  __shared__ double sh_bn;
+  __shared__ int sh_stop, sh_fin, sh_k0, sh_nrot, sh_done, sh_nev, sh_np, sh_nconv;
+
+  const int t = threadIdx.x, m = a.m;
+
+  // ---- 1. residual norm and checks for the last step -----------------------
+  if (t < 32) {
+    double nrm2 = 0.0;
+    for (int r = t; r < a.nrows_in; r += 32) nrm2 += a.part_in[(size_t)r * kPartStride + kPartScalar];
+    nrm2 = warp_sum(nrm2);
+    if (t == 0) {
+      const double bn = sqrt(nrm2);
+      int stop = STATUS_RUNNING;
+      if (a.skip_checks) {
+        // residual is exactly zero by construction
+      } else if (nrm2 <= 0.5 * a.scal[SC_R1N2]) {
+        stop = STATUS_PASS3;
+      } else {
+        double est = 0.0;
+        for (int i = 0; i < m; ++i) {
+          double rs = fabs(a.alpha[i]);
+          if (i > 0) rs += fabs(a.beta[i]);
+          if (i < m - 1) rs += fabs(a.beta[i + 1]);
+          est = fmax(est, rs);
+        }
+        if (bn < 3.6687695461231177e-11 * fmax(est, kSafeMin)) stop = STATUS_BREAKDOWN;
+      }
+      if (stop != STATUS_RUNNING) {
+        state[ST_STEP] = m - 1;
+        state[ST_STATUS] = stop;
+      } else {
+        a.beta[m] = bn;
+        a.scal[SC_BN] = bn;
+      }
+      sh_bn = bn;
+      sh_stop = stop;
+    }
+  }
+  __syncthreads();
+  if (sh_stop != STATUS_RUNNING) return;
+  const double bn = sh_bn;
+
+  // ---- 2. eigen-decomposition of T -----------------------------------------
+  if (t < m) {
+    d[t] = a.alpha[t];
+    e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
+  }
+  for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
+  if (t == 0) sh_fin = 0;
+  __syncthreads();
+
+  int sweeps = 0;  // meaningful in thread 0 only
+  for (;;) {
+    if (t == 0) {
+      int fin = 0;
+      for (int i = 0; i < m - 1; ++i)
+        if (e[i] != 0.0 && negligible(e[i], d[i], d[i + 1])) e[i] = 0.0;
+      int mm = m - 1;
+      while (mm > 0 && e[mm - 1] == 0.0) --mm;
+      if (mm == 0) {
+        fin = 1;
+      } else if (++sweeps > 30 * m) {
+        fin = 2;
+      } else {
+        int l = mm - 1;
+        while (l > 0 && e[l - 1] != 0.0) --l;
+        // Wilkinson shift from the trailing 2x2 of the block
+        const double aa = d[mm - 1], cc = d[mm], bb = e[mm - 1];
+        const double delta = 0.5 * (aa - cc);
+        const double den = delta + copysign(hypot(delta, bb), delta == 0.0 ? 1.0 : delta);
+        const double mu = (den != 0.0) ? cc - bb * (bb / den) : cc - fabs(bb);
+        chase(d, e, l, mm, mu, lc, ls);
+        sh_k0 = l;
+        sh_nrot = mm - l;
+      }
+      sh_fin = fin;
+    }
+    __syncthreads();
+    if (sh_fin) break;
+    if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
+    __syncthreads();
+  }
+  if (sh_fin == 2) {
+    if (t == 0) {
+      state[ST_ERRINFO] = 1;
+      state[ST_STATUS] = STATUS_TRIDIAG_FAIL;
+    }
+    return;
+  }
+
+  // ---- 3. ordering, Ritz estimates, convergence, NEV adjustment -------------
+  if (t == 0) {
+    // ascending sort of eigenvalue indices
+    for (int i = 0; i < m; ++i) id[i] = i;
+    for (int i = 1; i < m; ++i)
+      for (int k = i; k > 0 && d[id[k - 1]] > d[id[k]]; --k) {
+        const int u = id[k - 1]; id[k - 1] = id[k]; id[k] = u;
+      }
+  }
+  __syncthreads();
+  if (t < m) {
+    rz[t] = d[id[t]];
+    bd[t] = fabs(bn * M[(m - 1) + (size_t)id[t] * m]);
+  }
+  __syncthreads();
+
+  if (t == 0) {
+    const double tol = a.tol > 0.0 ? a.tol : kUnit;
+    int nev = a.nev0, np = m - a.nev0;
+    order_wanted(a.which, m, nev, rz, bd, id);
+    int nconv = 0;
+    for (int i = np; i < m; ++i)
+      if (bd[i] <= tol * fmax(kEps23Arpack, fabs(rz[i]))) ++nconv;
+    const int np0 = np;
+    for (int i = 0; i < np0; ++i)
+      if (bd[i] == 0.0) { --np; ++nev; }
+    int done = (nconv >= a.nev0) || (a.iter > a.maxiter) || (np == 0) || a.force_done;
+    if (!done) {
+      const int nevbef = nev;
+      nev = nev + (nconv < np / 2 ? nconv : np / 2);
+      if (nev == 1 && m >= 6) nev = m / 2;
+      else if (nev == 1 && m > 2) nev = 2;
+      np = m - nev;
+      if (nevbef < nev) {
+        // re-establish ascending order, then order for the new split
+        for (int i = 1; i < m; ++i)
+          for (int k = i; k > 0 && rz[k - 1] > rz[k]; --k) {
+            double u = rz[k - 1]; rz[k - 1] = rz[k]; rz[k] = u;
+            u = bd[k - 1]; bd[k - 1] = bd[k]; bd[k] = u;
+            const int w = id[k - 1]; id[k - 1] = id[k]; id[k] = w;
+          }
+        order_wanted(a.which, m, nev, rz, bd, id);
+      }
+      // shifts: unwanted values, largest Ritz estimate first
+      for (int i = 0; i < np; ++i) shifts[i] = rz[i];
+      for (int i = 1; i < np; ++i)
+        for (int k = i; k > 0 && bd[k - 1] < bd[k]; --k) {
+          double u = bd[k - 1]; bd[k - 1] = bd[k]; bd[k] = u;
+          u = shifts[k - 1]; shifts[k - 1] = shifts[k]; shifts[k] = u;
+        }
+    }
+    sh_done = done;
+    sh_nev = nev;
+    sh_np = np;
+    sh_nconv = nconv;
+  }
+  __syncthreads();
+
+  if (sh_done) {
+    // ---- 4a. selection of the wanted Ritz pairs, ascending by value --------
+    const int k = a.nev0, off = m - k;
+    if (t == 0) {
+      // sort the wanted block [off, m) ascending by value (carry bd, id)
+      for (int i = off + 1; i < m; ++i)
+        for (int q = i; q > off && rz[q - 1] > rz[q]; --q) {
+          double u = rz[q - 1]; rz[q - 1] = rz[q]; rz[q] = u;
+          u = bd[q - 1]; bd[q - 1] = bd[q]; bd[q] = u;
+          const int w = id[q - 1]; id[q - 1] = id[q]; id[q] = w;
+        }
+      const double tol = a.tol > 0.0 ? a.tol : kUnit;
+      for (int i = 0; i < k; ++i) {
+        a.ritz_out[i] = rz[off + i];
+        a.bounds_out[i] = bd[off + i];
+        a.conv_out[i] = bd[off + i] <= tol * fmax(kEps23Arpack, fabs(rz[off + i])) ? 1 : 0;
+      }
+      state[ST_NCONV] = sh_nconv;
+      state[ST_KSEL] = k;
+      state[ST_NEV_USE] = sh_nev;
+      state[ST_DONE] = 1;
+    }
+    __syncthreads();
+    for (int c = 0; c < k; ++c)
+      if (t < m) a.zsel[t + (size_t)c * m] = M[t + (size_t)id[off + c] * m];
+    return;
+  }
+
+  // ---- 4b. exact shifts by bulge chasing (ARPACK dsapps) -------------------
+  const int np = sh_np, nev = sh_nev;
+  if (t < m) {
+    d[t] = a.alpha[t];
+    e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
+  }
+  for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
+  __shared__ int sh_is, sh_istart;
+  if (t == 0) { sh_is = 0; sh_istart = 0; }
+  __syncthreads();
+  for (;;) {
+    if (t == 0) {
+      int have = 0;
+      while (!have && sh_is < np) {
+        if (sh_istart >= m - 1) { ++sh_is; sh_istart = 0; continue; }
+        int iend = m - 1;
+        for (int i = sh_istart; i < m - 1; ++i) {
+          if (fabs(e[i]) <= kUnit * (fabs(d[i]) + fabs(d[i + 1]))) { e[i] = 0.0; iend = i; break; }
+        }
+        if (sh_istart < iend) {
+          chase(d, e, sh_istart, iend, shifts[sh_is], lc, ls);
+          sh_k0 = sh_istart;
+          sh_nrot = iend - sh_istart;
+          have = 1;
+        }
+        sh_istart = iend + 1;
+      }
+      sh_fin = have ? 0 : 1;
+    }
+    __syncthreads();
+    if (sh_fin) break;
+    if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
+    __syncthreads();
+  }
+  if (t == 0)
+    for (int i = 0; i < m - 1; ++i)
+      if (fabs(e[i]) <= kUnit * (fabs(d[i]) + fabs(d[i + 1]))) e[i] = 0.0;
+  __syncthreads();
+
+  // outputs: Q[:, 0..nev], new T, restart residual coefficients
+  for (int c = 0; c <= nev && c < m; ++c)
+    if (t < m) a.Q[t + (size_t)c * m] = M[t + (size_t)c * m];
+  if (t < m) {
+    a.alpha[t] = (t < nev) ? d[t] : 0.0;
+  }
+  for (int i = t; i <= m + 1; i += kRsThreads) {
+    if (i >= 1 && i < nev) a.beta[i] = e[i - 1];
+    else if (i > nev) a.beta[i] = 0.0;
+  }
+  if (t == 0) {
+    a.scal[SC_RCOEF] = M[(m - 1) + (size_t)(nev - 1) * m];
+    a.scal[SC_TAU] = (nev < m) ? e[nev - 1] : 0.0;
+    state[ST_NCONV] = sh_nconv;
+    state[ST_NEV_USE] = nev;
+    state[ST_DONE] = 0;
+  }
+}
+
+cudaError_t restart_step(const RestartArgs& a, cudaStream_t st) {
+  const size_t smem = (size_t)a.m * a.m * sizeof(double);
+  cudaError_t e = cudaFuncSetAttribute(restart_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  restart_kernel<<<1, kRsThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace lg

@@ -1,0 +1,113 @@
+// lg_solver.h — host-side solver object behind the lg_eigsh_plan handle.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <string>
+#include <vector>
+
+#include "../../include/lanczos_b200.h"
+#include "lg_kernels.cuh"
+
+namespace lg {
+
+extern thread_local std::string g_last_error;
+
+class Solver {
+ public:
+  ~Solver();
+  int create(int n, long long nnz, const int* rowptr, const int* col, const double* vals, int device_ptrs,
+             int max_ncv, int mixed);
+  int run(const lg_eigsh_opts& o, const double* v0, double* evals, double* evecs, int io_on_device,
+          lg_eigsh_info* info);
+  int matvec(const double* x, double* y);
+  int factorize(const double* v0, int m, double* alpha_out, double* beta_out);
+
+ private:
+  void release();
+  int sync_state();
+  int clear_status();
+  int apply_step(int j, int beta_mode);
+  int extend(int j0, int j1, int first_mode);
+  int pass3(int s);
+  int random_restart(int s);
+  // shift-invert (lg_cg.cu)
+  int prepare_shift_invert();
+  int apply_shift_invert(int j, int beta_mode);
+  int cg_solve(const double* b, double* x);
+
+  int n = 0, ld = 0, max_ncv = 0, mixed = 0;
+  long long nnz = 0;
+  int device = 0, num_sm = 0, grid_gs = 0, grid_spmv = 0, grid_basis = 0;
+  size_t smem_budget = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+  CsrDev A;
+  int* d_rowptr = nullptr;
+  int* d_col = nullptr;
+  double* d_val64 = nullptr;
+  float* d_val32 = nullptr;
+
+  double* V = nullptr;      // ld x (max_ncv + 1), column-major
+  double* W = nullptr;      // operator output
+  double* R = nullptr;      // residual (unnormalised next basis vector)
+  double* partA = nullptr;  // partial sums: pass 1
+  double* partB = nullptr;  // pass 2
+  double* partC = nullptr;  // pass 3 / norms of R
+  int nrowsC = 0;
+  double* alpha = nullptr;
+  double* beta = nullptr;
+  double* scal = nullptr;
+  double* ritz = nullptr;
+  double* bounds = nullptr;
+  double* zsel = nullptr;
+  double* Q = nullptr;
+  int* conv = nullptr;
+  int* state = nullptr;
+  int* h_state = nullptr;
+  double* Ytmp = nullptr;
+  size_t ytmp_elems = 0;
+
+  // shift-invert CG workspace: x r pa pb Ap (ld each) + scalars
+  double* cg_ws = nullptr;
+  double* cg_part = nullptr;
+  double* cg_scal = nullptr;
+  unsigned* cg_counter = nullptr;
+  int* cg_flags = nullptr;
+  int* h_cg_flags = nullptr;
+  int cg_grid = 0;
+  int cg_chunk = 64;
+
+  // launch accounting and optional per-kernel-class event timing
+  struct KTime {
+    int cls;
+    cudaEvent_t a, b;
+    double bytes;
+  };
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<KTime> ktimes;
+  long long launches = 0;
+  cudaEvent_t next_event();
+  // Records an event pair around `launch` when profiling; counts `nlaunch`.
+  template <class F>
+  cudaError_t timed(int cls, double bytes, int nlaunch, F&& launch) {
+    launches += nlaunch;
+    if (!opts.profile) return launch();
+    KTime kt{cls, next_event(), next_event(), bytes};
+    cudaEventRecord(kt.a, stream);
+    cudaError_t e = launch();
+    cudaEventRecord(kt.b, stream);
+    ktimes.push_back(kt);
+    return e;
+  }
+  void collect_profile(lg_eigsh_info* info);
+
+  lg_eigsh_opts opts{};
+  int breakdowns = 0;
+  long long cg_iters = 0;
+  int cg_failures = 0;
+  int skip_checks_next = 0;
+};
+
+}  // namespace lg

@@ -1,0 +1,218 @@
+// lg_spmv.cu — CSR SpMV for the Lanczos step, plus small vector kernels.
+//
+// Replaces the operator layer of the reference (src/matvec_operator.cuh:56-135:
+// cuSPARSE SpMV, and the mixed fp32 path with its two cast kernels
+// src/cast_kernels.cu:7-15).  Here:
+//   * one kernel per step does  beta_j = ||r||, v_j = r / beta_j,
+//     w = A v_j  — the normalisation of the previous residual is folded into
+//     the SpMV (w = (A r) / beta_j), so no separate scale/copy launches;
+//   * the fp32-value variant keeps x and the accumulator in fp64
+//     (fp32 values halve the value stream; accuracy stays fp64);
+//   * rows are handled by a group of L lanes (vector-per-row, L picked from
+//     the mean row length), lanes read consecutive nonzeros (coalesced).
+#include "lg_common.cuh"
+#include "lg_kernels.cuh"
+#include "lg_csr.cuh"
+
+#include <cmath>
+
+namespace lg {
+
+// Reference: src/lanczos_ops.cuh:264-277 (adaptive_breakdown_tol), evaluated
+// for the step that produced the residual (index jr).
+__device__ double breakdown_tol(const double* alpha, const double* beta, int jr) {
+  double est = 0.0;
+  for (int i = 0; i <= jr; ++i) {
+    double rs = fabs(alpha[i]);
+    if (i > 0) rs += fabs(beta[i]);
+    if (i < jr) rs += fabs(beta[i + 1]);
+    est = fmax(est, rs);
+  }
+  const double eps23 = 3.6687695461231177e-11;  // DBL_EPSILON^(2/3)
+  return eps23 * fmax(est, kSafeMin);
+}
+
+// Prologue shared by the SpMV step and the normalise-only step: reduce the
+// norm partials of R, run the DGKS / breakdown checks, store beta_j.  Every
+// CTA computes the same values in the same order; block 0 publishes them.
+// Returns the block-uniform stop code; s1*s2 is the safe 1/||R||.
+__device__ int step_prologue(const double* __restrict__ part_in, int nrows_in, int j, int beta_mode,
+                             double* alpha, double* beta, double* scal, int* state, double& s1o, double& s2o) {
+  __shared__ double sh_s1, sh_s2;
+  __shared__ int sh_stop;
+  if (threadIdx.x < 32) {
+    double nrm2 = 0.0;
+    for (int r = threadIdx.x; r < nrows_in; r += 32) nrm2 += part_in[(size_t)r * kPartStride + kPartScalar];
+    nrm2 = warp_sum(nrm2);
+    if (threadIdx.x == 0) {
+      const double bn = sqrt(nrm2);
+      int stop = STATUS_RUNNING;
+      if (beta_mode == BETA_STEP) {
+        if (nrm2 <= 0.5 * scal[SC_R1N2]) stop = STATUS_PASS3;
+        else if (bn < breakdown_tol(alpha, beta, j - 1)) stop = STATUS_BREAKDOWN;
+      } else if (beta_mode == BETA_RESTART) {
+        if (bn < breakdown_tol(alpha, beta, j - 1)) stop = STATUS_BREAKDOWN;
+      }
+      double s1, s2;
+      safe_inv(bn, s1, s2);
+      sh_s1 = s1;
+      sh_s2 = s2;
+      sh_stop = stop;
+      if (blockIdx.x == 0) {
+        if (stop != STATUS_RUNNING) {
+          state[ST_STEP] = j - 1;
+          state[ST_STATUS] = stop;
+        } else {
+          if (beta_mode == BETA_STEP || beta_mode == BETA_RESTART) beta[j] = bn;
+          else if (beta_mode == BETA_ZERO) beta[j] = 0.0;
+          scal[SC_BETA_NEXT] = bn;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  s1o = sh_s1;
+  s2o = sh_s2;
+  return sh_stop;
+}
+
+template <typename VT, int L>
+__global__ void __launch_bounds__(256)
+spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ col,
+                 const VT* __restrict__ val, const double* __restrict__ R, double* __restrict__ W,
+                 double* __restrict__ Vj, const double* __restrict__ part_in, int nrows_in, int j,
+                 int beta_mode, double* alpha, double* beta, double* scal, int* state) {
+  if (state[ST_STATUS] != STATUS_RUNNING) return;
+  double s1, s2;
+  if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
+
+  const int lane = threadIdx.x & (L - 1);
+  const int warps_total = (gridDim.x * blockDim.x) >> 5;
+  const int rows_per_warp = 32 / L;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp < n;
+       w += warps_total) {
+    const int row = w * rows_per_warp + ((threadIdx.x & 31) / L);
+    const bool valid = row < n;
+    const double acc = row_dot<VT, L>(rowptr, col, val, R, row, valid, lane);
+    if (valid && lane == 0) {
+      W[row] = (acc * s1) * s2;
+      Vj[row] = (R[row] * s1) * s2;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+normalize_step_kernel(int n, const double* __restrict__ R, double* __restrict__ Vj,
+                      const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
+                      double* beta, double* scal, int* state) {
+  if (state[ST_STATUS] != STATUS_RUNNING) return;
+  double s1, s2;
+  if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    Vj[i] = (R[i] * s1) * s2;
+}
+
+cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, const double* part_in,
+                           int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
+                           int* state) {
+  normalize_step_kernel<<<grid, 256, 0, st>>>(n, R, Vj, part_in, nrows_in, j, beta_mode, alpha, beta, scal,
+                                              state);
+  return cudaGetLastError();
+}
+
+template <typename VT, int L>
+__global__ void __launch_bounds__(256)
+spmv_plain_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ col,
+                  const VT* __restrict__ val, const double* __restrict__ x, double* __restrict__ y,
+                  double shift) {
+  const int lane = threadIdx.x & (L - 1);
+  const int warps_total = (gridDim.x * blockDim.x) >> 5;
+  const int rows_per_warp = 32 / L;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp < n;
+       w += warps_total) {
+    const int row = w * rows_per_warp + ((threadIdx.x & 31) / L);
+    const bool valid = row < n;
+    const double acc = row_dot<VT, L>(rowptr, col, val, x, row, valid, lane);
+    if (valid && lane == 0) y[row] = acc + shift * x[row];
+  }
+}
+
+template <typename VT>
+static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, int grid, const double* R,
+                               double* W, double* Vj, const double* part_in, int nrows_in, int j,
+                               int beta_mode, double* alpha, double* beta, double* scal, int* state) {
+#define LG_STEP(LN)                                                                                    \
+  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(A.n, A.rowptr, A.col, val, R, W, Vj, part_in, nrows_in, \
+                                                 j, beta_mode, alpha, beta, scal, state)
+  switch (A.lanes) {
+    case 2: LG_STEP(2); break;
+    case 4: LG_STEP(4); break;
+    case 8: LG_STEP(8); break;
+    case 16: LG_STEP(16); break;
+    default: LG_STEP(32); break;
+  }
+#undef LG_STEP
+  return cudaGetLastError();
+}
+
+cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
+                      const double* part_in, int nrows_in, int j, int beta_mode, double* alpha, double* beta,
+                      double* scal, int* state) {
+  if (A.val32)
+    return launch_step<float>(A, A.val32, st, grid, R, W, Vj, part_in, nrows_in, j, beta_mode, alpha, beta,
+                              scal, state);
+  return launch_step<double>(A, A.val64, st, grid, R, W, Vj, part_in, nrows_in, j, beta_mode, alpha, beta,
+                             scal, state);
+}
+
+template <typename VT>
+static cudaError_t launch_plain(const CsrDev& A, const VT* val, cudaStream_t st, int grid, const double* x,
+                                double* y, double shift) {
+#define LG_PLAIN(LN) \
+  spmv_plain_kernel<VT, LN><<<grid, 256, 0, st>>>(A.n, A.rowptr, A.col, val, x, y, shift)
+  switch (A.lanes) {
+    case 2: LG_PLAIN(2); break;
+    case 4: LG_PLAIN(4); break;
+    case 8: LG_PLAIN(8); break;
+    case 16: LG_PLAIN(16); break;
+    default: LG_PLAIN(32); break;
+  }
+#undef LG_PLAIN
+  return cudaGetLastError();
+}
+
+cudaError_t spmv_plain(const CsrDev& A, cudaStream_t st, int grid, const double* x, double* y,
+                       double shift) {
+  if (A.val32) return launch_plain<float>(A, A.val32, st, grid, x, y, shift);
+  return launch_plain<double>(A, A.val64, st, grid, x, y, shift);
+}
+
+// ---------------------------------------------------------------------------
+__global__ void fill_random_kernel(double* x, int n, int ld, uint64_t seed) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ld; i += gridDim.x * blockDim.x)
+    x[i] = (i < n) ? uniform_centered(seed, (uint64_t)i) : 0.0;
+}
+
+cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed) {
+  int grid = (ld + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  fill_random_kernel<<<grid, 256, 0, st>>>(x, n, ld, seed);
+  return cudaGetLastError();
+}
+
+__global__ void norm_partials_kernel(const double* __restrict__ x, int ld, double* __restrict__ part_out) {
+  __shared__ double scr[32];
+  const long long b = (long long)ld * blockIdx.x / gridDim.x;
+  const long long e = (long long)ld * (blockIdx.x + 1) / gridDim.x;
+  double acc = 0.0;
+  for (long long i = b + threadIdx.x; i < e; i += blockDim.x) acc += x[i] * x[i];
+  acc = block_sum(acc, scr);
+  if (threadIdx.x == 0) part_out[(size_t)blockIdx.x * kPartStride + kPartScalar] = acc;
+}
+
+cudaError_t norm_partials(cudaStream_t st, int grid, const double* x, int ld, double* part_out) {
+  norm_partials_kernel<<<grid, 256, 0, st>>>(x, ld, part_out);
+  return cudaGetLastError();
+}
+
+}  // namespace lg

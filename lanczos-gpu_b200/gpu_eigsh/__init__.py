@@ -1,0 +1,252 @@
+"""gpu_eigsh — B200-native Lanczos eigensolver and stochastic Lanczos quadrature.
+
+Drop-in for the reference package of the same name:
+
+* ``gpu_eigsh(A, k, ...)`` — k eigenpairs of a sparse symmetric matrix by
+  implicitly restarted Lanczos on the GPU, with ``scipy.sparse.linalg.eigsh``
+  semantics (``k, which, sigma, ncv, maxiter, tol, v0``).  The reference's
+  positional order ``(A, k, ncv, maxiter, tol, which, sigma, cg_max_iters,
+  cg_tol)`` (python/gpu_eigsh/__init__.py:141-142) is accepted unchanged;
+  ``ncv=0`` means "automatic" as in the reference.
+* ``gpu_eigsh.funm_torch`` — ``slq_logdet``, ``funm_apply_kraemer``,
+  ``funm_qform_op`` (torch.autograd.Functions).
+* ``gpu_eigsh.imgp`` — ``make_imgp_precision_matvec``.
+
+All arithmetic runs in the CUDA library ``_lib/liblanczos_b200.so``; there is
+no CPU fallback.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _native
+from ._native import LanczosError
+
+__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence"]
+
+try:  # raise scipy's own exception type so existing handlers keep working
+    from scipy.sparse.linalg import ArpackNoConvergence
+except Exception:  # pragma: no cover - scipy is a dependency of the API
+    class ArpackNoConvergence(RuntimeError):
+        def __init__(self, msg, eigenvalues, eigenvectors):
+            super().__init__(msg)
+            self.eigenvalues = eigenvalues
+            self.eigenvectors = eigenvectors
+
+
+def _as_csr(A):
+    """scipy sparse / dense ndarray -> (n, indptr int32, indices int32, data float64)."""
+    import scipy.sparse as sp
+
+    if sp.issparse(A):
+        M = sp.csr_matrix(A, dtype=np.float64)
+    elif isinstance(A, np.ndarray) and A.ndim == 2:
+        M = sp.csr_matrix(np.asarray(A, dtype=np.float64))
+    else:
+        raise TypeError("A must be a scipy sparse matrix or a 2-D numpy array")
+    if M.shape[0] != M.shape[1]:
+        raise ValueError(f"Matrix must be square, got {M.shape}")
+    M.sum_duplicates()
+    indptr = np.ascontiguousarray(M.indptr, dtype=np.int32)
+    indices = np.ascontiguousarray(M.indices, dtype=np.int32)
+    data = np.ascontiguousarray(M.data, dtype=np.float64)
+    return M.shape[0], indptr, indices, data
+
+
+def _default_ncv(n: int, k: int) -> int:
+    # scipy.sparse.linalg._eigen.arpack.choose_ncv: max(2k+1, 20), capped at n
+    return min(n, max(2 * k + 1, 20))
+
+
+class EigshPlan:
+    """A matrix resident on the GPU plus the solver workspace.
+
+    Reusing a plan skips the CSR upload and all device allocations, which is
+    what a caller solving repeatedly on one matrix wants.  ``solve`` takes the
+    same keywords as :func:`gpu_eigsh`.
+    """
+
+    def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None):
+        self._plan = None
+        h = _native.C.c_void_p()
+        if device_csr is not None:
+            n, nnz, rp, ci, vals = device_csr
+            rc = _native.lib.lg_eigsh_plan_create(_native.C.byref(h), int(n), int(nnz), int(rp), int(ci),
+                                                  int(vals), 1, int(max_ncv), int(bool(mixed)))
+        else:
+            n, indptr, indices, data = _as_csr(A)
+            nnz = data.shape[0]
+            self._host = (indptr, indices, data)
+            rc = _native.lib.lg_eigsh_plan_create(_native.C.byref(h), n, nnz, _native.ptr(indptr),
+                                                  _native.ptr(indices), _native.ptr(data), 0, int(max_ncv),
+                                                  int(bool(mixed)))
+        _native.check(rc)
+        self._plan = h
+        self.n = int(n)
+        self.nnz = int(nnz)
+        self.mixed = bool(mixed)
+        self.max_ncv = int(max_ncv)
+        self.last_info: dict = {}
+
+    def close(self):
+        if self._plan is not None and self._plan.value:
+            _native.lib.lg_eigsh_plan_destroy(self._plan)
+        self._plan = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def factorize(self, v0, m):
+        """m Lanczos steps (no restart) from v0; returns (alpha (m,), beta (m+1,))."""
+        v0a = np.ascontiguousarray(np.asarray(v0, dtype=np.float64).reshape(-1))
+        if v0a.shape[0] != self.n:
+            raise ValueError("v0 has the wrong length")
+        a = np.zeros(int(m))
+        b = np.zeros(int(m) + 1)
+        P = _native.C.POINTER(_native.C.c_double)
+        _native.check(_native.lib.lg_eigsh_plan_factorize(self._plan, v0a.ctypes.data_as(P), int(m),
+                                                          a.ctypes.data_as(P), b.ctypes.data_as(P)))
+        return a, b
+
+    def matvec_device(self, x_ptr: int, y_ptr: int):
+        """y = A x on device buffers (raw CUDA pointers, n doubles each)."""
+        _native.check(_native.lib.lg_eigsh_plan_matvec(self._plan, int(x_ptr), int(y_ptr)))
+
+    def solve(self, k=6, ncv=None, maxiter=None, tol=0.0, which="LM", sigma=None, cg_max_iters=None,
+              cg_tol=1e-12, *, v0=None, return_eigenvectors=True, max_steps=None, seed=42,
+              evecs_out=None, v0_device=None, evecs_layout="rowmajor", raise_noconv=True, profile=False):
+        n = self.n
+        k = int(k)
+        if k <= 0:
+            raise ValueError("k must be greater than 0.")
+        if k >= n:
+            raise ValueError(f"k must be less than ndim(A), k={k}")
+        which = str(which).upper()
+        if which not in _native.WHICH:
+            raise ValueError("which must be one of LM SM LA SA BE")
+        ncv_eff = _default_ncv(n, k) if (ncv is None or int(ncv) <= 0) else min(int(ncv), n)
+        if ncv_eff <= k or ncv_eff > n:
+            raise ValueError(f"ncv must be k<ncv<=n, ncv={ncv_eff}")
+        if ncv_eff > self.max_ncv:
+            raise ValueError(f"ncv={ncv_eff} exceeds this plan's max_ncv={self.max_ncv}")
+        o = _native.EigshOpts()
+        _native.lib.lg_eigsh_opts_default(_native.C.byref(o))
+        o.k = k
+        o.ncv = ncv_eff
+        o.maxiter = 0 if maxiter is None else int(maxiter)
+        if maxiter is not None and int(maxiter) <= 0:
+            raise ValueError(f"maxiter must be positive, maxiter={maxiter}")
+        o.max_steps = 0 if max_steps is None else int(max_steps)
+        o.tol = float(tol) if tol is not None else 0.0
+        o.which = _native.WHICH[which]
+        o.use_sigma = 0 if sigma is None else 1
+        o.sigma = 0.0 if sigma is None else float(sigma)
+        o.cg_max_iters = 0 if cg_max_iters is None else int(cg_max_iters)
+        o.cg_tol = float(cg_tol)
+        o.mixed = int(self.mixed)
+        o.seed = int(seed) & ((1 << 64) - 1)
+        o.return_vectors = int(bool(return_eigenvectors))
+        o.evecs_rowmajor = 1 if evecs_layout == "rowmajor" else 0
+        o.profile = int(bool(profile))
+
+        v0p = 0
+        io_dev = 0
+        if v0_device is not None:
+            v0p, io_dev = int(v0_device), 1
+        elif v0 is not None:
+            v0a = np.ascontiguousarray(np.asarray(v0, dtype=np.float64).reshape(-1))
+            if v0a.shape[0] != n:
+                raise ValueError(f"v0 must have length {n}, got {v0a.shape[0]}")
+            if not np.any(v0a):
+                raise ValueError("v0 must not be the zero vector")
+            v0p = _native.ptr(v0a)
+        evals = np.zeros(k, dtype=np.float64)
+        evecs = None
+        evp = 0
+        if return_eigenvectors:
+            if evecs_out is not None:
+                evp, io_dev = int(evecs_out), 1
+            else:
+                if io_dev:
+                    raise ValueError("v0_device requires evecs_out (device pointer)")
+                shape = (n, k) if evecs_layout == "rowmajor" else (k, n)
+                evecs = np.zeros(shape, dtype=np.float64)
+                evp = _native.ptr(evecs)
+        info = _native.EigshInfo()
+        rc = _native.lib.lg_eigsh_plan_run(self._plan, _native.C.byref(o), v0p or None,
+                                           evals.ctypes.data_as(_native.C.POINTER(_native.C.c_double)),
+                                           evp or None, io_dev, _native.C.byref(info))
+        self.last_info = info.as_dict()
+        if rc == _native.LG_ERR_CG_NOCONV:
+            raise LanczosError(rc, _native.last_error() + "; increase cg_max_iters or cg_tol")
+        _native.check(rc)
+        if evecs is not None and evecs_layout != "rowmajor":
+            evecs = evecs.T
+        if rc == _native.LG_NOCONV and raise_noconv:
+            nconv = info.nconv
+            msg = (f"ARPACK error -1: No convergence ({info.restarts} iterations, "
+                   f"{nconv}/{k} eigenvectors converged)")
+            raise ArpackNoConvergence(msg, evals, evecs)
+        if return_eigenvectors:
+            return evals, evecs
+        return evals
+
+
+def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_max_iters=None,
+              cg_tol=1e-12, *, v0=None, return_eigenvectors=True, mixed=False, max_steps=None, seed=42,
+              return_info=False, M=None, mode="normal"):
+    """Compute k eigenvalues (and eigenvectors) of a sparse symmetric matrix on the GPU.
+
+    Semantics follow ``scipy.sparse.linalg.eigsh``:
+
+    k : number of eigenpairs (1 <= k < n).
+    ncv : Lanczos basis size; None or 0 -> min(n, max(2k+1, 20)).
+    maxiter : maximum number of implicit restarts (ARPACK iterations);
+        None -> 10 n.  ``max_steps`` additionally bounds the Lanczos steps
+        (the reference's meaning of ``maxiter``).
+    tol : relative accuracy of the Ritz values; 0 -> machine precision.
+    which : 'LM', 'SM', 'LA', 'SA' or 'BE'.
+    sigma : shift-invert about sigma: Lanczos on (A - sigma I)^-1 with an
+        inner CG solve (``cg_max_iters``, ``cg_tol``); ``which`` then refers
+        to the transformed eigenvalues (default 'LM' = nearest sigma).
+        CG requires A - sigma I to be definite.
+    v0 : starting vector (length n); None -> a seeded uniform random vector.
+    mixed : fp32 matrix values with fp64 accumulation and fp64 basis.
+
+    Returns ``(w, v)`` with ``w`` ascending and ``v`` of shape (n, k), or ``w``
+    alone when ``return_eigenvectors=False``.  Raises scipy's
+    ``ArpackNoConvergence`` (carrying the converged pairs) when maxiter is
+    exhausted, and ``LanczosError`` for device-side failures.
+    """
+    if M is not None or mode != "normal":
+        raise NotImplementedError("generalized problems (M) and non-normal shift-invert modes are not supported")
+    n = A.shape[0]
+    if k is not None and int(k) >= n:
+        import scipy.sparse as sp
+        if sp.issparse(A):
+            raise TypeError("Cannot use scipy.linalg.eigh for sparse A with k >= N. "
+                            "Use scipy.linalg.eigh(A.toarray()) or reduce k.")
+    ncv_eff = _default_ncv(n, int(k)) if (ncv is None or int(ncv) <= 0) else min(int(ncv), n)
+    plan = EigshPlan(A, max_ncv=max(ncv_eff, 2), mixed=mixed)
+    try:
+        try:
+            out = plan.solve(k=k, ncv=ncv_eff, maxiter=maxiter, tol=tol, which=which, sigma=sigma,
+                             cg_max_iters=cg_max_iters, cg_tol=cg_tol, v0=v0,
+                             return_eigenvectors=return_eigenvectors, max_steps=max_steps, seed=seed)
+        except ArpackNoConvergence as exc:
+            exc.info = plan.last_info
+            raise
+        if return_info:
+            return out, plan.last_info
+        return out
+    finally:
+        plan.close()

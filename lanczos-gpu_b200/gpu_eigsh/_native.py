@@ -1,0 +1,145 @@
+"""ctypes binding of liblanczos_b200.so (the C ABI in include/lanczos_b200.h).
+
+The library is built in-tree by ``python lanczos-gpu_b200/build.py``.  There is
+no CPU fallback: if the library is missing or cannot be loaded, importing this
+module raises ImportError.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblanczos_b200.so"
+
+LG_OK = 0
+LG_NOCONV = 1
+LG_ERR_INVALID = -1
+LG_ERR_CUDA = -2
+LG_ERR_NOMEM = -3
+LG_ERR_TIMEOUT = -4
+LG_ERR_NUMERIC = -5
+LG_ERR_CG_NOCONV = -6
+
+WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
+
+
+class EigshOpts(C.Structure):
+    _fields_ = [
+        ("k", C.c_int),
+        ("ncv", C.c_int),
+        ("maxiter", C.c_int),
+        ("max_steps", C.c_longlong),
+        ("tol", C.c_double),
+        ("which", C.c_int),
+        ("use_sigma", C.c_int),
+        ("sigma", C.c_double),
+        ("cg_max_iters", C.c_int),
+        ("cg_tol", C.c_double),
+        ("mixed", C.c_int),
+        ("seed", C.c_uint64),
+        ("return_vectors", C.c_int),
+        ("evecs_rowmajor", C.c_int),
+        ("profile", C.c_int),
+    ]
+
+
+KERNEL_CLASSES = ["spmv", "gs_project", "gs_correct_project", "gs_correct", "restart", "basis", "cg", "other"]
+
+
+class EigshInfo(C.Structure):
+    _fields_ = [
+        ("nconv", C.c_int),
+        ("restarts", C.c_int),
+        ("steps", C.c_longlong),
+        ("pass3", C.c_int),
+        ("breakdowns", C.c_int),
+        ("cg_iters", C.c_longlong),
+        ("cg_failures", C.c_int),
+        ("ms", C.c_double),
+        ("launches", C.c_longlong),
+        ("kernel_ms", C.c_double * 8),
+        ("kernel_calls", C.c_longlong * 8),
+        ("kernel_bytes", C.c_double * 8),
+    ]
+
+    def as_dict(self) -> dict:
+        out = {}
+        for name, _ in self._fields_:
+            v = getattr(self, name)
+            if name.startswith("kernel_"):
+                v = {cls: v[i] for i, cls in enumerate(KERNEL_CLASSES)}
+            out[name] = v
+        return out
+
+
+_PD = C.POINTER(C.c_double)
+_PI = C.POINTER(C.c_int)
+
+# Every exported symbol with its ctypes signature (restype, argtypes).
+SIGNATURES = {
+    "lg_eigsh_opts_default": (C.c_int, [C.POINTER(EigshOpts)]),
+    "lg_eigsh_plan_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "lg_eigsh_plan_run": (C.c_int, [C.c_void_p, C.POINTER(EigshOpts), C.c_void_p, _PD, C.c_void_p, C.c_int,
+                                    C.POINTER(EigshInfo)]),
+    "lg_eigsh_plan_destroy": (C.c_int, [C.c_void_p]),
+    "lg_eigsh_plan_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "lg_eigsh_plan_factorize": (C.c_int, [C.c_void_p, _PD, C.c_int, _PD, _PD]),
+    "lg_eigsh": (C.c_int, [C.c_int, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(EigshOpts),
+                           C.c_void_p, _PD, C.c_void_p, C.POINTER(EigshInfo)]),
+    "lg_status_string": (C.c_char_p, [C.c_int]),
+    "lg_last_error": (C.c_int, [C.c_char_p, C.c_int]),
+    "compute_eigsh": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double, _PD,
+                                _PD]),
+    "compute_eigsh_sigma": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double,
+                                      C.c_double, C.c_int, C.c_double, _PD, _PD]),
+}
+
+
+def _load() -> C.CDLL:
+    if not _LIB_PATH.exists():
+        raise ImportError(
+            f"{_LIB_PATH} is missing; build it with `python lanczos-gpu_b200/build.py` "
+            "(nvcc, sm_100a).  There is no CPU fallback.")
+    lib = C.CDLL(str(_LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+LIB_PATH = str(_LIB_PATH)
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    lib.lg_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def status_string(rc: int) -> str:
+    return lib.lg_status_string(rc).decode()
+
+
+class LanczosError(RuntimeError):
+    """A failure reported by the CUDA engine (status code + message)."""
+
+    def __init__(self, rc: int, msg: str = ""):
+        self.status = rc
+        super().__init__(f"{status_string(rc)} ({rc}): {msg or last_error()}")
+
+
+def check(rc: int) -> int:
+    if rc < 0:
+        raise LanczosError(rc)
+    return rc
+
+
+def ptr(a) -> int:
+    """Address of a C-contiguous numpy array (or 0 for None)."""
+    if a is None:
+        return 0
+    return a.ctypes.data

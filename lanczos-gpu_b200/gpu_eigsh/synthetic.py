@@ -1,0 +1,145 @@
+"""Seeded synthetic workloads for the Lanczos hot path.
+
+The reference measures only on seeded synthetic graphs (no public dataset);
+these builders produce the same families at the sizes used for parity tests
+and benchmarks.  All are deterministic functions of their arguments.
+
+* ``grid2d_dirichlet(N)``  — 5-point Dirichlet Laplacian on an N x N grid,
+  kron(I, T) + kron(T, I), T = tridiag(-1, 2, -1); analytic eigenvalues
+  ``grid_eigenvalues``.
+* ``grid3d_dirichlet(N)``  — 7-point Dirichlet Laplacian on N^3.
+* ``knn_laplacian(n, k, seed)`` — points uniform in [0,1]^2, k nearest
+  neighbours (self dropped), symmetrised by union (max(A, A^T), as the
+  reference's benchmark/generate_large_laplacian.py:60 does), weights
+  exp(-d^2 / 2h^2) with h the median k-th neighbour distance, L = D - W.
+* ``knn_edge_list(n, k, seed)`` — the undirected edges (i < j) of that graph
+  with squared lengths, in the IMGP operator's edge-list format
+  (python/gpu_eigsh/imgp.py: idx (2, M) int64, x_edge_dists (M,)).
+* ``rmat_edges(scale, edge_factor, abcd, seed)`` — R-MAT generator
+  (Chakrabarti, Zhan, Faloutsos 2004), symmetrised, duplicates and
+  self-loops removed; ``normalized_laplacian`` builds I - D^-1/2 W D^-1/2.
+"""
+from __future__ import annotations
+
+import numpy as np
+import scipy.sparse as sp
+
+
+def _tridiag_t(N: int) -> sp.csr_matrix:
+    e = np.ones(N)
+    return sp.diags([-e[:-1], 2.0 * e, -e[:-1]], [-1, 0, 1], format="csr")
+
+
+def grid2d_dirichlet(N: int) -> sp.csr_matrix:
+    T = _tridiag_t(N)
+    I = sp.identity(N, format="csr")
+    L = (sp.kron(I, T) + sp.kron(T, I)).tocsr()
+    L.sum_duplicates()
+    L.sort_indices()
+    return L
+
+
+def grid3d_dirichlet(N: int) -> sp.csr_matrix:
+    T = _tridiag_t(N)
+    I = sp.identity(N, format="csr")
+    L = (sp.kron(sp.kron(I, I), T) + sp.kron(sp.kron(I, T), I) + sp.kron(sp.kron(T, I), I)).tocsr()
+    L.sum_duplicates()
+    L.sort_indices()
+    return L
+
+
+def grid_eigenvalues(N: int, dim: int) -> np.ndarray:
+    """All eigenvalues of the dim-D Dirichlet grid Laplacian, ascending:
+    sum_d (2 - 2 cos(j_d pi / (N+1))), j_d = 1..N."""
+    lam1 = 2.0 - 2.0 * np.cos(np.arange(1, N + 1) * np.pi / (N + 1))
+    out = lam1
+    for _ in range(dim - 1):
+        out = (out[:, None] + lam1[None, :]).ravel()
+    return np.sort(out)
+
+
+def _knn(n: int, k: int, seed: int, dim: int = 2):
+    from scipy.spatial import cKDTree
+
+    pts = np.random.default_rng(seed).uniform(size=(n, dim))
+    tree = cKDTree(pts)
+    d, idx = tree.query(pts, k=k + 1, workers=-1)
+    return pts, d[:, 1:], idx[:, 1:]
+
+
+def knn_laplacian(n: int, k: int = 10, seed: int = 1, dim: int = 2):
+    """Returns (L csr float64, info dict)."""
+    _, d, idx = _knn(n, k, seed, dim)
+    h = float(np.median(d[:, k - 1]))
+    w = np.exp(-(d ** 2) / (2.0 * h * h))
+    rows = np.repeat(np.arange(n, dtype=np.int64), k)
+    A = sp.csr_matrix((w.ravel(), (rows, idx.ravel())), shape=(n, n))
+    A = A.maximum(A.T).tocsr()
+    deg = np.asarray(A.sum(axis=1)).ravel()
+    L = (sp.diags(deg) - A).tocsr()
+    L.sum_duplicates()
+    L.sort_indices()
+    info = {"n": n, "k": k, "seed": seed, "h": h, "nnz": int(L.nnz), "edges": int((A.nnz) // 2)}
+    return L, info
+
+
+def knn_edge_list(n: int, k: int = 10, seed: int = 1, dim: int = 2):
+    """Undirected edges (i < j) of the union-symmetrised kNN graph.
+    Returns (idx (2, M) int64, d2 (M,) float64)."""
+    _, d, idx = _knn(n, k, seed, dim)
+    rows = np.repeat(np.arange(n, dtype=np.int64), k)
+    cols = idx.ravel().astype(np.int64)
+    d2 = (d ** 2).ravel()
+    lo = np.minimum(rows, cols)
+    hi = np.maximum(rows, cols)
+    key = lo * n + hi
+    order = np.argsort(key, kind="stable")
+    key, d2 = key[order], d2[order]
+    first = np.ones(key.shape[0], dtype=bool)
+    first[1:] = key[1:] != key[:-1]
+    key, d2 = key[first], d2[first]
+    idx2 = np.stack([key // n, key % n]).astype(np.int64)
+    return idx2, d2
+
+
+def rmat_edges(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0.19, 0.05), seed: int = 2,
+               chunk: int = 1 << 24):
+    """R-MAT edges, symmetrised, without duplicates and self-loops.
+    Returns (src, dst) int64 arrays with src < dst."""
+    a, b, c, _ = abcd
+    n = 1 << scale
+    m = edge_factor * n
+    rng = np.random.default_rng(seed)
+    keys = []
+    for start in range(0, m, chunk):
+        cnt = min(chunk, m - start)
+        u = np.zeros(cnt, dtype=np.int64)
+        v = np.zeros(cnt, dtype=np.int64)
+        for lvl in range(scale):
+            r = rng.random(cnt)
+            bit_u = r >= a + b            # quadrants c, d -> lower half (row bit)
+            bit_v = ((r >= a) & (r < a + b)) | (r >= a + b + c)   # quadrants b, d -> right half
+            u |= bit_u.astype(np.int64) << lvl
+            v |= bit_v.astype(np.int64) << lvl
+        lo = np.minimum(u, v)
+        hi = np.maximum(u, v)
+        keep = lo != hi
+        keys.append(np.unique(lo[keep] * n + hi[keep]))
+    key = np.unique(np.concatenate(keys))
+    return key // n, key % n
+
+
+def normalized_laplacian(n: int, src, dst, dtype=np.float64) -> sp.csr_matrix:
+    """I - D^-1/2 W D^-1/2 for unit edge weights (isolated vertices: L_ii = 0)."""
+    w = np.ones(src.shape[0], dtype=np.float64)
+    A = sp.csr_matrix((np.concatenate([w, w]), (np.concatenate([src, dst]), np.concatenate([dst, src]))),
+                      shape=(n, n))
+    deg = np.asarray(A.sum(axis=1)).ravel()
+    dinv = np.zeros(n)
+    nz = deg > 0
+    dinv[nz] = 1.0 / np.sqrt(deg[nz])
+    S = sp.diags(dinv) @ A @ sp.diags(dinv)
+    L = (sp.diags(nz.astype(np.float64)) - S).tocsr().astype(dtype)
+    L.sum_duplicates()
+    L.sort_indices()
+    return L
