@@ -19,7 +19,7 @@ constexpr int kMaxCols = 128;          // basis columns held in one tile (ncv+1 
 constexpr int kPartStride = 136;       // doubles per partial-sum row: 128 columns + scalars
 constexpr int kPartScalar = 128;       // slot of the first scalar in a partial row
 constexpr int kRowAlign = 256;         // leading dimension of V is a multiple of this
-constexpr int kGsThreads = 512;        // threads of the Gram-Schmidt pass kernels
+constexpr int kGsThreads = 1024;       // threads of the Gram-Schmidt pass kernels (one CTA per SM)
 constexpr int kMaxStages = 8;          // deepest TMA ring
 
 constexpr double kDgks = 0.7071067811865476;      // 1/sqrt(2)

@@ -3,101 +3,92 @@
 // One Lanczos step j (reference: src/irlm_lanczos.cu:110-148 with
 // cgs_orthogonalize / dgks_reorth, src/lanczos_ops.cuh:113-192) is split into
 //
-//   spmv   : w = A v_j                                   (lg_spmv.cu)
-//   pass 1 : h = V^T w,  ||w||^2                         gs_project
-//   pass 2 : r1 = w - V h, then s = V^T r1, ||r1||^2     gs_correct_project
-//   pass 3 : r2 = r1 - V s, ||r2||^2, alpha_j = h_j+s_j  gs_correct
+//   spmv   : w = A v_j                                    (lg_spmv.cu)
+//   pass 1 : h = V^T w,  ||w||^2                          gs_project
+//   pass 2 : r1 = w - V h  and  s = V^T r1, ||r1||^2      gs_correct_project
+//   pass 3 : r2 = r1 - V s, ||r2||^2, alpha_j = h_j + s_j gs_correct
 //
-// so V (n x (j+1), column-major, leading dimension ld) is streamed three
-// times per step instead of four (cuBLAS Dgemv T/N twice in the reference).
-// Pass 2 needs every V element twice (row dot for r1, column dot for s); the
-// row tile therefore lives in shared memory, brought in by TMA bulk copies
-// (cp.async.bulk, one per column segment) through an S-stage mbarrier ring.
+// V is stored ROW-major (n x ldv): a basis row is contiguous, so a warp
+// streams rows with its lanes spread over the columns.  In pass 2 the lanes
+// hold one row of V in registers, reduce the row dot V[row,:]·h across the
+// lanes (shuffles), form r1[row], and immediately accumulate V[row,:]*r1[row]
+// into per-lane column sums — the two halves of the pass share one read of
+// V.  V is streamed once per pass (three times per step, against four Dgemv
+// passes plus copies in the reference); no shared-memory staging, no
+// barriers inside the stream.
 //
-// Each CTA owns a contiguous range of row tiles and writes one row of
-// partial sums; the consumer of those partials (the next kernel) reduces them
-// in a fixed order in every CTA, so results are bitwise repeatable and no
-// atomics or grid-wide spin waits are involved.
+// Lanes per row (LPR) adapt to the live column count: each lane owns two
+// adjacent columns per chunk (16-byte loads), a chunk covers 2*LPR columns,
+// CH chunks cover up to 2*LPR*CH columns; with fewer columns several rows
+// share a warp.  Each CTA owns a contiguous row range and writes one row of
+// partial sums; the next kernel reduces those rows in a fixed order in every
+// CTA, so results are bitwise repeatable without atomics.
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
-#include "lg_tma.cuh"
 
 namespace lg {
 
+constexpr int kGsWarps = kGsThreads / 32;
+
 // Reduce `nrows` partial rows: columns [0, nc) into out[0..nc), the scalar
 // slot into *scal_out.  Every thread of the block gets the same values.
-__device__ void reduce_partials(const double* __restrict__ part, int nrows, int nc,
-                                double* out, double* scal_out, double* red /* >= 512 doubles */) {
+// `red` needs blockDim.x doubles; blockDim.x must be a multiple of 128.
+__device__ void reduce_partials(const double* __restrict__ part, int nrows, int nc, double* out,
+                                double* scal_out, double* red) {
   const int t = threadIdx.x;
-  const int slot = t & 127, grp = t >> 7;   // 4 row groups of 128 column slots
+  const int ngrp = blockDim.x >> 7;
+  const int slot = t & 127, grp = t >> 7;
   double acc = 0.0;
   if (slot < nc) {
-    int r = grp;
 #pragma unroll 4
-    for (; r < nrows; r += 4) acc += part[(size_t)r * kPartStride + slot];
+    for (int r = grp; r < nrows; r += ngrp) acc += part[(size_t)r * kPartStride + slot];
   }
   red[grp * 128 + slot] = acc;
-  // scalar column: warp 0
   double sc = 0.0;
   if (t < 32) {
     for (int r = t; r < nrows; r += 32) sc += part[(size_t)r * kPartStride + kPartScalar];
     sc = warp_sum(sc);
   }
   __syncthreads();
-  if (t < nc) out[t] = red[t] + red[128 + t] + red[256 + t] + red[384 + t];
+  if (t < nc) {
+    double s = 0.0;
+    for (int g = 0; g < ngrp; ++g) s += red[g * 128 + t];
+    out[t] = s;
+  }
   if (t == 0) *scal_out = sc;
   __syncthreads();
 }
 
+namespace {
 
-// Shared-memory layout of the three pass kernels.
-struct GsSmem {
-  static constexpr int kBars = 0;                       // 8 mbarriers (64 B)
-  static constexpr int kFlag = 64;                      // int flag
-  static constexpr int kCoef = 128;                     // 128 doubles
-  static constexpr int kRed = kCoef + 128 * 8;          // 512 doubles
-  static constexpr int kRvec = kRed + 512 * 8;          // 256 doubles
-  static constexpr int kScr = kRvec + 256 * 8;          // 32 doubles
-  static constexpr int kBuf = kScr + 32 * 8;            // stages (16-byte aligned)
-};
-
-size_t gs_smem_bytes(int S, int T, int ncols) {
-  return (size_t)GsSmem::kBuf + (size_t)S * (ncols + 1) * T * sizeof(double);
+__device__ __forceinline__ double2 ld_stream(const double* p) {
+  return __ldcs(reinterpret_cast<const double2*>(p));
 }
 
-// MODE 1: project   (vec = W or R)           -> part_out: V^T vec, ||vec||^2
-// MODE 2: correct+project (vec = W)          -> R = vec - V coef ; part_out: V^T R, ||R||^2
-// MODE 3: correct   (vec = R)                -> R = vec - V coef ; part_out: ||R||^2
-template <int MODE>
+}  // namespace
+
+// MODE 1: project          (vec = W or R) -> part_out: V^T vec, ||vec||^2
+// MODE 2: correct+project  (vec = W)      -> R = vec - V coef ; part_out: V^T R, ||R||^2
+// MODE 3: correct          (vec = R)      -> R = vec - V coef ; part_out: ||R||^2
+template <int MODE, int LPR, int CH>
 __global__ void __launch_bounds__(kGsThreads, 1)
-gs_pass_kernel(const double* __restrict__ V, int ld, int ncols, int T, int S, int ntiles,
-               const double* vec, double* Rout, const double* __restrict__ part_in, int nrows_in,
-               double* __restrict__ part_out, double* scal, double* alpha, int j, int alpha_mode,
-               int* state) {
+gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* vec, double* Rout,
+          const double* __restrict__ part_in, int nrows_in, double* __restrict__ part_out, double* scal,
+          double* alpha, int j, int alpha_mode, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GsSmem::kBars);
-  int* flag = reinterpret_cast<int*>(smem + GsSmem::kFlag);
-  double* coef = reinterpret_cast<double*>(smem + GsSmem::kCoef);
-  double* red = reinterpret_cast<double*>(smem + GsSmem::kRed);
-  double* rvec = reinterpret_cast<double*>(smem + GsSmem::kRvec);
-  double* scr = reinterpret_cast<double*>(smem + GsSmem::kScr);
-  double* buf = reinterpret_cast<double*>(smem + GsSmem::kBuf);
+  constexpr int RW = 32 / LPR;     // rows per warp instruction
+  constexpr int U = (CH == 1) ? 4 : 2;   // row groups in flight per warp (64-register budget)
+  constexpr int COLS = 2 * LPR * CH;
+  __shared__ double coef[kMaxCols];
+  __shared__ double red[kGsThreads];
+  __shared__ double wsum[kGsWarps][COLS];
+  __shared__ double scr[32];
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int sub = lane & (LPR - 1), grp = lane / LPR;
 
-  TileRing ring{bars, buf, S, T, ncols, ld, V, vec};
-  ring.init_barriers();
-
-  // Tile range of this CTA.
-  const int tb = (int)(((long long)ntiles * blockIdx.x) / gridDim.x);
-  const int te = (int)(((long long)ntiles * (blockIdx.x + 1)) / gridDim.x);
-  const int nt = te - tb;
-
-  // Start streaming before the (latency-bound) reduction of the inputs.
-  if (warp == 0)
-    for (int s = 0; s < S && s < nt; ++s) ring.issue(tb + s, s);
-
+  if (t < kMaxCols) coef[t] = 0.0;
+  __syncthreads();
   if (MODE != 1) {
     double sc;
     reduce_partials(part_in, nrows_in, ncols, coef, &sc, red);
@@ -113,69 +104,92 @@ gs_pass_kernel(const double* __restrict__ V, int ld, int ncols, int T, int S, in
     }
   }
 
-  double acc[8];
+  double2 cf[CH];
+  bool live[CH];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) acc[k] = 0.0;
+  for (int ch = 0; ch < CH; ++ch) {
+    const int c0 = ch * 2 * LPR + 2 * sub;
+    live[ch] = c0 < ncols;
+    cf[ch] = make_double2(coef[c0], coef[c0 + 1]);
+  }
+  double2 acc[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) acc[ch] = make_double2(0.0, 0.0);
   double nrm = 0.0;
 
-  const int TPR = kGsThreads / T;         // threads per row in the row-dot phase
-  const int row = t & (T - 1), part = t / T;
+  const long long rb = (long long)n * blockIdx.x / gridDim.x;
+  const long long re = (long long)n * (blockIdx.x + 1) / gridDim.x;
+  const long long step = (long long)kGsWarps * RW;
 
-  for (int it = 0; it < nt; ++it) {
-    const int s = it % S;
-    if (!ring.wait(s, (uint32_t)((it / S) & 1), flag, state, 100 + MODE)) {
-      ring.drain(it, nt);
-      return;
-    }
-    const double* Vs = ring.stage_ptr(s);
-    const double* xs = Vs + (size_t)ncols * T;    // the vector segment
-    const size_t grow = (size_t)(tb + it) * T;
-
-    const double* colsrc = xs;                    // vector used by the column dots
-    if (MODE != 1) {
-      // row dots: y[row] = x[row] - sum_c V[row, c] * coef[c]
-      double p = 0.0;
-      for (int c = part; c < ncols; c += TPR) p += Vs[(size_t)c * T + row] * coef[c];
-      red[part * T + row] = p;
-      __syncthreads();
-      if (t < T) {
-        double y = xs[t];
-        for (int q = 0; q < TPR; ++q) y -= red[q * T + t];
-        rvec[t] = y;
-        Rout[grow + t] = y;
-        nrm += y * y;
-      }
-      __syncthreads();
-      colsrc = rvec;
-    } else {
-      if (t < T) nrm += xs[t] * xs[t];
-    }
-    if (MODE != 3) {
-      // column dots: acc[c] += sum_row V[row, c] * colsrc[row]
+  // the loop bound is warp-uniform (row groups only differ by grp < RW)
+  for (long long w0 = rb + (long long)warp * RW; w0 < re; w0 += step * U) {
+    const long long r0 = w0 + grp;
+    double2 v[U][CH];
+    double x[U];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int c = warp + 16 * k;
-        if (c < ncols) {
-          const double* vc = Vs + (size_t)c * T;
-          double a = 0.0;
-          for (int r = lane; r < T; r += 32) a += vc[r] * colsrc[r];
-          acc[k] += a;
+    for (int u = 0; u < U; ++u) {
+      const long long r = r0 + u * step;
+      const bool ok = r < re;
+      const double* row = V + r * ldv;
+#pragma unroll
+      for (int ch = 0; ch < CH; ++ch)
+        v[u][ch] = (ok && live[ch]) ? ld_stream(row + ch * 2 * LPR + 2 * sub) : make_double2(0.0, 0.0);
+      x[u] = ok ? vec[r] : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long r = r0 + u * step;
+      const bool ok = r < re;
+      if (MODE == 1) {
+#pragma unroll
+        for (int ch = 0; ch < CH; ++ch) {
+          acc[ch].x += v[u][ch].x * x[u];
+          acc[ch].y += v[u][ch].y * x[u];
+        }
+        if (ok && sub == 0) nrm += x[u] * x[u];
+      } else {
+        double d = 0.0;
+#pragma unroll
+        for (int ch = 0; ch < CH; ++ch) d += v[u][ch].x * cf[ch].x + v[u][ch].y * cf[ch].y;
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        const double y = x[u] - d;
+        if (ok && sub == 0) {
+          Rout[r] = y;
+          nrm += y * y;
+        }
+        if (MODE == 2) {
+#pragma unroll
+          for (int ch = 0; ch < CH; ++ch) {
+            acc[ch].x += v[u][ch].x * y;
+            acc[ch].y += v[u][ch].y * y;
+          }
         }
       }
     }
-    __syncthreads();
-    if (warp == 0 && it + S < nt) ring.issue(tb + it + S, s);
   }
 
   double* prow = part_out + (size_t)blockIdx.x * kPartStride;
   if (MODE != 3) {
+    // reduce the row groups of the warp, then the warps of the CTA
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int c = warp + 16 * k;
-      if (c < ncols) {
-        const double v = warp_sum(acc[k]);
-        if (lane == 0) prow[c] = v;
+    for (int ch = 0; ch < CH; ++ch) {
+#pragma unroll
+      for (int o = 16; o >= LPR; o >>= 1) {
+        acc[ch].x += __shfl_xor_sync(0xffffffffu, acc[ch].x, o);
+        acc[ch].y += __shfl_xor_sync(0xffffffffu, acc[ch].y, o);
       }
+      if (grp == 0) {
+        const int c0 = ch * 2 * LPR + 2 * sub;
+        wsum[warp][c0] = acc[ch].x;
+        wsum[warp][c0 + 1] = acc[ch].y;
+      }
+    }
+    __syncthreads();
+    if (t < ncols) {
+      double s = 0.0;
+      for (int w = 0; w < kGsWarps; ++w) s += wsum[w][t];
+      prow[t] = s;
     }
   }
   const double tot = block_sum(nrm, scr);
@@ -185,60 +199,50 @@ gs_pass_kernel(const double* __restrict__ V, int ld, int ncols, int T, int S, in
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
-static int pick_stages(int T, int ncols, size_t budget) {
-  const size_t per = (size_t)(ncols + 1) * T * sizeof(double);
-  size_t s = (budget - GsSmem::kBuf) / per;
-  if (s > (size_t)kMaxStages) s = kMaxStages;
-  return (int)s;
-}
-
-GsPlan gs_plan(int ld, int ncols, int grid, size_t smem_budget) {
+GsPlan gs_plan(int n, int ncols, int grid) {
   GsPlan p;
-  // Larger row tiles when few columns are live keep each stage >= ~16 KB.
-  int T = 64;
-  if ((ncols + 1) * 64 * 8 < 16384 && ld % 128 == 0) T = 128;
-  if ((ncols + 1) * 128 * 8 < 16384 && ld % 256 == 0) T = 256;
-  int S = pick_stages(T, ncols, smem_budget);
-  while (S < 2 && T > 64) { T >>= 1; S = pick_stages(T, ncols, smem_budget); }
-  if (S < 1) S = 1;
-  p.T = T;
-  p.S = S;
-  p.ntiles = ld / T;
-  p.grid = grid < p.ntiles ? grid : p.ntiles;
-  p.smem = gs_smem_bytes(S, T, ncols);
+  p.grid = grid;
+  if (ncols <= 16) { p.lpr = 8; p.ch = 1; }
+  else if (ncols <= 32) { p.lpr = 16; p.ch = 1; }
+  else if (ncols <= 64) { p.lpr = 32; p.ch = 1; }
+  else { p.lpr = 32; p.ch = 2; }
+  const long long rows_per_cta = (long long)(n + grid - 1) / grid;
+  if (rows_per_cta < 1) p.grid = n;
   return p;
 }
 
 template <int MODE>
-static cudaError_t launch_gs(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
-                             const double* vec, double* Rout, const double* part_in, int nrows_in,
-                             double* part_out, double* scal, double* alpha, int j, int alpha_mode,
-                             int* state) {
-  auto kern = gs_pass_kernel<MODE>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-  if (e != cudaSuccess) return e;
-  kern<<<p.grid, kGsThreads, p.smem, st>>>(V, ld, ncols, p.T, p.S, p.ntiles, vec, Rout, part_in, nrows_in,
-                                           part_out, scal, alpha, j, alpha_mode, state);
+static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+                               const double* vec, double* Rout, const double* part_in, int nrows_in,
+                               double* part_out, double* scal, double* alpha, int j, int alpha_mode, int* state) {
+#define LG_GS(LP, C)                                                                                          \
+  gs_kernel<MODE, LP, C><<<p.grid, kGsThreads, 0, st>>>(V, ldv, ncols, n, vec, Rout, part_in, nrows_in,      \
+                                                        part_out, scal, alpha, j, alpha_mode, state)
+  if (p.lpr == 8) LG_GS(8, 1);
+  else if (p.lpr == 16) LG_GS(16, 1);
+  else if (p.ch == 1) LG_GS(32, 1);
+  else LG_GS(32, 2);
+#undef LG_GS
   return cudaGetLastError();
 }
 
-cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                        const double* vec, double* part_out, int* state) {
-  return launch_gs<1>(p, st, V, ld, ncols, vec, nullptr, nullptr, 0, part_out, nullptr, nullptr, 0, 0,
-                      state);
+  return launch_mode<1>(p, st, V, ldv, ncols, n, vec, nullptr, nullptr, 0, part_out, nullptr, nullptr, 0, 0,
+                        state);
 }
 
-cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                                const double* W, double* R, const double* part_in, int nrows_in,
                                double* part_out, double* scal, int* state) {
-  return launch_gs<2>(p, st, V, ld, ncols, W, R, part_in, nrows_in, part_out, scal, nullptr, 0, 0, state);
+  return launch_mode<2>(p, st, V, ldv, ncols, n, W, R, part_in, nrows_in, part_out, scal, nullptr, 0, 0, state);
 }
 
-cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols, double* R,
+cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n, double* R,
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state) {
-  return launch_gs<3>(p, st, V, ld, ncols, R, R, part_in, nrows_in, part_out, scal, alpha, j, alpha_mode,
-                      state);
+  return launch_mode<3>(p, st, V, ldv, ncols, n, R, R, part_in, nrows_in, part_out, scal, alpha, j, alpha_mode,
+                        state);
 }
 
 }  // namespace lg

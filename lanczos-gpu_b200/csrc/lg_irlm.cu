@@ -118,19 +118,20 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
   mixed = mixed_;
   max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
   ld = round_up(n, kRowAlign);
+  ldv = round_up(max_ncv + 1, 4);
 
   LG_TRY(cudaGetDevice(&device));
   LG_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, device));
   int smem_optin = 0;
   LG_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-  smem_budget = (size_t)std::min(smem_optin, 200 * 1024);
+  smem_budget = (size_t)smem_optin;
   LG_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   LG_TRY(cudaEventCreate(&ev0));
   LG_TRY(cudaEventCreate(&ev1));
 
   grid_gs = num_sm;
   grid_spmv = num_sm * 8;
-  grid_basis = num_sm;
+  grid_basis = num_sm * 4;
 
   LG_TRY(cudaMalloc(&d_rowptr, sizeof(int) * (size_t)(n + 1)));
   LG_TRY(cudaMalloc(&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
@@ -147,11 +148,10 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
     LG_TRY(cudaGetLastError());
   }
 
-  const size_t cols = (size_t)max_ncv + 1;
-  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)ld * cols));
+  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
   LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
   LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * cols, stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
   LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
   LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
@@ -195,13 +195,14 @@ int Solver::clear_status() {
 
 // w = OP(v_j) preceded by the normalisation of R into V[:, j].
 int Solver::apply_step(int j, int beta_mode) {
-  double* Vj = V + (size_t)j * ld;
+  double* Vj = V + j;   // column j of the row-major basis
   if (!opts.use_sigma) {
     // CSR stream + x gather (counted once) + v_j and w written
     const double vb = mixed ? 4.0 : 8.0;
     const double bytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 16.0 * n;
     LG_TRY(timed(LG_K_SPMV, bytes, 1, [&] {
-      return spmv_step(A, stream, grid_spmv, R, W, Vj, partC, nrowsC, j, beta_mode, alpha, beta, scal, state);
+      return spmv_step(A, stream, grid_spmv, R, W, Vj, ldv, partC, nrowsC, j, beta_mode, alpha, beta, scal,
+                       state);
     }));
     return LG_OK;
   }
@@ -213,15 +214,15 @@ int Solver::extend(int j0, int j1, int first_mode) {
     int rc = apply_step(j, j == j0 ? first_mode : BETA_STEP);
     if (rc != LG_OK) return rc;
     const int ncols = j + 1;
-    const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+    const GsPlan p = gs_plan(n, ncols, grid_gs);
     const double vbytes = 8.0 * (double)n * ncols;
     LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
-                 [&] { return gs_project(p, stream, V, ld, ncols, W, partA, state); }));
+                 [&] { return gs_project(p, stream, V, ldv, ncols, n, W, partA, state); }));
     LG_TRY(timed(LG_K_CORRPROJ, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct_project(p, stream, V, ld, ncols, W, R, partA, p.grid, partB, scal, state);
+      return gs_correct_project(p, stream, V, ldv, ncols, n, W, R, partA, p.grid, partB, scal, state);
     }));
     LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct(p, stream, V, ld, ncols, R, partB, p.grid, partC, scal, alpha, j, 1, state);
+      return gs_correct(p, stream, V, ldv, ncols, n, R, partB, p.grid, partC, scal, alpha, j, 1, state);
     }));
     nrowsC = p.grid;
   }
@@ -254,10 +255,10 @@ void Solver::collect_profile(lg_eigsh_info* info) {
 // refinement pass of dgks_reorth, src/lanczos_ops.cuh:158-191).
 int Solver::pass3(int s) {
   const int ncols = s + 1;
-  const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+  const GsPlan p = gs_plan(n, ncols, grid_gs);
   launches += 2;
-  LG_TRY(gs_project(p, stream, V, ld, ncols, R, partA, state));
-  LG_TRY(gs_correct(p, stream, V, ld, ncols, R, partA, p.grid, partC, scal, alpha, s, 2, state));
+  LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
+  LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, partA, p.grid, partC, scal, alpha, s, 2, state));
   nrowsC = p.grid;
   return LG_OK;
 }
@@ -270,11 +271,11 @@ int Solver::random_restart(int s) {
   const int ncols = s + 1;
   ++breakdowns;
   LG_TRY(fill_random(stream, R, n, ld, mix64(opts.seed + 0x5bd1e995ull * (uint64_t)(breakdowns + 1) + (uint64_t)s)));
-  const GsPlan p = gs_plan(ld, ncols, grid_gs, smem_budget);
+  const GsPlan p = gs_plan(n, ncols, grid_gs);
   launches += 5;
   for (int pass = 0; pass < 2; ++pass) {
-    LG_TRY(gs_project(p, stream, V, ld, ncols, R, partA, state));
-    LG_TRY(gs_correct(p, stream, V, ld, ncols, R, partA, p.grid, partC, scal, alpha, s, 0, state));
+    LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
+    LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, partA, p.grid, partC, scal, alpha, s, 0, state));
   }
   nrowsC = p.grid;
   return LG_OK;
@@ -320,7 +321,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
   LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
   LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * (m + 1), stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
 
   // Starting vector into R.
   if (v0) {
@@ -421,8 +422,8 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     }
     BasisArgs ba;
     ba.V = V;
-    ba.ld = ld;
-    ba.nrows = n;
+    ba.ldv = ldv;
+    ba.n = n;
     ba.m = m;
     ba.kq = nev_use + 1;
     ba.Q = Q;
@@ -432,7 +433,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ba.scal = scal;
     ba.part_out = partC;
     ba.state = state;
-    const BasisPlan bp = basis_plan(ld, m, ba.kq, grid_basis, smem_budget);
+    const BasisPlan bp = basis_plan(n, m, ba.kq, grid_basis);
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + nev_use) + 16.0 * n, 1, [&] { return basis_update(bp, ba, stream); }));
     nrowsC = bp.grid;
     rc = extend(nev_use, m, BETA_RESTART);
@@ -483,8 +484,8 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     }
     BasisArgs ba;
     ba.V = V;
-    ba.ld = ld;
-    ba.nrows = n;
+    ba.ldv = ldv;
+    ba.n = n;
     ba.m = m;
     ba.kq = ksel;
     ba.Q = zsel;
@@ -494,7 +495,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ba.ldy = n;
     ba.rowmajor = o.evecs_rowmajor;
     ba.state = state;
-    const BasisPlan bp = basis_plan(ld, m, ksel, grid_basis, smem_budget);
+    const BasisPlan bp = basis_plan(n, m, ksel, grid_basis);
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + ksel), 1, [&] { return basis_update(bp, ba, stream); }));
     if (!io_on_device)
       LG_TRY(cudaMemcpyAsync(evecs, Ytmp, sizeof(double) * (size_t)n * ksel, cudaMemcpyDeviceToHost, stream));
@@ -559,7 +560,7 @@ int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_o
   LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
   LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)ld * (m + 1), stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
   LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
   LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));

@@ -7,27 +7,25 @@
 
 namespace lg {
 
-// Launch geometry of the Gram-Schmidt pass kernels (lg_gs.cu).
+// Launch geometry of the Gram-Schmidt pass kernels (lg_gs.cu).  V is
+// row-major n x ldv; `ncols` live columns.
 struct GsPlan {
-  int T = 64;        // rows per tile
-  int S = 2;         // TMA ring depth
-  int ntiles = 0;    // ld / T
-  int grid = 0;      // CTAs (each owns a contiguous range of tiles)
-  size_t smem = 0;   // dynamic shared memory bytes
+  int lpr = 32;      // lanes per basis row
+  int ch = 1;        // 2*lpr-column chunks per row
+  int grid = 0;      // CTAs (each owns a contiguous row range)
 };
 
-GsPlan gs_plan(int ld, int ncols, int grid, size_t smem_budget);
-size_t gs_smem_bytes(int S, int T, int ncols);
+GsPlan gs_plan(int n, int ncols, int grid);
 
 __device__ void reduce_partials(const double* part, int nrows, int nc, double* out, double* scal_out,
                                 double* red);
 
-cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                        const double* vec, double* part_out, int* state);
-cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols,
+cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                                const double* W, double* R, const double* part_in, int nrows_in,
                                double* part_out, double* scal, int* state);
-cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld, int ncols, double* R,
+cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n, double* R,
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state);
 
@@ -49,12 +47,15 @@ struct CsrDev {
   int lanes = 8;                   // lanes per row of the vector kernel
 };
 
+// Vj points at column j of the row-major basis (stride ldv).
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
-                      const double* part_in, int nrows_in, int j, int beta_mode, double* alpha, double* beta,
-                      double* scal, int* state);
+                      int ldv, const double* part_in, int nrows_in, int j, int beta_mode, double* alpha,
+                      double* beta, double* scal, int* state);
 
-// Normalise R into V[:, j] (same checks as spmv_step) without applying A.
-cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, const double* part_in,
+// Normalise R into V[:, j] (same checks as spmv_step) without applying A;
+// optionally also into the contiguous vector `out`.
+cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, int ldv, double* out,
+                           const double* part_in,
                            int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
                            int* state);
 
@@ -91,14 +92,14 @@ struct RestartArgs {
 enum Which { WHICH_LM = 0, WHICH_SM = 1, WHICH_LA = 2, WHICH_SA = 3, WHICH_BE = 4 };
 cudaError_t restart_step(const RestartArgs& a, cudaStream_t st);
 
-// Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq].
+// Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq], V row-major n x ldv.
 //  restart mode: V[:, 0:kq-1] <- out[:, 0:kq-1] in place;
 //                R <- rcoef * R + tau * out[:, kq-1];  norm partials of R.
 //  ritz mode   : Y[:, 0:kq] = out (column-major ldy, or row-major when rowmajor).
 struct BasisArgs {
   double* V = nullptr;
-  int ld = 0;
-  int nrows = 0;        // rows actually written in ritz mode (n)
+  int ldv = 0;
+  int n = 0;
   int m = 0;            // columns of V used
   int kq = 0;           // columns of Q used
   const double* Q = nullptr;   // m x kq col-major, leading dim ldq
@@ -113,10 +114,10 @@ struct BasisArgs {
   int* state = nullptr;
 };
 struct BasisPlan {
-  int T = 64, S = 2, ntiles = 0, grid = 0;
+  int TR = 32, grid = 0;
   size_t smem = 0;
 };
-BasisPlan basis_plan(int ld, int m, int kq, int grid, size_t smem_budget);
+BasisPlan basis_plan(int n, int m, int kq, int grid);
 cudaError_t basis_update(const BasisPlan& p, const BasisArgs& a, cudaStream_t st);
 
 }  // namespace lg

@@ -7,18 +7,20 @@
 //
 //   1. beta_m = ||r|| from the partial sums of the last Gram-Schmidt pass,
 //      DGKS / breakdown checks for the last step;
-//   2. eigen-decomposition of T (m x m) by implicit symmetric QR with the
-//      Wilkinson shift (Golub & Van Loan, Alg. 8.3.2/8.3.3).  Thread 0 runs
-//      the scalar recurrence on (d, e) one sweep at a time and logs the
-//      Givens rotations; all threads then apply the sweep to their own row
-//      of Z (rows are independent), so Z costs no serial time;
-//   3. Ritz estimates |beta_m * Z(m-1, i)|, ARPACK-style ordering of the
+//   2. Ritz values of T (m x m) by implicit symmetric QR with the Wilkinson
+//      shift (Golub & Van Loan, Alg. 8.3.2/8.3.3).  During restarts only the
+//      last row of the eigenvector matrix is needed (Ritz estimates), so
+//      thread 0 carries that one row through the rotations (as ARPACK's
+//      dstqrb does) and no barrier is taken per sweep;
+//   3. Ritz estimates |beta_m * z_last,i|, ARPACK-style ordering of the
 //      wanted end of the spectrum for which = LM/SM/LA/SA/BE, convergence
 //      test |bound| <= tol * max(eps^(2/3), |theta|), locking of zero
 //      bounds and the NEV adjustment of ARPACK's dsaup2;
-//   4. either the selection of the wanted Ritz pairs (finished), or the np
-//      exact shifts applied by bulge chases with deflation splitting
-//      (ARPACK dsapps), accumulating Q the same row-parallel way.
+//   4. either (finished) the same QR is run again with full eigenvectors —
+//      thread 0 logs each sweep's rotations and every thread applies them to
+//      its own row of Z — and the wanted pairs are selected; or the np exact
+//      shifts are applied by bulge chases with deflation splitting (ARPACK
+//      dsapps), accumulating Q the same row-parallel way.
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
 
@@ -29,50 +31,73 @@ namespace lg {
 namespace {
 
 constexpr int kRsThreads = 128;
-constexpr double kUnit = 1.1102230246251565e-16;      // 2^-53
-constexpr double kEps23Arpack = 2.3112508282095347e-11; // (2^-53)^(2/3)
+constexpr double kUnit = 1.1102230246251565e-16;        // 2^-53
+constexpr double kEps23Arpack = 2.3112508282095347e-11;  // (2^-53)^(2/3)
 
-// [c -s; s c] [a; b] = [r; 0]
+// [c -s; s c] [a; b] = [r; 0]; same signs as the classical formulation
+// (tau = -a/b or -b/a, Golub & Van Loan 5.1.3) with one reciprocal sqrt.
 __device__ __forceinline__ void givens(double a, double b, double& c, double& s) {
   if (b == 0.0) {
     c = 1.0;
     s = 0.0;
-  } else if (fabs(b) > fabs(a)) {
-    const double tau = -a / b;
-    s = 1.0 / sqrt(1.0 + tau * tau);
-    c = s * tau;
-  } else {
-    const double tau = -b / a;
-    c = 1.0 / sqrt(1.0 + tau * tau);
-    s = c * tau;
+    return;
   }
+  double r2 = a * a + b * b;
+  double rh;
+  if (r2 >= kSafeMin && r2 < 1e300) {
+    rh = rsqrt(r2);
+  } else {
+    rh = 1.0 / hypot(a, b);
+  }
+  const double sg = (fabs(b) > fabs(a)) ? (b > 0.0 ? -1.0 : 1.0) : (a >= 0.0 ? 1.0 : -1.0);
+  c = sg * a * rh;
+  s = -sg * b * rh;
 }
 
 // One implicit QR sweep with shift sigma on the unreduced block [l, mm] of the
-// symmetric tridiagonal (d, e) (e[i] couples i and i+1).  Logs the rotations
-// (rotation i acts on columns l+i, l+i+1).  Single thread.
-__device__ void chase(double* d, double* e, int l, int mm, double sigma, double* lc, double* ls) {
+// symmetric tridiagonal (d, e) (e[i] couples i and i+1).  Either logs the
+// rotations (lc/ls, rotation i acts on columns l+i, l+i+1) or applies them to
+// the single row z.  Single thread.
+template <bool LOG>
+__device__ void chase(double* d, double* e, int l, int mm, double sigma, double* lc, double* ls, double* z) {
   double bulge = 0.0;
+  double dk = d[l], ek = e[l];
+  double za = LOG ? 0.0 : z[l];
   for (int k = l; k < mm; ++k) {
     double c, s;
     if (k == l) {
-      givens(d[l] - sigma, e[l], c, s);
+      givens(dk - sigma, ek, c, s);
     } else {
       givens(e[k - 1], bulge, c, s);
       e[k - 1] = c * e[k - 1] - s * bulge;
     }
-    const double dk = d[k], dk1 = d[k + 1], ek = e[k];
+    const double dk1 = d[k + 1];
     const double cc = c * c, ss = s * s, cs = c * s;
-    d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
-    d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
-    e[k] = cs * (dk - dk1) + (cc - ss) * ek;
+    const double t2 = 2.0 * cs * ek;
+    d[k] = cc * dk - t2 + ss * dk1;
+    const double dnext = ss * dk + t2 + cc * dk1;
+    const double enew = cs * (dk - dk1) + (cc - ss) * ek;
+    e[k] = enew;
+    double enext = 0.0;
     if (k + 1 < mm) {
-      bulge = -s * e[k + 1];
-      e[k + 1] = c * e[k + 1];
+      const double ek1 = e[k + 1];
+      bulge = -s * ek1;
+      enext = c * ek1;
+      e[k + 1] = enext;
     }
-    lc[k - l] = c;
-    ls[k - l] = s;
+    d[k + 1] = dnext;
+    dk = dnext;
+    ek = enext;
+    if (LOG) {
+      lc[k - l] = c;
+      ls[k - l] = s;
+    } else {
+      const double zb = z[k + 1];
+      z[k] = c * za - s * zb;
+      za = s * za + c * zb;
+    }
   }
+  if (!LOG) z[mm] = za;
 }
 
 // Apply logged rotations (columns k0.., consecutive) to row `row` of the
@@ -94,6 +119,23 @@ __device__ __forceinline__ bool negligible(double e, double da, double db) {
   return e * e <= (kUnit * kUnit) * fabs(da) * fabs(db) + kSafeMin;
 }
 
+// Find the bottom unreduced block of (d, e) after zeroing negligible
+// couplings; returns false when T is diagonal.
+__device__ bool next_block(double* d, double* e, int m, int& l, int& mm, double& mu) {
+  for (int i = 0; i < m - 1; ++i)
+    if (e[i] != 0.0 && negligible(e[i], d[i], d[i + 1])) e[i] = 0.0;
+  mm = m - 1;
+  while (mm > 0 && e[mm - 1] == 0.0) --mm;
+  if (mm == 0) return false;
+  l = mm - 1;
+  while (l > 0 && e[l - 1] != 0.0) --l;
+  const double aa = d[mm - 1], cc = d[mm], bb = e[mm - 1];
+  const double delta = 0.5 * (aa - cc);
+  const double den = delta + copysign(hypot(delta, bb), delta == 0.0 ? 1.0 : delta);
+  mu = (den != 0.0) ? cc - bb * (bb / den) : cc - fabs(bb);
+  return true;
+}
+
 // Order (rz, bd, id) so that the nev wanted values are at the end
 // (ARPACK dsgets restated: LA ascending, SA descending, LM ascending |x|,
 // SM descending |x|, BE ascending then the low end swapped in front of the
@@ -107,7 +149,6 @@ __device__ void order_wanted(int which, int m, int nev, double* rz, double* bd, 
   if (which == WHICH_SA) {
     for (int i = 0; i < m / 2; ++i) swap3(i, m - 1 - i);
   } else if (which == WHICH_LM || which == WHICH_SM) {
-    // insertion sort on |rz| (ascending for LM, descending for SM)
     for (int i = 1; i < m; ++i) {
       for (int k = i; k > 0; --k) {
         const double a = fabs(rz[k - 1]), b = fabs(rz[k]);
@@ -124,7 +165,15 @@ __device__ void order_wanted(int which, int m, int nev, double* rz, double* bd, 
       for (int i = 0; i < cnt; ++i) swap3(i, off + i);
     }
   }
-  // WHICH_LA: already ascending
+}
+
+__device__ void sort_ascending(int lo, int hi, double* rz, double* bd, int* id) {
+  for (int i = lo + 1; i < hi; ++i)
+    for (int k = i; k > lo && rz[k - 1] > rz[k]; --k) {
+      double u = rz[k - 1]; rz[k - 1] = rz[k]; rz[k] = u;
+      u = bd[k - 1]; bd[k - 1] = bd[k]; bd[k] = u;
+      const int w = id[k - 1]; id[k - 1] = id[k]; id[k] = w;
+    }
 }
 
 }  // namespace
@@ -133,7 +182,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   int* state = a.state;
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   extern __shared__ __align__(16) double M[];   // m x m, column-major
-  __shared__ double d[kMaxCols], e[kMaxCols], lc[kMaxCols], ls[kMaxCols];
+  __shared__ double d[kMaxCols], e[kMaxCols], zl[kMaxCols], lc[kMaxCols], ls[kMaxCols];
   __shared__ double rz[kMaxCols], bd[kMaxCols], shifts[kMaxCols];
   __shared__ int id[kMaxCols];
   __shared__ double sh_bn;
@@ -178,46 +227,23 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   if (sh_stop != STATUS_RUNNING) return;
   const double bn = sh_bn;
 
-  // ---- 2. eigen-decomposition of T -----------------------------------------
+  // ---- 2. Ritz values and the last row of the eigenvector matrix -----------
   if (t < m) {
     d[t] = a.alpha[t];
     e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
+    zl[t] = (t == m - 1) ? 1.0 : 0.0;
   }
-  for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
-  if (t == 0) sh_fin = 0;
   __syncthreads();
-
-  int sweeps = 0;  // meaningful in thread 0 only
-  for (;;) {
-    if (t == 0) {
-      int fin = 0;
-      for (int i = 0; i < m - 1; ++i)
-        if (e[i] != 0.0 && negligible(e[i], d[i], d[i + 1])) e[i] = 0.0;
-      int mm = m - 1;
-      while (mm > 0 && e[mm - 1] == 0.0) --mm;
-      if (mm == 0) {
-        fin = 1;
-      } else if (++sweeps > 30 * m) {
-        fin = 2;
-      } else {
-        int l = mm - 1;
-        while (l > 0 && e[l - 1] != 0.0) --l;
-        // Wilkinson shift from the trailing 2x2 of the block
-        const double aa = d[mm - 1], cc = d[mm], bb = e[mm - 1];
-        const double delta = 0.5 * (aa - cc);
-        const double den = delta + copysign(hypot(delta, bb), delta == 0.0 ? 1.0 : delta);
-        const double mu = (den != 0.0) ? cc - bb * (bb / den) : cc - fabs(bb);
-        chase(d, e, l, mm, mu, lc, ls);
-        sh_k0 = l;
-        sh_nrot = mm - l;
-      }
-      sh_fin = fin;
+  if (t == 0) {
+    int fin = 1, sweeps = 0, l, mm;
+    double mu;
+    while (next_block(d, e, m, l, mm, mu)) {
+      if (++sweeps > 30 * m) { fin = 2; break; }
+      chase<false>(d, e, l, mm, mu, nullptr, nullptr, zl);
     }
-    __syncthreads();
-    if (sh_fin) break;
-    if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
-    __syncthreads();
+    sh_fin = fin;
   }
+  __syncthreads();
   if (sh_fin == 2) {
     if (t == 0) {
       state[ST_ERRINFO] = 1;
@@ -228,21 +254,12 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
 
   // ---- 3. ordering, Ritz estimates, convergence, NEV adjustment -------------
   if (t == 0) {
-    // ascending sort of eigenvalue indices
-    for (int i = 0; i < m; ++i) id[i] = i;
-    for (int i = 1; i < m; ++i)
-      for (int k = i; k > 0 && d[id[k - 1]] > d[id[k]]; --k) {
-        const int u = id[k - 1]; id[k - 1] = id[k]; id[k] = u;
-      }
-  }
-  __syncthreads();
-  if (t < m) {
-    rz[t] = d[id[t]];
-    bd[t] = fabs(bn * M[(m - 1) + (size_t)id[t] * m]);
-  }
-  __syncthreads();
-
-  if (t == 0) {
+    for (int i = 0; i < m; ++i) {
+      id[i] = i;
+      rz[i] = d[i];
+      bd[i] = fabs(bn * zl[i]);
+    }
+    sort_ascending(0, m, rz, bd, id);
     const double tol = a.tol > 0.0 ? a.tol : kUnit;
     int nev = a.nev0, np = m - a.nev0;
     order_wanted(a.which, m, nev, rz, bd, id);
@@ -252,7 +269,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
     const int np0 = np;
     for (int i = 0; i < np0; ++i)
       if (bd[i] == 0.0) { --np; ++nev; }
-    int done = (nconv >= a.nev0) || (a.iter > a.maxiter) || (np == 0) || a.force_done;
+    const int done = (nconv >= a.nev0) || (a.iter > a.maxiter) || (np == 0) || a.force_done;
     if (!done) {
       const int nevbef = nev;
       nev = nev + (nconv < np / 2 ? nconv : np / 2);
@@ -260,13 +277,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
       else if (nev == 1 && m > 2) nev = 2;
       np = m - nev;
       if (nevbef < nev) {
-        // re-establish ascending order, then order for the new split
-        for (int i = 1; i < m; ++i)
-          for (int k = i; k > 0 && rz[k - 1] > rz[k]; --k) {
-            double u = rz[k - 1]; rz[k - 1] = rz[k]; rz[k] = u;
-            u = bd[k - 1]; bd[k - 1] = bd[k]; bd[k] = u;
-            const int w = id[k - 1]; id[k - 1] = id[k]; id[k] = w;
-          }
+        sort_ascending(0, m, rz, bd, id);
         order_wanted(a.which, m, nev, rz, bd, id);
       }
       // shifts: unwanted values, largest Ritz estimate first
@@ -285,16 +296,34 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   __syncthreads();
 
   if (sh_done) {
-    // ---- 4a. selection of the wanted Ritz pairs, ascending by value --------
+    // ---- 4a. full eigenvectors (same QR again), wanted pairs ascending ----
     const int k = a.nev0, off = m - k;
-    if (t == 0) {
-      // sort the wanted block [off, m) ascending by value (carry bd, id)
-      for (int i = off + 1; i < m; ++i)
-        for (int q = i; q > off && rz[q - 1] > rz[q]; --q) {
-          double u = rz[q - 1]; rz[q - 1] = rz[q]; rz[q] = u;
-          u = bd[q - 1]; bd[q - 1] = bd[q]; bd[q] = u;
-          const int w = id[q - 1]; id[q - 1] = id[q]; id[q] = w;
+    if (t < m) {
+      d[t] = a.alpha[t];
+      e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
+    }
+    for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
+    __syncthreads();
+    for (;;) {
+      if (t == 0) {
+        int l, mm;
+        double mu;
+        if (next_block(d, e, m, l, mm, mu)) {
+          chase<true>(d, e, l, mm, mu, lc, ls, nullptr);
+          sh_k0 = l;
+          sh_nrot = mm - l;
+          sh_fin = 0;
+        } else {
+          sh_fin = 1;
         }
+      }
+      __syncthreads();
+      if (sh_fin) break;
+      if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
+      __syncthreads();
+    }
+    if (t == 0) {
+      sort_ascending(off, m, rz, bd, id);
       const double tol = a.tol > 0.0 ? a.tol : kUnit;
       for (int i = 0; i < k; ++i) {
         a.ritz_out[i] = rz[off + i];
@@ -332,7 +361,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
           if (fabs(e[i]) <= kUnit * (fabs(d[i]) + fabs(d[i + 1]))) { e[i] = 0.0; iend = i; break; }
         }
         if (sh_istart < iend) {
-          chase(d, e, sh_istart, iend, shifts[sh_is], lc, ls);
+          chase<true>(d, e, sh_istart, iend, shifts[sh_is], lc, ls, nullptr);
           sh_k0 = sh_istart;
           sh_nrot = iend - sh_istart;
           have = 1;
@@ -354,9 +383,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   // outputs: Q[:, 0..nev], new T, restart residual coefficients
   for (int c = 0; c <= nev && c < m; ++c)
     if (t < m) a.Q[t + (size_t)c * m] = M[t + (size_t)c * m];
-  if (t < m) {
-    a.alpha[t] = (t < nev) ? d[t] : 0.0;
-  }
+  if (t < m) a.alpha[t] = (t < nev) ? d[t] : 0.0;
   for (int i = t; i <= m + 1; i += kRsThreads) {
     if (i >= 1 && i < nev) a.beta[i] = e[i - 1];
     else if (i > nev) a.beta[i] = 0.0;

@@ -35,7 +35,7 @@ class Solver {
   int apply_shift_invert(int j, int beta_mode);
   int cg_solve(const double* b, double* x);
 
-  int n = 0, ld = 0, max_ncv = 0, mixed = 0;
+  int n = 0, ld = 0, ldv = 0, max_ncv = 0, mixed = 0;   // ld: vector length padding; ldv: basis row stride
   long long nnz = 0;
   int device = 0, num_sm = 0, grid_gs = 0, grid_spmv = 0, grid_basis = 0;
   size_t smem_budget = 0;
@@ -48,7 +48,7 @@ class Solver {
   double* d_val64 = nullptr;
   float* d_val32 = nullptr;
 
-  double* V = nullptr;      // ld x (max_ncv + 1), column-major
+  double* V = nullptr;      // n x ldv, row-major (ldv >= max_ncv + 1)
   double* W = nullptr;      // operator output
   double* R = nullptr;      // residual (unnormalised next basis vector)
   double* partA = nullptr;  // partial sums: pass 1

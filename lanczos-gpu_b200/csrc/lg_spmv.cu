@@ -80,7 +80,7 @@ template <typename VT, int L>
 __global__ void __launch_bounds__(256)
 spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ col,
                  const VT* __restrict__ val, const double* __restrict__ R, double* __restrict__ W,
-                 double* __restrict__ Vj, const double* __restrict__ part_in, int nrows_in, int j,
+                 double* __restrict__ Vj, int ldv, const double* __restrict__ part_in, int nrows_in, int j,
                  int beta_mode, double* alpha, double* beta, double* scal, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   double s1, s2;
@@ -96,26 +96,31 @@ spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ 
     const double acc = row_dot<VT, L>(rowptr, col, val, R, row, valid, lane);
     if (valid && lane == 0) {
       W[row] = (acc * s1) * s2;
-      Vj[row] = (R[row] * s1) * s2;
+      Vj[(size_t)row * ldv] = (R[row] * s1) * s2;
     }
   }
 }
 
 __global__ void __launch_bounds__(256)
-normalize_step_kernel(int n, const double* __restrict__ R, double* __restrict__ Vj,
+normalize_step_kernel(int n, const double* __restrict__ R, double* __restrict__ Vj, int ldv, double* __restrict__ out,
                       const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
                       double* beta, double* scal, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   double s1, s2;
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-    Vj[i] = (R[i] * s1) * s2;
+  {
+    const double v = (R[i] * s1) * s2;
+    Vj[(size_t)i * ldv] = v;
+    if (out) out[i] = v;
+  }
 }
 
-cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, const double* part_in,
+cudaError_t normalize_step(cudaStream_t st, int grid, int n, const double* R, double* Vj, int ldv, double* out,
+                           const double* part_in,
                            int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
                            int* state) {
-  normalize_step_kernel<<<grid, 256, 0, st>>>(n, R, Vj, part_in, nrows_in, j, beta_mode, alpha, beta, scal,
+  normalize_step_kernel<<<grid, 256, 0, st>>>(n, R, Vj, ldv, out, part_in, nrows_in, j, beta_mode, alpha, beta, scal,
                                               state);
   return cudaGetLastError();
 }
@@ -139,10 +144,10 @@ spmv_plain_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__
 
 template <typename VT>
 static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, int grid, const double* R,
-                               double* W, double* Vj, const double* part_in, int nrows_in, int j,
+                               double* W, double* Vj, int ldv, const double* part_in, int nrows_in, int j,
                                int beta_mode, double* alpha, double* beta, double* scal, int* state) {
 #define LG_STEP(LN)                                                                                    \
-  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(A.n, A.rowptr, A.col, val, R, W, Vj, part_in, nrows_in, \
+  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(A.n, A.rowptr, A.col, val, R, W, Vj, ldv, part_in, nrows_in, \
                                                  j, beta_mode, alpha, beta, scal, state)
   switch (A.lanes) {
     case 2: LG_STEP(2); break;
@@ -156,12 +161,12 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
 }
 
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
-                      const double* part_in, int nrows_in, int j, int beta_mode, double* alpha, double* beta,
-                      double* scal, int* state) {
+                      int ldv, const double* part_in, int nrows_in, int j, int beta_mode, double* alpha,
+                      double* beta, double* scal, int* state) {
   if (A.val32)
-    return launch_step<float>(A, A.val32, st, grid, R, W, Vj, part_in, nrows_in, j, beta_mode, alpha, beta,
+    return launch_step<float>(A, A.val32, st, grid, R, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta,
                               scal, state);
-  return launch_step<double>(A, A.val64, st, grid, R, W, Vj, part_in, nrows_in, j, beta_mode, alpha, beta,
+  return launch_step<double>(A, A.val64, st, grid, R, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta,
                              scal, state);
 }
 
