@@ -70,14 +70,16 @@ __device__ __forceinline__ double2 ld_stream(const double* p) {
 // MODE 1: project          (vec = W or R) -> part_out: V^T vec, ||vec||^2
 // MODE 2: correct+project  (vec = W)      -> R = vec - V coef ; part_out: V^T R, ||R||^2
 // MODE 3: correct          (vec = R)      -> R = vec - V coef ; part_out: ||R||^2
+// vec and Rout never alias (MODE 3 reads and writes R through Rout only).
 template <int MODE, int LPR, int CH>
 __global__ void __launch_bounds__(kGsThreads, 1)
-gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* vec, double* Rout,
-          const double* __restrict__ part_in, int nrows_in, double* __restrict__ part_out, double* scal,
-          double* alpha, int j, int alpha_mode, int* state) {
+gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ vec,
+          double* __restrict__ Rout, const double* __restrict__ part_in, int nrows_in,
+          double* __restrict__ part_out, double* scal, double* alpha, int j, int alpha_mode, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   constexpr int RW = 32 / LPR;     // rows per warp instruction
-  constexpr int U = (CH == 1) ? 4 : 2;   // row groups in flight per warp (64-register budget)
+  // row groups in flight per warp, within the 64-register budget of 1024 threads
+  constexpr int U = (MODE == 2) ? 2 : 3;
   constexpr int COLS = 2 * LPR * CH;
   __shared__ double coef[kMaxCols];
   __shared__ double red[kGsThreads];
@@ -134,7 +136,7 @@ gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double*
 #pragma unroll
       for (int ch = 0; ch < CH; ++ch)
         v[u][ch] = (ok && live[ch]) ? ld_stream(row + ch * 2 * LPR + 2 * sub) : make_double2(0.0, 0.0);
-      x[u] = ok ? vec[r] : 0.0;
+      x[u] = ok ? (MODE == 3 ? Rout[r] : vec[r]) : 0.0;
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -202,10 +204,13 @@ gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double*
 GsPlan gs_plan(int n, int ncols, int grid) {
   GsPlan p;
   p.grid = grid;
-  if (ncols <= 16) { p.lpr = 8; p.ch = 1; }
-  else if (ncols <= 32) { p.lpr = 16; p.ch = 1; }
-  else if (ncols <= 64) { p.lpr = 32; p.ch = 1; }
-  else { p.lpr = 32; p.ch = 2; }
+  // four columns per lane (two 16-byte chunks): the row-dot reduction is
+  // log2(lpr) shuffles shared by 32/lpr rows
+  p.ch = 2;
+  if (ncols <= 16) p.lpr = 4;
+  else if (ncols <= 32) p.lpr = 8;
+  else if (ncols <= 64) p.lpr = 16;
+  else p.lpr = 32;
   const long long rows_per_cta = (long long)(n + grid - 1) / grid;
   if (rows_per_cta < 1) p.grid = n;
   return p;
@@ -218,9 +223,9 @@ static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V
 #define LG_GS(LP, C)                                                                                          \
   gs_kernel<MODE, LP, C><<<p.grid, kGsThreads, 0, st>>>(V, ldv, ncols, n, vec, Rout, part_in, nrows_in,      \
                                                         part_out, scal, alpha, j, alpha_mode, state)
-  if (p.lpr == 8) LG_GS(8, 1);
-  else if (p.lpr == 16) LG_GS(16, 1);
-  else if (p.ch == 1) LG_GS(32, 1);
+  if (p.lpr == 4) LG_GS(4, 2);
+  else if (p.lpr == 8) LG_GS(8, 2);
+  else if (p.lpr == 16) LG_GS(16, 2);
   else LG_GS(32, 2);
 #undef LG_GS
   return cudaGetLastError();
@@ -241,8 +246,8 @@ cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V
 cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n, double* R,
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state) {
-  return launch_mode<3>(p, st, V, ldv, ncols, n, R, R, part_in, nrows_in, part_out, scal, alpha, j, alpha_mode,
-                        state);
+  return launch_mode<3>(p, st, V, ldv, ncols, n, nullptr, R, part_in, nrows_in, part_out, scal, alpha, j,
+                        alpha_mode, state);
 }
 
 }  // namespace lg

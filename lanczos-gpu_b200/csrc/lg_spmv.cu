@@ -86,17 +86,40 @@ spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ 
   double s1, s2;
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
 
+  // Each lane group works on two rows at once so the dependent load chains
+  // (row_ptr -> col -> x gather) of the two rows overlap.
   const int lane = threadIdx.x & (L - 1);
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
   const int rows_per_warp = 32 / L;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp < n;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp * 2 < n;
        w += warps_total) {
-    const int row = w * rows_per_warp + ((threadIdx.x & 31) / L);
-    const bool valid = row < n;
-    const double acc = row_dot<VT, L>(rowptr, col, val, R, row, valid, lane);
-    if (valid && lane == 0) {
-      W[row] = (acc * s1) * s2;
-      Vj[(size_t)row * ldv] = (R[row] * s1) * s2;
+    const int rowA = w * rows_per_warp * 2 + ((threadIdx.x & 31) / L);
+    const int rowB = rowA + rows_per_warp;
+    const bool okA = rowA < n, okB = rowB < n;
+    int kA = 0, eA = 0, kB = 0, eB = 0;
+    if (okA) { kA = __ldg(rowptr + rowA) + lane; eA = __ldg(rowptr + rowA + 1); }
+    if (okB) { kB = __ldg(rowptr + rowB) + lane; eB = __ldg(rowptr + rowB + 1); }
+    double accA = 0.0, accB = 0.0;
+    while (kA < eA || kB < eB) {
+      if (kA < eA) accA += (double)__ldg(val + kA) * __ldg(R + __ldg(col + kA));
+      if (kB < eB) accB += (double)__ldg(val + kB) * __ldg(R + __ldg(col + kB));
+      kA += L;
+      kB += L;
+    }
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) {
+      accA += __shfl_xor_sync(0xffffffffu, accA, o);
+      accB += __shfl_xor_sync(0xffffffffu, accB, o);
+    }
+    if (lane == 0) {
+      if (okA) {
+        W[rowA] = (accA * s1) * s2;
+        Vj[(size_t)rowA * ldv] = (R[rowA] * s1) * s2;
+      }
+      if (okB) {
+        W[rowB] = (accB * s1) * s2;
+        Vj[(size_t)rowB * ldv] = (R[rowB] * s1) * s2;
+      }
     }
   }
 }
