@@ -64,13 +64,13 @@ Solver::~Solver() { release(); }
 
 void Solver::release() {
   void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, V, W, R, partA, partB, partC, alpha, beta, scal,
-                  ritz, bounds, zsel, Q, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
+                  ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   d_rowptr = d_col = nullptr;
   d_val64 = nullptr;
   d_val32 = nullptr;
-  V = W = R = partA = partB = partC = alpha = beta = scal = ritz = bounds = zsel = Q = Ytmp = cg_ws = nullptr;
+  V = W = R = partA = partB = partC = alpha = beta = scal = ritz = bounds = zsel = Q = rs_scratch = Ytmp = cg_ws = nullptr;
   cg_part = cg_scal = nullptr;
   cg_counter = nullptr;
   conv = state = cg_flags = nullptr;
@@ -166,6 +166,7 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
   LG_TRY(cudaMalloc(&bounds, sizeof(double) * kMaxCols));
   LG_TRY(cudaMalloc(&zsel, sizeof(double) * kMaxCols * kMaxCols));
   LG_TRY(cudaMalloc(&Q, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(cudaMalloc(&rs_scratch, sizeof(double) * restart_scratch_doubles()));
   LG_TRY(cudaMalloc(&conv, sizeof(int) * kMaxCols));
   LG_TRY(cudaMalloc(&state, sizeof(int) * ST_WORDS));
   LG_TRY(cudaMallocHost(&h_state, sizeof(int) * ST_WORDS));
@@ -364,6 +365,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ra.conv_out = conv;
     ra.zsel = zsel;
     ra.Q = Q;
+    ra.scratch = rs_scratch;
     ra.state = state;
     LG_TRY(timed(LG_K_RESTART, 0.0, 1, [&] { return restart_step(ra, stream); }));
     rc = sync_state();

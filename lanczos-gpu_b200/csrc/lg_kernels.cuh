@@ -87,9 +87,11 @@ struct RestartArgs {
   int* conv_out = nullptr;      // m: converged flag of each selected value
   double* zsel = nullptr;       // m x m col-major: eigenvectors of T for the selection
   double* Q = nullptr;          // m x m col-major: accumulated shift rotations
+  double* scratch = nullptr;    // restart_scratch_doubles(): LU factors of the inverse iterations
   int* state = nullptr;
 };
 enum Which { WHICH_LM = 0, WHICH_SM = 1, WHICH_LA = 2, WHICH_SA = 3, WHICH_BE = 4 };
+size_t restart_scratch_doubles();
 cudaError_t restart_step(const RestartArgs& a, cudaStream_t st);
 
 // Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq], V row-major n x ldv.

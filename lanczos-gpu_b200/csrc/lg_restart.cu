@@ -2,25 +2,29 @@
 //
 // Reference: src/irlm_lanczos.cu:225-363 (host loop: LAPACK dstev, convergence
 // test, NEV adjustment, exact shifts, bulge chase, H2D of Q) and
-// src/tridiag.cuh:33-124 (givens, apply_shifts_tridiag).  Here everything runs
-// in one CTA so the host never touches the tridiagonal:
+// src/tridiag.cuh:33-124 (givens, apply_shifts_tridiag).  Everything runs in
+// one CTA so the host never touches the tridiagonal, and every phase that can
+// be parallel is:
 //
 //   1. beta_m = ||r|| from the partial sums of the last Gram-Schmidt pass,
 //      DGKS / breakdown checks for the last step;
-//   2. Ritz values of T (m x m) by implicit symmetric QR with the Wilkinson
-//      shift (Golub & Van Loan, Alg. 8.3.2/8.3.3).  During restarts only the
-//      last row of the eigenvector matrix is needed (Ritz estimates), so
-//      thread 0 carries that one row through the rotations (as ARPACK's
-//      dstqrb does) and no barrier is taken per sweep;
-//   3. Ritz estimates |beta_m * z_last,i|, ARPACK-style ordering of the
-//      wanted end of the spectrum for which = LM/SM/LA/SA/BE, convergence
-//      test |bound| <= tol * max(eps^(2/3), |theta|), locking of zero
-//      bounds and the NEV adjustment of ARPACK's dsaup2;
-//   4. either (finished) the same QR is run again with full eigenvectors —
-//      thread 0 logs each sweep's rotations and every thread applies them to
-//      its own row of Z — and the wanted pairs are selected; or the np exact
-//      shifts are applied by bulge chases with deflation splitting (ARPACK
-//      dsapps), accumulating Q the same row-parallel way.
+//   2. Ritz values: bisection on Sturm counts, one thread per eigenvalue
+//      (all eigenvalues to ~eps*||T|| absolute accuracy, the accuracy of QR);
+//   3. eigenvectors of T: inverse iteration with a pivoted tridiagonal LU,
+//      one thread per eigenvalue, vectors of eigenvalue clusters
+//      (gap <= 1e-3 ||T||) re-orthogonalised in rounds (the method of LAPACK
+//      dstein);
+//   4. Ritz estimates |beta_m * z_last,i|, ARPACK-style ordering of the wanted
+//      end of the spectrum for which = LM/SM/LA/SA/BE, convergence test
+//      |bound| <= tol * max(eps^(2/3), |theta|), locking of zero bounds and
+//      the NEV adjustment of ARPACK's dsaup2;
+//   5. either the wanted pairs are selected (finished), or the np exact shifts
+//      are applied by bulge chasing.  Up to 32 bulges run at once, one lane
+//      each, three rows apart (rotations of neighbouring bulges then touch
+//      disjoint entries), and every thread applies the step's rotations to its
+//      own row of Q.  The result equals the shift-after-shift chase of the
+//      reference; the deflation splitting of ARPACK's dsapps is not done
+//      (a negligible coupling just makes the chase pass identity rotations).
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
 
@@ -42,98 +46,23 @@ __device__ __forceinline__ void givens(double a, double b, double& c, double& s)
     s = 0.0;
     return;
   }
-  double r2 = a * a + b * b;
-  double rh;
-  if (r2 >= kSafeMin && r2 < 1e300) {
-    rh = rsqrt(r2);
-  } else {
-    rh = 1.0 / hypot(a, b);
-  }
+  const double r2 = a * a + b * b;
+  const double rh = (r2 >= kSafeMin && r2 < 1e300) ? rsqrt(r2) : 1.0 / hypot(a, b);
   const double sg = (fabs(b) > fabs(a)) ? (b > 0.0 ? -1.0 : 1.0) : (a >= 0.0 ? 1.0 : -1.0);
   c = sg * a * rh;
   s = -sg * b * rh;
 }
 
-// One implicit QR sweep with shift sigma on the unreduced block [l, mm] of the
-// symmetric tridiagonal (d, e) (e[i] couples i and i+1).  Either logs the
-// rotations (lc/ls, rotation i acts on columns l+i, l+i+1) or applies them to
-// the single row z.  Single thread.
-template <bool LOG>
-__device__ void chase(double* d, double* e, int l, int mm, double sigma, double* lc, double* ls, double* z) {
-  double bulge = 0.0;
-  double dk = d[l], ek = e[l];
-  double za = LOG ? 0.0 : z[l];
-  for (int k = l; k < mm; ++k) {
-    double c, s;
-    if (k == l) {
-      givens(dk - sigma, ek, c, s);
-    } else {
-      givens(e[k - 1], bulge, c, s);
-      e[k - 1] = c * e[k - 1] - s * bulge;
-    }
-    const double dk1 = d[k + 1];
-    const double cc = c * c, ss = s * s, cs = c * s;
-    const double t2 = 2.0 * cs * ek;
-    d[k] = cc * dk - t2 + ss * dk1;
-    const double dnext = ss * dk + t2 + cc * dk1;
-    const double enew = cs * (dk - dk1) + (cc - ss) * ek;
-    e[k] = enew;
-    double enext = 0.0;
-    if (k + 1 < mm) {
-      const double ek1 = e[k + 1];
-      bulge = -s * ek1;
-      enext = c * ek1;
-      e[k + 1] = enext;
-    }
-    d[k + 1] = dnext;
-    dk = dnext;
-    ek = enext;
-    if (LOG) {
-      lc[k - l] = c;
-      ls[k - l] = s;
-    } else {
-      const double zb = z[k + 1];
-      z[k] = c * za - s * zb;
-      za = s * za + c * zb;
-    }
+// Number of eigenvalues of T below x (Sturm sequence of the LDL^T pivots).
+__device__ int sturm_count(const double* d, const double* e2, int m, double x, double pivmin) {
+  double q = d[0] - x;
+  int cnt = q < 0.0;
+  for (int k = 1; k < m; ++k) {
+    if (fabs(q) < pivmin) q = -pivmin;
+    q = (d[k] - x) - e2[k - 1] / q;
+    cnt += q < 0.0;
   }
-  if (!LOG) z[mm] = za;
-}
-
-// Apply logged rotations (columns k0.., consecutive) to row `row` of the
-// column-major m x m matrix M: M <- M * G_0 * G_1 * ...
-__device__ __forceinline__ void apply_log(double* M, int m, int row, int k0, int nrot, const double* lc,
-                                          const double* ls) {
-  double a = M[row + (size_t)k0 * m];
-  for (int i = 0; i < nrot; ++i) {
-    const int k = k0 + i;
-    const double b = M[row + (size_t)(k + 1) * m];
-    const double c = lc[i], s = ls[i];
-    M[row + (size_t)k * m] = c * a - s * b;
-    a = s * a + c * b;
-  }
-  M[row + (size_t)(k0 + nrot) * m] = a;
-}
-
-__device__ __forceinline__ bool negligible(double e, double da, double db) {
-  return e * e <= (kUnit * kUnit) * fabs(da) * fabs(db) + kSafeMin;
-}
-
-// Find the bottom unreduced block of (d, e) after zeroing negligible
-// couplings; returns false when T is diagonal.
-__device__ bool next_block(double* d, double* e, int m, int& l, int& mm, double& mu) {
-  for (int i = 0; i < m - 1; ++i)
-    if (e[i] != 0.0 && negligible(e[i], d[i], d[i + 1])) e[i] = 0.0;
-  mm = m - 1;
-  while (mm > 0 && e[mm - 1] == 0.0) --mm;
-  if (mm == 0) return false;
-  l = mm - 1;
-  while (l > 0 && e[l - 1] != 0.0) --l;
-  const double aa = d[mm - 1], cc = d[mm], bb = e[mm - 1];
-  const double delta = 0.5 * (aa - cc);
-  const double den = delta + copysign(hypot(delta, bb), delta == 0.0 ? 1.0 : delta);
-  mu = (den != 0.0) ? cc - bb * (bb / den) : cc - fabs(bb);
-  return true;
+  return cnt;
 }
 
 // Order (rz, bd, id) so that the nev wanted values are at the end
@@ -176,19 +105,96 @@ __device__ void sort_ascending(int lo, int hi, double* rz, double* bd, int* id) 
     }
 }
 
+// Inverse iteration for eigenvalue lam of the tridiagonal (d, e): a pivoted
+// LU of T - lam I (factors in the thread's slice of F, stride kRsThreads), three
+// solves from a pseudo-random start, each followed by re-orthogonalisation
+// against the `nprev` finished vectors Z[:, c0 .. c0+nprev) of the same
+// cluster and normalisation.  Result in column `col` of Z (m x m, col-major).
+__device__ void inverse_iteration(const double* d, const double* e, int m, double lam, double pivtiny, double* F,
+                                  double* Z, int col, int c0, int nprev) {
+  const int t = threadIdx.x;
+  double* u1 = F;                                  // [k * kRsThreads + t]
+  double* u2 = F + kMaxCols * kRsThreads;
+  double* u3 = F + 2 * kMaxCols * kRsThreads;
+  double* L = F + 3 * kMaxCols * kRsThreads;
+  uint64_t piv[2] = {0ull, 0ull};
+  double a = d[0] - lam, c = (m > 1) ? e[0] : 0.0;
+  for (int k = 0; k < m - 1; ++k) {
+    const double b = e[k], a1 = d[k + 1] - lam, c1 = (k + 1 < m - 1) ? e[k + 1] : 0.0;
+    const size_t ix = (size_t)k * kRsThreads + t;
+    if (fabs(a) >= fabs(b)) {
+      const double l = (a != 0.0) ? b / a : 0.0;
+      u1[ix] = a; u2[ix] = c; u3[ix] = 0.0; L[ix] = l;
+      a = a1 - l * c;
+      c = c1;
+    } else {
+      const double l = a / b;
+      piv[k >> 6] |= 1ull << (k & 63);
+      u1[ix] = b; u2[ix] = a1; u3[ix] = c1; L[ix] = l;
+      a = c - l * a1;
+      c = -l * c1;
+    }
+  }
+  u1[(size_t)(m - 1) * kRsThreads + t] = a;
+
+  double* x = Z + (size_t)col * m;
+  for (int k = 0; k < m; ++k) x[k] = uniform_centered(0x9E3779B97F4A7C15ull + col, (uint64_t)k) * 2.0;
+  for (int it = 0; it < 3; ++it) {
+    // forward: row interchanges and L
+    for (int k = 0; k < m - 1; ++k) {
+      const size_t ix = (size_t)k * kRsThreads + t;
+      if ((piv[k >> 6] >> (k & 63)) & 1ull) {
+        const double tmp = x[k];
+        x[k] = x[k + 1];
+        x[k + 1] = tmp;
+      }
+      x[k + 1] -= L[ix] * x[k];
+    }
+    // back substitution with U (diagonal perturbed away from zero)
+    for (int k = m - 1; k >= 0; --k) {
+      const size_t ix = (size_t)k * kRsThreads + t;
+      double p = u1[ix];
+      if (fabs(p) < pivtiny) p = (p < 0.0) ? -pivtiny : pivtiny;
+      double r = x[k];
+      if (k + 1 < m) r -= u2[ix] * x[k + 1];
+      if (k + 2 < m) r -= u3[ix] * x[k + 2];
+      x[k] = r / p;
+    }
+    // re-orthogonalise against the cluster's finished vectors, normalise
+    for (int q = 0; q < nprev; ++q) {
+      const double* zq = Z + (size_t)(c0 + q) * m;
+      double s = 0.0;
+      for (int k = 0; k < m; ++k) s += zq[k] * x[k];
+      for (int k = 0; k < m; ++k) x[k] -= s * zq[k];
+    }
+    double mx = 0.0;
+    for (int k = 0; k < m; ++k) mx = fmax(mx, fabs(x[k]));
+    if (!(mx > 0.0)) mx = 1.0;
+    double s2 = 0.0;
+    for (int k = 0; k < m; ++k) {
+      x[k] /= mx;
+      s2 += x[k] * x[k];
+    }
+    const double inv = 1.0 / sqrt(s2);
+    for (int k = 0; k < m; ++k) x[k] *= inv;
+  }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   int* state = a.state;
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   extern __shared__ __align__(16) double M[];   // m x m, column-major
-  __shared__ double d[kMaxCols], e[kMaxCols], zl[kMaxCols], lc[kMaxCols], ls[kMaxCols];
+  __shared__ double d[kMaxCols], e[kMaxCols], e2[kMaxCols], th[kMaxCols];
   __shared__ double rz[kMaxCols], bd[kMaxCols], shifts[kMaxCols];
-  __shared__ int id[kMaxCols];
-  __shared__ double sh_bn;
-  __shared__ int sh_stop, sh_fin, sh_k0, sh_nrot, sh_done, sh_nev, sh_np, sh_nconv;
+  __shared__ double rot_c[32], rot_s[32];
+  __shared__ int rot_k[32];
+  __shared__ int id[kMaxCols], cl[kMaxCols];
+  __shared__ double sh_bn, sh_glo, sh_ghi, sh_pivmin, sh_onenrm;
+  __shared__ int sh_stop, sh_done, sh_nev, sh_np, sh_nconv, sh_rounds;
 
-  const int t = threadIdx.x, m = a.m;
+  const int t = threadIdx.x, m = a.m, lane = t & 31;
 
   // ---- 1. residual norm and checks for the last step -----------------------
   if (t < 32) {
@@ -223,43 +229,78 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
       sh_stop = stop;
     }
   }
+  if (t < m) {
+    d[t] = a.alpha[t];
+    e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
+    e2[t] = e[t] * e[t];
+  }
   __syncthreads();
   if (sh_stop != STATUS_RUNNING) return;
   const double bn = sh_bn;
 
-  // ---- 2. Ritz values and the last row of the eigenvector matrix -----------
-  if (t < m) {
-    d[t] = a.alpha[t];
-    e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
-    zl[t] = (t == m - 1) ? 1.0 : 0.0;
-  }
-  __syncthreads();
+  // ---- 2. Ritz values by bisection ------------------------------------------
   if (t == 0) {
-    int fin = 1, sweeps = 0, l, mm;
-    double mu;
-    while (next_block(d, e, m, l, mm, mu)) {
-      if (++sweeps > 30 * m) { fin = 2; break; }
-      chase<false>(d, e, l, mm, mu, nullptr, nullptr, zl);
+    double glo = d[0], ghi = d[0], onenrm = 0.0, emax2 = 0.0, finite = 0.0;
+    for (int k = 0; k < m; ++k) {
+      const double off = (k > 0 ? fabs(e[k - 1]) : 0.0) + (k < m - 1 ? fabs(e[k]) : 0.0);
+      glo = fmin(glo, d[k] - off);
+      ghi = fmax(ghi, d[k] + off);
+      onenrm = fmax(onenrm, fabs(d[k]) + off);
+      emax2 = fmax(emax2, e2[k]);
+      finite += d[k] + off;
     }
-    sh_fin = fin;
+    const double pivmin = kSafeMin * fmax(1.0, emax2);
+    const double tnorm = fmax(fabs(glo), fabs(ghi));
+    sh_glo = glo - 2.0 * kUnit * tnorm * m - 2.0 * pivmin;
+    sh_ghi = ghi + 2.0 * kUnit * tnorm * m + 2.0 * pivmin;
+    sh_pivmin = pivmin;
+    sh_onenrm = isfinite(finite) ? onenrm : -1.0;
   }
   __syncthreads();
-  if (sh_fin == 2) {
+  if (!(sh_onenrm >= 0.0)) {
     if (t == 0) {
       state[ST_ERRINFO] = 1;
       state[ST_STATUS] = STATUS_TRIDIAG_FAIL;
     }
     return;
   }
+  if (t < m) {
+    double lo = sh_glo, hi = sh_ghi;
+    for (int it = 0; it < 128; ++it) {
+      const double mid = 0.5 * (lo + hi);
+      if (hi - lo <= 2.0 * kUnit * fmax(fabs(lo), fabs(hi)) + 4.0 * sh_pivmin || mid <= lo || mid >= hi) break;
+      if (sturm_count(d, e2, m, mid, sh_pivmin) > t) hi = mid;
+      else lo = mid;
+    }
+    th[t] = 0.5 * (lo + hi);
+  }
+  __syncthreads();
 
-  // ---- 3. ordering, Ritz estimates, convergence, NEV adjustment -------------
+  // ---- 3. eigenvectors by inverse iteration, clusters in rounds -------------
+  if (t == 0) {
+    const double ortol = 1e-3 * sh_onenrm;
+    int rounds = 1;
+    cl[0] = 0;
+    for (int i = 1; i < m; ++i) {
+      cl[i] = (th[i] - th[i - 1] > ortol) ? i : cl[i - 1];
+      rounds = max(rounds, i - cl[i] + 1);
+    }
+    sh_rounds = rounds;
+  }
+  __syncthreads();
+  const double pivtiny = kUnit * fmax(sh_onenrm, kSafeMin);
+  for (int r = 0; r < sh_rounds; ++r) {
+    if (t < m && t - cl[t] == r) inverse_iteration(d, e, m, th[t], pivtiny, a.scratch, M, t, cl[t], r);
+    __syncthreads();
+  }
+
+  // ---- 4. ordering, Ritz estimates, convergence, NEV adjustment -------------
   if (t == 0) {
     for (int i = 0; i < m; ++i) {
       id[i] = i;
-      rz[i] = d[i];
-      bd[i] = fabs(bn * zl[i]);
+      rz[i] = th[i];
+      bd[i] = fabs(bn * M[(m - 1) + (size_t)i * m]);
     }
-    sort_ascending(0, m, rz, bd, id);
     const double tol = a.tol > 0.0 ? a.tol : kUnit;
     int nev = a.nev0, np = m - a.nev0;
     order_wanted(a.which, m, nev, rz, bd, id);
@@ -296,32 +337,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   __syncthreads();
 
   if (sh_done) {
-    // ---- 4a. full eigenvectors (same QR again), wanted pairs ascending ----
+    // ---- 5a. wanted Ritz pairs, ascending ----------------------------------
     const int k = a.nev0, off = m - k;
-    if (t < m) {
-      d[t] = a.alpha[t];
-      e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
-    }
-    for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
-    __syncthreads();
-    for (;;) {
-      if (t == 0) {
-        int l, mm;
-        double mu;
-        if (next_block(d, e, m, l, mm, mu)) {
-          chase<true>(d, e, l, mm, mu, lc, ls, nullptr);
-          sh_k0 = l;
-          sh_nrot = mm - l;
-          sh_fin = 0;
-        } else {
-          sh_fin = 1;
-        }
-      }
-      __syncthreads();
-      if (sh_fin) break;
-      if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
-      __syncthreads();
-    }
     if (t == 0) {
       sort_ascending(off, m, rz, bd, id);
       const double tol = a.tol > 0.0 ? a.tol : kUnit;
@@ -341,39 +358,77 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
     return;
   }
 
-  // ---- 4b. exact shifts by bulge chasing (ARPACK dsapps) -------------------
+  // ---- 5b. exact shifts: pipelined bulge chases ------------------------------
+  // T first splits at negligible couplings (an invariant subspace met earlier
+  // leaves an exact zero); as in ARPACK's dsapps every shift is applied to
+  // every unreduced block.  Couplings that become negligible during the
+  // chases are left alone (the bulge then just passes identity rotations).
   const int np = sh_np, nev = sh_nev;
-  if (t < m) {
-    d[t] = a.alpha[t];
-    e[t] = (t < m - 1) ? a.beta[t + 1] : 0.0;
-  }
+  __shared__ int blk_lo[kMaxCols], blk_hi[kMaxCols];
+  __shared__ int sh_nblk;
+  __syncthreads();   // M (eigenvectors) no longer needed
   for (int i = t; i < m * m; i += kRsThreads) M[i] = ((i % m) == (i / m)) ? 1.0 : 0.0;
-  __shared__ int sh_is, sh_istart;
-  if (t == 0) { sh_is = 0; sh_istart = 0; }
-  __syncthreads();
-  for (;;) {
-    if (t == 0) {
-      int have = 0;
-      while (!have && sh_is < np) {
-        if (sh_istart >= m - 1) { ++sh_is; sh_istart = 0; continue; }
-        int iend = m - 1;
-        for (int i = sh_istart; i < m - 1; ++i) {
-          if (fabs(e[i]) <= kUnit * (fabs(d[i]) + fabs(d[i + 1]))) { e[i] = 0.0; iend = i; break; }
-        }
-        if (sh_istart < iend) {
-          chase<true>(d, e, sh_istart, iend, shifts[sh_is], lc, ls, nullptr);
-          sh_k0 = sh_istart;
-          sh_nrot = iend - sh_istart;
-          have = 1;
-        }
-        sh_istart = iend + 1;
+  if (t == 0) {
+    int nblk = 0, lo = 0;
+    for (int i = 0; i < m - 1; ++i) {
+      if (fabs(e[i]) <= kUnit * (fabs(d[i]) + fabs(d[i + 1]))) {
+        e[i] = 0.0;
+        if (i > lo) { blk_lo[nblk] = lo; blk_hi[nblk] = i; ++nblk; }
+        lo = i + 1;
       }
-      sh_fin = have ? 0 : 1;
     }
-    __syncthreads();
-    if (sh_fin) break;
-    if (t < m) apply_log(M, m, t, sh_k0, sh_nrot, lc, ls);
-    __syncthreads();
+    if (m - 1 > lo) { blk_lo[nblk] = lo; blk_hi[nblk] = m - 1; ++nblk; }
+    sh_nblk = nblk;
+  }
+  __syncthreads();
+  for (int ib = 0; ib < sh_nblk; ++ib) {
+    const int bs = blk_lo[ib], be = blk_hi[ib];   // block rows bs..be (be > bs)
+    for (int b0 = 0; b0 < np; b0 += 32) {
+      const int nb = min(32, np - b0);
+      const int steps = (be - bs) + 3 * (nb - 1);
+      double bulge = 0.0;                       // lane's bulge (warp 0)
+      const double sigma = (t < 32 && lane < nb) ? shifts[b0 + lane] : 0.0;
+      for (int st = 0; st < steps; ++st) {
+        if (t < 32) {
+          const int k = bs + st - 3 * lane;
+          int kk = -1;
+          if (lane < nb && k >= bs && k < be) {
+            double c, s;
+            if (k == bs) {
+              givens(d[bs] - sigma, e[bs], c, s);
+            } else {
+              givens(e[k - 1], bulge, c, s);
+              e[k - 1] = c * e[k - 1] - s * bulge;
+            }
+            const double dk = d[k], dk1 = d[k + 1], ek = e[k];
+            const double cc = c * c, ss = s * s, cs = c * s;
+            d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
+            d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
+            e[k] = cs * (dk - dk1) + (cc - ss) * ek;
+            if (k + 1 < be) {
+              bulge = -s * e[k + 1];
+              e[k + 1] = c * e[k + 1];
+            }
+            rot_c[lane] = c;
+            rot_s[lane] = s;
+            kk = k;
+          }
+          rot_k[lane] = kk;
+        }
+        __syncthreads();
+        if (t < m) {
+          for (int s = 0; s < nb; ++s) {
+            const int k = rot_k[s];
+            if (k < 0) continue;
+            const double c = rot_c[s], sn = rot_s[s];
+            const double x0 = M[t + (size_t)k * m], x1 = M[t + (size_t)(k + 1) * m];
+            M[t + (size_t)k * m] = c * x0 - sn * x1;
+            M[t + (size_t)(k + 1) * m] = sn * x0 + c * x1;
+          }
+        }
+        __syncthreads();
+      }
+    }
   }
   if (t == 0)
     for (int i = 0; i < m - 1; ++i)
@@ -396,6 +451,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
     state[ST_DONE] = 0;
   }
 }
+
+size_t restart_scratch_doubles() { return (size_t)4 * kMaxCols * kRsThreads; }
 
 cudaError_t restart_step(const RestartArgs& a, cudaStream_t st) {
   const size_t smem = (size_t)a.m * a.m * sizeof(double);

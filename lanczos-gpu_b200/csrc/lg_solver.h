@@ -62,6 +62,7 @@ class Solver {
   double* bounds = nullptr;
   double* zsel = nullptr;
   double* Q = nullptr;
+  double* rs_scratch = nullptr;
   int* conv = nullptr;
   int* state = nullptr;
   int* h_state = nullptr;
