@@ -120,6 +120,17 @@ int lg_eigsh_plan_factorize(lg_eigsh_plan* plan, const double* v0, int m, double
 /* y = A x with the plan's matrix (device pointers, n doubles each). */
 int lg_eigsh_plan_matvec(lg_eigsh_plan* plan, const double* x, double* y);
 
+/* Two classical Gram-Schmidt passes of w against the first ncols columns of a
+ * row-major basis V (n x ldv doubles on the device, 16-byte aligned, even ldv
+ * >= ncols):  h1 = V^T w, r1 = w - V h1, s = V^T r1, r = r1 - V s.
+ * Outputs on the device: r (n doubles, must not alias w), coef = h1 + s
+ * (ncols doubles), norms = {||w||, ||r1||, ||r||}.  Asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream).  1 <= ncols <= 128.
+ * Counterpart of cgs_orthogonalize + dgks_reorth
+ * (src/lanczos_ops.cuh:113-192), always with the second pass. */
+int lg_cgs2_orthogonalize(const double* V, int ldv, int n, int ncols, const double* w, double* r, double* coef,
+                          double* norms, void* stream);
+
 const char* lg_status_string(int status);
 /* Copies the last error message of the calling thread; returns its length. */
 int lg_last_error(char* buf, int len);

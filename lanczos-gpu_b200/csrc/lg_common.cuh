@@ -91,6 +91,38 @@ __device__ inline double block_sum(double v, double* scratch) {
 }
 
 // ---------------------------------------------------------------------------
+// Partial-sum rows (one per CTA, kPartStride doubles: columns then scalars)
+// ---------------------------------------------------------------------------
+// Reduce `nrows` partial rows: columns [0, nc) into out[0..nc), the scalar
+// slot into *scal_out.  Every thread of the block gets the same values.
+// `red` needs blockDim.x doubles; blockDim.x must be a multiple of 128.
+__device__ inline void reduce_partials(const double* __restrict__ part, int nrows, int nc, double* out,
+                                double* scal_out, double* red) {
+  const int t = threadIdx.x;
+  const int ngrp = blockDim.x >> 7;
+  const int slot = t & 127, grp = t >> 7;
+  double acc = 0.0;
+  if (slot < nc) {
+#pragma unroll 4
+    for (int r = grp; r < nrows; r += ngrp) acc += part[(size_t)r * kPartStride + slot];
+  }
+  red[grp * 128 + slot] = acc;
+  double sc = 0.0;
+  if (t < 32) {
+    for (int r = t; r < nrows; r += 32) sc += part[(size_t)r * kPartStride + kPartScalar];
+    sc = warp_sum(sc);
+  }
+  __syncthreads();
+  if (t < nc) {
+    double s = 0.0;
+    for (int g = 0; g < ngrp; ++g) s += red[g * 128 + t];
+    out[t] = s;
+  }
+  if (t == 0) *scal_out = sc;
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
 // Safe scaling (two-step when the norm is below SAFE_MIN; the reference does
 // the same with two Dscal calls, src/lanczos_ops.cuh:204-216).
 // x * s1 * s2 where s2 == 1 in the normal case.

@@ -30,35 +30,6 @@ namespace lg {
 
 constexpr int kGsWarps = kGsThreads / 32;
 
-// Reduce `nrows` partial rows: columns [0, nc) into out[0..nc), the scalar
-// slot into *scal_out.  Every thread of the block gets the same values.
-// `red` needs blockDim.x doubles; blockDim.x must be a multiple of 128.
-__device__ void reduce_partials(const double* __restrict__ part, int nrows, int nc, double* out,
-                                double* scal_out, double* red) {
-  const int t = threadIdx.x;
-  const int ngrp = blockDim.x >> 7;
-  const int slot = t & 127, grp = t >> 7;
-  double acc = 0.0;
-  if (slot < nc) {
-#pragma unroll 4
-    for (int r = grp; r < nrows; r += ngrp) acc += part[(size_t)r * kPartStride + slot];
-  }
-  red[grp * 128 + slot] = acc;
-  double sc = 0.0;
-  if (t < 32) {
-    for (int r = t; r < nrows; r += 32) sc += part[(size_t)r * kPartStride + kPartScalar];
-    sc = warp_sum(sc);
-  }
-  __syncthreads();
-  if (t < nc) {
-    double s = 0.0;
-    for (int g = 0; g < ngrp; ++g) s += red[g * 128 + t];
-    out[t] = s;
-  }
-  if (t == 0) *scal_out = sc;
-  __syncthreads();
-}
-
 namespace {
 
 __device__ __forceinline__ double2 ld_stream(const double* p) {
@@ -107,11 +78,12 @@ gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double*
   }
 
   double2 cf[CH];
-  bool live[CH];
+  bool live[CH], pair[CH];   // pair: the second column of the lane's 16-byte chunk is live too
 #pragma unroll
   for (int ch = 0; ch < CH; ++ch) {
     const int c0 = ch * 2 * LPR + 2 * sub;
     live[ch] = c0 < ncols;
+    pair[ch] = c0 + 1 < ncols;
     cf[ch] = make_double2(coef[c0], coef[c0 + 1]);
   }
   double2 acc[CH];
@@ -134,8 +106,10 @@ gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double*
       const bool ok = r < re;
       const double* row = V + r * ldv;
 #pragma unroll
-      for (int ch = 0; ch < CH; ++ch)
+      for (int ch = 0; ch < CH; ++ch) {
         v[u][ch] = (ok && live[ch]) ? ld_stream(row + ch * 2 * LPR + 2 * sub) : make_double2(0.0, 0.0);
+        if (!pair[ch]) v[u][ch].y = 0.0;   // padding column: never let its contents in
+      }
       x[u] = ok ? (MODE == 3 ? Rout[r] : vec[r]) : 0.0;
     }
 #pragma unroll

@@ -17,9 +17,6 @@ struct GsPlan {
 
 GsPlan gs_plan(int n, int ncols, int grid);
 
-__device__ void reduce_partials(const double* part, int nrows, int nc, double* out, double* scal_out,
-                                double* red);
-
 cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                        const double* vec, double* part_out, int* state);
 cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,

@@ -88,6 +88,8 @@ SIGNATURES = {
     "lg_eigsh_plan_factorize": (C.c_int, [C.c_void_p, _PD, C.c_int, _PD, _PD]),
     "lg_eigsh": (C.c_int, [C.c_int, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(EigshOpts),
                            C.c_void_p, _PD, C.c_void_p, C.POINTER(EigshInfo)]),
+    "lg_cgs2_orthogonalize": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_status_string": (C.c_char_p, [C.c_int]),
     "lg_last_error": (C.c_int, [C.c_char_p, C.c_int]),
     "compute_eigsh": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double, _PD,
