@@ -131,6 +131,18 @@ int lg_eigsh_plan_matvec(lg_eigsh_plan* plan, const double* x, double* y);
 int lg_cgs2_orthogonalize(const double* V, int ldv, int n, int ncols, const double* w, double* r, double* coef,
                           double* norms, void* stream);
 
+/* Same contract and results as lg_cgs2_orthogonalize, for callers that must
+ * not allocate device memory (e.g. code running inside a device allocator or
+ * memory-pool hook, or a service whose device memory budget is fixed at
+ * start-up): no cudaMalloc/cudaFree or other allocating call is made.  The
+ * workspace is a fixed 0.5 MiB device array inside the library that every GPU
+ * loading it keeps until exit; 1 <= ncols <= 128.  The first call on a device
+ * resolves the array's address (make it before capturing any stream).  All
+ * calls share the array: calls that overlap on the GPU race, so order them on
+ * one stream.  This entry point has no counterpart in the reference. */
+int lg_cgs2_orthogonalize_noalloc(const double* V, int ldv, int n, int ncols, const double* w, double* r,
+                                  double* coef, double* norms, void* stream);
+
 const char* lg_status_string(int status);
 /* Copies the last error message of the calling thread; returns its length. */
 int lg_last_error(char* buf, int len);

@@ -90,6 +90,8 @@ SIGNATURES = {
                            C.c_void_p, _PD, C.c_void_p, C.POINTER(EigshInfo)]),
     "lg_cgs2_orthogonalize": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_void_p]),
+    "lg_cgs2_orthogonalize_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_status_string": (C.c_char_p, [C.c_int]),
     "lg_last_error": (C.c_int, [C.c_char_p, C.c_int]),
     "compute_eigsh": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double, _PD,
