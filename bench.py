@@ -17,9 +17,18 @@ needed between steps.
 With N GPUs (torchrun), every rank solves its own copy (replicas, weak
 scaling); value = all ranks' Lanczos steps / max-over-ranks time.
 
+The same line carries an "slq" object for the second half of the metric,
+"SLQ logdet+grad sec" (configuration 3): slq_logdet of the IMGP precision
+operator (nu = 2, theta = kappa = 1) on the undirected edges of the same kNN
+graph, fp32, 64 Rademacher probes (seed 0), lanczos_m = 30, forward plus the
+Kraemer backward for d/dtheta and d/dkappa.  One SLQ step = one log-det and
+its gradient through the public API (operator built once, probes resident,
+as in a training loop); the probe blocks (n x 64 fp32 = 256 MB) exceed L2.
+
 --impl reference times the reference's algorithm on the host cores: the CPU
 oracle (C restatement of the reference IRLM, OpenMP over all cores) running
-the initial 60-step Lanczos factorisation of the same matrix per step.
+the initial 60-step Lanczos factorisation of the same matrix per step, and the
+reference's torch SLQ algorithm (oracle/slq.py) on a bounded sample.
 """
 from __future__ import annotations
 
@@ -137,6 +146,151 @@ def cpu_baseline(L, v0, budget_s=20.0):
                       f"as the reference, n=1e6 config-1 matrix) in {el:.1f} s"}
 
 
+SLQ_PROBES, SLQ_M, SLQ_NU = 64, 30, 2
+SLQ_WORKLOAD = (f"slq_logdet of P = (2nu/theta^2 I + L_sym(kappa))^nu, nu={SLQ_NU}, theta=kappa=1, on the undirected "
+                f"edges of the n=1e6 config-1 kNN graph, fp32, m_probes={SLQ_PROBES} (seed 0), lanczos_m={SLQ_M}, "
+                "forward + Kraemer backward for d/dtheta, d/dkappa")
+
+
+def slq_bytes(n, nnz, B, nu, m, es):
+    """Algorithmic DRAM bytes of one fused SLQ forward and backward (blocks of
+    n x ld, each row read or written once; CSR once per sparse product)."""
+    ld = B + (B & 1)
+    blk = n * ld * es
+    csr = 8 * nnz + 8 * n                      # col + value per entry, rowptr + diag per row
+    dcsr = 12 * nnz + 12 * n                   # with the d/dkappa values
+    if nu == 1:
+        fwd_step = (3 * blk + csr) + 4 * blk
+    else:
+        fwd_step = (3 * blk + csr) + (nu - 2) * (2 * blk + csr) + (4 * blk + csr)
+    fwd = m * fwd_step + 2 * blk                # + ||z|| pass and the final normalisation
+    bwd_step = 4 * blk + (nu - 1) * (3 * blk + dcsr) + (7 * blk + dcsr)
+    return fwd, m * bwd_step
+
+
+def slq_edges(n=N_POINTS):
+    from gpu_eigsh import synthetic as syn
+
+    return syn.knn_edge_list(n, k=10, seed=1)
+
+
+def slq_cpu_baseline(idx, d2, n=N_POINTS, m_full=SLQ_M):
+    """The oracle (the reference's torch algorithm on the host cores) on a
+    bounded sample: the full workload (all probes, same graph) at Lanczos depth
+    1 and 2; the cost is affine in the depth (no re-orthogonalisation), so the
+    two timings extrapolate to depth SLQ_M."""
+    import torch
+    from oracle import slq as oslq
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    it, dt = torch.from_numpy(idx), torch.from_numpy(d2).to(torch.float32)
+    t = []
+    for m in (1, 2):
+        mv = oslq.make_precision_matvec(dt, it, n, SLQ_NU)
+        e = torch.tensor(1.0, dtype=torch.float32, requires_grad=True)
+        k = torch.tensor(1.0, dtype=torch.float32, requires_grad=True)
+        t0 = time.perf_counter()
+        ld = oslq.slq_logdet(mv, n, (e, k), m_probes=SLQ_PROBES, lanczos_m=m, seed=0, dtype=torch.float32)
+        ld.backward()
+        t.append(time.perf_counter() - t0)
+    per_step = t[1] - t[0]
+    est = t[0] + (m_full - 1) * per_step
+    return {"value": est, "unit": "s/logdet+grad", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle (reference torch algorithm) forward+backward, all {SLQ_PROBES} probes on the same "
+                      f"graph at lanczos_m=1 ({t[0]:.1f} s) and 2 ({t[1]:.1f} s), extrapolated linearly to "
+                      f"lanczos_m={m_full}"}
+
+
+def run_slq(args, dev, with_e2e, with_cpu):
+    import torch
+
+    from gpu_eigsh.funm_torch import slq_logdet
+    from gpu_eigsh.imgp import make_imgp_precision_matvec
+
+    n, M = args.slq_n, args.slq_m
+    idx, d2 = slq_edges(n)
+    mv = make_imgp_precision_matvec(x_edge_dists=torch.from_numpy(d2).to(dev, torch.float32),
+                                    idx=torch.from_numpy(idx).to(dev), operator_dim=n, nu=SLQ_NU)
+    ell = torch.tensor(1.0, dtype=torch.float32, device=dev, requires_grad=True)
+    kap = torch.tensor(1.0, dtype=torch.float32, device=dev, requires_grad=True)
+
+    def step(e, k, device):
+        e.grad = None
+        k.grad = None
+        ld = slq_logdet(mv, n, (e, k), m_probes=SLQ_PROBES, lanczos_m=M, seed=0, dtype=torch.float32,
+                        device=device)
+        ld.backward()
+        return ld
+
+    for _ in range(args.warmup):
+        step(ell, kap, dev)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        ld = step(ell, kap, dev)
+    ev1.record()
+    torch.cuda.synchronize()
+    sec = ev0.elapsed_time(ev1) / 1000.0 / args.steps
+    out = {"workload": SLQ_WORKLOAD if (n, M) == (N_POINTS, SLQ_M) else f"reduced: n={n}, lanczos_m={M}", "metric": "slq_logdet_grad_sec", "value": sec, "unit": "s/logdet+grad",
+           "higher_is_better": False, "n": n, "edges": int(idx.shape[1]), "csr_nnz": mv.nnz,
+           "logdet": float(ld.detach()), "grad_theta": float(ell.grad), "grad_kappa": float(kap.grad)}
+
+    # roofline: the fused forward (nu sparse products per step, recurrence
+    # folded in) and backward, timed alone with events on the launch stream
+    op = mv.operator(1.0, 1.0)
+    Z, B = None, SLQ_PROBES
+    from gpu_eigsh.funm_torch import _probes
+
+    Z = _probes(n, SLQ_PROBES, 0, torch.float32, dev)
+    fwd_b, bwd_b = slq_bytes(n, mv.nnz, B, SLQ_NU, M, 4)
+    tf, tb = [], []
+    for r in range(3):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        V, Y, al, be, zn = op.forward(Z, B, B + (B & 1), M)
+        e1.record()
+        from gpu_eigsh import _slq
+
+        q, ga, gb, _ = _slq.small_side(al, be, zn, "log", 0, g_scale=1.0 / B)
+        e2b = torch.cuda.Event(enable_timing=True)
+        e2b.record()
+        op.backward(V, Y, al, be, ga, gb, None, B, B + (B & 1), M)
+        e2.record()
+        torch.cuda.synchronize()
+        if r:
+            tf.append(e0.elapsed_time(e1))
+            tb.append(e2b.elapsed_time(e2))
+        del V, Y
+    peak, peak_kind = measured_peaks()
+    f_ms, b_ms = statistics.median(tf), statistics.median(tb)
+    fa, ba = fwd_b / (f_ms / 1000) / 1e9, bwd_b / (b_ms / 1000) / 1e9
+    dom = ("slq_backward", ba, b_ms, bwd_b) if b_ms >= f_ms else ("slq_forward", fa, f_ms, fwd_b)
+    out["roofline"] = {"bound": "hbm", "kernel": dom[0], "achieved": dom[1], "peak": peak, "unit": "GB/s",
+                       "frac": dom[1] / peak, "peak_source": peak_kind, "traffic": None,
+                       "algorithmic_bytes_per_launch": dom[3], "avg_launch_ms": dom[2]}
+    out["phases"] = {"forward_ms": f_ms, "forward_GBs": fa, "forward_frac": fa / peak, "forward_bytes": fwd_b,
+                     "backward_ms": b_ms, "backward_GBs": ba, "backward_frac": ba / peak, "backward_bytes": bwd_b}
+    nu = SLQ_NU
+    out["gpu_launches_per_step"] = (1 + M * nu + 1) + 1 + (M * (1 + nu) + 1)
+
+    if with_e2e:
+        # through the public API with host parameters: lengthscale and bandwidth
+        # live on the host, the log-det and both gradients come back to it
+        e_h = torch.tensor(1.0, dtype=torch.float32, requires_grad=True)
+        k_h = torch.tensor(1.0, dtype=torch.float32, requires_grad=True)
+        step(e_h, k_h, "cpu")
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(e_h, k_h, "cpu")
+        el = (time.perf_counter() - t0) / args.steps
+        out["e2e"] = {"value": el, "unit": "s/logdet+grad", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 12,
+                      "note": "operator and probes stay resident across steps (built once, as in a training loop)"}
+    if with_cpu:
+        out["cpu_baseline"] = slq_cpu_baseline(idx, d2, n, M)
+    return out
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -165,6 +319,14 @@ def run_reference(args):
                          "sample": f"{args.steps} x {NCV} Lanczos steps of the config-1 matrix on {cores} threads"},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_slq:
+        del L
+        idx, d2 = slq_edges()
+        cb = slq_cpu_baseline(idx, d2)
+        line["slq"] = {"workload": SLQ_WORKLOAD, "metric": "slq_logdet_grad_sec", "value": cb["value"],
+                       "unit": cb["unit"], "higher_is_better": False, "cpu_baseline": cb,
+                       "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                               "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -183,6 +345,11 @@ def run_ours(args):
 
     import gpu_eigsh
 
+    if args.only_slq:
+        out = run_slq(args, torch.device("cuda", local), with_e2e=False, with_cpu=False)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return 0
     L, v0, winfo = build_workload()
     n = L.shape[0]
     dev = torch.device("cuda", local)
@@ -283,6 +450,11 @@ def run_ours(args):
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(L, v0)
     plan.close()
+    del L
+    if not args.no_slq:
+        line["slq"] = run_slq(args, dev, with_e2e=(rank == 0 and not args.no_e2e),
+                              with_cpu=(rank == 0 and not args.no_cpu_baseline))
+        line["gpu_launches"] += line["slq"]["gpu_launches_per_step"] * args.steps
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -300,6 +472,10 @@ def main():
     ap.add_argument("--mixed", action="store_true", help="fp32 matrix values, fp64 accumulation")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-slq", action="store_true", help="skip the SLQ log-det + gradient leg")
+    ap.add_argument("--only-slq", action="store_true", help="run the SLQ leg alone (no eigsh)")
+    ap.add_argument("--slq-n", type=int, default=N_POINTS, help="SLQ graph size (reduced cases for profiling)")
+    ap.add_argument("--slq-m", type=int, default=SLQ_M, help="SLQ Lanczos depth (reduced cases for profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

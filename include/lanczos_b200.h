@@ -143,6 +143,136 @@ int lg_cgs2_orthogonalize(const double* V, int ldv, int n, int ncols, const doub
 int lg_cgs2_orthogonalize_noalloc(const double* V, int ldv, int n, int ncols, const double* w, double* r,
                                   double* coef, double* norms, void* stream);
 
+/* ---- stochastic Lanczos quadrature (SLQ) and the Kraemer adjoint ---------
+ *
+ * All pointers are device pointers; every call is asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) and allocates nothing.
+ *
+ * Blocks of probe vectors are n x ld row-major arrays of the operator's
+ * element type (LG_F32 / LG_F64), ld even, 8-byte (fp32) or 16-byte (fp64)
+ * aligned; columns [0, B) are the probes, 1 <= B <= 128.  When B is odd,
+ * column B is padding: it is read as zero and written as zero.  Reductions
+ * accumulate in fp64 and are bitwise repeatable.  Per-probe scalars (alpha,
+ * beta, g_alpha, g_beta: B x m row-major; znorm: B) are fp64.
+ *
+ * `ws` is a 256-byte aligned device workspace of at least
+ * lg_slq_workspace_bytes(op, B, ld) bytes (op = NULL: the size for the
+ * lg_slq_small_side / lg_slq_block_* calls alone).  Calls sharing a workspace
+ * must be ordered on one stream.
+ */
+enum { LG_F32 = 0, LG_F64 = 1 };
+enum { LG_FUNC_LOG = 0, LG_FUNC_EXP = 1, LG_FUNC_SQRT = 2, LG_FUNC_INV = 3 };
+
+/* P = A^power with A = shift I + L; L symmetric, given as its diagonal and its
+ * off-diagonal entries in CSR (every off-diagonal pair stored both ways).
+ * ddiag / doffval: dL/dq for one scalar parameter q of L (NULL: no q).
+ * The IMGP precision operator (python/gpu_eigsh/imgp.py:234-289) is
+ * shift = 2 nu / lengthscale^2, L = L_sym(graphbandwidth), power = nu. */
+typedef struct lg_slq_op {
+  int n;
+  long long nnz;          /* off-diagonal entries, < 2^31 */
+  const int* rowptr;      /* n + 1 */
+  const int* col;         /* nnz */
+  const void* offval;     /* nnz */
+  const void* diag;       /* n */
+  const void* doffval;    /* nnz or NULL */
+  const void* ddiag;      /* n or NULL */
+  double shift;
+  int power;              /* 1 .. 8 */
+  int dtype;              /* LG_F32 or LG_F64 */
+} lg_slq_op;
+
+size_t lg_slq_workspace_bytes(const lg_slq_op* op, int B, int ld);
+
+/* Batched three-term Lanczos without re-orthogonalisation of B probe columns
+ * of Z through P, m steps: V holds m+1 blocks (v_0 .. v_m, block stride n*ld),
+ * Y holds m*(power-1) blocks A^p v_j (j-major; NULL when power = 1), kept for
+ * lg_slq_backward; alpha/beta (B x m) the tridiagonals (beta[:, m-1] is the
+ * final residual norm), znorm the column norms of Z.
+ * Replaces lanczos_torch_noreortho_batched (python/gpu_eigsh/funm_torch.py:120-173)
+ * on the operator of python/gpu_eigsh/imgp.py:234-289. */
+int lg_slq_forward(const lg_slq_op* op, int B, int m, int ld, const void* Z, void* V, void* Y, double* alpha,
+                   double* beta, double* znorm, void* ws, size_t ws_bytes, void* stream);
+
+/* Kraemer reverse sweep of the batched recurrence for a scalar loss with
+ * gradient *g_out * (g_alpha, g_beta) with respect to (alpha, beta):
+ * g_params[0] = d loss / dq (through ddiag/doffval; 0 without them),
+ * g_params[1] = d loss / d shift.  g_out may be NULL (= 1).
+ * Replaces the sweep of _SLQLogdetBatched.backward
+ * (python/gpu_eigsh/funm_torch.py:681-727) with the parameter VJP formed
+ * inside the sparse products instead of by autograd through the matvec. */
+int lg_slq_backward(const lg_slq_op* op, int B, int m, int ld, const void* V, const void* Y, const double* alpha,
+                    const double* beta, const double* g_alpha, const double* g_beta, const double* g_out,
+                    double* g_params, void* ws, size_t ws_bytes, void* stream);
+
+/* Y = P X (B columns).  Replaces the precision matvec of
+ * make_imgp_precision_matvec (python/gpu_eigsh/imgp.py:279-287). */
+int lg_slq_apply(const lg_slq_op* op, int B, int ld, const void* X, void* Y, void* ws, size_t ws_bytes,
+                 void* stream);
+
+/* VJP of Y = P X for the cotangent G: gX = P G, g_params[0] = sum <G, (dP/dq) X>,
+ * g_params[1] = sum <G, (dP/dshift) X>. */
+int lg_slq_apply_vjp(const lg_slq_op* op, int B, int ld, const void* X, const void* G, void* gX,
+                     double* g_params, void* ws, size_t ws_bytes, void* stream);
+
+/* Small side of every probe b (T_b = tridiag(alpha[b, :], beta[b, :m-1]),
+ * f = LG_FUNC_*):
+ *   mode 0: out[b] = znorm[b]^2 e1^T f(T_b) e1, g_alpha/g_beta = g_scale * its gradient;
+ *   mode 1: out[b*m .. b*m+m) = f(T_b) e1;
+ *   mode 2: g_alpha/g_beta = g_scale * gradient of <gu[b, :], f(T_b) e1>.
+ * *status becomes nonzero when a T_b holds non-finite values (outputs NaN).
+ * Replaces the eigh-based small side of python/gpu_eigsh/funm_torch.py:62-76,
+ * 595-607 and its autograd (:634-660). */
+int lg_slq_small_side(int B, int m, int func, int mode, const double* alpha, const double* beta,
+                      const double* znorm, const double* gu, double g_scale, double* out, double* g_alpha,
+                      double* g_beta, int* status, void* ws, size_t ws_bytes, void* stream);
+
+/* Recurrence and reverse-sweep steps around a product P x formed by the
+ * caller (any operator the caller can apply):
+ *   block_start:  V0 = Z / ||Z|| per column, znorm = ||Z||;
+ *   block_step:   given W = P v_j: alpha_j = <v_j, W>, R = W - alpha_j v_j -
+ *                 beta_{j-1} v_{j-1}, beta_j = ||R||, Vnext = R / beta_j;
+ *   block_lambda: lambda of step j (xi = NULL starts the sweep at j = m-1);
+ *   block_xi:     given Plam = P lambda: xi of step j-1, i.e.
+ *                 -dcoef[b] G[:, b] - Plam + alpha_j lambda + beta_j lplus -
+ *                 beta_j nu_j xplus (dcoef, G optional; lplus NULL at j = m-1;
+ *                 xjm1 NULL at j = 0);
+ *   block_start_grad: gZ = (<xi, V0> V0 - xi) / znorm + g_znorm * Z / znorm.
+ * The workspace carries column sums from block_xi to the next block_lambda.
+ * Same arithmetic as lanczos_torch_noreortho(_batched) and the Kraemer sweeps
+ * of python/gpu_eigsh/funm_torch.py:83-173, 317-365, 681-727, 503-560. */
+int lg_slq_block_start(int n, int B, int ld, int dtype, const void* Z, void* V0, double* znorm, void* ws,
+                       size_t ws_bytes, void* stream);
+int lg_slq_block_step(int n, int B, int ld, int dtype, int j, int m, const void* W, const void* Vj,
+                      const void* Vjm1, void* R, void* Vnext, double* alpha, double* beta, void* ws,
+                      size_t ws_bytes, void* stream);
+int lg_slq_block_lambda(int n, int B, int ld, int dtype, int j, int m, const void* xi, const void* xplus,
+                        const void* xj, const double* beta, const double* g_alpha, const double* g_beta,
+                        const double* g_out, void* lam, void* ws, size_t ws_bytes, void* stream);
+int lg_slq_block_xi(int n, int B, int ld, int dtype, int j, int m, const void* Plam, const void* lam,
+                    const void* lplus, const void* xplus, const void* xj, const void* xjm1, const double* alpha,
+                    const double* beta, const double* dcoef, const void* G, void* xi, void* ws, size_t ws_bytes,
+                    void* stream);
+int lg_slq_block_start_grad(int n, int B, int ld, int dtype, const void* xi, const void* V0, const void* Z,
+                            const double* znorm, const double* g_znorm, void* gZ, void* ws, size_t ws_bytes,
+                            void* stream);
+
+/* The IMGP graph Laplacian L_sym(graphbandwidth) (symmetric normalisation,
+ * optional self loops) in the order of a CSR that stores every edge in both
+ * directions: d2 holds the squared edge distance of every CSR entry; outputs
+ * offval (nnz), diag (n) and, when doffval/ddiag are not NULL, dL/d
+ * graphbandwidth.  work: 4n doubles of device scratch.
+ * Replaces _build_laplacian_cache (python/gpu_eigsh/imgp.py:142-189). */
+int lg_imgp_laplacian(int n, long long nnz, const int* rowptr, const int* col, int dtype, const void* d2,
+                      double graphbandwidth, int self_loops, void* offval, void* diag, void* doffval, void* ddiag,
+                      double* work, void* stream);
+
+/* y = A x for a dense row-major n x n A (vectors with element strides ldx, ldy),
+ * and gA += lam x^T (fp64 gA, vectors with element stride ld): the dense-matrix
+ * operations of funm_apply_kraemer (python/gpu_eigsh/funm_torch.py:284, 347). */
+int lg_dense_matvec(int n, int dtype, const void* A, const void* x, int ldx, void* y, int ldy, void* stream);
+int lg_outer_accumulate(int n, int dtype, const void* lam, const void* x, int ld, double* gA, void* stream);
+
 const char* lg_status_string(int status);
 /* Copies the last error message of the calling thread; returns its length. */
 int lg_last_error(char* buf, int len);

@@ -27,6 +27,7 @@
 //      (a negligible coupling just makes the chase pass identity rotations).
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
+#include "lg_tridiag.cuh"
 
 #include <cmath>
 
@@ -37,33 +38,6 @@ namespace {
 constexpr int kRsThreads = 128;
 constexpr double kUnit = 1.1102230246251565e-16;        // 2^-53
 constexpr double kEps23Arpack = 2.3112508282095347e-11;  // (2^-53)^(2/3)
-
-// [c -s; s c] [a; b] = [r; 0]; same signs as the classical formulation
-// (tau = -a/b or -b/a, Golub & Van Loan 5.1.3) with one reciprocal sqrt.
-__device__ __forceinline__ void givens(double a, double b, double& c, double& s) {
-  if (b == 0.0) {
-    c = 1.0;
-    s = 0.0;
-    return;
-  }
-  const double r2 = a * a + b * b;
-  const double rh = (r2 >= kSafeMin && r2 < 1e300) ? rsqrt(r2) : 1.0 / hypot(a, b);
-  const double sg = (fabs(b) > fabs(a)) ? (b > 0.0 ? -1.0 : 1.0) : (a >= 0.0 ? 1.0 : -1.0);
-  c = sg * a * rh;
-  s = -sg * b * rh;
-}
-
-// Number of eigenvalues of T below x (Sturm sequence of the LDL^T pivots).
-__device__ int sturm_count(const double* d, const double* e2, int m, double x, double pivmin) {
-  double q = d[0] - x;
-  int cnt = q < 0.0;
-  for (int k = 1; k < m; ++k) {
-    if (fabs(q) < pivmin) q = -pivmin;
-    q = (d[k] - x) - e2[k - 1] / q;
-    cnt += q < 0.0;
-  }
-  return cnt;
-}
 
 // Order (rz, bd, id) so that the nev wanted values are at the end
 // (ARPACK dsgets restated: LA ascending, SA descending, LM ascending |x|,
@@ -105,81 +79,6 @@ __device__ void sort_ascending(int lo, int hi, double* rz, double* bd, int* id) 
     }
 }
 
-// Inverse iteration for eigenvalue lam of the tridiagonal (d, e): a pivoted
-// LU of T - lam I (factors in the thread's slice of F, stride kRsThreads), three
-// solves from a pseudo-random start, each followed by re-orthogonalisation
-// against the `nprev` finished vectors Z[:, c0 .. c0+nprev) of the same
-// cluster and normalisation.  Result in column `col` of Z (m x m, col-major).
-__device__ void inverse_iteration(const double* d, const double* e, int m, double lam, double pivtiny, double* F,
-                                  double* Z, int col, int c0, int nprev) {
-  const int t = threadIdx.x;
-  double* u1 = F;                                  // [k * kRsThreads + t]
-  double* u2 = F + kMaxCols * kRsThreads;
-  double* u3 = F + 2 * kMaxCols * kRsThreads;
-  double* L = F + 3 * kMaxCols * kRsThreads;
-  uint64_t piv[2] = {0ull, 0ull};
-  double a = d[0] - lam, c = (m > 1) ? e[0] : 0.0;
-  for (int k = 0; k < m - 1; ++k) {
-    const double b = e[k], a1 = d[k + 1] - lam, c1 = (k + 1 < m - 1) ? e[k + 1] : 0.0;
-    const size_t ix = (size_t)k * kRsThreads + t;
-    if (fabs(a) >= fabs(b)) {
-      const double l = (a != 0.0) ? b / a : 0.0;
-      u1[ix] = a; u2[ix] = c; u3[ix] = 0.0; L[ix] = l;
-      a = a1 - l * c;
-      c = c1;
-    } else {
-      const double l = a / b;
-      piv[k >> 6] |= 1ull << (k & 63);
-      u1[ix] = b; u2[ix] = a1; u3[ix] = c1; L[ix] = l;
-      a = c - l * a1;
-      c = -l * c1;
-    }
-  }
-  u1[(size_t)(m - 1) * kRsThreads + t] = a;
-
-  double* x = Z + (size_t)col * m;
-  for (int k = 0; k < m; ++k) x[k] = uniform_centered(0x9E3779B97F4A7C15ull + col, (uint64_t)k) * 2.0;
-  for (int it = 0; it < 3; ++it) {
-    // forward: row interchanges and L
-    for (int k = 0; k < m - 1; ++k) {
-      const size_t ix = (size_t)k * kRsThreads + t;
-      if ((piv[k >> 6] >> (k & 63)) & 1ull) {
-        const double tmp = x[k];
-        x[k] = x[k + 1];
-        x[k + 1] = tmp;
-      }
-      x[k + 1] -= L[ix] * x[k];
-    }
-    // back substitution with U (diagonal perturbed away from zero)
-    for (int k = m - 1; k >= 0; --k) {
-      const size_t ix = (size_t)k * kRsThreads + t;
-      double p = u1[ix];
-      if (fabs(p) < pivtiny) p = (p < 0.0) ? -pivtiny : pivtiny;
-      double r = x[k];
-      if (k + 1 < m) r -= u2[ix] * x[k + 1];
-      if (k + 2 < m) r -= u3[ix] * x[k + 2];
-      x[k] = r / p;
-    }
-    // re-orthogonalise against the cluster's finished vectors, normalise
-    for (int q = 0; q < nprev; ++q) {
-      const double* zq = Z + (size_t)(c0 + q) * m;
-      double s = 0.0;
-      for (int k = 0; k < m; ++k) s += zq[k] * x[k];
-      for (int k = 0; k < m; ++k) x[k] -= s * zq[k];
-    }
-    double mx = 0.0;
-    for (int k = 0; k < m; ++k) mx = fmax(mx, fabs(x[k]));
-    if (!(mx > 0.0)) mx = 1.0;
-    double s2 = 0.0;
-    for (int k = 0; k < m; ++k) {
-      x[k] /= mx;
-      s2 += x[k] * x[k];
-    }
-    const double inv = 1.0 / sqrt(s2);
-    for (int k = 0; k < m; ++k) x[k] *= inv;
-  }
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
@@ -191,8 +90,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   __shared__ double rot_c[32], rot_s[32];
   __shared__ int rot_k[32];
   __shared__ int id[kMaxCols], cl[kMaxCols];
-  __shared__ double sh_bn, sh_glo, sh_ghi, sh_pivmin, sh_onenrm;
-  __shared__ int sh_stop, sh_done, sh_nev, sh_np, sh_nconv, sh_rounds;
+  __shared__ double sh_bn, sh_onenrm;
+  __shared__ int sh_stop, sh_done, sh_nev, sh_np, sh_nconv;
 
   const int t = threadIdx.x, m = a.m, lane = t & 31;
 
@@ -238,60 +137,13 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   if (sh_stop != STATUS_RUNNING) return;
   const double bn = sh_bn;
 
-  // ---- 2. Ritz values by bisection ------------------------------------------
-  if (t == 0) {
-    double glo = d[0], ghi = d[0], onenrm = 0.0, emax2 = 0.0, finite = 0.0;
-    for (int k = 0; k < m; ++k) {
-      const double off = (k > 0 ? fabs(e[k - 1]) : 0.0) + (k < m - 1 ? fabs(e[k]) : 0.0);
-      glo = fmin(glo, d[k] - off);
-      ghi = fmax(ghi, d[k] + off);
-      onenrm = fmax(onenrm, fabs(d[k]) + off);
-      emax2 = fmax(emax2, e2[k]);
-      finite += d[k] + off;
-    }
-    const double pivmin = kSafeMin * fmax(1.0, emax2);
-    const double tnorm = fmax(fabs(glo), fabs(ghi));
-    sh_glo = glo - 2.0 * kUnit * tnorm * m - 2.0 * pivmin;
-    sh_ghi = ghi + 2.0 * kUnit * tnorm * m + 2.0 * pivmin;
-    sh_pivmin = pivmin;
-    sh_onenrm = isfinite(finite) ? onenrm : -1.0;
-  }
-  __syncthreads();
-  if (!(sh_onenrm >= 0.0)) {
+  // ---- 2./3. Ritz values (bisection) and eigenvectors of T (inverse iteration)
+  if (!tridiag_eigen_cta<kRsThreads>(d, e, e2, m, th, M, a.scratch, cl, &sh_onenrm)) {
     if (t == 0) {
       state[ST_ERRINFO] = 1;
       state[ST_STATUS] = STATUS_TRIDIAG_FAIL;
     }
     return;
-  }
-  if (t < m) {
-    double lo = sh_glo, hi = sh_ghi;
-    for (int it = 0; it < 128; ++it) {
-      const double mid = 0.5 * (lo + hi);
-      if (hi - lo <= 2.0 * kUnit * fmax(fabs(lo), fabs(hi)) + 4.0 * sh_pivmin || mid <= lo || mid >= hi) break;
-      if (sturm_count(d, e2, m, mid, sh_pivmin) > t) hi = mid;
-      else lo = mid;
-    }
-    th[t] = 0.5 * (lo + hi);
-  }
-  __syncthreads();
-
-  // ---- 3. eigenvectors by inverse iteration, clusters in rounds -------------
-  if (t == 0) {
-    const double ortol = 1e-3 * sh_onenrm;
-    int rounds = 1;
-    cl[0] = 0;
-    for (int i = 1; i < m; ++i) {
-      cl[i] = (th[i] - th[i - 1] > ortol) ? i : cl[i - 1];
-      rounds = max(rounds, i - cl[i] + 1);
-    }
-    sh_rounds = rounds;
-  }
-  __syncthreads();
-  const double pivtiny = kUnit * fmax(sh_onenrm, kSafeMin);
-  for (int r = 0; r < sh_rounds; ++r) {
-    if (t < m && t - cl[t] == r) inverse_iteration(d, e, m, th[t], pivtiny, a.scratch, M, t, cl[t], r);
-    __syncthreads();
   }
 
   // ---- 4. ordering, Ritz estimates, convergence, NEV adjustment -------------

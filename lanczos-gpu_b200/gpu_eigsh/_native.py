@@ -73,8 +73,34 @@ class EigshInfo(C.Structure):
         return out
 
 
+LG_F32 = 0
+LG_F64 = 1
+FUNCS = {"log": 0, "exp": 1, "sqrt": 2, "inv": 3}
+
+
+class SlqOp(C.Structure):
+    """lg_slq_op: P = (shift I + L)^power, L = diag + off-diagonal CSR."""
+    _fields_ = [
+        ("n", C.c_int),
+        ("nnz", C.c_longlong),
+        ("rowptr", C.c_void_p),
+        ("col", C.c_void_p),
+        ("offval", C.c_void_p),
+        ("diag", C.c_void_p),
+        ("doffval", C.c_void_p),
+        ("ddiag", C.c_void_p),
+        ("shift", C.c_double),
+        ("power", C.c_int),
+        ("dtype", C.c_int),
+    ]
+
+
 _PD = C.POINTER(C.c_double)
 _PI = C.POINTER(C.c_int)
+_V = C.c_void_p
+_I = C.c_int
+_SZ = C.c_size_t
+_POP = C.POINTER(SlqOp)
 
 # Every exported symbol with its ctypes signature (restype, argtypes).
 SIGNATURES = {
@@ -92,6 +118,20 @@ SIGNATURES = {
                                         C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_cgs2_orthogonalize_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "lg_slq_workspace_bytes": (_SZ, [_POP, _I, _I]),
+    "lg_slq_forward": (_I, [_POP, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_backward": (_I, [_POP, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_apply": (_I, [_POP, _I, _I, _V, _V, _V, _SZ, _V]),
+    "lg_slq_apply_vjp": (_I, [_POP, _I, _I, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_small_side": (_I, [_I, _I, _I, _I, _V, _V, _V, _V, C.c_double, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_block_start": (_I, [_I, _I, _I, _I, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_block_step": (_I, [_I, _I, _I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_block_lambda": (_I, [_I, _I, _I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_block_xi": (_I, [_I, _I, _I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_slq_block_start_grad": (_I, [_I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "lg_imgp_laplacian": (_I, [_I, C.c_longlong, _V, _V, _I, _V, C.c_double, _I, _V, _V, _V, _V, _V, _V]),
+    "lg_dense_matvec": (_I, [_I, _I, _V, _V, _I, _V, _I, _V]),
+    "lg_outer_accumulate": (_I, [_I, _I, _V, _V, _I, _V, _V]),
     "lg_status_string": (C.c_char_p, [C.c_int]),
     "lg_last_error": (C.c_int, [C.c_char_p, C.c_int]),
     "compute_eigsh": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double, _PD,

@@ -1,0 +1,246 @@
+"""IMGP graph-Matern precision operator on the GPU.
+
+``make_imgp_precision_matvec(*, x_edge_dists, idx, operator_dim, nu,
+normalization="symmetric", self_loops=True)`` returns a callable
+``matvec(rhs, lengthscale, graphbandwidth)`` computing
+
+    P(theta, kappa) rhs = (2 nu / theta^2 I + L_sym(kappa))^nu rhs
+
+for rhs of shape (n,) or (n, B), differentiable with respect to rhs,
+lengthscale (theta) and graphbandwidth (kappa) — the interface of the
+reference's make_imgp_precision_matvec (python/gpu_eigsh/imgp.py:234-289).
+
+How it runs:
+  * the edge list (idx (2, M), one entry per undirected edge) becomes, once,
+    a device CSR that stores every edge in both directions, with the squared
+    edge distances permuted into CSR order;
+  * L_sym(kappa) and dL/dkappa are built by the CUDA kernels of
+    lg_imgp_laplacian (the reference's _build_laplacian_cache, imgp.py:142-189)
+    and cached for the last kappa value;
+  * P X runs as nu fused sparse products (lg_slq_apply), its VJP as
+    lg_slq_apply_vjp; gradients reach kappa through dL/dkappa and theta
+    through d(2 nu / theta^2)/dtheta;
+  * slq_logdet (gpu_eigsh.funm_torch) recognises this object and runs the whole
+    stochastic Lanczos quadrature and its Kraemer backward on the fused kernels
+    (``_slq_logdet_fused``).
+
+Inputs may live on the CPU (as in the reference's examples); the operator is
+moved to the current CUDA device and results come back on the device of rhs.
+There is no CPU implementation: without CUDA the constructor raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native, _slq
+
+__all__ = ["make_imgp_precision_matvec", "ImgpPrecisionMatvec", "_matmul_symmetric_laplacian"]
+
+_MAXB = 128
+
+
+def _scalar(t) -> float:
+    return float(t.detach().reshape(-1)[0]) if torch.is_tensor(t) else float(t)
+
+
+class ImgpPrecisionMatvec:
+    """Callable P(theta, kappa) X on the GPU; see the module docstring."""
+
+    def __init__(self, x_edge_dists, idx, operator_dim: int, nu: int, self_loops: bool = True):
+        dev = _slq.require_cuda()
+        if x_edge_dists.is_cuda:
+            dev = x_edge_dists.device
+        d2 = torch.as_tensor(x_edge_dists).detach().to(dev)
+        if d2.dtype not in (torch.float32, torch.float64):
+            d2 = d2.to(torch.float64)
+        idx = torch.as_tensor(idx).to(dev, torch.int64)
+        if idx.dim() != 2 or idx.shape[0] != 2 or idx.shape[1] != d2.numel():
+            raise ValueError("idx must be (2, M) with one squared distance per edge")
+        n = int(operator_dim)
+        if nu < 1 or nu > 8 or int(nu) != nu:
+            raise ValueError("nu must be an integer in [1, 8]")
+        M = idx.shape[1]
+        if 2 * M >= 2 ** 31 or n >= 2 ** 31:
+            raise ValueError("graph too large for int32 CSR indices")
+        if M and (int(idx.min()) < 0 or int(idx.max()) >= n):
+            raise ValueError("edge index out of range [0, operator_dim)")
+        # CSR with both directions of every edge, rows sorted by (row, col)
+        rows = torch.cat([idx[0], idx[1]])
+        cols = torch.cat([idx[1], idx[0]])
+        eid = torch.arange(M, device=dev).repeat(2)
+        order = torch.argsort(rows * n + cols, stable=True)
+        counts = torch.bincount(rows, minlength=n)
+        self.rowptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+        self.rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        self.col = cols[order].to(torch.int32).contiguous()
+        self.d2 = d2[eid[order]].contiguous()
+        self.n, self.nu, self.self_loops = n, int(nu), bool(self_loops)
+        self.dtype = d2.dtype
+        self.device = dev
+        self.nnz = int(self.col.numel())
+        self._lap_key = None
+        self._lap = None
+
+    # -- L_sym(kappa) and dL/dkappa -----------------------------------------------
+    def laplacian(self, kappa: float):
+        """(offval (nnz,), diag (n,), doffval, ddiag) for graphbandwidth kappa, cached."""
+        if self._lap_key != kappa:
+            off = torch.empty(self.nnz, dtype=self.dtype, device=self.device)
+            doff = torch.empty_like(off)
+            diag = torch.empty(self.n, dtype=self.dtype, device=self.device)
+            ddiag = torch.empty_like(diag)
+            work = torch.empty(4 * self.n, dtype=torch.float64, device=self.device)
+            _native.check(_native.lib.lg_imgp_laplacian(
+                self.n, self.nnz, self.rowptr.data_ptr(), self.col.data_ptr() if self.nnz else None,
+                _slq.dtype_code(self.dtype), self.d2.data_ptr() if self.nnz else None, float(kappa),
+                int(self.self_loops), off.data_ptr() if self.nnz else None, diag.data_ptr(),
+                doff.data_ptr() if self.nnz else None, ddiag.data_ptr(), work.data_ptr(),
+                _slq.stream(self.device)))
+            self._lap_key, self._lap = kappa, (off, diag, doff, ddiag)
+        return self._lap
+
+    def operator(self, lengthscale: float, kappa: float) -> _slq.Operator:
+        off, diag, doff, ddiag = self.laplacian(kappa)
+        shift = 2.0 * self.nu / (lengthscale * lengthscale)
+        return _slq.Operator(self.n, self.rowptr, self.col, off, diag, doff, ddiag, shift, self.nu, self.dtype)
+
+    def shift_derivative(self, lengthscale: float) -> float:
+        """d(2 nu / theta^2) / d theta."""
+        return -4.0 * self.nu / lengthscale ** 3
+
+    def __call__(self, rhs, lengthscale, graphbandwidth):
+        return _PrecisionApply.apply(rhs, lengthscale, graphbandwidth, self)
+
+
+def _column_chunks(B: int):
+    k = (B + _MAXB - 1) // _MAXB
+    step = (B + k - 1) // k
+    return [(c, min(B, c + step)) for c in range(0, B, step)]
+
+
+def _blocked(X: torch.Tensor, dev, dtype):
+    """(n, B) -> list of (block (n, ld), b) per chunk of <= 128 columns."""
+    out = []
+    for c0, c1 in _column_chunks(X.shape[1]):
+        blk, b, _ = _slq.to_block(X[:, c0:c1], dev, dtype)
+        out.append((blk, b))
+    return out
+
+
+class _PrecisionApply(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, rhs, lengthscale, graphbandwidth, mv: ImgpPrecisionMatvec):
+        ell, kap = _scalar(lengthscale), _scalar(graphbandwidth)
+        op = mv.operator(ell, kap)
+        X2 = rhs.reshape(-1, 1) if rhs.dim() == 1 else rhs
+        if X2.shape[0] != mv.n:
+            raise ValueError(f"rhs has {X2.shape[0]} rows, the operator {mv.n}")
+        parts = _blocked(X2.detach(), mv.device, mv.dtype)
+        outs = [op.apply(blk, b, blk.shape[1])[:, :b] for blk, b in parts]
+        Y = torch.cat(outs, dim=1) if len(outs) > 1 else outs[0]
+        ctx.mv, ctx.ell, ctx.kap, ctx.shape = mv, ell, kap, rhs.shape
+        ctx.rhs_dev, ctx.rhs_dtype = rhs.device, rhs.dtype
+        ctx.parts = parts
+        ctx.pdev = (lengthscale.device if torch.is_tensor(lengthscale) else None,
+                    graphbandwidth.device if torch.is_tensor(graphbandwidth) else None)
+        ctx.pshape = (lengthscale.shape if torch.is_tensor(lengthscale) else None,
+                      graphbandwidth.shape if torch.is_tensor(graphbandwidth) else None)
+        ctx.pdtype = (lengthscale.dtype if torch.is_tensor(lengthscale) else None,
+                      graphbandwidth.dtype if torch.is_tensor(graphbandwidth) else None)
+        return Y.reshape(rhs.shape).to(rhs.device, rhs.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        mv = ctx.mv
+        op = mv.operator(ctx.ell, ctx.kap)
+        G2 = g.reshape(-1, 1) if g.dim() == 1 else g
+        gparts = _blocked(G2.detach(), mv.device, mv.dtype)
+        gxs, gp = [], torch.zeros(2, dtype=torch.float64, device=mv.device)
+        for (blk, b), (gblk, _) in zip(ctx.parts, gparts):
+            gX, gpp = op.apply_vjp(blk, gblk, b, blk.shape[1])
+            gxs.append(gX[:, :b])
+            gp = gp + gpp
+        g_rhs = (torch.cat(gxs, dim=1) if len(gxs) > 1 else gxs[0]).reshape(ctx.shape).to(ctx.rhs_dev, ctx.rhs_dtype)
+        g_ell = gp[1] * mv.shift_derivative(ctx.ell)
+        g_kap = gp[0]
+        out = [g_rhs]
+        for k, gv in enumerate((g_ell, g_kap)):
+            if ctx.pdev[k] is None:
+                out.append(None)
+            else:
+                out.append(gv.to(ctx.pdev[k], ctx.pdtype[k]).reshape(ctx.pshape[k]))
+        return out[0], out[1], out[2], None
+
+
+def make_imgp_precision_matvec(*, x_edge_dists, idx, operator_dim, nu, normalization="symmetric",
+                               self_loops=True):
+    """P(kappa, theta) = (2 nu / theta^2 I + L_sym(kappa))^nu as a differentiable
+    callable ``matvec(rhs, lengthscale, graphbandwidth)`` (imgp.py:234-289)."""
+    if normalization != "symmetric":
+        raise NotImplementedError(
+            "Only normalization='symmetric' is implemented (the case used by SS-IMGP-full).")
+    return ImgpPrecisionMatvec(x_edge_dists, idx, operator_dim, nu, self_loops)
+
+
+def _matmul_symmetric_laplacian(rhs, x_edge_dists, idx, operator_dim, graphbandwidth, self_loops=True):
+    """L_sym(kappa) rhs (the reference's one-shot helper, imgp.py:210-226): the
+    power-1 operator with zero shift."""
+    mv = ImgpPrecisionMatvec(x_edge_dists, idx, operator_dim, 1, self_loops)
+    kap = _scalar(graphbandwidth)
+    off, diag, doff, ddiag = mv.laplacian(kap)
+    op = _slq.Operator(mv.n, mv.rowptr, mv.col, off, diag, doff, ddiag, 0.0, 1, mv.dtype)
+    X2 = rhs.reshape(-1, 1) if rhs.dim() == 1 else rhs
+    outs = [op.apply(blk, b, blk.shape[1])[:, :b] for blk, b in _blocked(X2.detach(), mv.device, mv.dtype)]
+    Y = torch.cat(outs, dim=1) if len(outs) > 1 else outs[0]
+    return Y.reshape(rhs.shape).to(rhs.device, rhs.dtype)
+
+
+# ---------------------------------------------------------------------------
+# Fused stochastic Lanczos quadrature on this operator
+# ---------------------------------------------------------------------------
+class _SLQImgp(torch.autograd.Function):
+    """log det P(theta, kappa) by SLQ over the probe columns of Z, with the
+    Kraemer backward, entirely on the fused kernels (lg_slq_forward /
+    lg_slq_small_side / lg_slq_backward).  Follows _SLQLogdetBatched
+    (python/gpu_eigsh/funm_torch.py:571-727)."""
+
+    @staticmethod
+    def forward(ctx, mv: ImgpPrecisionMatvec, Z, lanczos_m: int, lengthscale, graphbandwidth):
+        ell, kap = _scalar(lengthscale), _scalar(graphbandwidth)
+        op = mv.operator(ell, kap)
+        P = Z.shape[1]
+        m = int(lanczos_m)
+        parts = _blocked(Z, mv.device, mv.dtype)
+        q_all, saved = [], []
+        for blk, b in parts:
+            ld = blk.shape[1]
+            V, Y, alpha, beta, znorm = op.forward(blk, b, ld, m)
+            q, ga, gb, _ = _slq.small_side(alpha, beta, znorm, "log", 0, g_scale=1.0 / P)
+            q_all.append(q)
+            saved.append((V, Y, alpha, beta, ga, gb, b, ld))
+        ld_val = torch.cat(q_all).sum() / P
+        need = any(ctx.needs_input_grad[3:5])
+        ctx.saved = saved if need else None
+        ctx.mv, ctx.ell, ctx.kap, ctx.m = mv, ell, kap, m
+        ctx.pinfo = [(t.device, t.dtype, t.shape) if torch.is_tensor(t) else None
+                     for t in (lengthscale, graphbandwidth)]
+        return ld_val.to(Z.dtype)
+
+    @staticmethod
+    def backward(ctx, g_ld):
+        mv = ctx.mv
+        op = mv.operator(ctx.ell, ctx.kap)
+        g_out = g_ld.detach().to(mv.device, torch.float64).reshape(1)
+        gp = torch.zeros(2, dtype=torch.float64, device=mv.device)
+        for V, Y, alpha, beta, ga, gb, b, ld in ctx.saved:
+            gp = gp + op.backward(V, Y, alpha, beta, ga, gb, g_out, b, ld, ctx.m)
+        grads = [gp[1] * mv.shift_derivative(ctx.ell), gp[0]]
+        out = []
+        for gv, info in zip(grads, ctx.pinfo):
+            out.append(None if info is None else gv.to(info[0], info[1]).reshape(info[2]))
+        ctx.saved = None
+        return None, None, None, out[0], out[1]
+
+
+def _slq_logdet_fused(mv: ImgpPrecisionMatvec, Z, lanczos_m, lengthscale, graphbandwidth):
+    return _SLQImgp.apply(mv, Z, lanczos_m, lengthscale, graphbandwidth)
