@@ -155,7 +155,7 @@ SLQ_WORKLOAD = (f"slq_logdet of P = (2nu/theta^2 I + L_sym(kappa))^nu, nu={SLQ_N
 def slq_bytes(n, nnz, B, nu, m, es):
     """Algorithmic DRAM bytes of one fused SLQ forward and backward (blocks of
     n x ld, each row read or written once; CSR once per sparse product)."""
-    ld = B + (B & 1)
+    ld = (B + 3) // 4 * 4 if es == 4 else B + (B & 1)
     blk = n * ld * es
     csr = 8 * nnz + 8 * n                      # col + value per entry, rowptr + diag per row
     dcsr = 12 * nnz + 12 * n                   # with the d/dkappa values
@@ -204,6 +204,7 @@ def slq_cpu_baseline(idx, d2, n=N_POINTS, m_full=SLQ_M):
 def run_slq(args, dev, with_e2e, with_cpu):
     import torch
 
+    from gpu_eigsh import _slq
     from gpu_eigsh.funm_torch import slq_logdet
     from gpu_eigsh.imgp import make_imgp_precision_matvec
 
@@ -248,14 +249,12 @@ def run_slq(args, dev, with_e2e, with_cpu):
     for r in range(3):
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        V, Y, al, be, zn = op.forward(Z, B, B + (B & 1), M)
+        V, Y, al, be, zn = op.forward(Z, B, _slq.ld_for(B, torch.float32), M)
         e1.record()
-        from gpu_eigsh import _slq
-
         q, ga, gb, _ = _slq.small_side(al, be, zn, "log", 0, g_scale=1.0 / B)
         e2b = torch.cuda.Event(enable_timing=True)
         e2b.record()
-        op.backward(V, Y, al, be, ga, gb, None, B, B + (B & 1), M)
+        op.backward(V, Y, al, be, ga, gb, None, B, _slq.ld_for(B, torch.float32), M)
         e2.record()
         torch.cuda.synchronize()
         if r:

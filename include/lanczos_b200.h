@@ -267,6 +267,15 @@ int lg_imgp_laplacian(int n, long long nnz, const int* rowptr, const int* col, i
                       double graphbandwidth, int self_loops, void* offval, void* diag, void* doffval, void* ddiag,
                       double* work, void* stream);
 
+/* Breadth-first levels of the graph of a CSR (every edge stored both ways)
+ * from vertex `start`: level[v] = hop distance, -1 where unreachable.  work:
+ * 2n + 2 ints of device scratch.  Synchronises `stream` every 16 levels;
+ * *nlevels receives the number of expansion rounds run.  Used to order the
+ * rows of the SLQ operator for locality (no counterpart in the reference,
+ * which keeps the caller's order). */
+int lg_graph_bfs_levels(int n, const int* rowptr, const int* col, int start, int* level, int* work, int* nlevels,
+                        void* stream);
+
 /* y = A x for a dense row-major n x n A (vectors with element strides ldx, ldy),
  * and gA += lam x^T (fp64 gA, vectors with element stride ld): the dense-matrix
  * operations of funm_apply_kraemer (python/gpu_eigsh/funm_torch.py:284, 347). */

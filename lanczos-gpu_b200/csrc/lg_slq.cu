@@ -51,12 +51,18 @@ extern thread_local std::string g_last_error;
 namespace lg {
 namespace slq {
 
-int slq_grid() {
+static int num_sms() {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return 2 * (sms > 0 ? sms : 1);
+  return sms > 0 ? sms : 1;
 }
+
+// The largest grid (sizes the partial-row buffers): the forward products and
+// the light reductions run kMinCta CTAs per SM; the backward products and the
+// streaming kernels, built for 2 CTAs per SM (64 registers), run grid2().
+int slq_grid() { return kMinCta * num_sms(); }
+static int grid2() { return 2 * num_sms(); }
 
 enum { kDotNone = 0, kDotSelf = 1, kDotVj = 2, kDotBlock = 3 };
 
@@ -84,11 +90,13 @@ struct FwdArgs {
   double* znorm;       // (B)
 };
 
-template <typename T, int NCH, bool FIRST, int DOT, bool AXPY>
-__global__ void __launch_bounds__(kT) fwd_spmm_kernel(const FwdArgs<T> a) {
+template <typename T, int LPR, int NCH, bool FIRST, int DOT, bool AXPY>
+__global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> a) {
   static_assert(!(FIRST && AXPY), "the first product cannot also close the recurrence");
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_k0[kMaxB], s_k1[kMaxB];
-  const int lane = threadIdx.x & 31;
+  const G g;
   const int B = a.B, ld = a.ld;
   if (FIRST || AXPY) {
     for (int b = threadIdx.x; b < B; b += kT) {
@@ -108,81 +116,94 @@ __global__ void __launch_bounds__(kT) fwd_spmm_kernel(const FwdArgs<T> a) {
     }
     __syncthreads();
   }
-  double k0[NCH][2], k1[NCH][2];
+  double k0[NCH][VEC], k1[NCH][VEC];
 #pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) {
-    const int c0 = ch * 64 + 2 * lane;
-    k0[ch][0] = (FIRST || AXPY) && c0 < B ? s_k0[c0] : 0.0;
-    k0[ch][1] = (FIRST || AXPY) && c0 + 1 < B ? s_k0[c0 + 1] : 0.0;
-    k1[ch][0] = AXPY && c0 < B ? s_k1[c0] : 0.0;
-    k1[ch][1] = AXPY && c0 + 1 < B ? s_k1[c0 + 1] : 0.0;
-  }
-  double acc[kQ][NCH][2] = {};
-  for (long long row = first_row(); row < a.op.n; row += row_stride()) {
-    double x[NCH][2], y[NCH][2], unused[NCH][2];
-    const double dg = a.op.shift + (double)__ldg(a.diag + row);
+  for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
-    for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
-      x[ch][0] = x[ch][1] = 0.0;
-      if (c0 < B) ld2m(a.X + row * ld + c0, c0 + 1 < B, x[ch][0], x[ch][1]);
-      y[ch][0] = dg * x[ch][0];
-      y[ch][1] = dg * x[ch][1];
+    for (int v = 0; v < VEC; ++v) {
+      const int c = g.col0(ch) + v;
+      k0[ch][v] = (FIRST || AXPY) && c < B ? s_k0[c] : 0.0;
+      k1[ch][v] = AXPY && c < B ? s_k1[c] : 0.0;
     }
-    gather_row<T, NCH, false>(a.op, a.off, nullptr, a.X, ld, B, row, lane, y, unused);
+  double acc[kQ][NCH][VEC] = {};
+  for (long long wrow = g.first_warp_row(); wrow < a.op.n; wrow += G::stride()) {
+    const long long row = wrow + g.sub;
+    const bool valid = row < a.op.n;
+    T x[NCH][VEC], y[NCH][VEC], unused[NCH][VEC];
+    const T dg = valid ? (T)(a.op.shift + (double)__ldg(a.diag + row)) : T(0);
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) x[ch][v] = T(0);
+      if (valid && c0 < B) ldvec<T, VEC>(a.X + row * ld + c0, B - c0, x[ch]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) y[ch][v] = dg * x[ch][v];
+    }
+    gather_rows<T, LPR, NCH, false>(a.op, a.off, nullptr, a.X, ld, B, valid, row, g, y, unused);
+    if (!valid) continue;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
+      const int nv = B - c0;
+      double xs[VEC], o[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        xs[v] = (double)x[ch][v];
+        o[v] = (double)y[ch][v];
+      }
       if (FIRST) {
         // the product is linear: A (x / ||r||) = (A x) / ||r|| per column
-        x[ch][0] *= k0[ch][0];
-        x[ch][1] *= k0[ch][1];
-        y[ch][0] *= k0[ch][0];
-        y[ch][1] *= k0[ch][1];
-        st2(a.Vj + row * ld + c0, x[ch][0], x[ch][1]);
-      }
-      double o0 = rnd<T>(y[ch][0]), o1 = rnd<T>(y[ch][1]);
-      if (DOT != kDotNone) {
-        double p0 = o0, p1 = o1;
-        if (DOT == kDotVj) {
-          if (FIRST) {
-            p0 = rnd<T>(x[ch][0]);
-            p1 = rnd<T>(x[ch][1]);
-          } else {
-            ld2m(a.Vj + row * ld + c0, sec, p0, p1);
-          }
-        } else if (DOT == kDotBlock) {
-          ld2m(a.Dsrc + row * ld + c0, sec, p0, p1);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          xs[v] *= k0[ch][v];
+          o[v] *= k0[ch][v];
         }
-        acc[0][ch][0] += p0 * o0;
-        acc[0][ch][1] += p1 * o1;
+        stvec<T, VEC>(a.Vj + row * ld + c0, xs, nv);
       }
       if (AXPY) {
-        double v0, v1;
-        ld2m(a.Vj + row * ld + c0, sec, v0, v1);
-        double r0 = y[ch][0] - k0[ch][0] * v0, r1 = y[ch][1] - k0[ch][1] * v1;
-        if (a.Vjm1) {
-          double q0, q1;
-          ld2m(a.Vjm1 + row * ld + c0, sec, q0, q1);
-          r0 -= k1[ch][0] * q0;
-          r1 -= k1[ch][1] * q1;
+        T vj[VEC], vm[VEC];
+        ldvec<T, VEC>(a.Vj + row * ld + c0, nv, vj);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) vm[v] = T(0);
+        if (a.Vjm1) ldvec<T, VEC>(a.Vjm1 + row * ld + c0, nv, vm);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          o[v] = rnd<T>(o[v] - k0[ch][v] * (double)vj[v] - k1[ch][v] * (double)vm[v]);
+          acc[0][ch][v] += o[v] * o[v];
         }
-        o0 = rnd<T>(r0);
-        o1 = rnd<T>(r1);
-        acc[0][ch][0] += o0 * o0;
-        acc[0][ch][1] += o1 * o1;
+      } else {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) o[v] = rnd<T>(o[v]);
       }
-      st2(a.Out + row * ld + c0, o0, o1);
+      if (DOT != kDotNone) {
+        double pv[VEC];
+        if (DOT == kDotVj) {
+          if (FIRST) {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) pv[v] = rnd<T>(xs[v]);
+          } else {
+            ldvecd<T, VEC>(a.Vj + row * ld + c0, nv, pv);
+          }
+        } else if (DOT == kDotBlock) {
+          ldvecd<T, VEC>(a.Dsrc + row * ld + c0, nv, pv);
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) pv[v] = o[v];
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[0][ch][v] += pv[v] * o[v];
+      }
+      stvec<T, VEC>(a.Out + row * ld + c0, o, nv);
     }
   }
-  if (DOT != kDotNone || AXPY) colsum_finish<NCH>(acc, 1, B, a.cout);
+  if (DOT != kDotNone || AXPY) colsum_finish<VEC, NCH, LPR>(acc, 1, B, a.cout);
 }
 
 // Column sums of X*Y (Y null: of X*X).
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT) coldot_kernel(int n, int ld, int B, const T* __restrict__ X,
+__global__ void __launch_bounds__(kT, kMinCta) coldot_kernel(int n, int ld, int B, const T* __restrict__ X,
                                                     const T* __restrict__ Y, ColSum cout) {
   const int lane = threadIdx.x & 31;
   double acc[kQ][NCH][2] = {};
@@ -203,13 +224,13 @@ __global__ void __launch_bounds__(kT) coldot_kernel(int n, int ld, int B, const 
       acc[0][ch][1] += x1 * y1;
     }
   }
-  colsum_finish<NCH>(acc, 1, B, cout);
+  colsum_finish<2, NCH, 32>(acc, 1, B, cout);
 }
 
 // r = W - alpha_j v_j - beta_{j-1} v_{j-1} (alpha_j from the column sums,
 // stored), ||r||^2 to the column sums.
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, 2)
 recur_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ W, const T* __restrict__ Vj,
              const T* __restrict__ Vjm1, const double* __restrict__ cin, double* alpha, const double* beta,
              T* __restrict__ R, ColSum cout) {
@@ -244,12 +265,12 @@ recur_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ W, const 
       acc[0][ch][1] += o1 * o1;
     }
   }
-  colsum_finish<NCH>(acc, 1, B, cout);
+  colsum_finish<2, NCH, 32>(acc, 1, B, cout);
 }
 
 // Vout = R / sqrt(cin) per column; dst[b * dst_stride] = sqrt(cin[b]).
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, kMinCta)
 normalize_kernel(int n, int ld, int B, const T* __restrict__ R, const double* __restrict__ cin, T* __restrict__ Vout,
                  double* dst, int dst_stride) {
   __shared__ double s_s[kMaxB];
@@ -391,7 +412,7 @@ small_side_kernel(int m, int func, int mode, const double* __restrict__ alpha, c
 // nu = g*ga_j + <x_j, xi>/b_j (g = *g_out; the three dots come from cin, null
 // with xi at j = m-1 where xi = 0).  mu, nu go to munu for the step's last kernel.
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, 2)
 lam_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ xi, const T* __restrict__ xplus,
            const T* __restrict__ xj, const double* __restrict__ cin, const double* __restrict__ g_alpha,
            const double* __restrict__ g_beta, const double* __restrict__ g_out, const double* __restrict__ beta,
@@ -457,10 +478,12 @@ struct BwdArgs {
   double* sacc;        // per CTA: [2b] += d/dq term, [2b+1] += shift term
 };
 
-template <typename T, int NCH, bool LAST, bool DERIV>
-__global__ void __launch_bounds__(kT) bwd_spmm_kernel(const BwdArgs<T> a) {
+template <typename T, int LPR, int NCH, bool LAST, bool DERIV>
+__global__ void __launch_bounds__(kT, 2) bwd_spmm_kernel(const BwdArgs<T> a) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_a[kMaxB], s_b[kMaxB], s_bn[kMaxB], scr[kW];
-  const int lane = threadIdx.x & 31;
+  const G g;
   const int B = a.B, ld = a.ld;
   if (LAST) {
     for (int b = threadIdx.x; b < B; b += kT) {
@@ -471,51 +494,63 @@ __global__ void __launch_bounds__(kT) bwd_spmm_kernel(const BwdArgs<T> a) {
     __syncthreads();
   }
   const bool dots = LAST && a.xjm1 != nullptr;
-  double acc[kQ][NCH][2] = {};
+  double acc[kQ][NCH][VEC] = {};
   double sk = 0.0, sc = 0.0;
-  for (long long row = first_row(); row < a.op.n; row += row_stride()) {
-    double mi[NCH][2], y[NCH][2], yk[NCH][2];
-    const double dg = a.op.shift + (double)__ldg(a.diag + row);
-    const double ddg = DERIV ? (double)__ldg(a.ddiag + row) : 0.0;
+  for (long long wrow = g.first_warp_row(); wrow < a.op.n; wrow += G::stride()) {
+    const long long row = wrow + g.sub;
+    const bool valid = row < a.op.n;
+    T mi[NCH][VEC], y[NCH][VEC], yk[NCH][VEC];
+    const T dg = valid ? (T)(a.op.shift + (double)__ldg(a.diag + row)) : T(0);
+    const T ddg = (DERIV && valid) ? __ldg(a.ddiag + row) : T(0);
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
-      mi[ch][0] = mi[ch][1] = 0.0;
-      if (c0 < B) ld2m(a.Min + row * ld + c0, c0 + 1 < B, mi[ch][0], mi[ch][1]);
-      y[ch][0] = dg * mi[ch][0];
-      y[ch][1] = dg * mi[ch][1];
-      yk[ch][0] = ddg * mi[ch][0];
-      yk[ch][1] = ddg * mi[ch][1];
+      const int c0 = g.col0(ch);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) mi[ch][v] = T(0);
+      if (valid && c0 < B) ldvec<T, VEC>(a.Min + row * ld + c0, B - c0, mi[ch]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        y[ch][v] = dg * mi[ch][v];
+        yk[ch][v] = ddg * mi[ch][v];
+      }
     }
-    gather_row<T, NCH, DERIV>(a.op, a.off, a.doff, a.Min, ld, B, row, lane, y, yk);
+    gather_rows<T, LPR, NCH, DERIV>(a.op, a.off, a.doff, a.Min, ld, B, valid, row, g, y, yk);
+    if (!valid) continue;
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double y0, y1;
-      ld2m(a.Y + row * ld + c0, sec, y0, y1);
-      if (DERIV) sk += y0 * yk[ch][0] + y1 * yk[ch][1];
-      sc += y0 * mi[ch][0] + y1 * mi[ch][1];
+      const int nv = B - c0;
+      T yv[VEC];
+      ldvec<T, VEC>(a.Y + row * ld + c0, nv, yv);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        if (DERIV) sk += (double)yv[v] * (double)yk[ch][v];
+        sc += (double)yv[v] * (double)mi[ch][v];
+      }
       if (!LAST) {
-        st2(a.Mout + row * ld + c0, y[ch][0], y[ch][1]);
+        stvec_t<T, VEC>(a.Mout + row * ld + c0, y[ch], nv);
       } else if (dots) {
         // xi_{j-1}; Y is x_j here (p = nu - 1)
-        double l0, l1, p0, p1, q0 = 0.0, q1 = 0.0, u0, u1;
-        ld2m(a.lam + row * ld + c0, sec, l0, l1);
-        ld2m(a.xplus + row * ld + c0, sec, p0, p1);
-        if (a.lplus) ld2m(a.lplus + row * ld + c0, sec, q0, q1);
-        ld2m(a.xjm1 + row * ld + c0, sec, u0, u1);
-        const double x0 = rnd<T>(-rnd<T>(y[ch][0]) + s_a[c0] * l0 + s_b[c0] * q0 - s_bn[c0] * p0);
-        const double x1 =
-            sec ? rnd<T>(-rnd<T>(y[ch][1]) + s_a[c0 + 1] * l1 + s_b[c0 + 1] * q1 - s_bn[c0 + 1] * p1) : 0.0;
-        st2(a.xi + row * ld + c0, x0, x1);
-        acc[0][ch][0] += l0 * u0;
-        acc[0][ch][1] += l1 * u1;
-        acc[1][ch][0] += y0 * x0;
-        acc[1][ch][1] += y1 * x1;
-        acc[2][ch][0] += u0 * x0;
-        acc[2][ch][1] += u1 * x1;
+        T l[VEC], p[VEC], q[VEC], u[VEC], xo[VEC];
+        ldvec<T, VEC>(a.lam + row * ld + c0, nv, l);
+        ldvec<T, VEC>(a.xplus + row * ld + c0, nv, p);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) q[v] = T(0);
+        if (a.lplus) ldvec<T, VEC>(a.lplus + row * ld + c0, nv, q);
+        ldvec<T, VEC>(a.xjm1 + row * ld + c0, nv, u);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          const int c = min(c0 + v, kMaxB - 1);
+          const double x = (v < nv) ? (double)(T)(-(double)y[ch][v] + s_a[c] * (double)l[v] +
+                                                  s_b[c] * (double)q[v] - s_bn[c] * (double)p[v])
+                                    : 0.0;
+          xo[v] = (T)x;
+          acc[0][ch][v] += (double)l[v] * (double)u[v];
+          acc[1][ch][v] += (double)yv[v] * x;
+          acc[2][ch][v] += (double)u[v] * x;
+        }
+        stvec_t<T, VEC>(a.xi + row * ld + c0, xo, nv);
       }
     }
   }
@@ -525,7 +560,7 @@ __global__ void __launch_bounds__(kT) bwd_spmm_kernel(const BwdArgs<T> a) {
     a.sacc[2 * blockIdx.x] += bsk;
     a.sacc[2 * blockIdx.x + 1] += bsc;
   }
-  if (dots) colsum_finish<NCH>(acc, 3, B, a.cout);
+  if (dots) colsum_finish<VEC, NCH, LPR>(acc, 3, B, a.cout);
 }
 
 // Generic reverse step around a caller-formed Plam = P lambda:
@@ -533,7 +568,7 @@ __global__ void __launch_bounds__(kT) bwd_spmm_kernel(const BwdArgs<T> a) {
 // x_{j-1}, the three dots of step j-1.  dcoef[b] G[:, b] is the dx term of a
 // forward output that depends on the basis directly (funm_apply_kraemer).
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, 2)
 xi_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ Plam, const T* __restrict__ lam,
           const T* __restrict__ lplus, const T* __restrict__ xplus, const T* __restrict__ xj,
           const T* __restrict__ xjm1, const double* __restrict__ alpha, const double* __restrict__ beta,
@@ -578,13 +613,13 @@ xi_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ Plam, const 
       }
     }
   }
-  if (xjm1) colsum_finish<NCH>(acc, 3, B, cout);
+  if (xjm1) colsum_finish<2, NCH, 32>(acc, 3, B, cout);
 }
 
 // gZ = (<xi, v0> v0 - xi) / ||z|| + g_zn * z / ||z||  per column (the gradient
 // with respect to the start vector; <xi, v0> from cin).
 template <typename T, int NCH>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, 2)
 start_grad_kernel(int n, int ld, int B, const T* __restrict__ xi, const T* __restrict__ V0, const T* __restrict__ Z,
                   const double* __restrict__ znorm, const double* __restrict__ g_zn, const double* __restrict__ cin,
                   T* __restrict__ gZ) {
@@ -649,7 +684,7 @@ __global__ void outer_acc_kernel(int n, int ld, const T* __restrict__ lam, const
 
 // y = A x for a dense row-major n x n A (one warp per row; B = 1 blocks).
 template <typename T>
-__global__ void __launch_bounds__(kT)
+__global__ void __launch_bounds__(kT, kMinCta)
 dense_matvec_kernel(int n, const T* __restrict__ A, const T* __restrict__ x, int ldx, T* __restrict__ y, int ldy) {
   const int lane = threadIdx.x & 31;
   for (long long row = first_row(); row < n; row += row_stride()) {
@@ -718,7 +753,8 @@ static int cuda_fail(const char* where, cudaError_t e) {
 static int check_block(int n, int B, int ld, int dtype) {
   if (n < 1) return fail("lg_slq: n must be >= 1");
   if (B < 1 || B > kMaxB) return fail("lg_slq: B (active columns) must be in [1, 128]");
-  if (ld < B || (ld & 1)) return fail("lg_slq: ld must be even and >= B");
+  if (ld < B || ld % (dtype == LG_F64 ? 2 : 4) != 0)
+    return fail("lg_slq: ld must be >= B and a multiple of 4 (fp32) or 2 (fp64)");
   if (dtype != LG_F32 && dtype != LG_F64) return fail("lg_slq: dtype must be LG_F32 or LG_F64");
   return LG_OK;
 }
@@ -759,38 +795,38 @@ static cudaError_t reset_counters(const Ws& w, cudaStream_t st) {
 }
 
 // ---- launch helpers ------------------------------------------------------
-template <typename T, int NCH>
+template <typename T, int LPR, int NCH>
 static void launch_fwd(bool first, int dot, bool axpy, const FwdArgs<T>& a, int grid, cudaStream_t st) {
   if (first) {
-    if (dot == kDotSelf) fwd_spmm_kernel<T, NCH, true, kDotSelf, false><<<grid, kT, 0, st>>>(a);
-    else if (dot == kDotVj) fwd_spmm_kernel<T, NCH, true, kDotVj, false><<<grid, kT, 0, st>>>(a);
-    else fwd_spmm_kernel<T, NCH, true, kDotNone, false><<<grid, kT, 0, st>>>(a);
+    if (dot == kDotSelf) fwd_spmm_kernel<T, LPR, NCH, true, kDotSelf, false><<<grid, kT, 0, st>>>(a);
+    else if (dot == kDotVj) fwd_spmm_kernel<T, LPR, NCH, true, kDotVj, false><<<grid, kT, 0, st>>>(a);
+    else fwd_spmm_kernel<T, LPR, NCH, true, kDotNone, false><<<grid, kT, 0, st>>>(a);
   } else if (axpy) {
-    fwd_spmm_kernel<T, NCH, false, kDotNone, true><<<grid, kT, 0, st>>>(a);
+    fwd_spmm_kernel<T, LPR, NCH, false, kDotNone, true><<<grid, kT, 0, st>>>(a);
   } else if (dot == kDotSelf) {
-    fwd_spmm_kernel<T, NCH, false, kDotSelf, false><<<grid, kT, 0, st>>>(a);
+    fwd_spmm_kernel<T, LPR, NCH, false, kDotSelf, false><<<grid, kT, 0, st>>>(a);
   } else if (dot == kDotBlock) {
-    fwd_spmm_kernel<T, NCH, false, kDotBlock, false><<<grid, kT, 0, st>>>(a);
+    fwd_spmm_kernel<T, LPR, NCH, false, kDotBlock, false><<<grid, kT, 0, st>>>(a);
   } else {
-    fwd_spmm_kernel<T, NCH, false, kDotNone, false><<<grid, kT, 0, st>>>(a);
+    fwd_spmm_kernel<T, LPR, NCH, false, kDotNone, false><<<grid, kT, 0, st>>>(a);
   }
 }
 
-template <typename T, int NCH>
+template <typename T, int LPR, int NCH>
 static void launch_bwd(bool last, bool deriv, const BwdArgs<T>& a, int grid, cudaStream_t st) {
   if (last) {
-    if (deriv) bwd_spmm_kernel<T, NCH, true, true><<<grid, kT, 0, st>>>(a);
-    else bwd_spmm_kernel<T, NCH, true, false><<<grid, kT, 0, st>>>(a);
+    if (deriv) bwd_spmm_kernel<T, LPR, NCH, true, true><<<grid2(), kT, 0, st>>>(a);
+    else bwd_spmm_kernel<T, LPR, NCH, true, false><<<grid2(), kT, 0, st>>>(a);
   } else {
-    if (deriv) bwd_spmm_kernel<T, NCH, false, true><<<grid, kT, 0, st>>>(a);
-    else bwd_spmm_kernel<T, NCH, false, false><<<grid, kT, 0, st>>>(a);
+    if (deriv) bwd_spmm_kernel<T, LPR, NCH, false, true><<<grid2(), kT, 0, st>>>(a);
+    else bwd_spmm_kernel<T, LPR, NCH, false, false><<<grid2(), kT, 0, st>>>(a);
   }
 }
 
 static Op make_op(const lg_slq_op& o) { return Op{o.n, o.rowptr, o.col, o.shift}; }
 
 // ---- fused forward (recurrence through the sparse products) --------------
-template <typename T, int NCH>
+template <typename T, int LPR, int NS, int NP>
 static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* Z, T* V, T* Yst, double* alpha,
                              double* beta, double* znorm, const Ws& w, int grid, cudaStream_t st) {
   const int nu = o.power, h = nu / 2, pdot = nu - h;
@@ -798,7 +834,7 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
   T* R = reinterpret_cast<T*>(block(w, 0));
   T* W = reinterpret_cast<T*>(block(w, 1));
   auto Yp = [&](int j, int p) { return Yst + ((size_t)j * (nu - 1) + (p - 1)) * bs; };   // A^p v_j, p >= 1
-  coldot_kernel<T, NCH><<<grid, kT, 0, st>>>(o.n, ld, B, Z, nullptr, w.cs[0]);
+  coldot_kernel<T, NP><<<grid, kT, 0, st>>>(o.n, ld, B, Z, nullptr, w.cs[0]);
   FwdArgs<T> a{};
   a.op = make_op(o);
   a.off = static_cast<const T*>(o.offval);
@@ -818,8 +854,8 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
       a.Out = W;
       a.cin = w.cs[0].out;
       a.cout = w.cs[1];
-      launch_fwd<T, NCH>(true, kDotVj, false, a, grid, st);
-      recur_kernel<T, NCH><<<grid, kT, 0, st>>>(o.n, ld, B, j, m, W, a.Vj, a.Vjm1, w.cs[1].out, alpha, beta, R,
+      launch_fwd<T, LPR, NS>(true, kDotVj, false, a, grid, st);
+      recur_kernel<T, NP><<<grid2(), kT, 0, st>>>(o.n, ld, B, j, m, W, a.Vj, a.Vjm1, w.cs[1].out, alpha, beta, R,
                                                 w.cs[0]);
       continue;
     }
@@ -832,15 +868,15 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
       a.Dsrc = (dot == kDotBlock) ? Yp(j, h) : nullptr;
       a.cin = first ? w.cs[0].out : (axpy ? w.cs[1].out : nullptr);
       a.cout = axpy ? w.cs[0] : w.cs[1];
-      launch_fwd<T, NCH>(first, dot, axpy, a, grid, st);
+      launch_fwd<T, LPR, NS>(first, dot, axpy, a, grid, st);
     }
   }
-  normalize_kernel<T, NCH><<<grid, kT, 0, st>>>(o.n, ld, B, R, w.cs[0].out, V + (size_t)m * bs, beta + (m - 1), m);
+  normalize_kernel<T, NP><<<grid, kT, 0, st>>>(o.n, ld, B, R, w.cs[0].out, V + (size_t)m * bs, beta + (m - 1), m);
   return cudaGetLastError();
 }
 
 // ---- fused backward --------------------------------------------------------
-template <typename T, int NCH>
+template <typename T, int LPR, int NS, int NP>
 static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T* V, const T* Yst,
                               const double* alpha, const double* beta, const double* g_alpha, const double* g_beta,
                               const double* g_out, double* g_params, const Ws& w, int grid, cudaStream_t st) {
@@ -873,7 +909,7 @@ static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T*
     const T* xj = V + (size_t)j * bs;
     const T* xplus = V + (size_t)(j + 1) * bs;
     const bool top = (j == m - 1);
-    lam_kernel<T, NCH><<<grid, kT, 0, st>>>(o.n, ld, B, j, m, top ? nullptr : xi, xplus, xj,
+    lam_kernel<T, NP><<<grid2(), kT, 0, st>>>(o.n, ld, B, j, m, top ? nullptr : xi, xplus, xj,
                                             top ? nullptr : w.cs[1].out, g_alpha, g_beta, g_out, beta, lam, w.munu);
     a.j = j;
     a.lam = lam;
@@ -887,7 +923,7 @@ static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T*
       a.Min = Min;
       a.Y = last ? xj : Yp(j, nu - 1 - p);
       a.Mout = last ? nullptr : M[p & 1];
-      launch_bwd<T, NCH>(last, deriv, a, grid, st);
+      launch_bwd<T, LPR, NS>(last, deriv, a, grid, st);
       Min = a.Mout;
     }
     std::swap(lam, lplus);
@@ -898,7 +934,7 @@ static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T*
 }
 
 // ---- operator apply and its VJP -------------------------------------------
-template <typename T, int NCH>
+template <typename T, int LPR, int NS, int NP>
 static cudaError_t apply_t(const lg_slq_op& o, int B, int ld, const T* X, T* Yout, const Ws& w, int grid,
                            cudaStream_t st) {
   FwdArgs<T> a{};
@@ -911,13 +947,13 @@ static cudaError_t apply_t(const lg_slq_op& o, int B, int ld, const T* X, T* You
   for (int p = 1; p <= o.power; ++p) {
     a.X = in;
     a.Out = (p == o.power) ? Yout : reinterpret_cast<T*>(block(w, p & 1));
-    launch_fwd<T, NCH>(false, kDotNone, false, a, grid, st);
+    launch_fwd<T, LPR, NS>(false, kDotNone, false, a, grid, st);
     in = a.Out;
   }
   return cudaGetLastError();
 }
 
-template <typename T, int NCH>
+template <typename T, int LPR, int NS, int NP>
 static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, const T* G, T* gX, double* g_params,
                                const Ws& w, int grid, cudaStream_t st) {
   const int nu = o.power;
@@ -932,7 +968,7 @@ static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, co
   for (int q = 1; q < nu; ++q) {
     f.X = (q == 1) ? X : Xq(q - 1);
     f.Out = Xq(q);
-    launch_fwd<T, NCH>(false, kDotNone, false, f, grid, st);
+    launch_fwd<T, LPR, NS>(false, kDotNone, false, f, grid, st);
   }
   cudaError_t e = cudaMemsetAsync(w.sacc, 0, (size_t)2 * grid * sizeof(double), st);
   if (e != cudaSuccess) return e;
@@ -952,7 +988,7 @@ static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, co
     a.Min = Min;
     a.Y = (p == nu - 1) ? X : Xq(nu - 1 - p);
     a.Mout = (p == nu - 1) ? gX : M[p & 1];
-    launch_bwd<T, NCH>(false, deriv, a, grid, st);
+    launch_bwd<T, LPR, NS>(false, deriv, a, grid, st);
     Min = a.Mout;
   }
   sacc_reduce_kernel<<<1, 32, 0, st>>>(w.sacc, grid, g_params);
@@ -965,7 +1001,12 @@ static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, co
 using namespace lg;
 using namespace lg::slq;
 
-#define LG_DISPATCH(DTYPE, B, CALL)                                    \
+// Lane layout of the sparse products <T, LPR, NS> and chunks of the pair
+// layout NP by element type and probe count.
+#define LG_DISPATCH(DTYPE, B, CALL)                                                 \
+  ((DTYPE) == LG_F64 ? ((B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
+                     : ((B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
+#define LG_DISPATCH_PAIR(DTYPE, B, CALL)                               \
   ((DTYPE) == LG_F64 ? ((B) <= 64 ? CALL(double, 1) : CALL(double, 2)) \
                      : ((B) <= 64 ? CALL(float, 1) : CALL(float, 2)))
 
@@ -1002,8 +1043,8 @@ extern "C" int lg_slq_forward(const lg_slq_op* op, int B, int m, int ld, const v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
-#define LG_FWD(TT, N)                                                                                             \
-  forward_t<TT, N>(*op, B, m, ld, static_cast<const TT*>(Z), static_cast<TT*>(V), static_cast<TT*>(Y), alpha, beta, \
+#define LG_FWD(TT, L, NS, NP)                                                                                           \
+  forward_t<TT, L, NS, NP>(*op, B, m, ld, static_cast<const TT*>(Z), static_cast<TT*>(V), static_cast<TT*>(Y), alpha, beta, \
                    znorm, w, grid, st)
     e = LG_DISPATCH(op->dtype, B, LG_FWD);
 #undef LG_FWD
@@ -1025,8 +1066,8 @@ extern "C" int lg_slq_backward(const lg_slq_op* op, int B, int m, int ld, const 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
-#define LG_BWD(TT, N)                                                                                         \
-  backward_t<TT, N>(*op, B, m, ld, static_cast<const TT*>(V), static_cast<const TT*>(Y), alpha, beta, g_alpha, \
+#define LG_BWD(TT, L, NS, NP)                                                                                       \
+  backward_t<TT, L, NS, NP>(*op, B, m, ld, static_cast<const TT*>(V), static_cast<const TT*>(Y), alpha, beta, g_alpha, \
                     g_beta, g_out, g_params, w, grid, st)
     e = LG_DISPATCH(op->dtype, B, LG_BWD);
 #undef LG_BWD
@@ -1043,7 +1084,7 @@ extern "C" int lg_slq_apply(const lg_slq_op* op, int B, int ld, const void* X, v
   if ((rc = check_ptr(X, op->dtype, "X")) || (rc = check_ptr(Y, op->dtype, "Y"))) return rc;
   if (X == Y) return fail("lg_slq_apply: X and Y must not alias");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LG_APPLY(TT, N) apply_t<TT, N>(*op, B, ld, static_cast<const TT*>(X), static_cast<TT*>(Y), w, grid, st)
+#define LG_APPLY(TT, L, NS, NP) apply_t<TT, L, NS, NP>(*op, B, ld, static_cast<const TT*>(X), static_cast<TT*>(Y), w, grid, st)
   cudaError_t e = LG_DISPATCH(op->dtype, B, LG_APPLY);
 #undef LG_APPLY
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_apply", e);
@@ -1061,8 +1102,8 @@ extern "C" int lg_slq_apply_vjp(const lg_slq_op* op, int B, int ld, const void* 
   if (!g_params) return fail("lg_slq_apply_vjp: null g_params");
   if (gX == X || gX == G) return fail("lg_slq_apply_vjp: gX must not alias X or G");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LG_VJP(TT, N)                                                                                         \
-  apply_vjp_t<TT, N>(*op, B, ld, static_cast<const TT*>(X), static_cast<const TT*>(G), static_cast<TT*>(gX), \
+#define LG_VJP(TT, L, NS, NP)                                                                                       \
+  apply_vjp_t<TT, L, NS, NP>(*op, B, ld, static_cast<const TT*>(X), static_cast<const TT*>(G), static_cast<TT*>(gX), \
                      g_params, w, grid, st)
   cudaError_t e = LG_DISPATCH(op->dtype, B, LG_VJP);
 #undef LG_VJP
@@ -1122,7 +1163,7 @@ extern "C" int lg_slq_block_start(int n, int B, int ld, int dtype, const void* Z
    normalize_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Z), w.cs[0].out,            \
                                                 static_cast<TT*>(V0), znorm, 1),                            \
    cudaGetLastError())
-    e = LG_DISPATCH(dtype, B, LG_START);
+    e = LG_DISPATCH_PAIR(dtype, B, LG_START);
 #undef LG_START
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_start", e);
@@ -1145,13 +1186,13 @@ extern "C" int lg_slq_block_step(int n, int B, int ld, int dtype, int j, int m, 
 #define LG_STEP(TT, N)                                                                                          \
   (coldot_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Vj), static_cast<const TT*>(W),    \
                                              w.cs[0]),                                                          \
-   recur_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(W), static_cast<const TT*>(Vj), \
+   recur_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(W), static_cast<const TT*>(Vj), \
                                             j > 0 ? static_cast<const TT*>(Vjm1) : nullptr, w.cs[0].out, alpha, \
                                             beta, static_cast<TT*>(R), w.cs[1]),                                \
    normalize_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(R), w.cs[1].out,               \
                                                 static_cast<TT*>(Vnext), beta + j, m),                          \
    cudaGetLastError())
-  cudaError_t e = LG_DISPATCH(dtype, B, LG_STEP);
+  cudaError_t e = LG_DISPATCH_PAIR(dtype, B, LG_STEP);
 #undef LG_STEP
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_step", e);
 }
@@ -1172,11 +1213,11 @@ extern "C" int lg_slq_block_lambda(int n, int B, int ld, int dtype, int j, int m
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // xi == NULL starts the sweep (xi = 0, no dots from a previous step)
 #define LG_LAM(TT, N)                                                                                              \
-  (lam_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(xi), static_cast<const TT*>(xplus), \
+  (lam_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(xi), static_cast<const TT*>(xplus), \
                                           static_cast<const TT*>(xj), xi ? w.cs[1].out : nullptr, g_alpha, g_beta,  \
                                           g_out, beta, static_cast<TT*>(lam), w.munu),                             \
    cudaGetLastError())
-  cudaError_t e = LG_DISPATCH(dtype, B, LG_LAM);
+  cudaError_t e = LG_DISPATCH_PAIR(dtype, B, LG_LAM);
 #undef LG_LAM
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_lambda", e);
 }
@@ -1203,12 +1244,12 @@ extern "C" int lg_slq_block_xi(int n, int B, int ld, int dtype, int j, int m, co
   cudaError_t e = (xjm1 ? reset_counters(w, st) : cudaSuccess);
   if (e == cudaSuccess) {
 #define LG_XI(TT, N)                                                                                               \
-  (xi_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(Plam), static_cast<const TT*>(lam), \
+  (xi_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(Plam), static_cast<const TT*>(lam), \
                                          static_cast<const TT*>(lplus), static_cast<const TT*>(xplus),             \
                                          static_cast<const TT*>(xj), static_cast<const TT*>(xjm1), alpha, beta,    \
                                          w.munu, dcoef, static_cast<const TT*>(G), static_cast<TT*>(xi), w.cs[1]), \
    cudaGetLastError())
-    e = LG_DISPATCH(dtype, B, LG_XI);
+    e = LG_DISPATCH_PAIR(dtype, B, LG_XI);
 #undef LG_XI
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_xi", e);
@@ -1231,11 +1272,11 @@ extern "C" int lg_slq_block_start_grad(int n, int B, int ld, int dtype, const vo
 #define LG_SG(TT, N)                                                                                              \
   (coldot_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0),     \
                                              w.cs[0]),                                                            \
-   start_grad_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0), \
+   start_grad_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0), \
                                                  static_cast<const TT*>(Z), znorm, g_znorm, w.cs[0].out,          \
                                                  static_cast<TT*>(gZ)),                                           \
    cudaGetLastError())
-    e = LG_DISPATCH(dtype, B, LG_SG);
+    e = LG_DISPATCH_PAIR(dtype, B, LG_SG);
 #undef LG_SG
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_start_grad", e);

@@ -1,18 +1,22 @@
-// lg_slq.cuh — building blocks shared by the SLQ kernels (lg_slq.cu: the fused
-// sparse-operator engine; lg_slq_block.cu: block kernels around a caller's
-// matvec).
+// lg_slq.cuh — building blocks shared by the SLQ kernels (lg_slq.cu).
 //
-// Block layout: every block of probe vectors is n x ld, row-major, ld even;
-// columns [0, B) are active (B <= 128).  When B is odd, column B is padding:
-// loads treat it as zero and stores write zero there.  One warp owns one row
-// at a time; lane l owns columns 2l, 2l+1 of each 64-column chunk, so a row
-// is one coalesced 256-byte (fp32) / 512-byte (fp64) access per chunk.
+// Block layout: every block of probe vectors is n x ld, row-major; columns
+// [0, B) are active (B <= 128) and columns [B, ld) are padding, read as zero
+// and written as zero.  ld is a multiple of 4 (fp32) or 2 (fp64) so that a
+// lane's vector of VEC = 16 / sizeof(T) elements is one aligned 16-byte load.
 //
-// Column reductions (dots and norms over the n rows, per probe column): each
-// CTA sums its warps into one partial row, and the last CTA to finish (an
-// atomic ticket, no waiting) reduces the partial rows in a fixed order into
-// `out`, so every result is bitwise repeatable.  The next kernel on the
-// stream reads `out`.
+// Lane layout <T, LPR>: a group of LPR lanes owns one row (RPW = 32 / LPR rows
+// per warp); lane l of the group owns columns ch * LPR * VEC + l * VEC + v.
+// For 64 fp32 probes LPR = 16: a half-warp reads a 256-byte row with one
+// float4 per lane, and every gather instruction of the warp fetches two
+// neighbour rows.  The streaming kernels use the pair layout (LPR = 32,
+// 2 elements per lane).
+//
+// Column reductions (dots and norms over the n rows, per probe column): the
+// row groups of a warp are combined by shuffles, the warps of a CTA in shared
+// memory into one partial row, and the last CTA to finish (an atomic ticket,
+// no waiting) reduces the partial rows in a fixed order into `out`, so every
+// result is bitwise repeatable.  The next kernel on the stream reads `out`.
 #pragma once
 
 #include "lg_common.cuh"
@@ -22,35 +26,67 @@ namespace slq {
 
 constexpr int kT = 512;                    // threads per CTA
 constexpr int kW = kT / 32;                // warps per CTA
+constexpr int kMinCta = 3;                 // CTAs per SM the kernels are built for
 constexpr int kMaxB = 128;                 // active columns per block
 constexpr int kQ = 4;                      // column-sum quantities per partial row
 constexpr int kRowStride = kQ * kMaxB;     // doubles per partial row
 constexpr int kQT = 128;                   // threads of the per-probe small-side kernel
 constexpr unsigned kFull = 0xffffffffu;
 
-template <typename T> struct Vec2;
-template <> struct Vec2<float> { using type = float2; };
-template <> struct Vec2<double> { using type = double2; };
+template <typename T, int N> struct VecT;
+template <> struct VecT<float, 2> { using type = float2; };
+template <> struct VecT<float, 4> { using type = float4; };
+template <> struct VecT<double, 2> { using type = double2; };
 
-// Pair load of columns c0, c0+1; the second is zero when it is padding.
+template <typename T> struct Lanes { static constexpr int VEC = 16 / (int)sizeof(T); };
+
+// Vector load of N consecutive elements (aligned); elements at or beyond
+// `valid` read as zero.
+template <typename T, int N>
+__device__ __forceinline__ void ldvec(const T* p, int valid, T (&v)[N]) {
+  const auto x = *reinterpret_cast<const typename VecT<T, N>::type*>(p);
+  const T* e = reinterpret_cast<const T*>(&x);
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = (i < valid) ? e[i] : T(0);
+}
+template <typename T, int N>
+__device__ __forceinline__ void ldvecd(const T* p, int valid, double (&v)[N]) {
+  T t[N];
+  ldvec<T, N>(p, valid, t);
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = (double)t[i];
+}
+template <typename T, int N>
+__device__ __forceinline__ void stvec(T* p, const double (&v)[N], int valid) {
+  typename VecT<T, N>::type x;
+  T* e = reinterpret_cast<T*>(&x);
+#pragma unroll
+  for (int i = 0; i < N; ++i) e[i] = (i < valid) ? (T)v[i] : T(0);
+  *reinterpret_cast<typename VecT<T, N>::type*>(p) = x;
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void stvec_t(T* p, const T (&v)[N], int valid) {
+  typename VecT<T, N>::type x;
+  T* e = reinterpret_cast<T*>(&x);
+#pragma unroll
+  for (int i = 0; i < N; ++i) e[i] = (i < valid) ? v[i] : T(0);
+  *reinterpret_cast<typename VecT<T, N>::type*>(p) = x;
+}
+
+// Pair-layout helpers (2 elements per lane) of the streaming kernels.
 template <typename T>
 __device__ __forceinline__ void ld2m(const T* p, bool second, double& x, double& y) {
-  const auto v = *reinterpret_cast<const typename Vec2<T>::type*>(p);
-  x = (double)v.x;
-  y = second ? (double)v.y : 0.0;
-}
-template <typename T>
-__device__ __forceinline__ void ld2m_cs(const T* p, bool second, double& x, double& y) {
-  const auto v = __ldcs(reinterpret_cast<const typename Vec2<T>::type*>(p));
+  const auto v = *reinterpret_cast<const typename VecT<T, 2>::type*>(p);
   x = (double)v.x;
   y = second ? (double)v.y : 0.0;
 }
 template <typename T>
 __device__ __forceinline__ void st2(T* p, double x, double y) {
-  typename Vec2<T>::type v;
+  typename VecT<T, 2>::type v;
   v.x = (T)x;
   v.y = (T)y;
-  *reinterpret_cast<typename Vec2<T>::type*>(p) = v;
+  *reinterpret_cast<typename VecT<T, 2>::type*>(p) = v;
 }
 // Value as stored in a block of element type T.
 template <typename T>
@@ -64,23 +100,26 @@ struct ColSum {
   unsigned* counter;   // zero between kernels
 };
 
-// acc[q][ch][i]: this lane's sum of quantity q for column ch*64 + 2*lane + i
-// over the rows it visited.  Called by every thread of the CTA, once, at the
-// end of the kernel.
-template <int NCH>
-__device__ void colsum_finish(const double (&acc)[kQ][NCH][2], int nq, int B, const ColSum cs) {
+// acc[q][ch][v]: this lane's sum of quantity q for its column
+// ch * LPR * VEC + (lane % LPR) * VEC + v over the rows it visited.  Called by
+// every thread of the CTA, once, at the end of the kernel.
+template <int VEC, int NCH, int LPR>
+__device__ void colsum_finish(double (&acc)[kQ][NCH][VEC], int nq, int B, const ColSum cs) {
   __shared__ double s_w[kW * kMaxB];
   __shared__ bool s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = threadIdx.x;
+  const int l = lane % LPR;
   for (int q = 0; q < nq; ++q) {
 #pragma unroll
-    for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
-      if (c0 < B) {
-        s_w[warp * kMaxB + c0] = acc[q][ch][0];
-        s_w[warp * kMaxB + c0 + 1] = acc[q][ch][1];
+    for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        double s = acc[q][ch][v];
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) s += __shfl_xor_sync(kFull, s, o);
+        const int c = ch * LPR * VEC + l * VEC + v;
+        if (lane < LPR && c < B) s_w[warp * kMaxB + c] = s;
       }
-    }
     __syncthreads();
     for (int c = t; c < B; c += kT) {
       double s = 0.0;
@@ -128,40 +167,63 @@ struct Op {
   double shift;
 };
 
-// y += sum_k off[k] X[col[k], :] over row `row` (and yk with doff when DERIV),
-// for this lane's columns.  The warp loads 32 (col, value) pairs at once and
-// broadcasts them by shuffle, so the row gathers issue back to back.
-template <typename T, int NCH, bool DERIV>
-__device__ __forceinline__ void gather_row(const Op& op, const T* __restrict__ off, const T* __restrict__ doff,
-                                           const T* __restrict__ X, int ld, int B, long long row, int lane,
-                                           double (&y)[NCH][2], double (&yk)[NCH][2]) {
-  const int kb = __ldg(op.rowptr + row), ke = __ldg(op.rowptr + row + 1);
-  for (int k0 = kb; k0 < ke; k0 += 32) {
-    const int kk = k0 + lane;
-    int ci = 0;
-    double av = 0.0, dv = 0.0;
-    if (kk < ke) {
-      ci = __ldg(op.col + kk);
-      av = (double)__ldg(off + kk);
-      if (DERIV) dv = (double)__ldg(doff + kk);
-    }
-    const int cnt = min(32, ke - k0);
-#pragma unroll 8
-    for (int s = 0; s < cnt; ++s) {
-      const long long c = __shfl_sync(kFull, ci, s);
-      const double a = __shfl_sync(kFull, av, s);
-      const double d = DERIV ? __shfl_sync(kFull, dv, s) : 0.0;
+// Row-group geometry of a lane in layout <T, LPR>.
+template <typename T, int LPR>
+struct RowLanes {
+  static constexpr int VEC = Lanes<T>::VEC;
+  static constexpr int RPW = 32 / LPR;
+  static constexpr int CPP = LPR * VEC;      // columns per pass
+  int lane, l, sub;
+  __device__ RowLanes() : lane(threadIdx.x & 31), l((threadIdx.x & 31) % LPR), sub((threadIdx.x & 31) / LPR) {}
+  __device__ int col0(int ch) const { return ch * CPP + l * VEC; }
+  __device__ long long first_row() const { return ((long long)blockIdx.x * kW + (threadIdx.x >> 5)) * RPW + sub; }
+  __device__ long long first_warp_row() const { return ((long long)blockIdx.x * kW + (threadIdx.x >> 5)) * RPW; }
+  __device__ static long long stride() { return (long long)gridDim.x * kW * RPW; }
+};
+
+// y += sum_k off[k] X[col[k], :] over the row of this lane group (and yk with
+// doff when DERIV), accumulated in T.  The group loads LPR (col, value) pairs
+// at once and broadcasts them by shuffle; the loop runs to the longest row of
+// the warp so that every lane takes part in every shuffle.
+template <typename T, int LPR, int NCH, bool DERIV>
+__device__ __forceinline__ void gather_rows(const Op& op, const T* __restrict__ off, const T* __restrict__ doff,
+                                            const T* __restrict__ X, int ld, int B, bool valid, long long row,
+                                            const RowLanes<T, LPR>& g, T (&y)[NCH][Lanes<T>::VEC],
+                                            T (&yk)[NCH][Lanes<T>::VEC]) {
+  constexpr int VEC = Lanes<T>::VEC;
+  const int kb = valid ? __ldg(op.rowptr + row) : 0;
+  const int cnt = valid ? __ldg(op.rowptr + row + 1) - kb : 0;
+  int mx = cnt;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        const int c0 = ch * 64 + 2 * lane;
-        if (c0 < B) {
-          double vx, vy;
-          ld2m(X + c * ld + c0, c0 + 1 < B, vx, vy);
-          y[ch][0] += a * vx;
-          y[ch][1] += a * vy;
-          if (DERIV) {
-            yk[ch][0] += d * vx;
-            yk[ch][1] += d * vy;
+  for (int o = LPR; o < 32; o <<= 1) mx = max(mx, __shfl_xor_sync(kFull, mx, o));
+  const int base = g.lane - g.l;
+  for (int k0 = 0; k0 < mx; k0 += LPR) {
+    const int kk = k0 + g.l;
+    int ci = 0;
+    T av = T(0), dv = T(0);
+    if (kk < cnt) {
+      ci = __ldg(op.col + kb + kk);
+      av = __ldg(off + kb + kk);
+      if (DERIV) dv = __ldg(doff + kb + kk);
+    }
+    const int nb = min(LPR, mx - k0);
+#pragma unroll 8
+    for (int s = 0; s < nb; ++s) {
+      const long long c = __shfl_sync(kFull, ci, base + s);
+      const T a = __shfl_sync(kFull, av, base + s);
+      const T d = DERIV ? __shfl_sync(kFull, dv, base + s) : T(0);
+      if (k0 + s < cnt) {
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) {
+          const int c0 = g.col0(ch);
+          if (c0 < B) {
+            T v[VEC];
+            ldvec<T, VEC>(X + c * ld + c0, B - c0, v);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+              y[ch][i] += a * v[i];
+              if (DERIV) yk[ch][i] += d * v[i];
+            }
           }
         }
       }

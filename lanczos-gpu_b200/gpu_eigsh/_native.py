@@ -130,6 +130,7 @@ SIGNATURES = {
     "lg_slq_block_xi": (_I, [_I, _I, _I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
     "lg_slq_block_start_grad": (_I, [_I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
     "lg_imgp_laplacian": (_I, [_I, C.c_longlong, _V, _V, _I, _V, C.c_double, _I, _V, _V, _V, _V, _V, _V]),
+    "lg_graph_bfs_levels": (_I, [_I, _V, _V, _I, _V, _V, _PI, _V]),
     "lg_dense_matvec": (_I, [_I, _I, _V, _V, _I, _V, _I, _V]),
     "lg_outer_accumulate": (_I, [_I, _I, _V, _V, _I, _V, _V]),
     "lg_status_string": (C.c_char_p, [C.c_int]),

@@ -36,8 +36,11 @@ def stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def even(b: int) -> int:
-    return b + (b & 1)
+def ld_for(b: int, dtype: torch.dtype) -> int:
+    """Row stride of a block of b probe columns: a multiple of 4 (fp32) or 2
+    (fp64) elements, so that every lane's vector is one 16-byte access."""
+    q = 4 if dtype == torch.float32 else 2
+    return (b + q - 1) // q * q
 
 
 def workspace(op: _native.SlqOp | None, B: int, ld: int, device: torch.device):
@@ -53,10 +56,10 @@ def blocks(k: int, n: int, ld: int, dtype: torch.dtype, device: torch.device, ze
 
 
 def to_block(X: torch.Tensor, device: torch.device, dtype: torch.dtype):
-    """(n,) or (n, B) -> contiguous (n, ld) block on `device` (padding column zero)."""
+    """(n,) or (n, B) -> contiguous (n, ld) block on `device` (padding columns zero)."""
     X2 = X.reshape(-1, 1) if X.dim() == 1 else X
     n, B = X2.shape
-    ld = even(B)
+    ld = ld_for(B, dtype)
     if ld == B and X2.is_contiguous() and X2.device == device and X2.dtype == dtype:
         return X2, B, ld
     out = torch.zeros((n, ld), dtype=dtype, device=device)

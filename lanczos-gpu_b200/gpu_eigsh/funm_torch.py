@@ -92,7 +92,7 @@ class _Basis:
     def __init__(self, n: int, B: int, m: int, dtype, user_device):
         self.dev = _slq.require_cuda()
         self.n, self.B, self.m, self.dtype = n, B, m, dtype
-        self.ld = _slq.even(B)
+        self.ld = _slq.ld_for(B, dtype)
         self.user_device = torch.device(user_device)
         self.rec = _slq.BlockRecurrence(n, B, self.ld, dtype, self.dev)
         self.V = _slq.blocks(m + 1, n, self.ld, dtype, self.dev)

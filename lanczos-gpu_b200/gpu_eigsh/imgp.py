@@ -46,11 +46,13 @@ def _scalar(t) -> float:
 class ImgpPrecisionMatvec:
     """Callable P(theta, kappa) X on the GPU; see the module docstring."""
 
-    def __init__(self, x_edge_dists, idx, operator_dim: int, nu: int, self_loops: bool = True):
+    def __init__(self, x_edge_dists, idx, operator_dim: int, nu: int, self_loops: bool = True,
+                 reorder: bool = True):
         dev = _slq.require_cuda()
-        if x_edge_dists.is_cuda:
-            dev = x_edge_dists.device
-        d2 = torch.as_tensor(x_edge_dists).detach().to(dev)
+        d2 = torch.as_tensor(x_edge_dists).detach()
+        if d2.is_cuda:
+            dev = d2.device
+        d2 = d2.to(dev)
         if d2.dtype not in (torch.float32, torch.float64):
             d2 = d2.to(torch.float64)
         idx = torch.as_tensor(idx).to(dev, torch.int64)
@@ -64,22 +66,61 @@ class ImgpPrecisionMatvec:
             raise ValueError("graph too large for int32 CSR indices")
         if M and (int(idx.min()) < 0 or int(idx.max()) >= n):
             raise ValueError("edge index out of range [0, operator_dim)")
-        # CSR with both directions of every edge, rows sorted by (row, col)
-        rows = torch.cat([idx[0], idx[1]])
-        cols = torch.cat([idx[1], idx[0]])
-        eid = torch.arange(M, device=dev).repeat(2)
-        order = torch.argsort(rows * n + cols, stable=True)
-        counts = torch.bincount(rows, minlength=n)
-        self.rowptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
-        self.rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
-        self.col = cols[order].to(torch.int32).contiguous()
-        self.d2 = d2[eid[order]].contiguous()
         self.n, self.nu, self.self_loops = n, int(nu), bool(self_loops)
         self.dtype = d2.dtype
         self.device = dev
+        rows = torch.cat([idx[0], idx[1]])
+        cols = torch.cat([idx[1], idx[0]])
+        eid = torch.arange(M, device=dev).repeat(2)
+        self.rowptr, self.col, self.d2 = self._csr(rows, cols, eid, d2)
+        # row order for locality of the neighbour gathers: BFS levels from a
+        # peripheral vertex; perm[new] = old, pos[old] = new
+        self.perm = self.pos = None
+        if reorder and M:
+            perm = self._bfs_order()
+            pos = torch.empty_like(perm)
+            pos[perm] = torch.arange(n, device=dev)
+            self.rowptr, self.col, self.d2 = self._csr(pos[rows], pos[cols], eid, d2)
+            self.perm, self.pos = perm, pos
         self.nnz = int(self.col.numel())
         self._lap_key = None
         self._lap = None
+
+    def _csr(self, rows, cols, eid, d2):
+        """CSR (rows sorted by (row, col)) with the squared distance of every entry."""
+        n = self.n
+        order = torch.argsort(rows * n + cols, stable=True)
+        counts = torch.bincount(rows, minlength=n)
+        rowptr = torch.zeros(n + 1, dtype=torch.int32, device=self.device)
+        rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        return rowptr, cols[order].to(torch.int32).contiguous(), d2[eid[order]].contiguous()
+
+    def _bfs_levels(self, start: int) -> torch.Tensor:
+        n = self.n
+        level = torch.empty(n, dtype=torch.int32, device=self.device)
+        work = torch.empty(2 * n + 2, dtype=torch.int32, device=self.device)
+        rounds = _native.C.c_int(0)
+        _native.check(_native.lib.lg_graph_bfs_levels(n, self.rowptr.data_ptr(), self.col.data_ptr(), int(start),
+                                                      level.data_ptr(), work.data_ptr(), _native.C.byref(rounds),
+                                                      _slq.stream(self.device)))
+        return level
+
+    def _bfs_order(self) -> torch.Tensor:
+        """Vertices sorted by (BFS level from a pseudo-peripheral vertex, index);
+        unreachable vertices last."""
+        n = self.n
+        level = self._bfs_levels(0)
+        start = int(torch.argmax(level))             # a farthest vertex from 0
+        level = self._bfs_levels(start).to(torch.int64)
+        level = torch.where(level < 0, torch.full_like(level, n), level)
+        return torch.argsort(level * n + torch.arange(n, device=self.device))
+
+    def to_internal(self, X: torch.Tensor) -> torch.Tensor:
+        """Rows of X (caller's vertex order) in the operator's row order."""
+        return X if self.perm is None else X.index_select(0, self.perm)
+
+    def to_caller(self, Y: torch.Tensor) -> torch.Tensor:
+        return Y if self.pos is None else Y.index_select(0, self.pos)
 
     # -- L_sym(kappa) and dL/dkappa -----------------------------------------------
     def laplacian(self, kappa: float):
@@ -135,9 +176,9 @@ class _PrecisionApply(torch.autograd.Function):
         X2 = rhs.reshape(-1, 1) if rhs.dim() == 1 else rhs
         if X2.shape[0] != mv.n:
             raise ValueError(f"rhs has {X2.shape[0]} rows, the operator {mv.n}")
-        parts = _blocked(X2.detach(), mv.device, mv.dtype)
+        parts = _blocked(mv.to_internal(X2.detach().to(mv.device, mv.dtype)), mv.device, mv.dtype)
         outs = [op.apply(blk, b, blk.shape[1])[:, :b] for blk, b in parts]
-        Y = torch.cat(outs, dim=1) if len(outs) > 1 else outs[0]
+        Y = mv.to_caller(torch.cat(outs, dim=1) if len(outs) > 1 else outs[0])
         ctx.mv, ctx.ell, ctx.kap, ctx.shape = mv, ell, kap, rhs.shape
         ctx.rhs_dev, ctx.rhs_dtype = rhs.device, rhs.dtype
         ctx.parts = parts
@@ -154,13 +195,14 @@ class _PrecisionApply(torch.autograd.Function):
         mv = ctx.mv
         op = mv.operator(ctx.ell, ctx.kap)
         G2 = g.reshape(-1, 1) if g.dim() == 1 else g
-        gparts = _blocked(G2.detach(), mv.device, mv.dtype)
+        gparts = _blocked(mv.to_internal(G2.detach().to(mv.device, mv.dtype)), mv.device, mv.dtype)
         gxs, gp = [], torch.zeros(2, dtype=torch.float64, device=mv.device)
         for (blk, b), (gblk, _) in zip(ctx.parts, gparts):
             gX, gpp = op.apply_vjp(blk, gblk, b, blk.shape[1])
             gxs.append(gX[:, :b])
             gp = gp + gpp
-        g_rhs = (torch.cat(gxs, dim=1) if len(gxs) > 1 else gxs[0]).reshape(ctx.shape).to(ctx.rhs_dev, ctx.rhs_dtype)
+        g_rhs = mv.to_caller(torch.cat(gxs, dim=1) if len(gxs) > 1 else gxs[0])
+        g_rhs = g_rhs.reshape(ctx.shape).to(ctx.rhs_dev, ctx.rhs_dtype)
         g_ell = gp[1] * mv.shift_derivative(ctx.ell)
         g_kap = gp[0]
         out = [g_rhs]
@@ -185,7 +227,7 @@ def make_imgp_precision_matvec(*, x_edge_dists, idx, operator_dim, nu, normaliza
 def _matmul_symmetric_laplacian(rhs, x_edge_dists, idx, operator_dim, graphbandwidth, self_loops=True):
     """L_sym(kappa) rhs (the reference's one-shot helper, imgp.py:210-226): the
     power-1 operator with zero shift."""
-    mv = ImgpPrecisionMatvec(x_edge_dists, idx, operator_dim, 1, self_loops)
+    mv = ImgpPrecisionMatvec(x_edge_dists, idx, operator_dim, 1, self_loops, reorder=False)
     kap = _scalar(graphbandwidth)
     off, diag, doff, ddiag = mv.laplacian(kap)
     op = _slq.Operator(mv.n, mv.rowptr, mv.col, off, diag, doff, ddiag, 0.0, 1, mv.dtype)
@@ -210,7 +252,7 @@ class _SLQImgp(torch.autograd.Function):
         op = mv.operator(ell, kap)
         P = Z.shape[1]
         m = int(lanczos_m)
-        parts = _blocked(Z, mv.device, mv.dtype)
+        parts = _blocked(mv.to_internal(Z), mv.device, mv.dtype)
         q_all, saved = [], []
         for blk, b in parts:
             ld = blk.shape[1]

@@ -249,6 +249,31 @@ def test_slq_cpu_inputs_come_back_on_cpu(torch_cuda):
     assert abs(float(k.grad) - float(k2.grad)) <= 1e-9 * abs(float(k2.grad))
 
 
+def test_row_order_does_not_change_results(torch_cuda):
+    """The locality ordering of the operator's rows (BFS levels) changes only the
+    summation order: log-det and gradients agree with the caller's order."""
+    torch = torch_cuda
+    from gpu_eigsh.funm_torch import slq_logdet
+    from gpu_eigsh.imgp import ImgpPrecisionMatvec
+
+    n = 3000
+    idx_np, d2_np = _knn_edges(n, seed=21)
+    d2, idx = torch.from_numpy(d2_np).cuda(), torch.from_numpy(idx_np).cuda()
+    res = []
+    for reorder in (True, False):
+        mv = ImgpPrecisionMatvec(d2, idx, n, 2, True, reorder=reorder)
+        assert (mv.perm is not None) == reorder
+        e = torch.tensor(0.9, dtype=torch.float64, device="cuda", requires_grad=True)
+        k = torch.tensor(1.2, dtype=torch.float64, device="cuda", requires_grad=True)
+        ld = slq_logdet(mv, n, (e, k), m_probes=12, lanczos_m=25, seed=4, device="cuda")
+        ld.backward()
+        X = torch.randn(n, 5, dtype=torch.float64, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+        res.append([float(ld.detach()), float(e.grad), float(k.grad), mv(X, e.detach(), k.detach())])
+    for a, b in zip(res[0][:3], res[1][:3]):
+        assert abs(a - b) <= 1e-10 * abs(b)
+    assert _rel(res[0][3].cpu(), res[1][3].cpu()) < 1e-13
+
+
 # ---------------------------------------------------------------------------
 # Generic operator paths
 # ---------------------------------------------------------------------------
