@@ -147,55 +147,49 @@ __global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> 
       const int c0 = g.col0(ch);
       if (c0 >= B) continue;
       const int nv = B - c0;
-      double xs[VEC], o[VEC];
+      T o[VEC];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        xs[v] = (double)x[ch][v];
-        o[v] = (double)y[ch][v];
-      }
+      for (int v = 0; v < VEC; ++v) o[v] = y[ch][v];
       if (FIRST) {
         // the product is linear: A (x / ||r||) = (A x) / ||r|| per column
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
-          xs[v] *= k0[ch][v];
-          o[v] *= k0[ch][v];
+          x[ch][v] *= (T)k0[ch][v];
+          o[v] *= (T)k0[ch][v];
         }
-        stvec<T, VEC>(a.Vj + row * ld + c0, xs, nv);
+        stvec_t<T, VEC>(a.Vj + row * ld + c0, x[ch], nv);
       }
       if (AXPY) {
         T vj[VEC], vm[VEC];
-        ldvec<T, VEC>(a.Vj + row * ld + c0, nv, vj);
+        ldvec<T, VEC>(a.Vj + row * ld + c0, VEC, vj);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) vm[v] = T(0);
-        if (a.Vjm1) ldvec<T, VEC>(a.Vjm1 + row * ld + c0, nv, vm);
+        if (a.Vjm1) ldvec<T, VEC>(a.Vjm1 + row * ld + c0, VEC, vm);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
-          o[v] = rnd<T>(o[v] - k0[ch][v] * (double)vj[v] - k1[ch][v] * (double)vm[v]);
-          acc[0][ch][v] += o[v] * o[v];
+          o[v] = o[v] - (T)k0[ch][v] * vj[v] - (T)k1[ch][v] * vm[v];
+          acc[0][ch][v] += (double)o[v] * (double)o[v];
         }
-      } else {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) o[v] = rnd<T>(o[v]);
       }
       if (DOT != kDotNone) {
-        double pv[VEC];
+        T pv[VEC];
         if (DOT == kDotVj) {
           if (FIRST) {
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) pv[v] = rnd<T>(xs[v]);
+            for (int v = 0; v < VEC; ++v) pv[v] = x[ch][v];
           } else {
-            ldvecd<T, VEC>(a.Vj + row * ld + c0, nv, pv);
+            ldvec<T, VEC>(a.Vj + row * ld + c0, VEC, pv);
           }
         } else if (DOT == kDotBlock) {
-          ldvecd<T, VEC>(a.Dsrc + row * ld + c0, nv, pv);
+          ldvec<T, VEC>(a.Dsrc + row * ld + c0, VEC, pv);
         } else {
 #pragma unroll
           for (int v = 0; v < VEC; ++v) pv[v] = o[v];
         }
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) acc[0][ch][v] += pv[v] * o[v];
+        for (int v = 0; v < VEC; ++v) acc[0][ch][v] += (double)pv[v] * (double)o[v];
       }
-      stvec<T, VEC>(a.Out + row * ld + c0, o, nv);
+      stvec_t<T, VEC>(a.Out + row * ld + c0, o, nv);
     }
   }
   if (DOT != kDotNone || AXPY) colsum_finish<VEC, NCH, LPR>(acc, 1, B, a.cout);
@@ -525,32 +519,32 @@ __global__ void __launch_bounds__(kT, 2) bwd_spmm_kernel(const BwdArgs<T> a) {
       ldvec<T, VEC>(a.Y + row * ld + c0, nv, yv);
 #pragma unroll
       for (int v = 0; v < VEC; ++v) {
-        if (DERIV) sk += (double)yv[v] * (double)yk[ch][v];
-        sc += (double)yv[v] * (double)mi[ch][v];
+        if (v < nv) {   // yk of a padding column may hold gathered padding values
+          if (DERIV) sk += (double)yv[v] * (double)yk[ch][v];
+          sc += (double)yv[v] * (double)mi[ch][v];
+        }
       }
       if (!LAST) {
         stvec_t<T, VEC>(a.Mout + row * ld + c0, y[ch], nv);
       } else if (dots) {
         // xi_{j-1}; Y is x_j here (p = nu - 1)
-        T l[VEC], p[VEC], q[VEC], u[VEC], xo[VEC];
-        ldvec<T, VEC>(a.lam + row * ld + c0, nv, l);
-        ldvec<T, VEC>(a.xplus + row * ld + c0, nv, p);
+        T l[VEC], p[VEC], q[VEC], u[VEC];
+        ldvec<T, VEC>(a.lam + row * ld + c0, VEC, l);
+        ldvec<T, VEC>(a.xplus + row * ld + c0, VEC, p);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) q[v] = T(0);
-        if (a.lplus) ldvec<T, VEC>(a.lplus + row * ld + c0, nv, q);
-        ldvec<T, VEC>(a.xjm1 + row * ld + c0, nv, u);
+        if (a.lplus) ldvec<T, VEC>(a.lplus + row * ld + c0, VEC, q);
+        ldvec<T, VEC>(a.xjm1 + row * ld + c0, VEC, u);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
           const int c = min(c0 + v, kMaxB - 1);
-          const double x = (v < nv) ? (double)(T)(-(double)y[ch][v] + s_a[c] * (double)l[v] +
-                                                  s_b[c] * (double)q[v] - s_bn[c] * (double)p[v])
-                                    : 0.0;
-          xo[v] = (T)x;
+          const T x = -y[ch][v] + (T)s_a[c] * l[v] + (T)s_b[c] * q[v] - (T)s_bn[c] * p[v];
+          y[ch][v] = x;
           acc[0][ch][v] += (double)l[v] * (double)u[v];
-          acc[1][ch][v] += (double)yv[v] * x;
-          acc[2][ch][v] += (double)u[v] * x;
+          acc[1][ch][v] += (double)yv[v] * (double)x;
+          acc[2][ch][v] += (double)u[v] * (double)x;
         }
-        stvec_t<T, VEC>(a.xi + row * ld + c0, xo, nv);
+        stvec_t<T, VEC>(a.xi + row * ld + c0, y[ch], nv);
       }
     }
   }

@@ -217,8 +217,10 @@ __device__ __forceinline__ void gather_rows(const Op& op, const T* __restrict__ 
         for (int ch = 0; ch < NCH; ++ch) {
           const int c0 = g.col0(ch);
           if (c0 < B) {
+            // padding columns (>= B) of X may hold anything: they only ever
+            // reach the padding columns of y, which are neither stored nor summed
             T v[VEC];
-            ldvec<T, VEC>(X + c * ld + c0, B - c0, v);
+            ldvec<T, VEC>(X + c * ld + c0, VEC, v);
 #pragma unroll
             for (int i = 0; i < VEC; ++i) {
               y[ch][i] += a * v[i];
