@@ -201,7 +201,11 @@ def slq_cpu_baseline(idx, d2, n=N_POINTS, m_full=SLQ_M):
                       f"lanczos_m={m_full}"}
 
 
-def run_slq(args, dev, with_e2e, with_cpu):
+def run_slq(args, dev, with_e2e, with_cpu, world=1, rank=0):
+    """The SLQ leg.  With N ranks the 64 probes are split across the GPUs
+    (gpu_eigsh.distributed: one all-reduce of the quadrature sums, one of the
+    parameter gradients), so the total work is fixed (strong scaling) and the
+    time is the max over ranks."""
     import torch
 
     from gpu_eigsh import _slq
@@ -214,17 +218,26 @@ def run_slq(args, dev, with_e2e, with_cpu):
                                     idx=torch.from_numpy(idx).to(dev), operator_dim=n, nu=SLQ_NU)
     ell = torch.tensor(1.0, dtype=torch.float32, device=dev, requires_grad=True)
     kap = torch.tensor(1.0, dtype=torch.float32, device=dev, requires_grad=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        from gpu_eigsh.distributed import probe_range, slq_logdet_sharded
 
     def step(e, k, device):
         e.grad = None
         k.grad = None
-        ld = slq_logdet(mv, n, (e, k), m_probes=SLQ_PROBES, lanczos_m=M, seed=0, dtype=torch.float32,
-                        device=device)
+        if world > 1:
+            ld = slq_logdet_sharded(mv, n, (e, k), m_probes=SLQ_PROBES, lanczos_m=M, seed=0, dtype=torch.float32)
+        else:
+            ld = slq_logdet(mv, n, (e, k), m_probes=SLQ_PROBES, lanczos_m=M, seed=0, dtype=torch.float32,
+                            device=device)
         ld.backward()
         return ld
 
     for _ in range(args.warmup):
         step(ell, kap, dev)
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -232,18 +245,30 @@ def run_slq(args, dev, with_e2e, with_cpu):
         ld = step(ell, kap, dev)
     ev1.record()
     torch.cuda.synchronize()
-    sec = ev0.elapsed_time(ev1) / 1000.0 / args.steps
-    out = {"workload": SLQ_WORKLOAD if (n, M) == (N_POINTS, SLQ_M) else f"reduced: n={n}, lanczos_m={M}", "metric": "slq_logdet_grad_sec", "value": sec, "unit": "s/logdet+grad",
-           "higher_is_better": False, "n": n, "edges": int(idx.shape[1]), "csr_nnz": mv.nnz,
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sec = ms / 1000.0 / args.steps
+    full = (n, M) == (N_POINTS, SLQ_M)
+    out = {"workload": SLQ_WORKLOAD if full else f"reduced: n={n}, lanczos_m={M}", "metric": "slq_logdet_grad_sec",
+           "value": sec, "unit": "s/logdet+grad", "higher_is_better": False,
+           "scaling": "strong" if world > 1 else None,
+           "parallelism": f"probes sharded over {world} GPUs" if world > 1 else "1 GPU",
+           "n": n, "edges": int(idx.shape[1]), "csr_nnz": mv.nnz,
            "logdet": float(ld.detach()), "grad_theta": float(ell.grad), "grad_kappa": float(kap.grad)}
+    B = SLQ_PROBES
+    if world > 1:
+        c0, c1 = probe_range(SLQ_PROBES, rank, world)
+        B = c1 - c0
 
     # roofline: the fused forward (nu sparse products per step, recurrence
     # folded in) and backward, timed alone with events on the launch stream
     op = mv.operator(1.0, 1.0)
-    Z, B = None, SLQ_PROBES
     from gpu_eigsh.funm_torch import _probes
 
-    Z = _probes(n, SLQ_PROBES, 0, torch.float32, dev)
+    Z = _probes(n, SLQ_PROBES, 0, torch.float32, dev)[:, :B].contiguous()
     fwd_b, bwd_b = slq_bytes(n, mv.nnz, B, SLQ_NU, M, 4)
     tf, tb = [], []
     for r in range(3):
@@ -345,7 +370,10 @@ def run_ours(args):
     import gpu_eigsh
 
     if args.only_slq:
-        out = run_slq(args, torch.device("cuda", local), with_e2e=False, with_cpu=False)
+        out = run_slq(args, torch.device("cuda", local), with_e2e=False, with_cpu=False, world=world, rank=rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         if rank == 0:
             print(json.dumps(out), flush=True)
         return 0
@@ -451,8 +479,9 @@ def run_ours(args):
     plan.close()
     del L
     if not args.no_slq:
-        line["slq"] = run_slq(args, dev, with_e2e=(rank == 0 and not args.no_e2e),
-                              with_cpu=(rank == 0 and not args.no_cpu_baseline))
+        # with N > 1 every rank takes part in the sharded e2e steps (collectives)
+        line["slq"] = run_slq(args, dev, with_e2e=(not args.no_e2e) and (world > 1 or rank == 0),
+                              with_cpu=(rank == 0 and not args.no_cpu_baseline), world=world, rank=rank)
         line["gpu_launches"] += line["slq"]["gpu_launches_per_step"] * args.steps
     if world > 1:
         dist.barrier()

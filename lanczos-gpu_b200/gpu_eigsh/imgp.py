@@ -240,6 +240,52 @@ def _matmul_symmetric_laplacian(rhs, x_edge_dists, idx, operator_dim, graphbandw
 # ---------------------------------------------------------------------------
 # Fused stochastic Lanczos quadrature on this operator
 # ---------------------------------------------------------------------------
+class ImgpSLQEngine:
+    """The fused SLQ of one probe set on one GPU, split into a forward that
+    returns the sum of the per-probe quadratures and a backward that returns
+    the gradient of that sum with respect to (lengthscale, graphbandwidth).
+    `p_total` is the number of probes of the whole estimate (the mean divides by
+    it), so that shards of the probes on several GPUs add up."""
+
+    def __init__(self, mv: ImgpPrecisionMatvec, lanczos_m: int, lengthscale: float, graphbandwidth: float):
+        self.mv, self.m = mv, int(lanczos_m)
+        self.ell, self.kap = float(lengthscale), float(graphbandwidth)
+
+    def forward(self, Z, p_total: int, keep: bool = True):
+        """Z: (n, b) probes in the caller's vertex order.  Returns (sum_b q_b as
+        a 0-d fp64 tensor, state for backward)."""
+        mv = self.mv
+        op = mv.operator(self.ell, self.kap)
+        q_all, saved = [], []
+        for blk, b in _blocked(mv.to_internal(Z), mv.device, mv.dtype):
+            ld = blk.shape[1]
+            V, Y, alpha, beta, znorm = op.forward(blk, b, ld, self.m)
+            q, ga, gb, _ = _slq.small_side(alpha, beta, znorm, "log", 0, g_scale=1.0 / p_total)
+            q_all.append(q)
+            if keep:
+                saved.append((V, Y, alpha, beta, ga, gb, b, ld))
+        return torch.cat(q_all).sum(), saved
+
+    def backward(self, saved, g_out):
+        """g_out: gradient of the loss with respect to the mean (fp64, 1 element
+        on the operator's device).  Returns [d/d lengthscale, d/d graphbandwidth]
+        of this shard's contribution as fp64 device tensors."""
+        mv = self.mv
+        op = mv.operator(self.ell, self.kap)
+        gp = torch.zeros(2, dtype=torch.float64, device=mv.device)
+        for V, Y, alpha, beta, ga, gb, b, ld in saved:
+            gp = gp + op.backward(V, Y, alpha, beta, ga, gb, g_out, b, ld, self.m)
+        return [gp[1] * mv.shift_derivative(self.ell), gp[0]]
+
+
+def _param_info(params):
+    return [(t.device, t.dtype, t.shape) if torch.is_tensor(t) else None for t in params]
+
+
+def _grads_to_params(grads, pinfo):
+    return [None if info is None else g.to(info[0], info[1]).reshape(info[2]) for g, info in zip(grads, pinfo)]
+
+
 class _SLQImgp(torch.autograd.Function):
     """log det P(theta, kappa) by SLQ over the probe columns of Z, with the
     Kraemer backward, entirely on the fused kernels (lg_slq_forward /
@@ -248,39 +294,20 @@ class _SLQImgp(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, mv: ImgpPrecisionMatvec, Z, lanczos_m: int, lengthscale, graphbandwidth):
-        ell, kap = _scalar(lengthscale), _scalar(graphbandwidth)
-        op = mv.operator(ell, kap)
-        P = Z.shape[1]
-        m = int(lanczos_m)
-        parts = _blocked(mv.to_internal(Z), mv.device, mv.dtype)
-        q_all, saved = [], []
-        for blk, b in parts:
-            ld = blk.shape[1]
-            V, Y, alpha, beta, znorm = op.forward(blk, b, ld, m)
-            q, ga, gb, _ = _slq.small_side(alpha, beta, znorm, "log", 0, g_scale=1.0 / P)
-            q_all.append(q)
-            saved.append((V, Y, alpha, beta, ga, gb, b, ld))
-        ld_val = torch.cat(q_all).sum() / P
+        eng = ImgpSLQEngine(mv, lanczos_m, _scalar(lengthscale), _scalar(graphbandwidth))
         need = any(ctx.needs_input_grad[3:5])
-        ctx.saved = saved if need else None
-        ctx.mv, ctx.ell, ctx.kap, ctx.m = mv, ell, kap, m
-        ctx.pinfo = [(t.device, t.dtype, t.shape) if torch.is_tensor(t) else None
-                     for t in (lengthscale, graphbandwidth)]
-        return ld_val.to(Z.dtype)
+        total, saved = eng.forward(Z, Z.shape[1], keep=need)
+        ctx.eng, ctx.saved = eng, saved
+        ctx.pinfo = _param_info((lengthscale, graphbandwidth))
+        return (total / Z.shape[1]).to(Z.dtype)
 
     @staticmethod
     def backward(ctx, g_ld):
-        mv = ctx.mv
-        op = mv.operator(ctx.ell, ctx.kap)
-        g_out = g_ld.detach().to(mv.device, torch.float64).reshape(1)
-        gp = torch.zeros(2, dtype=torch.float64, device=mv.device)
-        for V, Y, alpha, beta, ga, gb, b, ld in ctx.saved:
-            gp = gp + op.backward(V, Y, alpha, beta, ga, gb, g_out, b, ld, ctx.m)
-        grads = [gp[1] * mv.shift_derivative(ctx.ell), gp[0]]
-        out = []
-        for gv, info in zip(grads, ctx.pinfo):
-            out.append(None if info is None else gv.to(info[0], info[1]).reshape(info[2]))
+        eng = ctx.eng
+        g_out = g_ld.detach().to(eng.mv.device, torch.float64).reshape(1)
+        grads = eng.backward(ctx.saved, g_out)
         ctx.saved = None
+        out = _grads_to_params(grads, ctx.pinfo)
         return None, None, None, out[0], out[1]
 
 
