@@ -20,7 +20,6 @@ constexpr int kPartStride = 136;       // doubles per partial-sum row: 128 colum
 constexpr int kPartScalar = 128;       // slot of the first scalar in a partial row
 constexpr int kRowAlign = 256;         // leading dimension of V is a multiple of this
 constexpr int kGsThreads = 1024;       // threads of the Gram-Schmidt pass kernels (one CTA per SM)
-constexpr int kMaxStages = 8;          // deepest TMA ring
 
 constexpr double kDgks = 0.7071067811865476;      // 1/sqrt(2)
 constexpr double kSafeMin = DBL_MIN;
@@ -43,7 +42,7 @@ enum Status {
   STATUS_PASS3 = 1,       // DGKS wants a third Gram-Schmidt pass at step ST_STEP
   STATUS_BREAKDOWN = 2,   // invariant subspace found after step ST_STEP
   STATUS_TRIDIAG_FAIL = 3,
-  STATUS_TIMEOUT = 4,     // a bounded wait on a TMA barrier gave up
+  STATUS_TIMEOUT = 4,     // a bounded device-side wait gave up
 };
 
 // Device-side double scalars.
@@ -147,65 +146,6 @@ __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __host__ __device__ __forceinline__ double uniform_centered(uint64_t seed, uint64_t i) {
   uint64_t r = mix64(seed * 0x100000001B3ull + mix64(i));
   return (double)(r >> 11) * (1.0 / 9007199254740992.0) - 0.5;
-}
-
-// ---------------------------------------------------------------------------
-// TMA bulk copies (cp.async.bulk, global -> shared, completion on an
-// mbarrier).  No multicast anywhere: every copy reads this GPU's own memory.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init_fence() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-// dst and src 16-byte aligned; bytes a multiple of 16.
-__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: gives up after ~`limit_cycles` SM clock cycles and returns
-// false.  A TMA read of resident memory completes in microseconds, so the
-// limit (about a second) is only reached when something is badly wrong.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  long long limit_cycles = 2000000000ll) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit_cycles) return false;
-  }
-  return true;
 }
 
 }  // namespace lg
