@@ -997,9 +997,10 @@ using namespace lg::slq;
 
 // Lane layout of the sparse products <T, LPR, NS> and chunks of the pair
 // layout NP by element type and probe count.
-#define LG_DISPATCH(DTYPE, B, CALL)                                                 \
-  ((DTYPE) == LG_F64 ? ((B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
-                     : ((B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
+#define LG_DISPATCH(DTYPE, B, CALL)                                                                   \
+  ((DTYPE) == LG_F64                                                                                   \
+       ? ((B) <= 32 ? CALL(double, 16, 1, 1) : (B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
+       : ((B) <= 32 ? CALL(float, 8, 1, 1) : (B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
 #define LG_DISPATCH_PAIR(DTYPE, B, CALL)                               \
   ((DTYPE) == LG_F64 ? ((B) <= 64 ? CALL(double, 1) : CALL(double, 2)) \
                      : ((B) <= 64 ? CALL(float, 1) : CALL(float, 2)))
