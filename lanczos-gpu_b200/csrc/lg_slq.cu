@@ -66,8 +66,6 @@ static int grid2() { return 2 * num_sms(); }
 
 enum { kDotNone = 0, kDotSelf = 1, kDotVj = 2, kDotBlock = 3 };
 
-__device__ __forceinline__ long long first_row() { return (long long)blockIdx.x * kW + (threadIdx.x >> 5); }
-__device__ __forceinline__ long long row_stride() { return (long long)gridDim.x * kW; }
 
 // ---------------------------------------------------------------------------
 // Forward
@@ -116,16 +114,16 @@ __global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> 
     }
     __syncthreads();
   }
-  double k0[NCH][VEC], k1[NCH][VEC];
+  T k0[NCH][VEC], k1[NCH][VEC];
 #pragma unroll
   for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
     for (int v = 0; v < VEC; ++v) {
       const int c = g.col0(ch) + v;
-      k0[ch][v] = (FIRST || AXPY) && c < B ? s_k0[c] : 0.0;
-      k1[ch][v] = AXPY && c < B ? s_k1[c] : 0.0;
+      k0[ch][v] = (FIRST || AXPY) && c < B ? (T)s_k0[c] : T(0);
+      k1[ch][v] = AXPY && c < B ? (T)s_k1[c] : T(0);
     }
-  double acc[kQ][NCH][VEC] = {};
+  double acc[1][NCH][VEC] = {};
   for (long long wrow = g.first_warp_row(); wrow < a.op.n; wrow += G::stride()) {
     const long long row = wrow + g.sub;
     const bool valid = row < a.op.n;
@@ -154,8 +152,8 @@ __global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> 
         // the product is linear: A (x / ||r||) = (A x) / ||r|| per column
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
-          x[ch][v] *= (T)k0[ch][v];
-          o[v] *= (T)k0[ch][v];
+          x[ch][v] *= k0[ch][v];
+          o[v] *= k0[ch][v];
         }
         stvec_t<T, VEC>(a.Vj + row * ld + c0, x[ch], nv);
       }
@@ -167,7 +165,7 @@ __global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> 
         if (a.Vjm1) ldvec<T, VEC>(a.Vjm1 + row * ld + c0, VEC, vm);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
-          o[v] = o[v] - (T)k0[ch][v] * vj[v] - (T)k1[ch][v] * vm[v];
+          o[v] = o[v] - k0[ch][v] * vj[v] - k1[ch][v] * vm[v];
           acc[0][ch][v] += (double)o[v] * (double)o[v];
         }
       }
@@ -192,98 +190,120 @@ __global__ void __launch_bounds__(kT, kMinCta) fwd_spmm_kernel(const FwdArgs<T> 
       stvec_t<T, VEC>(a.Out + row * ld + c0, o, nv);
     }
   }
-  if (DOT != kDotNone || AXPY) colsum_finish<VEC, NCH, LPR>(acc, 1, B, a.cout);
+  if (DOT != kDotNone || AXPY) colsum_finish<1, VEC, NCH, LPR>(acc, B, a.cout);
 }
 
 // Column sums of X*Y (Y null: of X*X).
-template <typename T, int NCH>
+template <typename T, int LPR, int NCH>
 __global__ void __launch_bounds__(kT, kMinCta) coldot_kernel(int n, int ld, int B, const T* __restrict__ X,
-                                                    const T* __restrict__ Y, ColSum cout) {
-  const int lane = threadIdx.x & 31;
-  double acc[kQ][NCH][2] = {};
-  for (long long row = first_row(); row < n; row += row_stride()) {
+                                                            const T* __restrict__ Y, ColSum cout) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
+  const G g;
+  double acc[1][NCH][VEC] = {};
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      double x0, x1, y0, y1;
-      ld2m(X + row * ld + c0, c0 + 1 < B, x0, x1);
+      T x[VEC], y[VEC];
+      ldvec<T, VEC>(X + row * ld + c0, B - c0, x);
       if (Y) {
-        ld2m(Y + row * ld + c0, c0 + 1 < B, y0, y1);
+        ldvec<T, VEC>(Y + row * ld + c0, B - c0, y);
       } else {
-        y0 = x0;
-        y1 = x1;
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) y[v] = x[v];
       }
-      acc[0][ch][0] += x0 * y0;
-      acc[0][ch][1] += x1 * y1;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) acc[0][ch][v] += (double)x[v] * (double)y[v];
     }
   }
-  colsum_finish<2, NCH, 32>(acc, 1, B, cout);
+  colsum_finish<1, VEC, NCH, LPR>(acc, B, cout);
 }
 
 // r = W - alpha_j v_j - beta_{j-1} v_{j-1} (alpha_j from the column sums,
 // stored), ||r||^2 to the column sums.
-template <typename T, int NCH>
-__global__ void __launch_bounds__(kT, 2)
+template <typename T, int LPR, int NCH>
+__global__ void __launch_bounds__(kT, kMinCta)
 recur_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ W, const T* __restrict__ Vj,
              const T* __restrict__ Vjm1, const double* __restrict__ cin, double* alpha, const double* beta,
              T* __restrict__ R, ColSum cout) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_a[kMaxB], s_b[kMaxB];
-  const int lane = threadIdx.x & 31;
+  const G g;
   for (int b = threadIdx.x; b < B; b += kT) {
     s_a[b] = cin[b];
     s_b[b] = (j > 0) ? beta[(size_t)b * m + j - 1] : 0.0;
     if (blockIdx.x == 0) alpha[(size_t)b * m + j] = cin[b];
   }
   __syncthreads();
-  double acc[kQ][NCH][2] = {};
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  T ka[NCH][VEC], kb[NCH][VEC];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const int c = g.col0(ch) + v;
+      ka[ch][v] = c < B ? (T)s_a[c] : T(0);
+      kb[ch][v] = c < B ? (T)s_b[c] : T(0);
+    }
+  double acc[1][NCH][VEC] = {};
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double w0, w1, v0, v1;
-      ld2m(W + row * ld + c0, sec, w0, w1);
-      ld2m(Vj + row * ld + c0, sec, v0, v1);
-      double r0 = w0 - s_a[c0] * v0, r1 = sec ? w1 - s_a[c0 + 1] * v1 : 0.0;
-      if (Vjm1) {
-        double q0, q1;
-        ld2m(Vjm1 + row * ld + c0, sec, q0, q1);
-        r0 -= s_b[c0] * q0;
-        if (sec) r1 -= s_b[c0 + 1] * q1;
+      const int nv = B - c0;
+      T w[VEC], v[VEC], q[VEC];
+      ldvec<T, VEC>(W + row * ld + c0, nv, w);
+      ldvec<T, VEC>(Vj + row * ld + c0, nv, v);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) q[i] = T(0);
+      if (Vjm1) ldvec<T, VEC>(Vjm1 + row * ld + c0, nv, q);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        w[i] = w[i] - ka[ch][i] * v[i] - kb[ch][i] * q[i];
+        acc[0][ch][i] += (double)w[i] * (double)w[i];
       }
-      const double o0 = rnd<T>(r0), o1 = rnd<T>(r1);
-      st2(R + row * ld + c0, o0, o1);
-      acc[0][ch][0] += o0 * o0;
-      acc[0][ch][1] += o1 * o1;
+      stvec_t<T, VEC>(R + row * ld + c0, w, nv);
     }
   }
-  colsum_finish<2, NCH, 32>(acc, 1, B, cout);
+  colsum_finish<1, VEC, NCH, LPR>(acc, B, cout);
 }
 
 // Vout = R / sqrt(cin) per column; dst[b * dst_stride] = sqrt(cin[b]).
-template <typename T, int NCH>
+template <typename T, int LPR, int NCH>
 __global__ void __launch_bounds__(kT, kMinCta)
 normalize_kernel(int n, int ld, int B, const T* __restrict__ R, const double* __restrict__ cin, T* __restrict__ Vout,
                  double* dst, int dst_stride) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_s[kMaxB];
-  const int lane = threadIdx.x & 31;
+  const G g;
   for (int b = threadIdx.x; b < B; b += kT) {
     const double nb = sqrt(cin[b]);
     s_s[b] = 1.0 / nb;
     if (blockIdx.x == 0 && dst) dst[(size_t)b * dst_stride] = nb;
   }
   __syncthreads();
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  T ks[NCH][VEC];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const int c = g.col0(ch) + v;
+      ks[ch][v] = c < B ? (T)s_s[c] : T(0);
+    }
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double r0, r1;
-      ld2m(R + row * ld + c0, sec, r0, r1);
-      st2(Vout + row * ld + c0, r0 * s_s[c0], sec ? r1 * s_s[c0 + 1] : 0.0);
+      T r[VEC];
+      ldvec<T, VEC>(R + row * ld + c0, B - c0, r);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) r[i] *= ks[ch][i];
+      stvec_t<T, VEC>(Vout + row * ld + c0, r, B - c0);
     }
   }
 }
@@ -405,15 +425,17 @@ small_side_kernel(int m, int func, int mode, const double* __restrict__ alpha, c
 // lambda = -xi/b_j + mu x+ + nu x_j with mu = g*gb_j - <l+, x_j> + <x+, xi>/b_j,
 // nu = g*ga_j + <x_j, xi>/b_j (g = *g_out; the three dots come from cin, null
 // with xi at j = m-1 where xi = 0).  mu, nu go to munu for the step's last kernel.
-template <typename T, int NCH>
-__global__ void __launch_bounds__(kT, 2)
+template <typename T, int LPR, int NCH>
+__global__ void __launch_bounds__(kT, kMinCta)
 lam_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ xi, const T* __restrict__ xplus,
            const T* __restrict__ xj, const double* __restrict__ cin, const double* __restrict__ g_alpha,
            const double* __restrict__ g_beta, const double* __restrict__ g_out, const double* __restrict__ beta,
            T* __restrict__ lam, double* munu) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_ib[kMaxB], s_mu[kMaxB], s_nu[kMaxB];
-  const int lane = threadIdx.x & 31;
-  const double g = g_out ? *g_out : 1.0;
+  const G g;
+  const double gs = g_out ? *g_out : 1.0;
   for (int b = threadIdx.x; b < B; b += kT) {
     const double bj = beta[(size_t)b * m + j];
     const double ib = 1.0 / bj;
@@ -424,27 +446,39 @@ lam_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ xi, const T
       c3 = cin[2 * kMaxB + b];
     }
     s_ib[b] = ib;
-    s_mu[b] = g * g_beta[(size_t)b * m + j] - c1 + c2 * ib;
-    s_nu[b] = g * g_alpha[(size_t)b * m + j] + c3 * ib;
+    s_mu[b] = gs * g_beta[(size_t)b * m + j] - c1 + c2 * ib;
+    s_nu[b] = gs * g_alpha[(size_t)b * m + j] + c3 * ib;
     if (blockIdx.x == 0) {
       munu[b] = s_mu[b];
       munu[kMaxB + b] = s_nu[b];
     }
   }
   __syncthreads();
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  T kib[NCH][VEC], kmu[NCH][VEC], knu[NCH][VEC];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const int c = g.col0(ch) + v;
+      kib[ch][v] = c < B ? (T)s_ib[c] : T(0);
+      kmu[ch][v] = c < B ? (T)s_mu[c] : T(0);
+      knu[ch][v] = c < B ? (T)s_nu[c] : T(0);
+    }
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double p0, p1, v0, v1, x0 = 0.0, x1 = 0.0;
-      ld2m(xplus + row * ld + c0, sec, p0, p1);
-      ld2m(xj + row * ld + c0, sec, v0, v1);
-      if (xi) ld2m(xi + row * ld + c0, sec, x0, x1);
-      const double l0 = -x0 * s_ib[c0] + s_mu[c0] * p0 + s_nu[c0] * v0;
-      const double l1 = sec ? -x1 * s_ib[c0 + 1] + s_mu[c0 + 1] * p1 + s_nu[c0 + 1] * v1 : 0.0;
-      st2(lam + row * ld + c0, l0, l1);
+      const int nv = B - c0;
+      T p[VEC], v[VEC], x[VEC];
+      ldvec<T, VEC>(xplus + row * ld + c0, nv, p);
+      ldvec<T, VEC>(xj + row * ld + c0, nv, v);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = T(0);
+      if (xi) ldvec<T, VEC>(xi + row * ld + c0, nv, x);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = -x[i] * kib[ch][i] + kmu[ch][i] * p[i] + knu[ch][i] * v[i];
+      stvec_t<T, VEC>(lam + row * ld + c0, x, nv);
     }
   }
 }
@@ -488,7 +522,7 @@ __global__ void __launch_bounds__(kT, 2) bwd_spmm_kernel(const BwdArgs<T> a) {
     __syncthreads();
   }
   const bool dots = LAST && a.xjm1 != nullptr;
-  double acc[kQ][NCH][VEC] = {};
+  double acc[LAST ? 3 : 1][NCH][VEC] = {};
   double sk = 0.0, sc = 0.0;
   for (long long wrow = g.first_warp_row(); wrow < a.op.n; wrow += G::stride()) {
     const long long row = wrow + g.sub;
@@ -554,22 +588,26 @@ __global__ void __launch_bounds__(kT, 2) bwd_spmm_kernel(const BwdArgs<T> a) {
     a.sacc[2 * blockIdx.x] += bsk;
     a.sacc[2 * blockIdx.x + 1] += bsc;
   }
-  if (dots) colsum_finish<VEC, NCH, LPR>(acc, 3, B, a.cout);
+  if constexpr (LAST) {
+    if (dots) colsum_finish<3, VEC, NCH, LPR>(acc, B, a.cout);
+  }
 }
 
 // Generic reverse step around a caller-formed Plam = P lambda:
 // xi = -dcoef (x) G - Plam + alpha_j lam + beta_j l+ - beta_j nu x+ and, with
 // x_{j-1}, the three dots of step j-1.  dcoef[b] G[:, b] is the dx term of a
 // forward output that depends on the basis directly (funm_apply_kraemer).
-template <typename T, int NCH>
+template <typename T, int LPR, int NCH>
 __global__ void __launch_bounds__(kT, 2)
 xi_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ Plam, const T* __restrict__ lam,
           const T* __restrict__ lplus, const T* __restrict__ xplus, const T* __restrict__ xj,
           const T* __restrict__ xjm1, const double* __restrict__ alpha, const double* __restrict__ beta,
-          const double* __restrict__ munu, const double* __restrict__ dcoef, const T* __restrict__ G,
+          const double* __restrict__ munu, const double* __restrict__ dcoef, const T* __restrict__ Gm,
           T* __restrict__ xi, ColSum cout) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_a[kMaxB], s_b[kMaxB], s_bn[kMaxB], s_d[kMaxB];
-  const int lane = threadIdx.x & 31;
+  const G g;
   for (int b = threadIdx.x; b < B; b += kT) {
     s_a[b] = alpha[(size_t)b * m + j];
     s_b[b] = beta[(size_t)b * m + j];
@@ -577,67 +615,77 @@ xi_kernel(int n, int ld, int B, int j, int m, const T* __restrict__ Plam, const 
     s_d[b] = dcoef ? dcoef[b] : 0.0;
   }
   __syncthreads();
-  double acc[kQ][NCH][2] = {};
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  double acc[3][NCH][VEC] = {};
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double w0, w1, l0, l1, p0, p1, q0 = 0.0, q1 = 0.0, g0 = 0.0, g1 = 0.0;
-      ld2m(Plam + row * ld + c0, sec, w0, w1);
-      ld2m(lam + row * ld + c0, sec, l0, l1);
-      ld2m(xplus + row * ld + c0, sec, p0, p1);
-      if (lplus) ld2m(lplus + row * ld + c0, sec, q0, q1);
-      if (G) ld2m(G + row * ld + c0, sec, g0, g1);
-      const double x0 = rnd<T>(-s_d[c0] * g0 - w0 + s_a[c0] * l0 + s_b[c0] * q0 - s_bn[c0] * p0);
-      const double x1 =
-          sec ? rnd<T>(-s_d[c0 + 1] * g1 - w1 + s_a[c0 + 1] * l1 + s_b[c0 + 1] * q1 - s_bn[c0 + 1] * p1) : 0.0;
-      st2(xi + row * ld + c0, x0, x1);
+      const int nv = B - c0;
+      T w[VEC], l[VEC], p[VEC], q[VEC], gg[VEC];
+      ldvec<T, VEC>(Plam + row * ld + c0, nv, w);
+      ldvec<T, VEC>(lam + row * ld + c0, nv, l);
+      ldvec<T, VEC>(xplus + row * ld + c0, nv, p);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) q[i] = gg[i] = T(0);
+      if (lplus) ldvec<T, VEC>(lplus + row * ld + c0, nv, q);
+      if (Gm) ldvec<T, VEC>(Gm + row * ld + c0, nv, gg);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int c = min(c0 + i, kMaxB - 1);
+        w[i] = -(T)s_d[c] * gg[i] - w[i] + (T)s_a[c] * l[i] + (T)s_b[c] * q[i] - (T)s_bn[c] * p[i];
+      }
+      stvec_t<T, VEC>(xi + row * ld + c0, w, nv);
       if (xjm1) {
-        double u0, u1, v0, v1;
-        ld2m(xjm1 + row * ld + c0, sec, u0, u1);
-        ld2m(xj + row * ld + c0, sec, v0, v1);
-        acc[0][ch][0] += l0 * u0;
-        acc[0][ch][1] += l1 * u1;
-        acc[1][ch][0] += v0 * x0;
-        acc[1][ch][1] += v1 * x1;
-        acc[2][ch][0] += u0 * x0;
-        acc[2][ch][1] += u1 * x1;
+        T u[VEC], v[VEC];
+        ldvec<T, VEC>(xjm1 + row * ld + c0, nv, u);
+        ldvec<T, VEC>(xj + row * ld + c0, nv, v);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          acc[0][ch][i] += (double)l[i] * (double)u[i];
+          acc[1][ch][i] += (double)v[i] * (double)w[i];
+          acc[2][ch][i] += (double)u[i] * (double)w[i];
+        }
       }
     }
   }
-  if (xjm1) colsum_finish<2, NCH, 32>(acc, 3, B, cout);
+  if (xjm1) colsum_finish<3, VEC, NCH, LPR>(acc, B, cout);
 }
 
 // gZ = (<xi, v0> v0 - xi) / ||z|| + g_zn * z / ||z||  per column (the gradient
 // with respect to the start vector; <xi, v0> from cin).
-template <typename T, int NCH>
-__global__ void __launch_bounds__(kT, 2)
+template <typename T, int LPR, int NCH>
+__global__ void __launch_bounds__(kT, kMinCta)
 start_grad_kernel(int n, int ld, int B, const T* __restrict__ xi, const T* __restrict__ V0, const T* __restrict__ Z,
                   const double* __restrict__ znorm, const double* __restrict__ g_zn, const double* __restrict__ cin,
                   T* __restrict__ gZ) {
+  using G = RowLanes<T, LPR>;
+  constexpr int VEC = G::VEC;
   __shared__ double s_d[kMaxB], s_i[kMaxB], s_g[kMaxB];
-  const int lane = threadIdx.x & 31;
+  const G g;
   for (int b = threadIdx.x; b < B; b += kT) {
     s_d[b] = cin[b];
     s_i[b] = 1.0 / znorm[b];
     s_g[b] = g_zn ? g_zn[b] : 0.0;
   }
   __syncthreads();
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  for (long long row = g.first_row(); row < n; row += G::stride()) {
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      const int c0 = ch * 64 + 2 * lane;
+      const int c0 = g.col0(ch);
       if (c0 >= B) continue;
-      const bool sec = c0 + 1 < B;
-      double x0, x1, v0, v1, z0, z1;
-      ld2m(xi + row * ld + c0, sec, x0, x1);
-      ld2m(V0 + row * ld + c0, sec, v0, v1);
-      ld2m(Z + row * ld + c0, sec, z0, z1);
-      const double r0 = ((s_d[c0] * v0 - x0) + s_g[c0] * z0) * s_i[c0];
-      const double r1 = sec ? ((s_d[c0 + 1] * v1 - x1) + s_g[c0 + 1] * z1) * s_i[c0 + 1] : 0.0;
-      st2(gZ + row * ld + c0, r0, r1);
+      const int nv = B - c0;
+      T x[VEC], v[VEC], z[VEC];
+      ldvec<T, VEC>(xi + row * ld + c0, nv, x);
+      ldvec<T, VEC>(V0 + row * ld + c0, nv, v);
+      ldvec<T, VEC>(Z + row * ld + c0, nv, z);
+      double r[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int c = min(c0 + i, kMaxB - 1);
+        r[i] = ((s_d[c] * (double)v[i] - (double)x[i]) + s_g[c] * (double)z[i]) * s_i[c];
+      }
+      stvec<T, VEC>(gZ + row * ld + c0, r, nv);
     }
   }
 }
@@ -681,7 +729,7 @@ template <typename T>
 __global__ void __launch_bounds__(kT, kMinCta)
 dense_matvec_kernel(int n, const T* __restrict__ A, const T* __restrict__ x, int ldx, T* __restrict__ y, int ldy) {
   const int lane = threadIdx.x & 31;
-  for (long long row = first_row(); row < n; row += row_stride()) {
+  for (long long row = (long long)blockIdx.x * kW + (threadIdx.x >> 5); row < n; row += (long long)gridDim.x * kW) {
     double s = 0.0;
     for (int c = lane; c < n; c += 32) s += (double)A[row * n + c] * (double)x[(long long)c * ldx];
     s = warp_sum(s);
@@ -820,7 +868,7 @@ static void launch_bwd(bool last, bool deriv, const BwdArgs<T>& a, int grid, cud
 static Op make_op(const lg_slq_op& o) { return Op{o.n, o.rowptr, o.col, o.shift}; }
 
 // ---- fused forward (recurrence through the sparse products) --------------
-template <typename T, int LPR, int NS, int NP>
+template <typename T, int LPR, int NS>
 static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* Z, T* V, T* Yst, double* alpha,
                              double* beta, double* znorm, const Ws& w, int grid, cudaStream_t st) {
   const int nu = o.power, h = nu / 2, pdot = nu - h;
@@ -828,7 +876,7 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
   T* R = reinterpret_cast<T*>(block(w, 0));
   T* W = reinterpret_cast<T*>(block(w, 1));
   auto Yp = [&](int j, int p) { return Yst + ((size_t)j * (nu - 1) + (p - 1)) * bs; };   // A^p v_j, p >= 1
-  coldot_kernel<T, NP><<<grid, kT, 0, st>>>(o.n, ld, B, Z, nullptr, w.cs[0]);
+  coldot_kernel<T, LPR, NS><<<grid, kT, 0, st>>>(o.n, ld, B, Z, nullptr, w.cs[0]);
   FwdArgs<T> a{};
   a.op = make_op(o);
   a.off = static_cast<const T*>(o.offval);
@@ -849,7 +897,7 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
       a.cin = w.cs[0].out;
       a.cout = w.cs[1];
       launch_fwd<T, LPR, NS>(true, kDotVj, false, a, grid, st);
-      recur_kernel<T, NP><<<grid2(), kT, 0, st>>>(o.n, ld, B, j, m, W, a.Vj, a.Vjm1, w.cs[1].out, alpha, beta, R,
+      recur_kernel<T, LPR, NS><<<grid, kT, 0, st>>>(o.n, ld, B, j, m, W, a.Vj, a.Vjm1, w.cs[1].out, alpha, beta, R,
                                                 w.cs[0]);
       continue;
     }
@@ -865,12 +913,12 @@ static cudaError_t forward_t(const lg_slq_op& o, int B, int m, int ld, const T* 
       launch_fwd<T, LPR, NS>(first, dot, axpy, a, grid, st);
     }
   }
-  normalize_kernel<T, NP><<<grid, kT, 0, st>>>(o.n, ld, B, R, w.cs[0].out, V + (size_t)m * bs, beta + (m - 1), m);
+  normalize_kernel<T, LPR, NS><<<grid, kT, 0, st>>>(o.n, ld, B, R, w.cs[0].out, V + (size_t)m * bs, beta + (m - 1), m);
   return cudaGetLastError();
 }
 
 // ---- fused backward --------------------------------------------------------
-template <typename T, int LPR, int NS, int NP>
+template <typename T, int LPR, int NS>
 static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T* V, const T* Yst,
                               const double* alpha, const double* beta, const double* g_alpha, const double* g_beta,
                               const double* g_out, double* g_params, const Ws& w, int grid, cudaStream_t st) {
@@ -903,7 +951,7 @@ static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T*
     const T* xj = V + (size_t)j * bs;
     const T* xplus = V + (size_t)(j + 1) * bs;
     const bool top = (j == m - 1);
-    lam_kernel<T, NP><<<grid2(), kT, 0, st>>>(o.n, ld, B, j, m, top ? nullptr : xi, xplus, xj,
+    lam_kernel<T, LPR, NS><<<grid, kT, 0, st>>>(o.n, ld, B, j, m, top ? nullptr : xi, xplus, xj,
                                             top ? nullptr : w.cs[1].out, g_alpha, g_beta, g_out, beta, lam, w.munu);
     a.j = j;
     a.lam = lam;
@@ -928,7 +976,7 @@ static cudaError_t backward_t(const lg_slq_op& o, int B, int m, int ld, const T*
 }
 
 // ---- operator apply and its VJP -------------------------------------------
-template <typename T, int LPR, int NS, int NP>
+template <typename T, int LPR, int NS>
 static cudaError_t apply_t(const lg_slq_op& o, int B, int ld, const T* X, T* Yout, const Ws& w, int grid,
                            cudaStream_t st) {
   FwdArgs<T> a{};
@@ -947,7 +995,7 @@ static cudaError_t apply_t(const lg_slq_op& o, int B, int ld, const T* X, T* You
   return cudaGetLastError();
 }
 
-template <typename T, int LPR, int NS, int NP>
+template <typename T, int LPR, int NS>
 static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, const T* G, T* gX, double* g_params,
                                const Ws& w, int grid, cudaStream_t st) {
   const int nu = o.power;
@@ -995,16 +1043,12 @@ static cudaError_t apply_vjp_t(const lg_slq_op& o, int B, int ld, const T* X, co
 using namespace lg;
 using namespace lg::slq;
 
-// Lane layout of the sparse products <T, LPR, NS> and chunks of the pair
-// layout NP by element type and probe count.
+// Lane layout <T, LPR, NS> of every block kernel by element type and probe
+// count (the last argument is unused).
 #define LG_DISPATCH(DTYPE, B, CALL)                                                                   \
   ((DTYPE) == LG_F64                                                                                   \
        ? ((B) <= 32 ? CALL(double, 16, 1, 1) : (B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
        : ((B) <= 32 ? CALL(float, 8, 1, 1) : (B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
-#define LG_DISPATCH_PAIR(DTYPE, B, CALL)                               \
-  ((DTYPE) == LG_F64 ? ((B) <= 64 ? CALL(double, 1) : CALL(double, 2)) \
-                     : ((B) <= 64 ? CALL(float, 1) : CALL(float, 2)))
-
 extern "C" size_t lg_slq_workspace_bytes(const lg_slq_op* op, int B, int ld) {
   if (op) {
     if (check_op(op, B, ld) != LG_OK) return 0;
@@ -1039,7 +1083,7 @@ extern "C" int lg_slq_forward(const lg_slq_op* op, int B, int m, int ld, const v
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
 #define LG_FWD(TT, L, NS, NP)                                                                                           \
-  forward_t<TT, L, NS, NP>(*op, B, m, ld, static_cast<const TT*>(Z), static_cast<TT*>(V), static_cast<TT*>(Y), alpha, beta, \
+  forward_t<TT, L, NS>(*op, B, m, ld, static_cast<const TT*>(Z), static_cast<TT*>(V), static_cast<TT*>(Y), alpha, beta, \
                    znorm, w, grid, st)
     e = LG_DISPATCH(op->dtype, B, LG_FWD);
 #undef LG_FWD
@@ -1062,7 +1106,7 @@ extern "C" int lg_slq_backward(const lg_slq_op* op, int B, int m, int ld, const 
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
 #define LG_BWD(TT, L, NS, NP)                                                                                       \
-  backward_t<TT, L, NS, NP>(*op, B, m, ld, static_cast<const TT*>(V), static_cast<const TT*>(Y), alpha, beta, g_alpha, \
+  backward_t<TT, L, NS>(*op, B, m, ld, static_cast<const TT*>(V), static_cast<const TT*>(Y), alpha, beta, g_alpha, \
                     g_beta, g_out, g_params, w, grid, st)
     e = LG_DISPATCH(op->dtype, B, LG_BWD);
 #undef LG_BWD
@@ -1079,7 +1123,7 @@ extern "C" int lg_slq_apply(const lg_slq_op* op, int B, int ld, const void* X, v
   if ((rc = check_ptr(X, op->dtype, "X")) || (rc = check_ptr(Y, op->dtype, "Y"))) return rc;
   if (X == Y) return fail("lg_slq_apply: X and Y must not alias");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LG_APPLY(TT, L, NS, NP) apply_t<TT, L, NS, NP>(*op, B, ld, static_cast<const TT*>(X), static_cast<TT*>(Y), w, grid, st)
+#define LG_APPLY(TT, L, NS, NP) apply_t<TT, L, NS>(*op, B, ld, static_cast<const TT*>(X), static_cast<TT*>(Y), w, grid, st)
   cudaError_t e = LG_DISPATCH(op->dtype, B, LG_APPLY);
 #undef LG_APPLY
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_apply", e);
@@ -1098,7 +1142,7 @@ extern "C" int lg_slq_apply_vjp(const lg_slq_op* op, int B, int ld, const void* 
   if (gX == X || gX == G) return fail("lg_slq_apply_vjp: gX must not alias X or G");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define LG_VJP(TT, L, NS, NP)                                                                                       \
-  apply_vjp_t<TT, L, NS, NP>(*op, B, ld, static_cast<const TT*>(X), static_cast<const TT*>(G), static_cast<TT*>(gX), \
+  apply_vjp_t<TT, L, NS>(*op, B, ld, static_cast<const TT*>(X), static_cast<const TT*>(G), static_cast<TT*>(gX), \
                      g_params, w, grid, st)
   cudaError_t e = LG_DISPATCH(op->dtype, B, LG_VJP);
 #undef LG_VJP
@@ -1153,12 +1197,12 @@ extern "C" int lg_slq_block_start(int n, int B, int ld, int dtype, const void* Z
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
-#define LG_START(TT, N)                                                                                     \
-  (coldot_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Z), nullptr, w.cs[0]),         \
-   normalize_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Z), w.cs[0].out,            \
+#define LG_START(TT, L, NS, NP)                                                                                     \
+  (coldot_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Z), nullptr, w.cs[0]),         \
+   normalize_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Z), w.cs[0].out,            \
                                                 static_cast<TT*>(V0), znorm, 1),                            \
    cudaGetLastError())
-    e = LG_DISPATCH_PAIR(dtype, B, LG_START);
+    e = LG_DISPATCH(dtype, B, LG_START);
 #undef LG_START
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_start", e);
@@ -1178,16 +1222,16 @@ extern "C" int lg_slq_block_step(int n, int B, int ld, int dtype, int j, int m, 
   if (j > 0 && (rc = check_ptr(Vjm1, dtype, "Vjm1"))) return rc;
   if (!alpha || !beta) return fail("lg_slq_block_step: null alpha/beta");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LG_STEP(TT, N)                                                                                          \
-  (coldot_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Vj), static_cast<const TT*>(W),    \
+#define LG_STEP(TT, L, NS, NP)                                                                                          \
+  (coldot_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(Vj), static_cast<const TT*>(W),    \
                                              w.cs[0]),                                                          \
-   recur_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(W), static_cast<const TT*>(Vj), \
+   recur_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(W), static_cast<const TT*>(Vj), \
                                             j > 0 ? static_cast<const TT*>(Vjm1) : nullptr, w.cs[0].out, alpha, \
                                             beta, static_cast<TT*>(R), w.cs[1]),                                \
-   normalize_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(R), w.cs[1].out,               \
+   normalize_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(R), w.cs[1].out,               \
                                                 static_cast<TT*>(Vnext), beta + j, m),                          \
    cudaGetLastError())
-  cudaError_t e = LG_DISPATCH_PAIR(dtype, B, LG_STEP);
+  cudaError_t e = LG_DISPATCH(dtype, B, LG_STEP);
 #undef LG_STEP
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_step", e);
 }
@@ -1207,12 +1251,12 @@ extern "C" int lg_slq_block_lambda(int n, int B, int ld, int dtype, int j, int m
   if (!beta || !g_alpha || !g_beta) return fail("lg_slq_block_lambda: null scalar arrays");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // xi == NULL starts the sweep (xi = 0, no dots from a previous step)
-#define LG_LAM(TT, N)                                                                                              \
-  (lam_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(xi), static_cast<const TT*>(xplus), \
+#define LG_LAM(TT, L, NS, NP)                                                                                              \
+  (lam_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(xi), static_cast<const TT*>(xplus), \
                                           static_cast<const TT*>(xj), xi ? w.cs[1].out : nullptr, g_alpha, g_beta,  \
                                           g_out, beta, static_cast<TT*>(lam), w.munu),                             \
    cudaGetLastError())
-  cudaError_t e = LG_DISPATCH_PAIR(dtype, B, LG_LAM);
+  cudaError_t e = LG_DISPATCH(dtype, B, LG_LAM);
 #undef LG_LAM
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_lambda", e);
 }
@@ -1238,13 +1282,13 @@ extern "C" int lg_slq_block_xi(int n, int B, int ld, int dtype, int j, int m, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = (xjm1 ? reset_counters(w, st) : cudaSuccess);
   if (e == cudaSuccess) {
-#define LG_XI(TT, N)                                                                                               \
-  (xi_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(Plam), static_cast<const TT*>(lam), \
+#define LG_XI(TT, L, NS, NP)                                                                                               \
+  (xi_kernel<TT, L, NS><<<grid2(), kT, 0, st>>>(n, ld, B, j, m, static_cast<const TT*>(Plam), static_cast<const TT*>(lam), \
                                          static_cast<const TT*>(lplus), static_cast<const TT*>(xplus),             \
                                          static_cast<const TT*>(xj), static_cast<const TT*>(xjm1), alpha, beta,    \
                                          w.munu, dcoef, static_cast<const TT*>(G), static_cast<TT*>(xi), w.cs[1]), \
    cudaGetLastError())
-    e = LG_DISPATCH_PAIR(dtype, B, LG_XI);
+    e = LG_DISPATCH(dtype, B, LG_XI);
 #undef LG_XI
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_xi", e);
@@ -1264,14 +1308,14 @@ extern "C" int lg_slq_block_start_grad(int n, int B, int ld, int dtype, const vo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = reset_counters(w, st);
   if (e == cudaSuccess) {
-#define LG_SG(TT, N)                                                                                              \
-  (coldot_kernel<TT, N><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0),     \
+#define LG_SG(TT, L, NS, NP)                                                                                              \
+  (coldot_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0),     \
                                              w.cs[0]),                                                            \
-   start_grad_kernel<TT, N><<<grid2(), kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0), \
+   start_grad_kernel<TT, L, NS><<<grid, kT, 0, st>>>(n, ld, B, static_cast<const TT*>(xi), static_cast<const TT*>(V0), \
                                                  static_cast<const TT*>(Z), znorm, g_znorm, w.cs[0].out,          \
                                                  static_cast<TT*>(gZ)),                                           \
    cudaGetLastError())
-    e = LG_DISPATCH_PAIR(dtype, B, LG_SG);
+    e = LG_DISPATCH(dtype, B, LG_SG);
 #undef LG_SG
   }
   return e == cudaSuccess ? LG_OK : cuda_fail("lg_slq_block_start_grad", e);

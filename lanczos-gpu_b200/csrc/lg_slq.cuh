@@ -100,11 +100,13 @@ struct ColSum {
   unsigned* counter;   // zero between kernels
 };
 
-// acc[q][ch][v]: this lane's sum of quantity q for its column
+// acc[q][ch][v] (q < NQ): this lane's sum of quantity q for its column
 // ch * LPR * VEC + (lane % LPR) * VEC + v over the rows it visited.  Called by
 // every thread of the CTA, once, at the end of the kernel.
-template <int VEC, int NCH, int LPR>
-__device__ void colsum_finish(double (&acc)[kQ][NCH][VEC], int nq, int B, const ColSum cs) {
+template <int NQ, int VEC, int NCH, int LPR>
+__device__ void colsum_finish(double (&acc)[NQ][NCH][VEC], int B, const ColSum cs) {
+  static_assert(NQ >= 1 && NQ <= kQ, "at most kQ quantities per partial row");
+  constexpr int nq = NQ;
   __shared__ double s_w[kW * kMaxB];
   __shared__ bool s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = threadIdx.x;
@@ -207,7 +209,7 @@ __device__ __forceinline__ void gather_rows(const Op& op, const T* __restrict__ 
       if (DERIV) dv = __ldg(doff + kb + kk);
     }
     const int nb = min(LPR, mx - k0);
-#pragma unroll 8
+#pragma unroll 4
     for (int s = 0; s < nb; ++s) {
       const long long c = __shfl_sync(kFull, ci, base + s);
       const T a = __shfl_sync(kFull, av, base + s);
