@@ -14,6 +14,7 @@
 //  * workspace lives in a plan that can be reused across solves; nothing is
 //    allocated inside the iteration.
 #include "lg_common.cuh"
+#include "lg_csr.cuh"
 #include "lg_kernels.cuh"
 #include "lg_solver.h"
 
@@ -63,13 +64,17 @@ __global__ void scale_kernel(double* x, int n, double s) {
 Solver::~Solver() { release(); }
 
 void Solver::release() {
-  void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, V, W, R, partA, partB, partC, alpha, beta, scal,
+  void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, d_long, d_chunk_sum, d_classes, V, W, R, partA, partB, partC, alpha, beta, scal,
                   ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   d_rowptr = d_col = nullptr;
   d_val64 = nullptr;
   d_val32 = nullptr;
+  d_long = nullptr;
+  d_chunk_sum = nullptr;
+  d_classes = nullptr;
+  A = CsrDev();
   V = W = R = partA = partB = partC = alpha = beta = scal = ritz = bounds = zsel = Q = rs_scratch = Ytmp = cg_ws = nullptr;
   cg_part = cg_scal = nullptr;
   cg_counter = nullptr;
@@ -179,7 +184,90 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
   A.val32 = mixed ? d_val32 : nullptr;
   A.lanes = pick_lanes(nnz / (double)n);
 
+  if (device_ptrs) {
+    std::vector<int> hrp((size_t)n + 1);
+    LG_TRY(cudaMemcpyAsync(hrp.data(), rowptr, sizeof(int) * hrp.size(), cudaMemcpyDeviceToHost, stream));
+    LG_TRY(cudaStreamSynchronize(stream));
+    int rc = build_long_rows(hrp.data());
+    if (rc != LG_OK) return rc;
+  } else {
+    int rc = build_long_rows(rowptr);
+    if (rc != LG_OK) return rc;
+  }
+
   LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+// Tables of the rows longer than kLongRow (see CsrDev): row index, range of
+// chunks, chunk bounds; nothing is allocated for graphs without such rows.
+int Solver::build_long_rows(const int* hrp) {
+  std::vector<int> rows, first{0}, cb, ce;
+  for (int i = 0; i < n; ++i) {
+    const int b = hrp[i], e = hrp[i + 1];
+    if (e - b <= kLongRow) continue;
+    rows.push_back(i);
+    for (int k = b + kLongRow; k < e; k += kLongRow) {
+      cb.push_back(k);
+      ce.push_back(std::min(e, k + kLongRow));
+    }
+    first.push_back((int)cb.size());
+  }
+  // Row-length classes: when no single lane count suits 90 % of the rows
+  // (power-law graphs), each class gets its own launch over its row list.
+  {
+    static const int kLanes[5] = {2, 4, 8, 16, 32};
+    std::vector<int> cls(n);
+    int hist[5] = {0, 0, 0, 0, 0};
+    for (int i = 0; i < n; ++i) {
+      const int len = std::min(hrp[i + 1] - hrp[i], kLongRow);
+      const int l = pick_lanes((double)len);
+      int c = 0;
+      while (kLanes[c] != l) ++c;
+      cls[i] = c;
+      ++hist[c];
+    }
+    const int top = *std::max_element(hist, hist + 5);
+    if ((double)top < 0.9 * n) {
+      std::vector<int> lists;
+      lists.reserve(n);
+      int off[5];
+      A.nclasses = 0;
+      for (int c = 0; c < 5; ++c) {
+        off[c] = (int)lists.size();
+        for (int i = 0; i < n; ++i)
+          if (cls[i] == c) lists.push_back(i);
+        if (hist[c] > 0) {
+          A.class_lanes[A.nclasses] = kLanes[c];
+          A.class_count[A.nclasses] = hist[c];
+          A.class_rows[A.nclasses] = reinterpret_cast<const int*>((size_t)off[c]);   // offset, fixed below
+          ++A.nclasses;
+        }
+      }
+      LG_TRY(cudaMalloc(&d_classes, sizeof(int) * (size_t)n));
+      LG_TRY(cudaMemcpyAsync(d_classes, lists.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream));
+      LG_TRY(cudaStreamSynchronize(stream));
+      for (int c = 0; c < A.nclasses; ++c)
+        A.class_rows[c] = d_classes + reinterpret_cast<size_t>(A.class_rows[c]);
+    }
+  }
+  A.nlong = (int)rows.size();
+  A.nchunks = (int)cb.size();
+  if (A.nlong == 0) return LG_OK;
+  const size_t total = rows.size() + first.size() + cb.size() + ce.size();
+  LG_TRY(cudaMalloc(&d_long, sizeof(int) * total));
+  LG_TRY(cudaMalloc(&d_chunk_sum, sizeof(double) * cb.size()));
+  int* p = d_long;
+  for (const std::vector<int>* v : {&rows, &first, &cb, &ce}) {
+    LG_TRY(cudaMemcpyAsync(p, v->data(), sizeof(int) * v->size(), cudaMemcpyHostToDevice, stream));
+    p += v->size();
+  }
+  LG_TRY(cudaStreamSynchronize(stream));   // the host vectors go out of scope
+  A.long_rows = d_long;
+  A.long_first = d_long + rows.size();
+  A.chunk_begin = A.long_first + first.size();
+  A.chunk_end = A.chunk_begin + cb.size();
+  A.chunk_sum = d_chunk_sum;
   return LG_OK;
 }
 
@@ -201,7 +289,7 @@ int Solver::apply_step(int j, int beta_mode) {
     // CSR stream + x gather (counted once) + v_j and w written
     const double vb = mixed ? 4.0 : 8.0;
     const double bytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 16.0 * n;
-    LG_TRY(timed(LG_K_SPMV, bytes, 1, [&] {
+    LG_TRY(timed(LG_K_SPMV, bytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
       return spmv_step(A, stream, grid_spmv, R, W, Vj, ldv, partC, nrowsC, j, beta_mode, alpha, beta, scal,
                        state);
     }));

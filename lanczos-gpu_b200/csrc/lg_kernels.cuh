@@ -42,6 +42,22 @@ struct CsrDev {
   const double* val64 = nullptr;   // fp64 values (or null)
   const float* val32 = nullptr;    // fp32 values (mixed mode) (or null)
   int lanes = 8;                   // lanes per row of the vector kernel
+  // Rows with more than kLongRow nonzeros (power-law graphs): the row kernels
+  // of spmv_step / spmv_plain stop after kLongRow; the remainder is split into
+  // chunks of kLongRow summed by one warp each and added in a fixed order.
+  int nlong = 0, nchunks = 0;
+  const int* long_rows = nullptr;    // nlong row indices
+  const int* long_first = nullptr;   // nlong + 1: chunk range of each long row
+  const int* chunk_begin = nullptr;  // nchunks
+  const int* chunk_end = nullptr;    // nchunks
+  double* chunk_sum = nullptr;       // nchunks
+  // Skewed row lengths (power-law graphs): rows bucketed by the lane count
+  // that suits them (2, 4, 8, 16, 32 lanes); one launch per non-empty bucket
+  // over its row list.  nclasses == 0: all rows with `lanes`.
+  int nclasses = 0;
+  int class_lanes[5] = {0, 0, 0, 0, 0};
+  int class_count[5] = {0, 0, 0, 0, 0};
+  const int* class_rows[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
 // Vj points at column j of the row-major basis (stride ldv).

@@ -24,6 +24,7 @@ class Solver {
 
  private:
   void release();
+  int build_long_rows(const int* host_rowptr);
   int sync_state();
   int clear_status();
   int apply_step(int j, int beta_mode);
@@ -47,6 +48,9 @@ class Solver {
   int* d_col = nullptr;
   double* d_val64 = nullptr;
   float* d_val32 = nullptr;
+  int* d_long = nullptr;          // long-row tables (rows, chunk ranges, chunk bounds)
+  int* d_classes = nullptr;       // row lists of the row-length classes
+  double* d_chunk_sum = nullptr;  // one partial per long-row chunk
 
   double* V = nullptr;      // n x ldv, row-major (ldv >= max_ncv + 1)
   double* W = nullptr;      // operator output

@@ -76,12 +76,13 @@ __device__ int step_prologue(const double* __restrict__ part_in, int nrows_in, i
   return sh_stop;
 }
 
+// `list` (optional, `count` entries): the rows to process, else rows 0..count-1.
 template <typename VT, int L>
 __global__ void __launch_bounds__(256)
-spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ col,
-                 const VT* __restrict__ val, const double* __restrict__ R, double* __restrict__ W,
-                 double* __restrict__ Vj, int ldv, const double* __restrict__ part_in, int nrows_in, int j,
-                 int beta_mode, double* alpha, double* beta, double* scal, int* state) {
+spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict__ rowptr,
+                 const int* __restrict__ col, const VT* __restrict__ val, const double* __restrict__ R,
+                 double* __restrict__ W, double* __restrict__ Vj, int ldv, const double* __restrict__ part_in,
+                 int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   double s1, s2;
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
@@ -91,14 +92,16 @@ spmv_step_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ 
   const int lane = threadIdx.x & (L - 1);
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
   const int rows_per_warp = 32 / L;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp * 2 < n;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp * 2 < count;
        w += warps_total) {
-    const int rowA = w * rows_per_warp * 2 + ((threadIdx.x & 31) / L);
-    const int rowB = rowA + rows_per_warp;
-    const bool okA = rowA < n, okB = rowB < n;
+    const int iA = w * rows_per_warp * 2 + ((threadIdx.x & 31) / L);
+    const int iB = iA + rows_per_warp;
+    const bool okA = iA < count, okB = iB < count;
+    const int rowA = okA ? (list ? __ldg(list + iA) : iA) : 0;
+    const int rowB = okB ? (list ? __ldg(list + iB) : iB) : 0;
     int kA = 0, eA = 0, kB = 0, eB = 0;
-    if (okA) { kA = __ldg(rowptr + rowA) + lane; eA = __ldg(rowptr + rowA + 1); }
-    if (okB) { kB = __ldg(rowptr + rowB) + lane; eB = __ldg(rowptr + rowB + 1); }
+    if (okA) { kA = __ldg(rowptr + rowA); eA = min(__ldg(rowptr + rowA + 1), kA + kLongRow); kA += lane; }
+    if (okB) { kB = __ldg(rowptr + rowB); eB = min(__ldg(rowptr + rowB + 1), kB + kLongRow); kB += lane; }
     double accA = 0.0, accB = 0.0;
     while (kA < eA || kB < eB) {
       if (kA < eA) accA += (double)__ldg(val + kA) * __ldg(R + __ldg(col + kA));
@@ -160,27 +163,79 @@ spmv_plain_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__
        w += warps_total) {
     const int row = w * rows_per_warp + ((threadIdx.x & 31) / L);
     const bool valid = row < n;
-    const double acc = row_dot<VT, L>(rowptr, col, val, x, row, valid, lane);
+    const double acc = row_dot<VT, L>(rowptr, col, val, x, row, valid, lane, true);
     if (valid && lane == 0) y[row] = acc + shift * x[row];
   }
+}
+
+// Remainders of the long rows: one warp per chunk of kLongRow nonzeros.
+template <typename VT>
+__global__ void __launch_bounds__(256)
+long_chunk_kernel(int nchunks, const int* __restrict__ cb, const int* __restrict__ ce, const int* __restrict__ col,
+                  const VT* __restrict__ val, const double* __restrict__ x, double* __restrict__ csum,
+                  const int* __restrict__ state) {
+  if (state && state[ST_STATUS] != STATUS_RUNNING) return;
+  const int lane = threadIdx.x & 31;
+  for (int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks; c += (gridDim.x * blockDim.x) >> 5) {
+    double acc = 0.0;
+    for (int k = cb[c] + lane; k < ce[c]; k += 32) acc += (double)__ldg(val + k) * __ldg(x + __ldg(col + k));
+    acc = warp_sum(acc);
+    if (lane == 0) csum[c] = acc;
+  }
+}
+
+// y[row] += (sum of its chunks, in chunk order) / ||r|| for the Lanczos step
+// (scal: the norm published by the step's prologue), or unscaled.
+__global__ void long_combine_kernel(int nlong, const int* __restrict__ rows, const int* __restrict__ first,
+                                    const double* __restrict__ csum, double* __restrict__ y,
+                                    const double* __restrict__ scal, const int* __restrict__ state) {
+  if (state && state[ST_STATUS] != STATUS_RUNNING) return;
+  double s1 = 1.0, s2 = 1.0;
+  if (scal) safe_inv(scal[SC_BETA_NEXT], s1, s2);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nlong; i += gridDim.x * blockDim.x) {
+    double acc = 0.0;
+    for (int c = first[i]; c < first[i + 1]; ++c) acc += csum[c];
+    y[rows[i]] += (acc * s1) * s2;
+  }
+}
+
+template <typename VT>
+static cudaError_t long_rows_finish(const CsrDev& A, const VT* val, cudaStream_t st, const double* x, double* y,
+                                    const double* scal, const int* state) {
+  if (A.nlong == 0) return cudaSuccess;
+  int grid = (A.nchunks * 32 + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  long_chunk_kernel<VT><<<grid, 256, 0, st>>>(A.nchunks, A.chunk_begin, A.chunk_end, A.col, val, x, A.chunk_sum,
+                                              state);
+  long_combine_kernel<<<(A.nlong + 255) / 256, 256, 0, st>>>(A.nlong, A.long_rows, A.long_first, A.chunk_sum, y,
+                                                             scal, state);
+  return cudaGetLastError();
 }
 
 template <typename VT>
 static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, int grid, const double* R,
                                double* W, double* Vj, int ldv, const double* part_in, int nrows_in, int j,
                                int beta_mode, double* alpha, double* beta, double* scal, int* state) {
-#define LG_STEP(LN)                                                                                    \
-  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(A.n, A.rowptr, A.col, val, R, W, Vj, ldv, part_in, nrows_in, \
-                                                 j, beta_mode, alpha, beta, scal, state)
-  switch (A.lanes) {
-    case 2: LG_STEP(2); break;
-    case 4: LG_STEP(4); break;
-    case 8: LG_STEP(8); break;
-    case 16: LG_STEP(16); break;
-    default: LG_STEP(32); break;
+#define LG_STEP(LN, CNT, LIST)                                                                          \
+  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(CNT, LIST, A.rowptr, A.col, val, R, W, Vj, ldv, part_in,     \
+                                                 nrows_in, j, beta_mode, alpha, beta, scal, state)
+  const int ncls = A.nclasses > 0 ? A.nclasses : 1;
+  for (int c = 0; c < ncls; ++c) {
+    const int lanes = A.nclasses > 0 ? A.class_lanes[c] : A.lanes;
+    const int cnt = A.nclasses > 0 ? A.class_count[c] : A.n;
+    const int* list = A.nclasses > 0 ? A.class_rows[c] : nullptr;
+    switch (lanes) {
+      case 2: LG_STEP(2, cnt, list); break;
+      case 4: LG_STEP(4, cnt, list); break;
+      case 8: LG_STEP(8, cnt, list); break;
+      case 16: LG_STEP(16, cnt, list); break;
+      default: LG_STEP(32, cnt, list); break;
+    }
   }
 #undef LG_STEP
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return long_rows_finish<VT>(A, val, st, R, W, scal, state);
 }
 
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
@@ -206,7 +261,9 @@ static cudaError_t launch_plain(const CsrDev& A, const VT* val, cudaStream_t st,
     default: LG_PLAIN(32); break;
   }
 #undef LG_PLAIN
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return long_rows_finish<VT>(A, val, st, x, y, nullptr, nullptr);
 }
 
 cudaError_t spmv_plain(const CsrDev& A, cudaStream_t st, int grid, const double* x, double* y,

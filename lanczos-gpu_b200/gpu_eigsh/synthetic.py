@@ -129,6 +129,64 @@ def rmat_edges(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0.19, 0.05),
     return key // n, key % n
 
 
+def rmat_laplacian_device(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0.19, 0.05), seed: int = 2,
+                          device=None, chunk: int = 1 << 26):
+    """The R-MAT normalised Laplacian I - D^-1/2 W D^-1/2 (configuration 4),
+    generated and assembled on the GPU with torch.
+
+    Same construction as rmat_edges + normalized_laplacian (Chakrabarti, Zhan,
+    Faloutsos 2004: every edge picks one quadrant (a, b, c, d) per level;
+    symmetrised, duplicates and self-loops dropped, unit weights, isolated
+    vertices get L_ii = 0), drawn from the torch CUDA generator seeded with
+    `seed`, so the graph differs from the numpy one of the same seed.
+    Returns (n, rowptr int32, col int32, val float64) device tensors (rows
+    sorted by column, the diagonal stored for every row) and an info dict."""
+    import torch
+
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    a, b, c, _ = abcd
+    n = 1 << scale
+    m = edge_factor * n
+    g = torch.Generator(device=dev).manual_seed(seed)
+    keys = []
+    for start in range(0, m, chunk):
+        cnt = min(chunk, m - start)
+        u = torch.zeros(cnt, dtype=torch.int64, device=dev)
+        v = torch.zeros(cnt, dtype=torch.int64, device=dev)
+        for lvl in range(scale):
+            r = torch.rand(cnt, generator=g, device=dev, dtype=torch.float64)
+            u |= (r >= a + b).to(torch.int64) << lvl
+            v |= (((r >= a) & (r < a + b)) | (r >= a + b + c)).to(torch.int64) << lvl
+        lo, hi = torch.minimum(u, v), torch.maximum(u, v)
+        keep = lo != hi
+        keys.append(torch.unique(lo[keep] * n + hi[keep]))
+        del u, v, lo, hi, keep
+    key = torch.unique(torch.cat(keys))
+    del keys
+    src, dst = key // n, key % n
+    del key
+    deg = torch.bincount(src, minlength=n) + torch.bincount(dst, minlength=n)
+    dinv = torch.where(deg > 0, deg.to(torch.float64).clamp(min=1).rsqrt(), torch.zeros((), dtype=torch.float64,
+                                                                                           device=dev))
+    w = -(dinv[src] * dinv[dst])
+    diag = torch.arange(n, device=dev, dtype=torch.int64)
+    rows = torch.cat([src, dst, diag])
+    cols = torch.cat([dst, src, diag])
+    vals = torch.cat([w, w, (deg > 0).to(torch.float64)])
+    edges = int(src.numel())
+    del src, dst, w
+    order = torch.argsort(rows * n + cols)
+    col = cols[order].to(torch.int32)
+    val = vals[order]
+    counts = torch.bincount(rows, minlength=n)
+    del rows, cols, vals, order
+    rowptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+    rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+    info = {"n": n, "edges": edges, "nnz": int(col.numel()), "max_degree": int(deg.max()),
+            "isolated": int((deg == 0).sum()), "scale": scale, "edge_factor": edge_factor, "seed": seed}
+    return n, rowptr, col, val, info
+
+
 def normalized_laplacian(n: int, src, dst, dtype=np.float64) -> sp.csr_matrix:
     """I - D^-1/2 W D^-1/2 for unit edge weights (isolated vertices: L_ii = 0)."""
     w = np.ones(src.shape[0], dtype=np.float64)
