@@ -110,6 +110,29 @@ int lg_eigsh(int n, long long nnz, const int* row_ptr, const int* col_idx, const
              const lg_eigsh_opts* opts, const double* v0, double* evals, double* evecs,
              lg_eigsh_info* info);
 
+/* ---- row-partitioned eigsh over several GPUs (one process per GPU) --------
+ *
+ * Rank r owns the rows [r*nb, min((r+1)*nb, n)) of the n x n matrix, with
+ * nb = lg_partition_block(n, nranks); its CSR holds those rows with global
+ * column indices.  Every step all-gathers the residual (NCCL, in place) for
+ * the sparse product and all-reduces one row of partial sums per
+ * Gram-Schmidt pass; the restart logic runs replicated on every rank.  With a
+ * partitioned plan, lg_eigsh_plan_run takes this rank's slice of v0 and
+ * returns this rank's rows of the eigenvectors (n_local x k); the
+ * eigenvalues are returned on every rank.  Shift-invert, factorize and
+ * matvec are single-GPU only.  The communicator is NCCL's, created from a
+ * unique id that rank 0 draws and the caller distributes (e.g. with
+ * torch.distributed); NCCL is loaded on first use. */
+typedef struct lg_comm lg_comm;
+#define LG_COMM_ID_BYTES 128
+int lg_comm_unique_id(void* out, int len);
+int lg_comm_create(lg_comm** comm, const void* id, int len, int nranks, int rank);
+int lg_comm_destroy(lg_comm* comm);
+int lg_partition_block(int n, int nranks);
+int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global, int n_local, long long nnz,
+                              const int* row_ptr, const int* col_idx, const double* vals, int device_ptrs,
+                              int max_ncv, int mixed);
+
 /* m Lanczos steps (CGS2) from the host vector v0 without restarts: alpha
  * (m doubles) and beta (m+1 doubles; beta[0] = 0, beta[m] = final residual
  * norm) of the tridiagonal, copied to the host.  A test and debugging hook

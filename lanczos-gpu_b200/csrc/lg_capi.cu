@@ -1,5 +1,6 @@
 // lg_capi.cu — extern "C" entry points of liblanczos_b200.so (declared in
 // include/lanczos_b200.h).
+#include "lg_common.cuh"
 #include "lg_solver.h"
 
 #include <algorithm>
@@ -40,6 +41,29 @@ int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* 
   lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();
   if (!p) return LG_ERR_NOMEM;
   const int rc = p->solver.create(n, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv, mixed);
+  if (rc != LG_OK) {
+    delete p;
+    return rc;
+  }
+  *plan = p;
+  return LG_OK;
+}
+
+int lg_partition_block(int n, int nranks) {
+  if (n < 1 || nranks < 1) return 0;
+  const long long per = ((long long)n + nranks - 1) / nranks;
+  return (int)((per + lg::kRowAlign - 1) / lg::kRowAlign * lg::kRowAlign);
+}
+
+int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global, int n_local, long long nnz,
+                              const int* row_ptr, const int* col_idx, const double* vals, int device_ptrs,
+                              int max_ncv, int mixed) {
+  if (!plan) return LG_ERR_INVALID;
+  *plan = nullptr;
+  lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();
+  if (!p) return LG_ERR_NOMEM;
+  const int rc = p->solver.create_dist(comm, n_global, n_local, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv,
+                                       mixed);
   if (rc != LG_OK) {
     delete p;
     return rc;

@@ -1,0 +1,18 @@
+// lg_comm.h — collectives used by the row-partitioned eigensolver (lg_comm.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "../../include/lanczos_b200.h"
+
+namespace lg {
+
+int comm_rank(const lg_comm* c);
+int comm_size(const lg_comm* c);
+// Sum of `count` doubles over all ranks, in place, on stream `st`.
+int comm_allreduce_sum(const lg_comm* c, double* buf, size_t count, cudaStream_t st);
+// full holds nranks blocks of count_per_rank doubles; this rank's block is
+// already in place; afterwards every rank holds all blocks.
+int comm_allgather_inplace(const lg_comm* c, double* full, size_t count_per_rank, cudaStream_t st);
+
+}  // namespace lg

@@ -64,6 +64,13 @@ __global__ void scale_kernel(double* x, int n, double s) {
 Solver::~Solver() { release(); }
 
 void Solver::release() {
+  if (Rfull) {
+    cudaFree(Rfull);
+    Rfull = nullptr;
+    R = nullptr;
+  }
+  if (red) cudaFree(red);
+  red = nullptr;
   void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, d_long, d_chunk_sum, d_classes, V, W, R, partA, partB, partC, alpha, beta, scal,
                   ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
@@ -93,6 +100,39 @@ void Solver::release() {
 
 int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, const double* vals, int device_ptrs,
                    int max_ncv_, int mixed_) {
+  comm = nullptr;
+  n_global = n_;
+  row0 = 0;
+  nranks = 1;
+  rank = 0;
+  return create_impl(n_, n_, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_);
+}
+
+int Solver::create_dist(lg_comm* c, int n_glob, int n_local, long long nnz_, const int* rowptr, const int* col,
+                        const double* vals, int device_ptrs, int max_ncv_, int mixed_) {
+  if (!c) {
+    g_last_error = "null communicator";
+    return LG_ERR_INVALID;
+  }
+  comm = c;
+  nranks = comm_size(c);
+  rank = comm_rank(c);
+  n_global = n_glob;
+  const int nb = lg_partition_block(n_glob, nranks);
+  row0 = rank * nb;
+  const int expect = std::min(nb, n_glob - row0);
+  if (nb <= 0 || expect < 1 || n_local != expect) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "rank %d must own rows [%d, %d) (block %d of n=%d over %d ranks; every rank needs rows)",
+             rank, row0, row0 + std::max(expect, 0), nb, n_glob, nranks);
+    g_last_error = buf;
+    return LG_ERR_INVALID;
+  }
+  return create_impl(n_local, n_glob, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_);
+}
+
+int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, const int* col, const double* vals,
+                        int device_ptrs, int max_ncv_, int mixed_) {
   if (n_ < 1 || nnz_ < 0 || !rowptr || (nnz_ > 0 && (!col || !vals))) {
     g_last_error = "invalid CSR arguments";
     return LG_ERR_INVALID;
@@ -113,7 +153,7 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
         return LG_ERR_INVALID;
       }
     for (long long k = 0; k < nnz_; ++k)
-      if (col[k] < 0 || col[k] >= n_) {
+      if (col[k] < 0 || col[k] >= n_cols) {
         g_last_error = "column index out of range";
         return LG_ERR_INVALID;
       }
@@ -122,7 +162,7 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
   nnz = nnz_;
   mixed = mixed_;
   max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
-  ld = round_up(n, kRowAlign);
+  ld = comm ? lg_partition_block(n_global, nranks) : round_up(n, kRowAlign);
   ldv = round_up(max_ncv + 1, 4);
 
   LG_TRY(cudaGetDevice(&device));
@@ -155,10 +195,18 @@ int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, co
 
   LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
   LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
-  LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
+  if (comm) {
+    LG_TRY(cudaMalloc(&Rfull, sizeof(double) * (size_t)ld * nranks));
+    LG_TRY(cudaMemsetAsync(Rfull, 0, sizeof(double) * (size_t)ld * nranks, stream));
+    R = Rfull + (size_t)rank * ld;
+    LG_TRY(cudaMalloc(&red, sizeof(double) * 3 * kPartStride));
+    LG_TRY(cudaMemsetAsync(red, 0, sizeof(double) * 3 * kPartStride, stream));
+  } else {
+    LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
+    LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+  }
   LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
   LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
-  LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
   for (double** p : {&partA, &partB, &partC}) {
     LG_TRY(cudaMalloc(p, sizeof(double) * (size_t)prow * kPartStride));
@@ -271,6 +319,39 @@ int Solver::build_long_rows(const int* hrp) {
   return LG_OK;
 }
 
+// Fixed-order sum of `nrows` partial rows into one row (one thread per entry).
+__global__ void sum_rows_kernel(const double* __restrict__ part, int nrows, double* __restrict__ out) {
+  for (int i = threadIdx.x; i < kPartStride; i += blockDim.x) {
+    double s = 0.0;
+    for (int r = 0; r < nrows; ++r) s += part[(size_t)r * kPartStride + i];
+    out[i] = s;
+  }
+}
+
+int Solver::reduce_partials_all(double* part, int nrows, int slot, const double** in, int* nin) {
+  if (!comm) {
+    *in = part;
+    *nin = nrows;
+    return LG_OK;
+  }
+  double* row = red + (size_t)slot * kPartStride;
+  sum_rows_kernel<<<1, 160, 0, stream>>>(part, nrows, row);
+  LG_TRY(cudaGetLastError());
+  launches += 2;
+  int rc = comm_allreduce_sum(comm, row, kPartStride, stream);
+  if (rc != LG_OK) return rc;
+  *in = row;
+  *nin = 1;
+  return LG_OK;
+}
+
+// Every rank's residual block into Rfull (in place) before a sparse product.
+int Solver::gather_residual() {
+  if (!comm) return LG_OK;
+  ++launches;
+  return comm_allgather_inplace(comm, Rfull, (size_t)ld, stream);
+}
+
 int Solver::sync_state() {
   LG_TRY(cudaMemcpyAsync(h_state, state, sizeof(int) * ST_WORDS, cudaMemcpyDeviceToHost, stream));
   LG_TRY(cudaStreamSynchronize(stream));
@@ -289,9 +370,12 @@ int Solver::apply_step(int j, int beta_mode) {
     // CSR stream + x gather (counted once) + v_j and w written
     const double vb = mixed ? 4.0 : 8.0;
     const double bytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 16.0 * n;
+    int rc = gather_residual();
+    if (rc != LG_OK) return rc;
+    const double* Rg = comm ? Rfull : R;
     LG_TRY(timed(LG_K_SPMV, bytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
-      return spmv_step(A, stream, grid_spmv, R, W, Vj, ldv, partC, nrowsC, j, beta_mode, alpha, beta, scal,
-                       state);
+      return spmv_step(A, stream, grid_spmv, Rg, W, Vj, ldv, inC, nrowsC, j, beta_mode, alpha, beta, scal, state,
+                       R);
     }));
     return LG_OK;
   }
@@ -305,15 +389,22 @@ int Solver::extend(int j0, int j1, int first_mode) {
     const int ncols = j + 1;
     const GsPlan p = gs_plan(n, ncols, grid_gs);
     const double vbytes = 8.0 * (double)n * ncols;
+    const double *inA = nullptr, *inB = nullptr;
+    int nA = 0, nB = 0;
     LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
                  [&] { return gs_project(p, stream, V, ldv, ncols, n, W, partA, state); }));
+    rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
+    if (rc != LG_OK) return rc;
     LG_TRY(timed(LG_K_CORRPROJ, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct_project(p, stream, V, ldv, ncols, n, W, R, partA, p.grid, partB, scal, state);
+      return gs_correct_project(p, stream, V, ldv, ncols, n, W, R, inA, nA, partB, scal, state);
     }));
+    rc = reduce_partials_all(partB, p.grid, 1, &inB, &nB);
+    if (rc != LG_OK) return rc;
     LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct(p, stream, V, ldv, ncols, n, R, partB, p.grid, partC, scal, alpha, j, 1, state);
+      return gs_correct(p, stream, V, ldv, ncols, n, R, inB, nB, partC, scal, alpha, j, 1, state);
     }));
-    nrowsC = p.grid;
+    rc = reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
+    if (rc != LG_OK) return rc;
   }
   return LG_OK;
 }
@@ -346,10 +437,13 @@ int Solver::pass3(int s) {
   const int ncols = s + 1;
   const GsPlan p = gs_plan(n, ncols, grid_gs);
   launches += 2;
+  const double* inA = nullptr;
+  int nA = 0;
   LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
-  LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, partA, p.grid, partC, scal, alpha, s, 2, state));
-  nrowsC = p.grid;
-  return LG_OK;
+  int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
+  if (rc != LG_OK) return rc;
+  LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state));
+  return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
 
 // Invariant subspace after step s: a random vector made orthogonal to
@@ -359,14 +453,20 @@ int Solver::pass3(int s) {
 int Solver::random_restart(int s) {
   const int ncols = s + 1;
   ++breakdowns;
-  LG_TRY(fill_random(stream, R, n, ld, mix64(opts.seed + 0x5bd1e995ull * (uint64_t)(breakdowns + 1) + (uint64_t)s)));
+  LG_TRY(fill_random(stream, R, n, ld, mix64(opts.seed + 0x5bd1e995ull * (uint64_t)(breakdowns + 1) + (uint64_t)s),
+                     row0));
   const GsPlan p = gs_plan(n, ncols, grid_gs);
   launches += 5;
   for (int pass = 0; pass < 2; ++pass) {
+    const double* inA = nullptr;
+    int nA = 0;
     LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
-    LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, partA, p.grid, partC, scal, alpha, s, 0, state));
+    int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
+    if (rc != LG_OK) return rc;
+    LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 0, state));
+    rc = reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
+    if (rc != LG_OK) return rc;
   }
-  nrowsC = p.grid;
   return LG_OK;
 }
 
@@ -400,6 +500,10 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
   ktimes.clear();
   ev_used = 0;
 
+  if (comm && o.use_sigma) {
+    g_last_error = "shift-invert is not available with a row-partitioned plan";
+    return LG_ERR_INVALID;
+  }
   if (o.use_sigma) {
     int rc = prepare_shift_invert();
     if (rc != LG_OK) return rc;
@@ -418,12 +522,15 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n,
                            io_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream));
   } else {
-    LG_TRY(fill_random(stream, R, n, ld, o.seed));
+    LG_TRY(fill_random(stream, R, n, ld, o.seed, row0));
     ++launches;
   }
   LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
   ++launches;
-  nrowsC = grid_gs;
+  {
+    int rc0 = reduce_partials_all(partC, grid_gs, 2, &inC, &nrowsC);
+    if (rc0 != LG_OK) return rc0;
+  }
 
   long long steps = 0;
   int rc = extend(0, m, BETA_INIT);
@@ -443,7 +550,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ra.force_done = (o.max_steps > 0 && steps >= o.max_steps) ? 1 : 0;
     ra.skip_checks = skip_checks_next;
     skip_checks_next = 0;
-    ra.part_in = partC;
+    ra.part_in = inC;
     ra.nrows_in = nrowsC;
     ra.alpha = alpha;
     ra.beta = beta;
@@ -497,7 +604,8 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
         LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
         LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
         ++launches;
-        nrowsC = grid_gs;
+        rc = reduce_partials_all(partC, grid_gs, 2, &inC, &nrowsC);
+        if (rc != LG_OK) return rc;
         skip_checks_next = 1;
       }
       continue;  // re-run the Ritz computation for this restart
@@ -525,7 +633,8 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ba.state = state;
     const BasisPlan bp = basis_plan(n, m, ba.kq, grid_basis);
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + nev_use) + 16.0 * n, 1, [&] { return basis_update(bp, ba, stream); }));
-    nrowsC = bp.grid;
+    rc = reduce_partials_all(partC, bp.grid, 2, &inC, &nrowsC);
+    if (rc != LG_OK) return rc;
     rc = extend(nev_use, m, BETA_RESTART);
     if (rc != LG_OK) return rc;
     steps += m - nev_use;
@@ -639,6 +748,10 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
 // m Lanczos steps from v0 (host vector) without restarts; returns the
 // tridiagonal (alpha[0..m), beta[0..m], beta[m] = final residual norm).
 int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_out) {
+  if (comm) {
+    g_last_error = "factorize is not available with a row-partitioned plan";
+    return LG_ERR_INVALID;
+  }
   if (m < 1 || m > max_ncv || m > n || !v0) {
     g_last_error = "factorize: need 1 <= m <= min(n, max_ncv) and a starting vector";
     return LG_ERR_INVALID;
@@ -655,6 +768,7 @@ int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_o
   LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
   LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
   nrowsC = grid_gs;
+  inC = partC;
   int rc = extend(0, m, BETA_INIT);
   if (rc != LG_OK) return rc;
   std::vector<double> part((size_t)nrowsC * kPartStride);
@@ -674,6 +788,10 @@ int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_o
 }
 
 int Solver::matvec(const double* x, double* y) {
+  if (comm) {
+    g_last_error = "matvec is not available with a row-partitioned plan";
+    return LG_ERR_INVALID;
+  }
   LG_TRY(spmv_plain(A, stream, grid_spmv, x, y, 0.0));
   LG_TRY(cudaStreamSynchronize(stream));
   return LG_OK;

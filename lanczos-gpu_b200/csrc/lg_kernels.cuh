@@ -63,7 +63,7 @@ struct CsrDev {
 // Vj points at column j of the row-major basis (stride ldv).
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
                       int ldv, const double* part_in, int nrows_in, int j, int beta_mode, double* alpha,
-                      double* beta, double* scal, int* state);
+                      double* beta, double* scal, int* state, const double* R_own = nullptr);
 
 // Normalise R into V[:, j] (same checks as spmv_step) without applying A;
 // optionally also into the contiguous vector `out`.
@@ -77,7 +77,7 @@ cudaError_t spmv_plain(const CsrDev& A, cudaStream_t st, int grid, const double*
                        double shift);
 
 // Misc vector kernels (lg_spmv.cu).
-cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed);
+cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed, long long index0 = 0);
 cudaError_t norm_partials(cudaStream_t st, int grid, const double* x, int ld, double* part_out);
 
 // Restart (lg_restart.cu).

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "../../include/lanczos_b200.h"
+#include "lg_comm.h"
 #include "lg_kernels.cuh"
 
 namespace lg {
@@ -17,6 +18,9 @@ class Solver {
   ~Solver();
   int create(int n, long long nnz, const int* rowptr, const int* col, const double* vals, int device_ptrs,
              int max_ncv, int mixed);
+  // Row-partitioned solver: this rank's n_local rows of an n_global x n_global matrix.
+  int create_dist(lg_comm* comm, int n_global, int n_local, long long nnz, const int* rowptr, const int* col,
+                  const double* vals, int device_ptrs, int max_ncv, int mixed);
   int run(const lg_eigsh_opts& o, const double* v0, double* evals, double* evecs, int io_on_device,
           lg_eigsh_info* info);
   int matvec(const double* x, double* y);
@@ -24,6 +28,13 @@ class Solver {
 
  private:
   void release();
+  int create_impl(int n_rows, int n_cols, long long nnz, const int* rowptr, const int* col, const double* vals,
+                  int device_ptrs, int max_ncv, int mixed);
+  // Partitioned runs: sum `nrows` partial-sum rows into row `slot` of `red`
+  // and all-reduce it over the ranks; *in / *nin become that single row.
+  // Single GPU: *in = part, *nin = nrows.
+  int reduce_partials_all(double* part, int nrows, int slot, const double** in, int* nin);
+  int gather_residual();
   int build_long_rows(const int* host_rowptr);
   int sync_state();
   int clear_status();
@@ -37,6 +48,14 @@ class Solver {
   int cg_solve(const double* b, double* x);
 
   int n = 0, ld = 0, ldv = 0, max_ncv = 0, mixed = 0;   // ld: vector length padding; ldv: basis row stride
+  // row partition (comm set): this rank owns global rows [row0, row0 + n); the
+  // residuals of all ranks live in Rfull (nranks blocks of ld = nb doubles)
+  // and R is this rank's block, so global column indices address Rfull.
+  lg_comm* comm = nullptr;
+  int n_global = 0, row0 = 0, nranks = 1, rank = 0;
+  double* Rfull = nullptr;
+  double* red = nullptr;          // 3 x kPartStride: all-reduced partial rows
+  const double* inC = nullptr;    // partial sums read by the next step / restart
   long long nnz = 0;
   int device = 0, num_sm = 0, grid_gs = 0, grid_spmv = 0, grid_basis = 0;
   size_t smem_budget = 0;

@@ -81,8 +81,9 @@ template <typename VT, int L>
 __global__ void __launch_bounds__(256)
 spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict__ rowptr,
                  const int* __restrict__ col, const VT* __restrict__ val, const double* __restrict__ R,
-                 double* __restrict__ W, double* __restrict__ Vj, int ldv, const double* __restrict__ part_in,
-                 int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal, int* state) {
+                 const double* __restrict__ R_own, double* __restrict__ W, double* __restrict__ Vj, int ldv,
+                 const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
+                 double* beta, double* scal, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   double s1, s2;
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
@@ -117,11 +118,11 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
     if (lane == 0) {
       if (okA) {
         W[rowA] = (accA * s1) * s2;
-        Vj[(size_t)rowA * ldv] = (R[rowA] * s1) * s2;
+        Vj[(size_t)rowA * ldv] = (R_own[rowA] * s1) * s2;
       }
       if (okB) {
         W[rowB] = (accB * s1) * s2;
-        Vj[(size_t)rowB * ldv] = (R[rowB] * s1) * s2;
+        Vj[(size_t)rowB * ldv] = (R_own[rowB] * s1) * s2;
       }
     }
   }
@@ -214,10 +215,11 @@ static cudaError_t long_rows_finish(const CsrDev& A, const VT* val, cudaStream_t
 
 template <typename VT>
 static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, int grid, const double* R,
-                               double* W, double* Vj, int ldv, const double* part_in, int nrows_in, int j,
-                               int beta_mode, double* alpha, double* beta, double* scal, int* state) {
+                               const double* R_own, double* W, double* Vj, int ldv, const double* part_in,
+                               int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
+                               int* state) {
 #define LG_STEP(LN, CNT, LIST)                                                                          \
-  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(CNT, LIST, A.rowptr, A.col, val, R, W, Vj, ldv, part_in,     \
+  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(CNT, LIST, A.rowptr, A.col, val, R, R_own, W, Vj, ldv, part_in, \
                                                  nrows_in, j, beta_mode, alpha, beta, scal, state)
   const int ncls = A.nclasses > 0 ? A.nclasses : 1;
   for (int c = 0; c < ncls; ++c) {
@@ -240,12 +242,13 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
 
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
                       int ldv, const double* part_in, int nrows_in, int j, int beta_mode, double* alpha,
-                      double* beta, double* scal, int* state) {
+                      double* beta, double* scal, int* state, const double* R_own) {
+  if (!R_own) R_own = R;
   if (A.val32)
-    return launch_step<float>(A, A.val32, st, grid, R, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta,
-                              scal, state);
-  return launch_step<double>(A, A.val64, st, grid, R, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta,
-                             scal, state);
+    return launch_step<float>(A, A.val32, st, grid, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha,
+                              beta, scal, state);
+  return launch_step<double>(A, A.val64, st, grid, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha,
+                             beta, scal, state);
 }
 
 template <typename VT>
@@ -273,15 +276,17 @@ cudaError_t spmv_plain(const CsrDev& A, cudaStream_t st, int grid, const double*
 }
 
 // ---------------------------------------------------------------------------
-__global__ void fill_random_kernel(double* x, int n, int ld, uint64_t seed) {
+// x[i] = uniform(seed, index0 + i): a row-partitioned vector is the slice of
+// the same global vector on every partition.
+__global__ void fill_random_kernel(double* x, int n, int ld, uint64_t seed, long long index0) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ld; i += gridDim.x * blockDim.x)
-    x[i] = (i < n) ? uniform_centered(seed, (uint64_t)i) : 0.0;
+    x[i] = (i < n) ? uniform_centered(seed, (uint64_t)(index0 + i)) : 0.0;
 }
 
-cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed) {
+cudaError_t fill_random(cudaStream_t st, double* x, int n, int ld, uint64_t seed, long long index0) {
   int grid = (ld + 255) / 256;
   if (grid > 4096) grid = 4096;
-  fill_random_kernel<<<grid, 256, 0, st>>>(x, n, ld, seed);
+  fill_random_kernel<<<grid, 256, 0, st>>>(x, n, ld, seed, index0);
   return cudaGetLastError();
 }
 

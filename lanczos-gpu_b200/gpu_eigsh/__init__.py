@@ -66,10 +66,16 @@ class EigshPlan:
     same keywords as :func:`gpu_eigsh`.
     """
 
-    def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None):
+    def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None):
         self._plan = None
         h = _native.C.c_void_p()
-        if device_csr is not None:
+        if comm is not None:
+            # row-partitioned: device_csr holds this rank's rows (global column indices)
+            n, nnz, rp, ci, vals = device_csr
+            rc = _native.lib.lg_eigsh_plan_create_dist(_native.C.byref(h), comm.handle, int(n_global), int(n),
+                                                       int(nnz), int(rp), int(ci), int(vals), 1, int(max_ncv),
+                                                       int(bool(mixed)))
+        elif device_csr is not None:
             n, nnz, rp, ci, vals = device_csr
             rc = _native.lib.lg_eigsh_plan_create(_native.C.byref(h), int(n), int(nnz), int(rp), int(ci),
                                                   int(vals), 1, int(max_ncv), int(bool(mixed)))

@@ -110,6 +110,12 @@ SIGNATURES = {
     "lg_eigsh_plan_run": (C.c_int, [C.c_void_p, C.POINTER(EigshOpts), C.c_void_p, _PD, C.c_void_p, C.c_int,
                                     C.POINTER(EigshInfo)]),
     "lg_eigsh_plan_destroy": (C.c_int, [C.c_void_p]),
+    "lg_comm_unique_id": (C.c_int, [C.c_void_p, C.c_int]),
+    "lg_comm_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "lg_comm_destroy": (C.c_int, [C.c_void_p]),
+    "lg_partition_block": (C.c_int, [C.c_int, C.c_int]),
+    "lg_eigsh_plan_create_dist": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_longlong,
+                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
     "lg_eigsh_plan_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_eigsh_plan_factorize": (C.c_int, [C.c_void_p, _PD, C.c_int, _PD, _PD]),
     "lg_eigsh": (C.c_int, [C.c_int, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(EigshOpts),

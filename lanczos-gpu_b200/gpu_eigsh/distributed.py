@@ -1,4 +1,13 @@
-"""Multi-GPU stochastic Lanczos quadrature: probes sharded across ranks.
+"""Multi-GPU paths (one process per GPU, torch.distributed over NCCL).
+
+1. eigsh, row-partitioned (``Communicator``, ``partition_rows``,
+   ``PartitionedEigsh``): rank r owns the rows [r*nb, min((r+1)*nb, n)) of the
+   matrix (nb = lg_partition_block); the CUDA engine all-gathers the residual
+   before each sparse product and all-reduces one row of partial sums per
+   Gram-Schmidt pass with NCCL, and runs the restart logic replicated.  The
+   reference runs on one GPU only.
+
+2. Stochastic Lanczos quadrature, probes sharded across ranks:
 
 The probe columns of an SLQ estimate are independent, so N ranks (one process
 per GPU, torch.distributed over NCCL) split them: every rank draws the same
@@ -24,7 +33,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-__all__ = ["probe_range", "slq_logdet_sharded", "sharded_slq"]
+__all__ = ["probe_range", "slq_logdet_sharded", "sharded_slq", "Communicator", "partition_rows",
+           "PartitionedEigsh"]
 
 
 def probe_range(p_total: int, rank: int, world: int):
@@ -104,3 +114,86 @@ def slq_logdet_sharded(matvec, n, params, m_probes=20, lanczos_m=50, seed=0, dty
     Z = _probes(n, m_probes, seed, dtype, matvec.device).to(matvec.dtype)
     engine = ImgpSLQEngine(matvec, lanczos_m, _scalar(params[0]), _scalar(params[1]))
     return sharded_slq(engine, Z, params, group)
+
+
+# ---------------------------------------------------------------------------
+# Row-partitioned eigsh
+# ---------------------------------------------------------------------------
+def partition_rows(n: int, world: int, rank: int):
+    """Global rows [r0, r1) owned by `rank` (block size from the engine)."""
+    from . import _native
+
+    nb = _native.lib.lg_partition_block(int(n), int(world))
+    r0 = min(rank * nb, n)
+    return r0, min(r0 + nb, n)
+
+
+class Communicator:
+    """The engine's NCCL communicator over the ranks of a torch.distributed
+    group: rank 0 draws the unique id, the group broadcasts it."""
+
+    def __init__(self, group=None):
+        import ctypes as C
+
+        from . import _native
+
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        obj = [None]
+        if self.rank == 0:
+            buf = C.create_string_buffer(128)
+            _native.check(_native.lib.lg_comm_unique_id(buf, 128))
+            obj = [bytes(buf.raw)]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        h = C.c_void_p()
+        _native.check(_native.lib.lg_comm_create(C.byref(h), obj[0], 128, self.world, self.rank))
+        self.handle = h
+
+    def close(self):
+        from . import _native
+
+        if self.handle is not None and self.handle.value:
+            _native.lib.lg_comm_destroy(self.handle)
+        self.handle = None
+
+
+class PartitionedEigsh:
+    """eigsh of an n x n matrix whose rows are split over the ranks.
+
+    rowptr, col, vals: this rank's rows [r0, r1) (see partition_rows) as a CSR
+    with global column indices, torch tensors on this rank's GPU (int32,
+    int32, float64).  solve() takes the keywords of gpu_eigsh.EigshPlan.solve
+    with v0 = this rank's slice and returns (eigenvalues, this rank's rows of
+    the eigenvectors as an (r1 - r0) x k tensor)."""
+
+    def __init__(self, comm: Communicator, n_global: int, rowptr, col, vals, max_ncv: int = 127,
+                 mixed: bool = False):
+        import torch
+
+        from . import EigshPlan
+
+        self.comm, self.n_global = comm, int(n_global)
+        self.r0, self.r1 = partition_rows(n_global, comm.world, comm.rank)
+        n_local = self.r1 - self.r0
+        if rowptr.numel() != n_local + 1:
+            raise ValueError(f"rank {comm.rank} must pass rows [{self.r0}, {self.r1}) ({n_local} rows)")
+        self._keep = (rowptr, col, vals)
+        self.plan = EigshPlan(None, max_ncv=max_ncv, mixed=mixed, comm=comm, n_global=n_global,
+                              device_csr=(n_local, int(col.numel()), rowptr.data_ptr(), col.data_ptr(),
+                                          vals.data_ptr()))
+        self.device = vals.device
+        self.torch = torch
+
+    def solve(self, k, v0_local, **kw):
+        torch = self.torch
+        v0 = torch.as_tensor(v0_local, dtype=torch.float64).to(self.device).contiguous()
+        Y = torch.empty((self.r1 - self.r0, int(k)), dtype=torch.float64, device=self.device)
+        w, _ = self.plan.solve(k=k, v0_device=v0.data_ptr(), evecs_out=Y.data_ptr(), **kw)
+        return w, Y
+
+    @property
+    def last_info(self):
+        return self.plan.last_info
+
+    def close(self):
+        self.plan.close()

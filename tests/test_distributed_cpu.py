@@ -98,3 +98,20 @@ def test_probe_range_partitions():
                 assert 0 <= c1 - c0 <= P // world + 1
                 cols += list(range(c0, c1))
             assert cols == list(range(P))
+
+
+def test_partition_rows_covers_every_row_once():
+    from gpu_eigsh import _native
+    from gpu_eigsh.distributed import partition_rows
+
+    for n in (1000, 60000, 1 << 20, 16777216):
+        for world in (1, 2, 3, 4, 8):
+            nb = _native.lib.lg_partition_block(n, world)
+            assert nb % 256 == 0 and nb * world >= n
+            rows = []
+            for r in range(world):
+                r0, r1 = partition_rows(n, world, r)
+                assert r0 == min(r * nb, n)
+                rows.append((r0, r1))
+            assert rows[0][0] == 0 and rows[-1][1] == n
+            assert all(rows[i][1] == rows[i + 1][0] for i in range(world - 1))

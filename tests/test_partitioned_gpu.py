@@ -1,0 +1,97 @@
+"""GPU (2+ devices): the row-partitioned eigsh equals the single-GPU solve.
+
+Two ranks (processes, one GPU each, NCCL) split the rows of a kNN graph
+Laplacian and of an R-MAT normalised Laplacian (configuration 4's family,
+with rows longer than the row kernels' cut).  Every rank must report the same
+eigenvalues, equal to the single-GPU plan's at 1e-10, and the assembled
+eigenvector rows must satisfy ||A v - lambda v|| <= tol ||A||.  Skipped with
+fewer than two GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _matrix(case):
+    from gpu_eigsh import synthetic as syn
+
+    if case == "knn":
+        L, _ = syn.knn_laplacian(60000, k=10, seed=4)
+        return L, dict(k=10, which="LA", ncv=30, tol=1e-10), False
+    import torch
+
+    n, rp, col, val, _ = syn.rmat_laplacian_device(15, device="cpu")
+    L = sp.csr_matrix((val.numpy(), col.numpy(), rp.numpy()), shape=(n, n))
+    return L, dict(k=12, which="LA", ncv=40, tol=1e-10), False
+
+
+def _worker(rank, world, port, case, out_w, out_y):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from gpu_eigsh.distributed import Communicator, PartitionedEigsh, partition_rows
+
+    comm = Communicator()
+    try:
+        L, kw, _ = _matrix(case)
+        n = L.shape[0]
+        r0, r1 = partition_rows(n, world, rank)
+        a, b = L.indptr[r0], L.indptr[r1]
+        dev = torch.device("cuda", rank)
+        rp = torch.from_numpy((L.indptr[r0:r1 + 1] - a).astype(np.int32)).to(dev)
+        col = torch.from_numpy(L.indices[a:b].astype(np.int32)).to(dev)
+        val = torch.from_numpy(L.data[a:b].astype(np.float64)).to(dev)
+        v0 = np.random.default_rng(0).standard_normal(n)
+        pe = PartitionedEigsh(comm, n, rp, col, val, max_ncv=kw["ncv"])
+        k = kw.pop("k")
+        w, Y = pe.solve(k, v0[r0:r1], **kw)
+        torch.cuda.synchronize()
+        out_w[rank, :k] = torch.from_numpy(np.asarray(w))
+        out_y[r0:r1, :k] = Y.cpu()
+        pe.close()
+    finally:
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["knn", "rmat"])
+def test_partitioned_equals_single_gpu(case):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import gpu_eigsh
+
+    world = 2
+    L, kw, _ = _matrix(case)
+    n, k = L.shape[0], kw["k"]
+    out_w = torch.zeros(world, k, dtype=torch.float64).share_memory_()
+    out_y = torch.zeros(n, k, dtype=torch.float64).share_memory_()
+    mp.spawn(_worker, args=(world, _free_port(), case, out_w, out_y), nprocs=world, join=True)
+    assert torch.equal(out_w[0], out_w[1]), "ranks disagree on the eigenvalues"
+    v0 = np.random.default_rng(0).standard_normal(n)
+    ref = gpu_eigsh.gpu_eigsh(L, v0=v0, return_eigenvectors=False, **kw)
+    w = out_w[0].numpy()
+    assert np.max(np.abs(w - np.sort(ref)) / np.maximum(np.abs(ref), 1e-300)) < 1e-10
+    Y = out_y.numpy()
+    res = np.linalg.norm(L @ Y - Y * w, axis=0).max()
+    assert res <= kw["tol"] * abs(L).sum(axis=1).max()
