@@ -317,11 +317,11 @@ def run_slq(args, dev, with_e2e, with_cpu, world=1, rank=0):
     return out
 
 
-RMAT_SCALE, RMAT_K, RMAT_NCV, RMAT_TOL = 24, 32, 96, 1e-8
+RMAT_SCALE, RMAT_K, RMAT_NCV, RMAT_TOL, RMAT_RELABEL_SEED = 24, 32, 96, 1e-8, 3
 RMAT_WORKLOAD = (f"eigsh k={RMAT_K} which=LA ncv={RMAT_NCV} tol={RMAT_TOL:g} on the normalised Laplacian of an R-MAT "
                  f"graph, scale {RMAT_SCALE} (n=16,777,216), edge factor 16, (a,b,c,d)=(.57,.19,.19,.05), seed 2 "
-                 "(torch CUDA generator), symmetrised, no duplicates or self-loops; fp32 CSR values, fp64 "
-                 "accumulation and basis")
+                 "(torch CUDA generator), symmetrised, no duplicates or self-loops, vertices renumbered by a seeded "
+                 "random permutation; fp32 CSR values, fp64 accumulation and basis")
 
 
 def run_rmat(args, dev, world=1, rank=0):
@@ -334,15 +334,38 @@ def run_rmat(args, dev, world=1, rank=0):
 
     scale = args.rmat_scale
     t0 = time.time()
-    n, rp, col, val, info = syn.rmat_laplacian_device(scale, device=dev)
+    # vertices renumbered by a seeded random permutation (the same graph) so
+    # that equal row blocks carry equal shares of the nonzeros; the same matrix
+    # and v0 at every GPU count
+    n, rp, col, val, info = syn.rmat_laplacian_device(scale, device=dev, relabel_seed=RMAT_RELABEL_SEED)
     torch.cuda.synchronize()
     gen_s = time.time() - t0
     nnz = int(col.numel())
-    plan = gpu_eigsh.EigshPlan(None, max_ncv=RMAT_NCV, mixed=True,
-                               device_csr=(n, nnz, rp.data_ptr(), col.data_ptr(), val.data_ptr()))
+    v0_full = np.random.default_rng(0).standard_normal(n)
+    info.pop("perm", None)
+    comm = None
+    if world > 1:
+        # rows split over the ranks (every rank generated the same graph)
+        import torch.distributed as dist
+
+        from gpu_eigsh.distributed import Communicator, partition_rows
+
+        comm = Communicator()
+        r0, r1 = partition_rows(n, world, rank)
+        a, b = int(rp[r0]), int(rp[r1])
+        rp = (rp[r0:r1 + 1] - a).contiguous()
+        col = col[a:b].contiguous()
+        val = val[a:b].contiguous()
+        plan = gpu_eigsh.EigshPlan(None, max_ncv=RMAT_NCV, mixed=True, comm=comm, n_global=n,
+                                   device_csr=(r1 - r0, int(col.numel()), rp.data_ptr(), col.data_ptr(),
+                                               val.data_ptr()))
+    else:
+        r0, r1 = 0, n
+        plan = gpu_eigsh.EigshPlan(None, max_ncv=RMAT_NCV, mixed=True,
+                                   device_csr=(n, nnz, rp.data_ptr(), col.data_ptr(), val.data_ptr()))
     del val
-    v0 = torch.from_numpy(np.random.default_rng(0).standard_normal(n)).to(dev)
-    Y = torch.empty((n, RMAT_K), dtype=torch.float64, device=dev)
+    v0 = torch.from_numpy(v0_full[r0:r1].copy()).to(dev)
+    Y = torch.empty((r1 - r0, RMAT_K), dtype=torch.float64, device=dev)
 
     def solve(profile=False):
         w, _ = plan.solve(k=RMAT_K, which="LA", ncv=RMAT_NCV, tol=RMAT_TOL, v0_device=v0.data_ptr(),
@@ -351,6 +374,8 @@ def run_rmat(args, dev, world=1, rank=0):
 
     solve()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     steps = max(1, min(args.steps, 2))
     torch.cuda.nvtx.range_push("rmat_timed")
@@ -360,6 +385,10 @@ def run_rmat(args, dev, world=1, rank=0):
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     w, _ = solve()
     peak, peak_kind = measured_peaks()
     classes = infos[0]["kernel_ms"].keys()
@@ -378,8 +407,12 @@ def run_rmat(args, dev, world=1, rank=0):
            "step_roofline": {"kernels": step_cls, "achieved": sbytes / (sms / 1000) / 1e9 if sms else None,
                              "peak": peak, "unit": "GB/s", "peak_source": peak_kind,
                              "frac": (sbytes / (sms / 1000) / 1e9 / peak) if sms else None},
-           "gpu_launches_per_solve": infos[0]["launches"]}
+           "gpu_launches_per_solve": infos[0]["launches"],
+           "parallelism": f"rows partitioned over {world} GPUs (NCCL)" if world > 1 else "1 GPU",
+           "scaling": "strong" if world > 1 else None}
     plan.close()
+    if comm is not None:
+        comm.close()
     return out
 
 
@@ -561,6 +594,8 @@ def run_ours(args):
         line["slq"] = run_slq(args, dev, with_e2e=(not args.no_e2e) and (world > 1 or rank == 0),
                               with_cpu=(rank == 0 and not args.no_cpu_baseline), world=world, rank=rank)
         line["gpu_launches"] += line["slq"]["gpu_launches_per_step"] * args.steps
+    if not args.no_rmat:
+        line["rmat"] = run_rmat(args, dev, world=world, rank=rank)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -581,6 +616,7 @@ def main():
     ap.add_argument("--no-slq", action="store_true", help="skip the SLQ log-det + gradient leg")
     ap.add_argument("--only-slq", action="store_true", help="run the SLQ leg alone (no eigsh)")
     ap.add_argument("--only-rmat", action="store_true", help="run the configuration-4 (R-MAT) eigsh leg alone")
+    ap.add_argument("--no-rmat", action="store_true", help="skip the configuration-4 (R-MAT) eigsh leg")
     ap.add_argument("--rmat-scale", type=int, default=RMAT_SCALE, help="R-MAT scale (reduced cases for profiling)")
     ap.add_argument("--slq-n", type=int, default=N_POINTS, help="SLQ graph size (reduced cases for profiling)")
     ap.add_argument("--slq-m", type=int, default=SLQ_M, help="SLQ Lanczos depth (reduced cases for profiling)")

@@ -130,7 +130,7 @@ def rmat_edges(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0.19, 0.05),
 
 
 def rmat_laplacian_device(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0.19, 0.05), seed: int = 2,
-                          device=None, chunk: int = 1 << 26):
+                          device=None, chunk: int = 1 << 26, relabel_seed=None):
     """The R-MAT normalised Laplacian I - D^-1/2 W D^-1/2 (configuration 4),
     generated and assembled on the GPU with torch.
 
@@ -139,6 +139,12 @@ def rmat_laplacian_device(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0
     symmetrised, duplicates and self-loops dropped, unit weights, isolated
     vertices get L_ii = 0), drawn from the torch CUDA generator seeded with
     `seed`, so the graph differs from the numpy one of the same seed.
+    relabel_seed (not None) renumbers the vertices by a seeded random
+    permutation (a symmetric permutation: same graph, same spectrum), so that
+    equal row blocks carry about the same number of nonzeros: every level of
+    the R-MAT recursion biases one index bit, so contiguous blocks of the
+    original numbering are unbalanced (76 % / 24 % of the nonzeros for two
+    halves at a = 0.57).  info["perm"] holds the permutation (old -> new).
     Returns (n, rowptr int32, col int32, val float64) device tensors (rows
     sorted by column, the diagonal stored for every row) and an info dict."""
     import torch
@@ -165,6 +171,11 @@ def rmat_laplacian_device(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0
     del keys
     src, dst = key // n, key % n
     del key
+    perm = None
+    if relabel_seed is not None:
+        pg = torch.Generator(device=dev).manual_seed(int(relabel_seed))
+        perm = torch.randperm(n, generator=pg, device=dev)
+        src, dst = perm[src], perm[dst]
     deg = torch.bincount(src, minlength=n) + torch.bincount(dst, minlength=n)
     dinv = torch.where(deg > 0, deg.to(torch.float64).clamp(min=1).rsqrt(), torch.zeros((), dtype=torch.float64,
                                                                                            device=dev))
@@ -183,7 +194,8 @@ def rmat_laplacian_device(scale: int, edge_factor: int = 16, abcd=(0.57, 0.19, 0
     rowptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
     rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
     info = {"n": n, "edges": edges, "nnz": int(col.numel()), "max_degree": int(deg.max()),
-            "isolated": int((deg == 0).sum()), "scale": scale, "edge_factor": edge_factor, "seed": seed}
+            "isolated": int((deg == 0).sum()), "scale": scale, "edge_factor": edge_factor, "seed": seed,
+            "relabel_seed": relabel_seed, "perm": perm}
     return n, rowptr, col, val, info
 
 
