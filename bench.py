@@ -54,6 +54,14 @@ WORKLOAD = (f"eigsh k={K_EIG} which=LA ncv={NCV} tol={TOL:g} on the n=1e6 kNN gr
             "(2-D uniform points seed 1, k=10, union-symmetrised, exp(-d^2/2h^2)), fp64 CSR")
 
 
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) over the
+# algorithmic bytes of the same launch, from the captures summarised under
+# profiles/ (captured on the configuration-1 / reduced configuration-3
+# workloads); `traffic` = ratio x the bench's algorithmic bytes per launch.
+TRAFFIC_RATIO = {"spmv": 1.29, "gs_project": 1.056, "gs_correct_project": 1.044, "gs_correct": 1.049,
+                 "basis": 1.035, "slq_forward": 0.955, "slq_backward": 0.96}
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -293,7 +301,9 @@ def run_slq(args, dev, with_e2e, with_cpu, world=1, rank=0):
     fa, ba = fwd_b / (f_ms / 1000) / 1e9, bwd_b / (b_ms / 1000) / 1e9
     dom = ("slq_backward", ba, b_ms, bwd_b) if b_ms >= f_ms else ("slq_forward", fa, f_ms, fwd_b)
     out["roofline"] = {"bound": "hbm", "kernel": dom[0], "achieved": dom[1], "peak": peak, "unit": "GB/s",
-                       "frac": dom[1] / peak, "peak_source": peak_kind, "traffic": None,
+                       "frac": dom[1] / peak, "peak_source": peak_kind,
+                       "traffic": TRAFFIC_RATIO[dom[0]] * dom[3], "traffic_unit": "bytes per phase (all steps)",
+                       "traffic_source": "ncu ratio (profiles/slq_products_knn6e5.md) x algorithmic bytes",
                        "algorithmic_bytes_per_launch": dom[3], "avg_launch_ms": dom[2]}
     out["phases"] = {"forward_ms": f_ms, "forward_GBs": fa, "forward_frac": fa / peak, "forward_bytes": fwd_b,
                      "backward_ms": b_ms, "backward_GBs": ba, "backward_frac": ba / peak, "backward_bytes": bwd_b}
@@ -558,7 +568,10 @@ def run_ours(args):
         "nconv": infos[0]["nconv"],
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
-                     "traffic": None, "avg_launch_us": 1000.0 * kms[dom] / max(1, kcalls[dom]),
+                     "traffic": (TRAFFIC_RATIO[dom] * kbytes[dom] / max(1, kcalls[dom])) if dom in TRAFFIC_RATIO
+                     else None,
+                     "traffic_source": "ncu DRAM/algorithmic ratio of this kernel (profiles/) x algorithmic bytes",
+                     "avg_launch_us": 1000.0 * kms[dom] / max(1, kcalls[dom]),
                      "algorithmic_bytes_per_launch": kbytes[dom] / max(1, kcalls[dom])},
         "step_roofline": {"kernels": step_cls, "achieved": step_ach, "peak": peak, "unit": "GB/s",
                           "frac": (step_ach / peak) if step_ach else None},

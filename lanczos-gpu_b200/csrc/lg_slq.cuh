@@ -9,8 +9,8 @@
 // per warp); lane l of the group owns columns ch * LPR * VEC + l * VEC + v.
 // For 64 fp32 probes LPR = 16: a half-warp reads a 256-byte row with one
 // float4 per lane, and every gather instruction of the warp fetches two
-// neighbour rows.  The streaming kernels use the pair layout (LPR = 32,
-// 2 elements per lane).
+// neighbour rows.  The streaming kernels (recurrence, lambda, xi, norms) use
+// the same layout.
 //
 // Column reductions (dots and norms over the n rows, per probe column): the
 // row groups of a warp are combined by shuffles, the warps of a CTA in shared
@@ -74,20 +74,6 @@ __device__ __forceinline__ void stvec_t(T* p, const T (&v)[N], int valid) {
   *reinterpret_cast<typename VecT<T, N>::type*>(p) = x;
 }
 
-// Pair-layout helpers (2 elements per lane) of the streaming kernels.
-template <typename T>
-__device__ __forceinline__ void ld2m(const T* p, bool second, double& x, double& y) {
-  const auto v = *reinterpret_cast<const typename VecT<T, 2>::type*>(p);
-  x = (double)v.x;
-  y = second ? (double)v.y : 0.0;
-}
-template <typename T>
-__device__ __forceinline__ void st2(T* p, double x, double y) {
-  typename VecT<T, 2>::type v;
-  v.x = (T)x;
-  v.y = (T)y;
-  *reinterpret_cast<typename VecT<T, 2>::type*>(p) = v;
-}
 // Value as stored in a block of element type T.
 template <typename T>
 __device__ __forceinline__ double rnd(double x) {
