@@ -25,6 +25,12 @@ Kraemer backward for d/dtheta and d/dkappa.  One SLQ step = one log-det and
 its gradient through the public API (operator built once, probes resident,
 as in a training loop); the probe blocks (n x 64 fp32 = 256 MB) exceed L2.
 
+Two more objects time complete solves of the other eigsh configurations:
+"rmat" (configuration 4: R-MAT scale 24, k=32 LA ncv=96 tol=1e-8, fp32
+values; rows partitioned over the ranks at N > 1) and "sinv" (configuration
+2: shift-invert about 0 on the 128^3 Dirichlet grid, k=16 ncv=48 tol=1e-10,
+inner CG to 1e-12; one GPU, N = 1 only).
+
 --impl reference times the reference's algorithm on the host cores: the CPU
 oracle (C restatement of the reference IRLM, OpenMP over all cores) running
 the initial 60-step Lanczos factorisation of the same matrix per step, and the
@@ -426,6 +432,119 @@ def run_rmat(args, dev, world=1, rank=0):
     return out
 
 
+SINV_N, SINV_K, SINV_NCV, SINV_TOL, SINV_CG_TOL = 128, 16, 48, 1e-10, 1e-12
+SINV_WORKLOAD = (f"eigsh sigma=0 k={SINV_K} ncv={SINV_NCV} tol={SINV_TOL:g} (shift-invert, inner CG to "
+                 f"{SINV_CG_TOL:g}) on the 7-point Dirichlet Laplacian of a {SINV_N}^3 grid (n=2,097,152, "
+                 "nnz=14,581,760), fp64")
+
+
+def run_sinv(args, dev):
+    """Configuration 2 on one GPU: the shift-invert path (Lanczos on
+    (A - sigma I)^-1, every operator application one CG solve on the device),
+    matrix assembled on the GPU, complete solves timed with CUDA events."""
+    import torch
+
+    import gpu_eigsh
+    from gpu_eigsh import synthetic as syn
+
+    N = args.sinv_n
+    n, rp, col, val = syn.grid3d_dirichlet_device(N, device=dev)
+    nnz = int(col.numel())
+    plan = gpu_eigsh.EigshPlan(None, max_ncv=SINV_NCV, device_csr=(n, nnz, rp.data_ptr(), col.data_ptr(),
+                                                                    val.data_ptr()))
+    v0 = torch.from_numpy(np.random.default_rng(0).standard_normal(n)).to(dev)
+    Y = torch.empty((n, SINV_K), dtype=torch.float64, device=dev)
+
+    def solve(profile=False):
+        w, _ = plan.solve(k=SINV_K, sigma=0.0, ncv=SINV_NCV, tol=SINV_TOL, cg_tol=SINV_CG_TOL,
+                          v0_device=v0.data_ptr(), evecs_out=Y.data_ptr(), profile=profile)
+        return w, dict(plan.last_info)
+
+    solve()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("sinv_timed")
+    ev0.record()
+    w, info = solve(profile=True)
+    ev1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    peak, peak_kind = measured_peaks()
+    cg_ms, cg_b, cg_calls = info["kernel_ms"]["cg"], info["kernel_bytes"]["cg"], info["kernel_calls"]["cg"]
+    exact = syn.grid_eigenvalues(N, 3)[:400]
+    near = exact[np.abs(exact[None, :] - w[:, None]).argmin(1)]
+    out = {"workload": SINV_WORKLOAD if N == SINV_N else f"reduced: {N}^3 grid",
+           "metric": "time_to_converge_s", "value": ms / 1000.0, "unit": "s", "higher_is_better": False,
+           "n": n, "nnz": nnz, "lanczos_steps_per_solve": info["steps"], "restarts_per_solve": info["restarts"],
+           "cg_iterations_per_solve": info["cg_iters"],
+           "cg_iterations_per_operator_application": info["cg_iters"] / max(1, info["steps"]),
+           "nconv": info["nconv"], "max_rel_err_vs_analytic": float(np.max(np.abs(w - near) / near)),
+           "eigenvalues": [float(x) for x in w[:4]],
+           "kernel_ms_per_solve": dict(info["kernel_ms"]),
+           "roofline": {"bound": "hbm", "kernel": "cg (cg_k1 + cg_k2, one CG iteration)",
+                        "achieved": cg_b / (cg_ms / 1000.0) / 1e9 if cg_ms else None, "peak": peak, "unit": "GB/s",
+                        "frac": (cg_b / (cg_ms / 1000.0) / 1e9 / peak) if cg_ms else None, "peak_source": peak_kind,
+                        "avg_iteration_us": 1000.0 * cg_ms / max(1, cg_calls),
+                        "algorithmic_bytes_per_iteration": cg_b / max(1, cg_calls)},
+           "gpu_launches_per_solve": info["launches"], "parallelism": "1 GPU"}
+    plan.close()
+    return out
+
+
+def run_knn_partitioned(args, L, v0, dev, world, rank):
+    """Configuration 1 with its rows split over the ranks (strong scaling):
+    the matrix renumbered by BFS level (gpu_eigsh.ordering) so that the row
+    blocks touch only their neighbours, then the halo exchange carries the
+    boundary rows before each sparse product.  Complete solves timed with CUDA
+    events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from gpu_eigsh.distributed import Communicator, PartitionedEigsh, partition_rows
+    from gpu_eigsh.ordering import bfs_order, permute_symmetric
+
+    n = L.shape[0]
+    rp = torch.from_numpy(L.indptr.astype(np.int32)).to(dev)
+    ci = torch.from_numpy(L.indices.astype(np.int32)).to(dev)
+    va = torch.from_numpy(L.data.astype(np.float64)).to(dev)
+    perm = bfs_order(rp, ci)
+    rp, ci, va, _ = permute_symmetric(rp, ci, va, perm)
+    r0, r1 = partition_rows(n, world, rank)
+    a, b = int(rp[r0]), int(rp[r1])
+    lrp = (rp[r0:r1 + 1] - a).contiguous()
+    lci, lva = ci[a:b].contiguous(), va[a:b].contiguous()
+    v0l = torch.from_numpy(v0).to(dev)[perm][r0:r1].contiguous()
+    del rp, ci, va
+    comm = Communicator()
+    pe = PartitionedEigsh(comm, n, lrp, lci, lva, max_ncv=NCV)
+    kw = dict(which="LA", ncv=NCV, tol=TOL)
+    pe.solve(K_EIG, v0l, **kw)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, min(args.steps, 3))
+    ev0.record()
+    for _ in range(reps):
+        w, _ = pe.solve(K_EIG, v0l, **kw)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / reps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    info = dict(pe.last_info)
+    mode, recv_rows, send_rows = pe.exchange_info
+    pe.close()
+    comm.close()
+    return {"workload": WORKLOAD + "; rows renumbered by BFS level, then split in equal blocks",
+            "metric": "time_to_converge_s", "value": ms / 1000.0, "unit": "s", "higher_is_better": False,
+            "lanczos_steps_per_solve": info["steps"], "steps_per_sec": info["steps"] / (ms / 1000.0),
+            "exchange": mode, "halo_rows_received_rank0": recv_rows, "halo_rows_sent_rank0": send_rows,
+            "top_eigenvalues": [float(x) for x in w[-4:]], "parallelism": f"rows partitioned over {world} GPUs",
+            "scaling": "strong"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -488,6 +607,14 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps(out), flush=True)
         return 0
+    if args.only_sinv:
+        out = run_sinv(args, torch.device("cuda", local)) if rank == 0 else None
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return 0
     if args.only_slq:
         out = run_slq(args, torch.device("cuda", local), with_e2e=False, with_cpu=False, world=world, rank=rank)
         if world > 1:
@@ -505,8 +632,10 @@ def run_ours(args):
     v0d = torch.from_numpy(v0).to(dev)
     Y = torch.empty((n, K_EIG), dtype=torch.float64, device=dev)
     torch.cuda.synchronize()
-    plan = gpu_eigsh.EigshPlan(None, max_ncv=NCV, mixed=args.mixed,
+    t_plan = time.perf_counter()
+    plan = gpu_eigsh.EigshPlan(None, max_ncv=NCV, mixed=args.mixed, reorder=args.reorder,
                                device_csr=(n, L.nnz, rp.data_ptr(), ci.data_ptr(), va.data_ptr()))
+    plan_s = time.perf_counter() - t_plan
 
     def solve(profile=False):
         w, _ = plan.solve(k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0_device=v0d.data_ptr(), evecs_out=Y.data_ptr(),
@@ -560,10 +689,12 @@ def run_ours(args):
         "metric": "lanczos_steps_per_sec", "value": value, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": WORKLOAD + (" (fp32 values, fp64 accumulation)" if args.mixed else ""),
+        "config": {"workload": WORKLOAD + (" (fp32 values, fp64 accumulation)" if args.mixed else "")
+                   + ("; rows renumbered by BFS level inside the plan at creation (outside the timed solves)"
+                      if args.reorder else ""),
                    "n": n, "nnz": int(L.nnz), "edges": winfo["edges"], "parallelism": f"replicas{world}",
                    "l2": "inputs larger than L2 (basis 488 MB), no flush"},
-        "time_to_converge_s": ms / args.steps / 1000.0,
+        "time_to_converge_s": ms / args.steps / 1000.0, "plan_create_s": plan_s,
         "lanczos_steps_per_solve": infos[0]["steps"], "restarts_per_solve": infos[0]["restarts"],
         "nconv": infos[0]["nconv"],
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
@@ -601,6 +732,8 @@ def run_ours(args):
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(L, v0)
     plan.close()
+    if world > 1 and not args.no_partitioned:
+        line["partitioned"] = run_knn_partitioned(args, L, v0, dev, world, rank)
     del L
     if not args.no_slq:
         # with N > 1 every rank takes part in the sharded e2e steps (collectives)
@@ -609,6 +742,9 @@ def run_ours(args):
         line["gpu_launches"] += line["slq"]["gpu_launches_per_step"] * args.steps
     if not args.no_rmat:
         line["rmat"] = run_rmat(args, dev, world=world, rank=rank)
+    if not args.no_sinv and world == 1:
+        # the shift-invert path is single-GPU (every rank would repeat it)
+        line["sinv"] = run_sinv(args, dev)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -631,6 +767,13 @@ def main():
     ap.add_argument("--only-rmat", action="store_true", help="run the configuration-4 (R-MAT) eigsh leg alone")
     ap.add_argument("--no-rmat", action="store_true", help="skip the configuration-4 (R-MAT) eigsh leg")
     ap.add_argument("--rmat-scale", type=int, default=RMAT_SCALE, help="R-MAT scale (reduced cases for profiling)")
+    ap.add_argument("--reorder", action="store_true",
+                    help="renumber the rows by BFS level inside the plan (LG_PLAN_REORDER_BFS)")
+    ap.add_argument("--no-partitioned", action="store_true",
+                    help="at N > 1, skip the row-partitioned configuration-1 solve")
+    ap.add_argument("--only-sinv", action="store_true", help="run the configuration-2 (shift-invert) leg alone")
+    ap.add_argument("--no-sinv", action="store_true", help="skip the configuration-2 (shift-invert) leg")
+    ap.add_argument("--sinv-n", type=int, default=SINV_N, help="grid side of the shift-invert leg (reduced cases)")
     ap.add_argument("--slq-n", type=int, default=N_POINTS, help="SLQ graph size (reduced cases for profiling)")
     ap.add_argument("--slq-m", type=int, default=SLQ_M, help="SLQ Lanczos depth (reduced cases for profiling)")
     args = ap.parse_args()

@@ -98,6 +98,20 @@ int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* 
                          const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
                          int mixed);
 
+/* lg_eigsh_plan_create with flags.  LG_PLAN_REORDER_BFS renumbers the rows
+ * inside the plan by breadth-first level from a pseudo-peripheral vertex
+ * (the matrix pattern must be symmetric), so that the gathers of the sparse
+ * product stay in L2 for graphs whose input numbering has no locality (the
+ * kNN graph of randomly ordered points).  The caller sees its own numbering
+ * everywhere: v0, the eigenvectors and lg_eigsh_plan_matvec are mapped
+ * through the permutation; the eigenvalues are those of the same matrix.
+ * Creation costs two BFS sweeps (a few tens of ms at n = 1e6), so the flag
+ * pays off for plans that solve more than once. */
+#define LG_PLAN_REORDER_BFS 1
+int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr,
+                            const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
+                            int mixed, int flags);
+
 /* Solve.  evals: host, k doubles, ascending.  evecs: n x k per opts layout.
  * io_on_device = 1: v0 and evecs are device pointers.  v0 may be NULL. */
 int lg_eigsh_plan_run(lg_eigsh_plan* plan, const lg_eigsh_opts* opts, const double* v0, double* evals,
@@ -114,9 +128,12 @@ int lg_eigsh(int n, long long nnz, const int* row_ptr, const int* col_idx, const
  *
  * Rank r owns the rows [r*nb, min((r+1)*nb, n)) of the n x n matrix, with
  * nb = lg_partition_block(n, nranks); its CSR holds those rows with global
- * column indices.  Every step all-gathers the residual (NCCL, in place) for
- * the sparse product and all-reduces one row of partial sums per
- * Gram-Schmidt pass; the restart logic runs replicated on every rank.  With a
+ * column indices.  Before every sparse product the residual rows that other
+ * ranks read reach them (NCCL): by a halo exchange (grouped point-to-point
+ * sends of exactly the rows the other ranks' columns name) when the halos
+ * are small, else by an in-place all-gather of the whole residual; one row
+ * of partial sums is all-reduced per Gram-Schmidt pass; the restart logic
+ * runs replicated on every rank.  With a
  * partitioned plan, lg_eigsh_plan_run takes this rank's slice of v0 and
  * returns this rank's rows of the eigenvectors (n_local x k); the
  * eigenvalues are returned on every rank.  Shift-invert, factorize and
@@ -132,6 +149,19 @@ int lg_partition_block(int n, int nranks);
 int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global, int n_local, long long nnz,
                               const int* row_ptr, const int* col_idx, const double* vals, int device_ptrs,
                               int max_ncv, int mixed);
+
+/* Residual exchange of a partitioned plan.  lg_eigsh_plan_create_dist builds
+ * the halo lists (a collective call) and picks LG_EXCHANGE_HALO when every
+ * rank receives at most half of the rows an all-gather would bring, else
+ * LG_EXCHANGE_ALLGATHER.  set_exchange overrides the choice (LG_EXCHANGE_AUTO
+ * restores it); every rank must pass the same mode before its next run.
+ * exchange_info reports the mode in use and this rank's halo sizes in rows
+ * (received from / sent to the other ranks).  Single-GPU plans: LG_ERR_INVALID. */
+#define LG_EXCHANGE_AUTO 0
+#define LG_EXCHANGE_ALLGATHER 1
+#define LG_EXCHANGE_HALO 2
+int lg_eigsh_plan_set_exchange(lg_eigsh_plan* plan, int mode);
+int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long* recv_rows, long long* send_rows);
 
 /* m Lanczos steps (CGS2) from the host vector v0 without restarts: alpha
  * (m doubles) and beta (m+1 doubles; beta[0] = 0, beta[m] = final residual

@@ -134,13 +134,13 @@ basis_kernel(BasisArgs a) {
       for (int i = t; i < kTR * kq; i += kBsThreads) {
         const int rr = i / kq, k = i % kq;
         const long long row = row0 + rr;
-        if (row < n) a.Y[row * kq + k] = Vs[rr * g.sv + k];
+        if (row < n) a.Y[(a.ymap ? (long long)a.ymap[row] : row) * kq + k] = Vs[rr * g.sv + k];
       }
     } else {
       for (int i = t; i < kTR * kq; i += kBsThreads) {
         const int k = i / kTR, rr = i % kTR;
         const long long row = row0 + rr;
-        if (row < n) a.Y[row + (long long)k * a.ldy] = Vs[rr * g.sv + k];
+        if (row < n) a.Y[(a.ymap ? (long long)a.ymap[row] : row) + (long long)k * a.ldy] = Vs[rr * g.sv + k];
       }
     }
   }

@@ -36,11 +36,20 @@ int lg_eigsh_opts_default(lg_eigsh_opts* o) {
 
 int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr, const int* col_idx,
                          const double* vals, int device_ptrs, int max_ncv, int mixed) {
+  return lg_eigsh_plan_create_ex(plan, n, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv, mixed, 0);
+}
+
+int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr, const int* col_idx,
+                            const double* vals, int device_ptrs, int max_ncv, int mixed, int flags) {
   if (!plan) return LG_ERR_INVALID;
   *plan = nullptr;
+  if (flags & ~LG_PLAN_REORDER_BFS) {
+    lg::g_last_error = "unknown plan flags";
+    return LG_ERR_INVALID;
+  }
   lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();
   if (!p) return LG_ERR_NOMEM;
-  const int rc = p->solver.create(n, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv, mixed);
+  const int rc = p->solver.create(n, nnz, row_ptr, col_idx, vals, device_ptrs, max_ncv, mixed, flags);
   if (rc != LG_OK) {
     delete p;
     return rc;
@@ -70,6 +79,16 @@ int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global,
   }
   *plan = p;
   return LG_OK;
+}
+
+int lg_eigsh_plan_set_exchange(lg_eigsh_plan* plan, int mode) {
+  if (!plan) return LG_ERR_INVALID;
+  return plan->solver.set_exchange(mode);
+}
+
+int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long* recv_rows, long long* send_rows) {
+  if (!plan) return LG_ERR_INVALID;
+  return plan->solver.exchange_info(mode, recv_rows, send_rows);
 }
 
 int lg_eigsh_plan_run(lg_eigsh_plan* plan, const lg_eigsh_opts* opts, const double* v0, double* evals,

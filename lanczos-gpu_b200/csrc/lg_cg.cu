@@ -100,30 +100,53 @@ cg_k1_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__ col,
     }
     beta = rr / rrp;
   }
+  // Each lane group works on two rows at once so that the dependent load
+  // chains (row_ptr -> col -> r, p gathers) of the two rows overlap.
   const int lane = threadIdx.x & (L - 1);
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
   const int rows_per_warp = 32 / L;
   double local = 0.0;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp < n;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp * 2 < n;
        w += warps_total) {
-    const int row = w * rows_per_warp + ((threadIdx.x & 31) / L);
-    const bool valid = row < n;
-    double acc = 0.0;
-    if (valid) {
-      const int b = __ldg(rowptr + row), e = __ldg(rowptr + row + 1);
-      for (int k = b + lane; k < e; k += L) {
-        const int c = __ldg(col + k);
-        acc += (double)__ldg(val + k) * (r[c] + beta * p_old[c]);
+    const int rowA = w * rows_per_warp * 2 + ((threadIdx.x & 31) / L);
+    const int rowB = rowA + rows_per_warp;
+    const bool okA = rowA < n, okB = rowB < n;
+    int kA = 0, eA = 0, kB = 0, eB = 0;
+    if (okA) { kA = __ldg(rowptr + rowA) + lane; eA = __ldg(rowptr + rowA + 1); }
+    if (okB) { kB = __ldg(rowptr + rowB) + lane; eB = __ldg(rowptr + rowB + 1); }
+    double accA = 0.0, accB = 0.0;
+    while (kA < eA || kB < eB) {
+      if (kA < eA) {
+        const int c = __ldg(col + kA);
+        accA += (double)__ldg(val + kA) * (r[c] + beta * p_old[c]);
       }
+      if (kB < eB) {
+        const int c = __ldg(col + kB);
+        accB += (double)__ldg(val + kB) * (r[c] + beta * p_old[c]);
+      }
+      kA += L;
+      kB += L;
     }
 #pragma unroll
-    for (int o = L / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (valid && lane == 0) {
-      const double pn = r[row] + beta * p_old[row];
-      const double ap = acc - sigma * pn;
-      p_new[row] = pn;
-      Ap[row] = ap;
-      local += pn * ap;
+    for (int o = L / 2; o > 0; o >>= 1) {
+      accA += __shfl_xor_sync(0xffffffffu, accA, o);
+      accB += __shfl_xor_sync(0xffffffffu, accB, o);
+    }
+    if (lane == 0) {
+      if (okA) {
+        const double pn = r[rowA] + beta * p_old[rowA];
+        const double ap = accA - sigma * pn;
+        p_new[rowA] = pn;
+        Ap[rowA] = ap;
+        local += pn * ap;
+      }
+      if (okB) {
+        const double pn = r[rowB] + beta * p_old[rowB];
+        const double ap = accB - sigma * pn;
+        p_new[rowB] = pn;
+        Ap[rowB] = ap;
+        local += pn * ap;
+      }
     }
   }
   local = block_sum(local, scr);
@@ -189,7 +212,7 @@ int Solver::prepare_shift_invert() {
   if (!cg_ws) {
     LG_TRY(cudaMalloc(&cg_ws, sizeof(double) * (size_t)ld * 5));
     LG_TRY(cudaMemsetAsync(cg_ws, 0, sizeof(double) * (size_t)ld * 5, stream));
-    cg_grid = num_sm * 4;
+    cg_grid = num_sm * 8;   // 8 CTAs of 256 threads: every SM at full thread occupancy
     LG_TRY(cudaMalloc(&cg_part, sizeof(double) * (size_t)cg_grid));
     LG_TRY(cudaMalloc(&cg_scal, sizeof(double) * CG_SCAL_WORDS));
     LG_TRY(cudaMalloc(&cg_counter, sizeof(unsigned)));

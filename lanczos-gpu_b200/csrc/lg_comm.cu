@@ -5,7 +5,9 @@
 // it — torch.distributed does — the loaded copy is reused) and resolves the
 // handful of entry points it needs.  Collectives run on the solver's stream:
 //   all-reduce (sum) of one partial-sum row per Gram-Schmidt pass, and
-//   in-place all-gather of the residual before each sparse product.
+//   before each sparse product either the in-place all-gather of the residual
+//   or the halo exchange (grouped point-to-point sends and receives of the
+//   residual rows that other ranks' sparse products read).
 // Every rank issues the same collectives in the same order; the solver's
 // control decisions derive only from all-reduced values, so they agree.
 #include "lg_comm.h"
@@ -31,6 +33,10 @@ struct NcclApi {
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -53,8 +59,13 @@ bool load_nccl() {
   a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
   a.AllReduce = reinterpret_cast<decltype(a.AllReduce)>(dlsym(h, "ncclAllReduce"));
   a.AllGather = reinterpret_cast<decltype(a.AllGather)>(dlsym(h, "ncclAllGather"));
+  a.Send = reinterpret_cast<decltype(a.Send)>(dlsym(h, "ncclSend"));
+  a.Recv = reinterpret_cast<decltype(a.Recv)>(dlsym(h, "ncclRecv"));
+  a.GroupStart = reinterpret_cast<decltype(a.GroupStart)>(dlsym(h, "ncclGroupStart"));
+  a.GroupEnd = reinterpret_cast<decltype(a.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
   a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
-  if (!a.GetUniqueId || !a.CommInitRank || !a.CommDestroy || !a.AllReduce || !a.AllGather || !a.GetErrorString) {
+  if (!a.GetUniqueId || !a.CommInitRank || !a.CommDestroy || !a.AllReduce || !a.AllGather || !a.Send || !a.Recv ||
+      !a.GroupStart || !a.GroupEnd || !a.GetErrorString) {
     g_last_error = "libnccl.so.2 lacks a required entry point";
     dlclose(h);
     return false;
@@ -89,6 +100,32 @@ int comm_allgather_inplace(const lg_comm* c, double* full, size_t count_per_rank
   ncclResult_t r = g_nccl.AllGather(full + (size_t)ci->rank * count_per_rank, full, count_per_rank, ncclDouble,
                                     ci->comm, st);
   return r == ncclSuccess ? LG_OK : nccl_fail("ncclAllGather", r);
+}
+
+int comm_sendrecv(const lg_comm* c, int elem_bytes, const void* sendbuf, const long long* send_off,
+                  const long long* send_cnt, void* recvbuf, const long long* recv_off, const long long* recv_cnt,
+                  cudaStream_t st) {
+  const CommImpl* ci = reinterpret_cast<const CommImpl*>(c);
+  const ncclDataType_t t = elem_bytes == 8 ? ncclDouble : ncclInt32;
+  ncclResult_t r = g_nccl.GroupStart();
+  if (r != ncclSuccess) return nccl_fail("ncclGroupStart", r);
+  ncclResult_t first = ncclSuccess;
+  for (int p = 0; p < ci->nranks; ++p) {
+    if (p == ci->rank) continue;
+    if (send_cnt[p] > 0) {
+      r = g_nccl.Send(static_cast<const char*>(sendbuf) + (size_t)send_off[p] * elem_bytes, (size_t)send_cnt[p], t, p,
+                      ci->comm, st);
+      if (r != ncclSuccess && first == ncclSuccess) first = r;
+    }
+    if (recv_cnt[p] > 0) {
+      r = g_nccl.Recv(static_cast<char*>(recvbuf) + (size_t)recv_off[p] * elem_bytes, (size_t)recv_cnt[p], t, p,
+                      ci->comm, st);
+      if (r != ncclSuccess && first == ncclSuccess) first = r;
+    }
+  }
+  r = g_nccl.GroupEnd();   // always closes the group, also after a failed call inside it
+  if (first != ncclSuccess) return nccl_fail("ncclSend/ncclRecv", first);
+  return r == ncclSuccess ? LG_OK : nccl_fail("ncclGroupEnd", r);
 }
 
 }  // namespace lg

@@ -71,6 +71,16 @@ void Solver::release() {
   }
   if (red) cudaFree(red);
   red = nullptr;
+  for (void* p : {(void*)d_send_idx, (void*)d_recv_pos, (void*)d_send_buf, (void*)d_recv_buf, (void*)d_perm})
+    if (p) cudaFree(p);
+  d_perm = nullptr;
+  d_send_idx = d_recv_pos = nullptr;
+  d_send_buf = d_recv_buf = nullptr;
+  send_off.clear();
+  send_cnt.clear();
+  recv_off.clear();
+  recv_cnt.clear();
+  halo_send = halo_recv = 0;
   void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, d_long, d_chunk_sum, d_classes, V, W, R, partA, partB, partC, alpha, beta, scal,
                   ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
@@ -99,13 +109,13 @@ void Solver::release() {
 }
 
 int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, const double* vals, int device_ptrs,
-                   int max_ncv_, int mixed_) {
+                   int max_ncv_, int mixed_, int flags) {
   comm = nullptr;
   n_global = n_;
   row0 = 0;
   nranks = 1;
   rank = 0;
-  return create_impl(n_, n_, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_);
+  return create_impl(n_, n_, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_, flags);
 }
 
 int Solver::create_dist(lg_comm* c, int n_glob, int n_local, long long nnz_, const int* rowptr, const int* col,
@@ -128,11 +138,11 @@ int Solver::create_dist(lg_comm* c, int n_glob, int n_local, long long nnz_, con
     g_last_error = buf;
     return LG_ERR_INVALID;
   }
-  return create_impl(n_local, n_glob, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_);
+  return create_impl(n_local, n_glob, nnz_, rowptr, col, vals, device_ptrs, max_ncv_, mixed_, 0);
 }
 
 int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, const int* col, const double* vals,
-                        int device_ptrs, int max_ncv_, int mixed_) {
+                        int device_ptrs, int max_ncv_, int mixed_, int flags) {
   if (n_ < 1 || nnz_ < 0 || !rowptr || (nnz_ > 0 && (!col || !vals))) {
     g_last_error = "invalid CSR arguments";
     return LG_ERR_INVALID;
@@ -187,11 +197,6 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
     LG_TRY(cudaMemcpyAsync(d_col, col, sizeof(int) * (size_t)nnz, kind, stream));
     LG_TRY(cudaMemcpyAsync(d_val64, vals, sizeof(double) * (size_t)nnz, kind, stream));
   }
-  if (mixed) {
-    LG_TRY(cudaMalloc(&d_val32, sizeof(float) * (size_t)std::max<long long>(nnz, 1)));
-    cast_f64_f32_kernel<<<num_sm * 4, 256, 0, stream>>>(d_val64, d_val32, nnz);
-    LG_TRY(cudaGetLastError());
-  }
 
   LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
   LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
@@ -229,21 +234,282 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   A.rowptr = d_rowptr;
   A.col = d_col;
   A.val64 = d_val64;
-  A.val32 = mixed ? d_val32 : nullptr;
+  A.val32 = nullptr;   // set once the fp32 copy exists (after any reordering)
   A.lanes = pick_lanes(nnz / (double)n);
 
+  std::vector<int> hrp((size_t)n + 1);
   if (device_ptrs) {
-    std::vector<int> hrp((size_t)n + 1);
     LG_TRY(cudaMemcpyAsync(hrp.data(), rowptr, sizeof(int) * hrp.size(), cudaMemcpyDeviceToHost, stream));
     LG_TRY(cudaStreamSynchronize(stream));
+  } else {
+    std::copy(rowptr, rowptr + n + 1, hrp.begin());
+  }
+  if ((flags & LG_PLAN_REORDER_BFS) && !comm) {
+    int rc = reorder_bfs(hrp);
+    if (rc != LG_OK) return rc;
+  }
+  if (mixed) {
+    LG_TRY(cudaMalloc(&d_val32, sizeof(float) * (size_t)std::max<long long>(nnz, 1)));
+    cast_f64_f32_kernel<<<num_sm * 4, 256, 0, stream>>>(d_val64, d_val32, nnz);
+    LG_TRY(cudaGetLastError());
+    A.val32 = d_val32;
+  }
+  {
     int rc = build_long_rows(hrp.data());
     if (rc != LG_OK) return rc;
-  } else {
-    int rc = build_long_rows(rowptr);
+  }
+  if (comm) {
+    int rc = setup_halo();
     if (rc != LG_OK) return rc;
   }
 
   LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+// Row i of the renumbered CSR is row perm[i] of the caller's, its column
+// indices mapped through pos = perm^-1 (one warp per row, entries in the
+// caller's order).
+__global__ void permute_csr_kernel(int n, const int* __restrict__ perm, const int* __restrict__ pos,
+                                   const int* __restrict__ rp_old, const int* __restrict__ col_old,
+                                   const double* __restrict__ val_old, const int* __restrict__ rp_new,
+                                   int* __restrict__ col_new, double* __restrict__ val_new) {
+  const int lane = threadIdx.x & 31;
+  for (long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; w < n;
+       w += ((long long)gridDim.x * blockDim.x) >> 5) {
+    const int i = (int)w;
+    const int src = rp_old[perm[i]], len = rp_old[perm[i] + 1] - src, dst = rp_new[i];
+    for (int k = lane; k < len; k += 32) {
+      col_new[dst + k] = pos[col_old[src + k]];
+      val_new[dst + k] = val_old[src + k];
+    }
+  }
+}
+
+// out[i] = in[perm[i]]  (caller's order -> plan order)
+__global__ void gather_perm_kernel(double* __restrict__ out, const double* __restrict__ in,
+                                   const int* __restrict__ perm, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = in[perm[i]];
+}
+
+// out[perm[i]] = in[i]  (plan order -> caller's order)
+__global__ void scatter_perm_kernel(double* __restrict__ out, const double* __restrict__ in,
+                                    const int* __restrict__ perm, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[perm[i]] = in[i];
+}
+
+// Renumbers the rows by breadth-first level from a pseudo-peripheral vertex
+// (two sweeps of lg_graph_bfs_levels; ties by index, unreachable vertices
+// last) so that neighbouring rows get nearby numbers and the gathers of the
+// sparse product hit L2.  The plan keeps perm (plan row -> caller row): v0 is
+// gathered through it and the Ritz vectors are written through it, so the
+// caller sees its own numbering.  hrp (host row pointer) becomes the new one.
+int Solver::reorder_bfs(std::vector<int>& hrp) {
+  int* d_level = nullptr;
+  int* d_work = nullptr;
+  LG_TRY(cudaMalloc(&d_level, sizeof(int) * (size_t)n));
+  cudaError_t e = cudaMalloc(&d_work, sizeof(int) * (2 * (size_t)n + 2));
+  if (e != cudaSuccess) {
+    cudaFree(d_level);
+    LG_TRY(e);
+  }
+  std::vector<int> lev((size_t)n);
+  int start = 0, rounds = 0, rc = LG_OK;
+  for (int sweep = 0; sweep < 2 && rc == LG_OK; ++sweep) {
+    rc = lg_graph_bfs_levels(n, d_rowptr, d_col, start, d_level, d_work, &rounds, stream);
+    if (rc != LG_OK) break;
+    e = cudaMemcpyAsync(lev.data(), d_level, sizeof(int) * (size_t)n, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      set_error("CUDA error %s at lg_irlm.cu:%d", cudaGetErrorString(e), __LINE__);
+      rc = LG_ERR_CUDA;
+      break;
+    }
+    if (sweep == 0) start = (int)(std::max_element(lev.begin(), lev.end()) - lev.begin());
+  }
+  cudaFree(d_level);
+  cudaFree(d_work);
+  if (rc != LG_OK) return rc;
+  // counting sort by level, stable in the vertex index
+  const int maxl = std::max(0, *std::max_element(lev.begin(), lev.end()));
+  std::vector<long long> bucket((size_t)maxl + 3, 0);
+  for (int v = 0; v < n; ++v) ++bucket[(size_t)(lev[v] < 0 ? maxl + 1 : lev[v]) + 1];
+  for (size_t b = 1; b < bucket.size(); ++b) bucket[b] += bucket[b - 1];
+  std::vector<int> perm((size_t)n), pos((size_t)n), nrp((size_t)n + 1);
+  for (int v = 0; v < n; ++v) perm[(size_t)bucket[(size_t)(lev[v] < 0 ? maxl + 1 : lev[v])]++] = v;
+  for (int i = 0; i < n; ++i) pos[(size_t)perm[i]] = i;
+  nrp[0] = 0;
+  for (int i = 0; i < n; ++i) nrp[(size_t)i + 1] = nrp[i] + (hrp[(size_t)perm[i] + 1] - hrp[perm[i]]);
+
+  int *d_pos = nullptr, *rp2 = nullptr, *col2 = nullptr;
+  double* val2 = nullptr;
+  LG_TRY(cudaMalloc(&d_perm, sizeof(int) * (size_t)n));
+  LG_TRY(cudaMalloc(&d_pos, sizeof(int) * (size_t)n));
+  e = cudaMalloc(&rp2, sizeof(int) * ((size_t)n + 1));
+  if (e == cudaSuccess) e = cudaMalloc(&col2, sizeof(int) * (size_t)std::max<long long>(nnz, 1));
+  if (e == cudaSuccess) e = cudaMalloc(&val2, sizeof(double) * (size_t)std::max<long long>(nnz, 1));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_perm, perm.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_pos, pos.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(rp2, nrp.data(), sizeof(int) * ((size_t)n + 1), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess && nnz > 0) {
+    permute_csr_kernel<<<num_sm * 8, 256, 0, stream>>>(n, d_perm, d_pos, d_rowptr, d_col, d_val64, rp2, col2, val2);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);   // the host vectors go out of scope
+  cudaFree(d_pos);
+  if (e != cudaSuccess) {
+    cudaFree(rp2);
+    cudaFree(col2);
+    cudaFree(val2);
+    LG_TRY(e);
+  }
+  cudaFree(d_rowptr);
+  cudaFree(d_col);
+  cudaFree(d_val64);
+  d_rowptr = rp2;
+  d_col = col2;
+  d_val64 = val2;
+  A.rowptr = d_rowptr;
+  A.col = d_col;
+  A.val64 = d_val64;
+  hrp.swap(nrp);
+  return LG_OK;
+}
+
+// Marks every column outside this rank's rows [lo, hi) in a bitmap over the
+// global index range.
+__global__ void mark_remote_kernel(const int* __restrict__ col, long long nnz, int lo, int hi, int ncols,
+                                   unsigned* bits) {
+  for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < nnz;
+       k += (long long)gridDim.x * blockDim.x) {
+    const int c = col[k];
+    if ((c >= lo && c < hi) || c < 0 || c >= ncols) continue;
+    const unsigned m = 1u << (c & 31);
+    if (!(__ldcg(bits + (c >> 5)) & m)) atomicOr(bits + (c >> 5), m);
+  }
+}
+
+__global__ void halo_pack_kernel(const double* __restrict__ full, const int* __restrict__ idx, long long cnt,
+                                 double* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < cnt; i += (long long)gridDim.x * blockDim.x)
+    out[i] = full[idx[i]];
+}
+
+__global__ void halo_unpack_kernel(const double* __restrict__ in, const int* __restrict__ pos, long long cnt,
+                                   double* __restrict__ full) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < cnt; i += (long long)gridDim.x * blockDim.x)
+    full[pos[i]] = in[i];
+}
+
+// Halo lists of a partitioned plan (collective: every rank calls it once, at
+// creation).  The columns of this rank's rows that other ranks own, grouped by
+// owner in ascending order, are the rows it receives; one all-reduce of the
+// ranks x ranks count matrix tells every rank what it sends to whom, and one
+// grouped exchange hands each owner the positions it must pack.  Halo mode is
+// chosen (identically on every rank, from the all-reduced counts) when every
+// rank receives at most half of the rows an all-gather would bring.
+int Solver::setup_halo() {
+  const long long total = (long long)ld * nranks;
+  const size_t words = (size_t)((total + 31) / 32);
+  unsigned* d_bits = nullptr;
+  LG_TRY(cudaMalloc(&d_bits, sizeof(unsigned) * words));
+  cudaError_t e = cudaMemsetAsync(d_bits, 0, sizeof(unsigned) * words, stream);
+  if (e == cudaSuccess && nnz > 0) {
+    mark_remote_kernel<<<num_sm * 4, 256, 0, stream>>>(d_col, nnz, row0, row0 + n, n_global, d_bits);
+    e = cudaGetLastError();
+  }
+  std::vector<unsigned> bits(words);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(bits.data(), d_bits, sizeof(unsigned) * words, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  cudaFree(d_bits);
+  LG_TRY(e);
+
+  std::vector<int> pos;
+  recv_off.assign(nranks, 0);
+  recv_cnt.assign(nranks, 0);
+  send_off.assign(nranks, 0);
+  send_cnt.assign(nranks, 0);
+  for (int o = 0; o < nranks; ++o) {
+    recv_off[o] = (long long)pos.size();
+    if (o == rank) continue;
+    const long long lo = (long long)o * ld, hi = std::min<long long>((long long)(o + 1) * ld, n_global);
+    for (long long c = lo; c < hi; ++c) {
+      const unsigned w = bits[(size_t)(c >> 5)];
+      if (w == 0u) {   // skip the rest of an empty word (block starts are multiples of 32)
+        c |= 31;
+        continue;
+      }
+      if ((w >> (c & 31)) & 1u) pos.push_back((int)c);
+    }
+    recv_cnt[o] = (long long)pos.size() - recv_off[o];
+  }
+  halo_recv = (long long)pos.size();
+
+  // count matrix: row r = the rows rank r receives from each rank
+  const size_t nn = (size_t)nranks * nranks;
+  std::vector<double> cnt(nn, 0.0);
+  for (int o = 0; o < nranks; ++o) cnt[(size_t)rank * nranks + o] = (double)recv_cnt[o];
+  double* d_cnt = nullptr;
+  LG_TRY(cudaMalloc(&d_cnt, sizeof(double) * nn));
+  e = cudaMemcpyAsync(d_cnt, cnt.data(), sizeof(double) * nn, cudaMemcpyHostToDevice, stream);
+  int rc = LG_OK;
+  if (e == cudaSuccess) rc = comm_allreduce_sum(comm, d_cnt, nn, stream);
+  if (e == cudaSuccess && rc == LG_OK)
+    e = cudaMemcpyAsync(cnt.data(), d_cnt, sizeof(double) * nn, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess && rc == LG_OK) e = cudaStreamSynchronize(stream);
+  cudaFree(d_cnt);
+  if (rc != LG_OK) return rc;
+  LG_TRY(e);
+  long long off = 0;
+  bool small = true;
+  for (int p = 0; p < nranks; ++p) {
+    send_off[p] = off;
+    send_cnt[p] = p == rank ? 0 : (long long)cnt[(size_t)p * nranks + rank];
+    off += send_cnt[p];
+    double recv_p = 0.0;
+    for (int o = 0; o < nranks; ++o) recv_p += cnt[(size_t)p * nranks + o];
+    if (2.0 * recv_p > (double)(nranks - 1) * (double)ld) small = false;
+  }
+  halo_send = off;
+  exchange_auto = small ? LG_EXCHANGE_HALO : LG_EXCHANGE_ALLGATHER;
+  exchange = exchange_auto;
+
+  LG_TRY(cudaMalloc(&d_recv_pos, sizeof(int) * (size_t)std::max<long long>(halo_recv, 1)));
+  LG_TRY(cudaMalloc(&d_send_idx, sizeof(int) * (size_t)std::max<long long>(halo_send, 1)));
+  LG_TRY(cudaMalloc(&d_recv_buf, sizeof(double) * (size_t)std::max<long long>(halo_recv, 1)));
+  LG_TRY(cudaMalloc(&d_send_buf, sizeof(double) * (size_t)std::max<long long>(halo_send, 1)));
+  if (halo_recv > 0)
+    LG_TRY(cudaMemcpyAsync(d_recv_pos, pos.data(), sizeof(int) * (size_t)halo_recv, cudaMemcpyHostToDevice, stream));
+  // my receive positions go to their owners, which keep them as send lists
+  rc = comm_sendrecv(comm, 4, d_recv_pos, recv_off.data(), recv_cnt.data(), d_send_idx, send_off.data(),
+                     send_cnt.data(), stream);
+  if (rc != LG_OK) return rc;
+  LG_TRY(cudaStreamSynchronize(stream));   // pos goes out of scope
+  return LG_OK;
+}
+
+int Solver::set_exchange(int mode) {
+  if (!comm) {
+    g_last_error = "set_exchange: not a partitioned plan";
+    return LG_ERR_INVALID;
+  }
+  if (mode == LG_EXCHANGE_AUTO) exchange = exchange_auto;
+  else if (mode == LG_EXCHANGE_ALLGATHER || mode == LG_EXCHANGE_HALO) exchange = mode;
+  else {
+    g_last_error = "set_exchange: mode must be LG_EXCHANGE_AUTO, _ALLGATHER or _HALO";
+    return LG_ERR_INVALID;
+  }
+  return LG_OK;
+}
+
+int Solver::exchange_info(int* mode, long long* recv_rows, long long* send_rows) const {
+  if (!comm) {
+    g_last_error = "exchange_info: not a partitioned plan";
+    return LG_ERR_INVALID;
+  }
+  if (mode) *mode = exchange;
+  if (recv_rows) *recv_rows = halo_recv;
+  if (send_rows) *send_rows = halo_send;
   return LG_OK;
 }
 
@@ -345,9 +611,31 @@ int Solver::reduce_partials_all(double* part, int nrows, int slot, const double*
   return LG_OK;
 }
 
-// Every rank's residual block into Rfull (in place) before a sparse product.
+// Before a sparse product: the other ranks' residual rows that this rank's
+// columns name into Rfull, by the halo exchange (pack the rows others read,
+// grouped sends and receives, unpack at their global positions) or by an
+// in-place all-gather of every block.
 int Solver::gather_residual() {
   if (!comm) return LG_OK;
+  if (exchange == LG_EXCHANGE_HALO) {
+    if (halo_send > 0) {
+      const int g = (int)std::min<long long>((long long)num_sm * 4, (halo_send + 255) / 256);
+      halo_pack_kernel<<<g, 256, 0, stream>>>(Rfull, d_send_idx, halo_send, d_send_buf);
+      LG_TRY(cudaGetLastError());
+      ++launches;
+    }
+    int rc = comm_sendrecv(comm, 8, d_send_buf, send_off.data(), send_cnt.data(), d_recv_buf, recv_off.data(),
+                           recv_cnt.data(), stream);
+    if (rc != LG_OK) return rc;
+    ++launches;
+    if (halo_recv > 0) {
+      const int g = (int)std::min<long long>((long long)num_sm * 4, (halo_recv + 255) / 256);
+      halo_unpack_kernel<<<g, 256, 0, stream>>>(d_recv_buf, d_recv_pos, halo_recv, Rfull);
+      LG_TRY(cudaGetLastError());
+      ++launches;
+    }
+    return LG_OK;
+  }
   ++launches;
   return comm_allgather_inplace(comm, Rfull, (size_t)ld, stream);
 }
@@ -519,8 +807,15 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
   // Starting vector into R.
   if (v0) {
     LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
-    LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n,
-                           io_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream));
+    const cudaMemcpyKind kind = io_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    if (d_perm) {   // caller's numbering -> the plan's
+      LG_TRY(cudaMemcpyAsync(W, v0, sizeof(double) * (size_t)n, kind, stream));
+      gather_perm_kernel<<<num_sm * 4, 256, 0, stream>>>(R, W, d_perm, n);
+      LG_TRY(cudaGetLastError());
+      ++launches;
+    } else {
+      LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, kind, stream));
+    }
   } else {
     LG_TRY(fill_random(stream, R, n, ld, o.seed, row0));
     ++launches;
@@ -693,6 +988,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ba.Y = Y;
     ba.ldy = n;
     ba.rowmajor = o.evecs_rowmajor;
+    ba.ymap = d_perm;   // rows back in the caller's numbering
     ba.state = state;
     const BasisPlan bp = basis_plan(n, m, ksel, grid_basis);
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + ksel), 1, [&] { return basis_update(bp, ba, stream); }));
@@ -765,7 +1061,13 @@ int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_o
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
   LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
-  LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
+  if (d_perm) {
+    LG_TRY(cudaMemcpyAsync(W, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
+    gather_perm_kernel<<<num_sm * 4, 256, 0, stream>>>(R, W, d_perm, n);
+    LG_TRY(cudaGetLastError());
+  } else {
+    LG_TRY(cudaMemcpyAsync(R, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));
+  }
   LG_TRY(norm_partials(stream, grid_gs, R, ld, partC));
   nrowsC = grid_gs;
   inC = partC;
@@ -792,7 +1094,15 @@ int Solver::matvec(const double* x, double* y) {
     g_last_error = "matvec is not available with a row-partitioned plan";
     return LG_ERR_INVALID;
   }
-  LG_TRY(spmv_plain(A, stream, grid_spmv, x, y, 0.0));
+  if (d_perm) {   // y = A x in the caller's numbering: gather x, product, scatter y
+    gather_perm_kernel<<<num_sm * 4, 256, 0, stream>>>(R, x, d_perm, n);
+    LG_TRY(cudaGetLastError());
+    LG_TRY(spmv_plain(A, stream, grid_spmv, R, W, 0.0));
+    scatter_perm_kernel<<<num_sm * 4, 256, 0, stream>>>(y, W, d_perm, n);
+    LG_TRY(cudaGetLastError());
+  } else {
+    LG_TRY(spmv_plain(A, stream, grid_spmv, x, y, 0.0));
+  }
   LG_TRY(cudaStreamSynchronize(stream));
   return LG_OK;
 }

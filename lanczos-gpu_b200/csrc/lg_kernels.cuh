@@ -126,6 +126,7 @@ struct BasisArgs {
   double* Y = nullptr;
   long long ldy = 0;
   int rowmajor = 0;
+  const int* ymap = nullptr;   // ritz mode: row r of out goes to row ymap[r] of Y (null: r)
   int* state = nullptr;
 };
 struct BasisPlan {

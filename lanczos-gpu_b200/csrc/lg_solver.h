@@ -17,7 +17,7 @@ class Solver {
  public:
   ~Solver();
   int create(int n, long long nnz, const int* rowptr, const int* col, const double* vals, int device_ptrs,
-             int max_ncv, int mixed);
+             int max_ncv, int mixed, int flags);
   // Row-partitioned solver: this rank's n_local rows of an n_global x n_global matrix.
   int create_dist(lg_comm* comm, int n_global, int n_local, long long nnz, const int* rowptr, const int* col,
                   const double* vals, int device_ptrs, int max_ncv, int mixed);
@@ -25,16 +25,22 @@ class Solver {
           lg_eigsh_info* info);
   int matvec(const double* x, double* y);
   int factorize(const double* v0, int m, double* alpha_out, double* beta_out);
+  // Partitioned runs: how the residual reaches the other ranks before each
+  // sparse product (LG_EXCHANGE_*); the same mode on every rank.
+  int set_exchange(int mode);
+  int exchange_info(int* mode, long long* recv_rows, long long* send_rows) const;
 
  private:
   void release();
   int create_impl(int n_rows, int n_cols, long long nnz, const int* rowptr, const int* col, const double* vals,
-                  int device_ptrs, int max_ncv, int mixed);
+                  int device_ptrs, int max_ncv, int mixed, int flags);
+  int reorder_bfs(std::vector<int>& host_rowptr);
   // Partitioned runs: sum `nrows` partial-sum rows into row `slot` of `red`
   // and all-reduce it over the ranks; *in / *nin become that single row.
   // Single GPU: *in = part, *nin = nrows.
   int reduce_partials_all(double* part, int nrows, int slot, const double** in, int* nin);
   int gather_residual();
+  int setup_halo();
   int build_long_rows(const int* host_rowptr);
   int sync_state();
   int clear_status();
@@ -56,6 +62,17 @@ class Solver {
   double* Rfull = nullptr;
   double* red = nullptr;          // 3 x kPartStride: all-reduced partial rows
   const double* inC = nullptr;    // partial sums read by the next step / restart
+  // Halo exchange: the residual rows of other ranks that this rank's sparse
+  // product reads (recv, by global position in Rfull) and the rows of this
+  // rank that others read (send, by global position); per-peer offsets and
+  // counts in rows, host side.
+  int exchange = LG_EXCHANGE_ALLGATHER, exchange_auto = LG_EXCHANGE_ALLGATHER;
+  std::vector<long long> send_off, send_cnt, recv_off, recv_cnt;
+  long long halo_send = 0, halo_recv = 0;
+  int* d_send_idx = nullptr;
+  int* d_recv_pos = nullptr;
+  double* d_send_buf = nullptr;
+  double* d_recv_buf = nullptr;
   long long nnz = 0;
   int device = 0, num_sm = 0, grid_gs = 0, grid_spmv = 0, grid_basis = 0;
   size_t smem_budget = 0;
@@ -69,6 +86,7 @@ class Solver {
   float* d_val32 = nullptr;
   int* d_long = nullptr;          // long-row tables (rows, chunk ranges, chunk bounds)
   int* d_classes = nullptr;       // row lists of the row-length classes
+  int* d_perm = nullptr;          // reordered plans: plan row -> caller row
   double* d_chunk_sum = nullptr;  // one partial per long-row chunk
 
   double* V = nullptr;      // n x ldv, row-major (ldv >= max_ncv + 1)

@@ -19,15 +19,21 @@
 namespace lg {
 
 // Reference: src/lanczos_ops.cuh:264-277 (adaptive_breakdown_tol), evaluated
-// for the step that produced the residual (index jr).
-__device__ double breakdown_tol(const double* alpha, const double* beta, int jr) {
+// for the step that produced the residual (index jr): eps^(2/3) times the
+// largest absolute row sum of the tridiagonal T[0..jr].  Called by all 32
+// lanes of a warp (one row per lane, max-reduced by shuffles: the same value
+// as a serial scan, without a serial chain of loads in front of the kernel);
+// the result is valid in every lane.
+__device__ double breakdown_tol_warp(const double* alpha, const double* beta, int jr) {
   double est = 0.0;
-  for (int i = 0; i <= jr; ++i) {
+  for (int i = threadIdx.x & 31; i <= jr; i += 32) {
     double rs = fabs(alpha[i]);
     if (i > 0) rs += fabs(beta[i]);
     if (i < jr) rs += fabs(beta[i + 1]);
     est = fmax(est, rs);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) est = fmax(est, __shfl_xor_sync(0xffffffffu, est, o));
   const double eps23 = 3.6687695461231177e-11;  // DBL_EPSILON^(2/3)
   return eps23 * fmax(est, kSafeMin);
 }
@@ -42,16 +48,19 @@ __device__ int step_prologue(const double* __restrict__ part_in, int nrows_in, i
   __shared__ int sh_stop;
   if (threadIdx.x < 32) {
     double nrm2 = 0.0;
+#pragma unroll 4
     for (int r = threadIdx.x; r < nrows_in; r += 32) nrm2 += part_in[(size_t)r * kPartStride + kPartScalar];
     nrm2 = warp_sum(nrm2);
+    const double btol =
+        (beta_mode == BETA_STEP || beta_mode == BETA_RESTART) ? breakdown_tol_warp(alpha, beta, j - 1) : 0.0;
     if (threadIdx.x == 0) {
       const double bn = sqrt(nrm2);
       int stop = STATUS_RUNNING;
       if (beta_mode == BETA_STEP) {
         if (nrm2 <= 0.5 * scal[SC_R1N2]) stop = STATUS_PASS3;
-        else if (bn < breakdown_tol(alpha, beta, j - 1)) stop = STATUS_BREAKDOWN;
+        else if (bn < btol) stop = STATUS_BREAKDOWN;
       } else if (beta_mode == BETA_RESTART) {
-        if (bn < breakdown_tol(alpha, beta, j - 1)) stop = STATUS_BREAKDOWN;
+        if (bn < btol) stop = STATUS_BREAKDOWN;
       }
       double s1, s2;
       safe_inv(bn, s1, s2);

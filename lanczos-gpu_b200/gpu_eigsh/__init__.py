@@ -63,11 +63,18 @@ class EigshPlan:
 
     Reusing a plan skips the CSR upload and all device allocations, which is
     what a caller solving repeatedly on one matrix wants.  ``solve`` takes the
-    same keywords as :func:`gpu_eigsh`.
+    same keywords as :func:`gpu_eigsh`.  ``reorder=True`` renumbers the rows
+    inside the plan by BFS level (LG_PLAN_REORDER_BFS) for locality of the
+    sparse product; v0, eigenvectors and ``matvec_device`` keep the caller's
+    numbering.
     """
 
-    def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None):
+    def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None,
+                 reorder: bool = False):
         self._plan = None
+        flags = _native.LG_PLAN_REORDER_BFS if reorder else 0
+        if reorder and comm is not None:
+            raise ValueError("reorder a partitioned matrix before splitting it (gpu_eigsh.ordering)")
         h = _native.C.c_void_p()
         if comm is not None:
             # row-partitioned: device_csr holds this rank's rows (global column indices)
@@ -77,15 +84,15 @@ class EigshPlan:
                                                        int(bool(mixed)))
         elif device_csr is not None:
             n, nnz, rp, ci, vals = device_csr
-            rc = _native.lib.lg_eigsh_plan_create(_native.C.byref(h), int(n), int(nnz), int(rp), int(ci),
-                                                  int(vals), 1, int(max_ncv), int(bool(mixed)))
+            rc = _native.lib.lg_eigsh_plan_create_ex(_native.C.byref(h), int(n), int(nnz), int(rp), int(ci),
+                                                     int(vals), 1, int(max_ncv), int(bool(mixed)), flags)
         else:
             n, indptr, indices, data = _as_csr(A)
             nnz = data.shape[0]
             self._host = (indptr, indices, data)
-            rc = _native.lib.lg_eigsh_plan_create(_native.C.byref(h), n, nnz, _native.ptr(indptr),
-                                                  _native.ptr(indices), _native.ptr(data), 0, int(max_ncv),
-                                                  int(bool(mixed)))
+            rc = _native.lib.lg_eigsh_plan_create_ex(_native.C.byref(h), n, nnz, _native.ptr(indptr),
+                                                     _native.ptr(indices), _native.ptr(data), 0, int(max_ncv),
+                                                     int(bool(mixed)), flags)
         _native.check(rc)
         self._plan = h
         self.n = int(n)
@@ -209,7 +216,7 @@ class EigshPlan:
 
 def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_max_iters=None,
               cg_tol=1e-12, *, v0=None, return_eigenvectors=True, mixed=False, max_steps=None, seed=42,
-              return_info=False, M=None, mode="normal"):
+              return_info=False, M=None, mode="normal", reorder=False):
     """Compute k eigenvalues (and eigenvectors) of a sparse symmetric matrix on the GPU.
 
     Semantics follow ``scipy.sparse.linalg.eigsh``:
@@ -227,6 +234,8 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
         CG requires A - sigma I to be definite.
     v0 : starting vector (length n); None -> a seeded uniform random vector.
     mixed : fp32 matrix values with fp64 accumulation and fp64 basis.
+    reorder : renumber the rows by BFS level inside the solver for locality of
+        the sparse product (see EigshPlan); results keep the caller's order.
 
     Returns ``(w, v)`` with ``w`` ascending and ``v`` of shape (n, k), or ``w``
     alone when ``return_eigenvectors=False``.  Raises scipy's
@@ -242,7 +251,7 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
             raise TypeError("Cannot use scipy.linalg.eigh for sparse A with k >= N. "
                             "Use scipy.linalg.eigh(A.toarray()) or reduce k.")
     ncv_eff = _default_ncv(n, int(k)) if (ncv is None or int(ncv) <= 0) else min(int(ncv), n)
-    plan = EigshPlan(A, max_ncv=max(ncv_eff, 2), mixed=mixed)
+    plan = EigshPlan(A, max_ncv=max(ncv_eff, 2), mixed=mixed, reorder=reorder)
     try:
         try:
             out = plan.solve(k=k, ncv=ncv_eff, maxiter=maxiter, tol=tol, which=which, sigma=sigma,

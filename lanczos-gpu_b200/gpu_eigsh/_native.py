@@ -22,6 +22,8 @@ LG_ERR_NUMERIC = -5
 LG_ERR_CG_NOCONV = -6
 
 WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
+EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
+LG_PLAN_REORDER_BFS = 1
 
 
 class EigshOpts(C.Structure):
@@ -107,6 +109,8 @@ SIGNATURES = {
     "lg_eigsh_opts_default": (C.c_int, [C.POINTER(EigshOpts)]),
     "lg_eigsh_plan_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "lg_eigsh_plan_create_ex": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]),
     "lg_eigsh_plan_run": (C.c_int, [C.c_void_p, C.POINTER(EigshOpts), C.c_void_p, _PD, C.c_void_p, C.c_int,
                                     C.POINTER(EigshInfo)]),
     "lg_eigsh_plan_destroy": (C.c_int, [C.c_void_p]),
@@ -116,6 +120,8 @@ SIGNATURES = {
     "lg_partition_block": (C.c_int, [C.c_int, C.c_int]),
     "lg_eigsh_plan_create_dist": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_longlong,
                                             C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "lg_eigsh_plan_set_exchange": (C.c_int, [C.c_void_p, C.c_int]),
+    "lg_eigsh_plan_exchange_info": (C.c_int, [C.c_void_p, _PI, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "lg_eigsh_plan_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_eigsh_plan_factorize": (C.c_int, [C.c_void_p, _PD, C.c_int, _PD, _PD]),
     "lg_eigsh": (C.c_int, [C.c_int, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(EigshOpts),

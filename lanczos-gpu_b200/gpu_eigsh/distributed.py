@@ -2,8 +2,11 @@
 
 1. eigsh, row-partitioned (``Communicator``, ``partition_rows``,
    ``PartitionedEigsh``): rank r owns the rows [r*nb, min((r+1)*nb, n)) of the
-   matrix (nb = lg_partition_block); the CUDA engine all-gathers the residual
-   before each sparse product and all-reduces one row of partial sums per
+   matrix (nb = lg_partition_block); before each sparse product the CUDA
+   engine exchanges the residual rows other ranks read (a halo exchange of
+   grouped NCCL sends and receives when the halos are small, as for a graph
+   numbered by ``gpu_eigsh.ordering.bfs_order``; an all-gather otherwise, as
+   for power-law graphs), all-reduces one row of partial sums per
    Gram-Schmidt pass with NCCL, and runs the restart logic replicated.  The
    reference runs on one GPU only.
 
@@ -167,7 +170,7 @@ class PartitionedEigsh:
     the eigenvectors as an (r1 - r0) x k tensor)."""
 
     def __init__(self, comm: Communicator, n_global: int, rowptr, col, vals, max_ncv: int = 127,
-                 mixed: bool = False):
+                 mixed: bool = False, exchange: str = "auto"):
         import torch
 
         from . import EigshPlan
@@ -183,6 +186,28 @@ class PartitionedEigsh:
                                           vals.data_ptr()))
         self.device = vals.device
         self.torch = torch
+        if exchange != "auto":
+            self.set_exchange(exchange)
+
+    def set_exchange(self, mode: str):
+        """'auto', 'allgather' or 'halo' (every rank must choose the same)."""
+        from . import _native
+
+        if mode not in _native.EXCHANGE:
+            raise ValueError("exchange must be 'auto', 'allgather' or 'halo'")
+        _native.check(_native.lib.lg_eigsh_plan_set_exchange(self.plan._plan, _native.EXCHANGE[mode]))
+
+    @property
+    def exchange_info(self):
+        """(mode, rows received from other ranks, rows sent to them) per sparse product."""
+        import ctypes as C
+
+        from . import _native
+
+        m, r, s = C.c_int(0), C.c_longlong(0), C.c_longlong(0)
+        _native.check(_native.lib.lg_eigsh_plan_exchange_info(self.plan._plan, C.byref(m), C.byref(r), C.byref(s)))
+        names = {v: k for k, v in _native.EXCHANGE.items()}
+        return names[m.value], int(r.value), int(s.value)
 
     def solve(self, k, v0_local, **kw):
         torch = self.torch

@@ -95,25 +95,12 @@ class ImgpPrecisionMatvec:
         rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
         return rowptr, cols[order].to(torch.int32).contiguous(), d2[eid[order]].contiguous()
 
-    def _bfs_levels(self, start: int) -> torch.Tensor:
-        n = self.n
-        level = torch.empty(n, dtype=torch.int32, device=self.device)
-        work = torch.empty(2 * n + 2, dtype=torch.int32, device=self.device)
-        rounds = _native.C.c_int(0)
-        _native.check(_native.lib.lg_graph_bfs_levels(n, self.rowptr.data_ptr(), self.col.data_ptr(), int(start),
-                                                      level.data_ptr(), work.data_ptr(), _native.C.byref(rounds),
-                                                      _slq.stream(self.device)))
-        return level
-
     def _bfs_order(self) -> torch.Tensor:
         """Vertices sorted by (BFS level from a pseudo-peripheral vertex, index);
         unreachable vertices last."""
-        n = self.n
-        level = self._bfs_levels(0)
-        start = int(torch.argmax(level))             # a farthest vertex from 0
-        level = self._bfs_levels(start).to(torch.int64)
-        level = torch.where(level < 0, torch.full_like(level, n), level)
-        return torch.argsort(level * n + torch.arange(n, device=self.device))
+        from .ordering import bfs_order
+
+        return bfs_order(self.rowptr, self.col)
 
     def to_internal(self, X: torch.Tensor) -> torch.Tensor:
         """Rows of X (caller's vertex order) in the operator's row order."""

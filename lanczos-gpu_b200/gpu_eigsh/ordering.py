@@ -1,0 +1,74 @@
+"""Row orderings of symmetric sparse matrices for locality.
+
+``bfs_order`` numbers the vertices of the graph of a symmetric CSR by
+breadth-first level from a pseudo-peripheral vertex (two sweeps of
+lg_graph_bfs_levels on the GPU), ties broken by the old index: rows that are
+neighbours in the graph get nearby numbers, so
+
+* the sparse products of the SLQ operator gather from rows that a CTA's
+  neighbours also read (L2 hits), and
+* a contiguous row partition over several GPUs has small halos (the rows a
+  rank's columns name outside its own block lie in the adjacent levels).
+
+``permute_symmetric`` applies the numbering: P A P^T, which has the same
+eigenvalues; eigenvectors come back with ``x_old = x_new[pos]``.
+
+The reference keeps the caller's order (python/gpu_eigsh/imgp.py builds its
+operator on the caller's vertex numbering; src/ has no reordering).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+__all__ = ["bfs_levels", "bfs_order", "permute_symmetric"]
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def bfs_levels(rowptr: torch.Tensor, col: torch.Tensor, start: int) -> torch.Tensor:
+    """Hop distance of every vertex from `start` (-1 where unreachable) in the
+    graph of a CSR with every edge stored both ways (int32 device tensors)."""
+    n = rowptr.numel() - 1
+    dev = rowptr.device
+    level = torch.empty(n, dtype=torch.int32, device=dev)
+    work = torch.empty(2 * n + 2, dtype=torch.int32, device=dev)
+    rounds = _native.C.c_int(0)
+    _native.check(_native.lib.lg_graph_bfs_levels(n, rowptr.data_ptr(), col.data_ptr(), int(start), level.data_ptr(),
+                                                  work.data_ptr(), _native.C.byref(rounds), _stream(dev)))
+    return level
+
+
+def bfs_order(rowptr: torch.Tensor, col: torch.Tensor) -> torch.Tensor:
+    """perm (int64, device): perm[new] = old, vertices sorted by (BFS level
+    from a pseudo-peripheral vertex, old index); unreachable vertices last."""
+    n = rowptr.numel() - 1
+    level = bfs_levels(rowptr, col, 0)
+    start = int(torch.argmax(level))             # a farthest vertex from 0
+    level = bfs_levels(rowptr, col, start).to(torch.int64)
+    level = torch.where(level < 0, torch.full_like(level, n), level)
+    return torch.argsort(level * n + torch.arange(n, device=rowptr.device))
+
+
+def permute_symmetric(rowptr: torch.Tensor, col: torch.Tensor, val: torch.Tensor, perm: torch.Tensor):
+    """P A P^T of a CSR (row i of the result = row perm[i] of A, columns
+    renumbered by pos = perm^-1 and sorted).  Returns (rowptr int32, col
+    int32, val, pos int64) on the device of the inputs."""
+    n = rowptr.numel() - 1
+    dev = rowptr.device
+    perm = perm.to(dev, torch.int64)
+    pos = torch.empty_like(perm)
+    pos[perm] = torch.arange(n, device=dev)
+    rp = rowptr.to(torch.int64)
+    counts = rp[1:] - rp[:-1]
+    rows_old = torch.repeat_interleave(torch.arange(n, device=dev), counts)
+    r_new = pos[rows_old]
+    c_new = pos[col.to(torch.int64)]
+    order = torch.argsort(r_new * n + c_new)
+    new_counts = counts[perm]
+    out_rp = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+    out_rp[1:] = torch.cumsum(new_counts, 0).to(torch.int32)
+    return out_rp, c_new[order].to(torch.int32).contiguous(), val[order].contiguous(), pos

@@ -7,7 +7,8 @@ and benchmarks.  All are deterministic functions of their arguments.
 * ``grid2d_dirichlet(N)``  — 5-point Dirichlet Laplacian on an N x N grid,
   kron(I, T) + kron(T, I), T = tridiag(-1, 2, -1); analytic eigenvalues
   ``grid_eigenvalues``.
-* ``grid3d_dirichlet(N)``  — 7-point Dirichlet Laplacian on N^3.
+* ``grid3d_dirichlet(N)``  — 7-point Dirichlet Laplacian on N^3
+  (``grid3d_dirichlet_device``: the same matrix assembled on the GPU).
 * ``knn_laplacian(n, k, seed)`` — points uniform in [0,1]^2, k nearest
   neighbours (self dropped), symmetrised by union (max(A, A^T), as the
   reference's benchmark/generate_large_laplacian.py:60 does), weights
@@ -46,6 +47,37 @@ def grid3d_dirichlet(N: int) -> sp.csr_matrix:
     L.sum_duplicates()
     L.sort_indices()
     return L
+
+
+def grid3d_dirichlet_device(N: int, device=None):
+    """grid3d_dirichlet(N) assembled on the GPU with torch (configuration 2:
+    N = 128, n = 2,097,152, nnz = 7n - 6N^2).  Vertex (z, y, x) is row
+    z*N^2 + y*N + x; its row holds -1 at the in-grid neighbours and 6 on the
+    diagonal, columns ascending.  Returns (n, rowptr int32, col int32,
+    val float64) device tensors."""
+    import torch
+
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    n = N ** 3
+    i = torch.arange(n, device=dev, dtype=torch.int64)
+    x, y, z = i % N, (i // N) % N, i // (N * N)
+    # offsets in ascending column order, with the test that keeps each in the grid
+    offs = [(-N * N, z > 0), (-N, y > 0), (-1, x > 0), (0, None), (1, x < N - 1), (N, y < N - 1),
+            (N * N, z < N - 1)]
+    cols, vals, keep = [], [], []
+    for off, ok in offs:
+        cols.append(i + off)
+        vals.append(torch.full((n,), 6.0 if off == 0 else -1.0, dtype=torch.float64, device=dev))
+        keep.append(torch.ones(n, dtype=torch.bool, device=dev) if ok is None else ok)
+    C = torch.stack(cols, 1)
+    Vv = torch.stack(vals, 1)
+    K = torch.stack(keep, 1)
+    counts = K.sum(1)
+    rowptr = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+    rowptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+    col = C[K].to(torch.int32)
+    val = Vv[K]
+    return n, rowptr, col, val
 
 
 def grid_eigenvalues(N: int, dim: int) -> np.ndarray:

@@ -115,3 +115,23 @@ def test_partition_rows_covers_every_row_once():
                 rows.append((r0, r1))
             assert rows[0][0] == 0 and rows[-1][1] == n
             assert all(rows[i][1] == rows[i + 1][0] for i in range(world - 1))
+
+
+def test_permute_symmetric_matches_scipy():
+    """P A P^T of a CSR (the renumbering applied before a row partition) equals
+    scipy's on CPU tensors, with sorted columns."""
+    import numpy as np
+
+    from gpu_eigsh import synthetic as syn
+    from gpu_eigsh.ordering import permute_symmetric
+
+    L, _ = syn.knn_laplacian(3000, k=6, seed=3)
+    perm = torch.from_numpy(np.random.default_rng(1).permutation(L.shape[0]))
+    rp, ci, va, pos = permute_symmetric(torch.from_numpy(L.indptr.astype(np.int32)),
+                                        torch.from_numpy(L.indices.astype(np.int32)), torch.from_numpy(L.data), perm)
+    P = L[perm.numpy()][:, perm.numpy()].tocsr()
+    P.sort_indices()
+    np.testing.assert_array_equal(rp.numpy(), P.indptr)
+    np.testing.assert_array_equal(ci.numpy(), P.indices)
+    np.testing.assert_array_equal(va.numpy(), P.data)
+    np.testing.assert_array_equal(pos.numpy()[perm.numpy()], np.arange(L.shape[0]))

@@ -250,3 +250,75 @@ def test_knn_1e6_properties(ge):
     G = V.T @ V
     assert np.abs(G - np.eye(20)).max() < 1e-9
     assert np.all(np.diff(w) >= 0)
+
+
+def test_cfg2_shift_invert_grid3d_full_size(ge):
+    """Configuration 2 at full size: 7-point Dirichlet Laplacian on 128^3
+    (n = 2,097,152), sigma = 0, k = 16, ncv = 48, tol = 1e-10, inner CG to
+    1e-12.  The spectrum is known in closed form: every eigenvalue must be an
+    analytic one to 1e-10 relative, no distinct analytic eigenvalue below the
+    largest one returned may be missing (single-vector Lanczos sees one
+    direction per multiple eigenvalue until rounding seeds the others, so
+    multiplicities may be incomplete, never the distinct values), and every
+    pair satisfies ||A y - lambda y|| <= 1e-8 ||A||."""
+    import torch
+
+    from gpu_eigsh import synthetic as syn
+
+    N = 128
+    n, rp, col, val = syn.grid3d_dirichlet_device(N, device="cuda")
+    assert int(col.numel()) == 14_581_760
+    plan = ge.EigshPlan(None, max_ncv=48, device_csr=(n, int(col.numel()), rp.data_ptr(), col.data_ptr(),
+                                                       val.data_ptr()))
+    v0 = torch.from_numpy(np.random.default_rng(0).standard_normal(n)).cuda()
+    Y = torch.empty((n, 16), dtype=torch.float64, device="cuda")
+    w, _ = plan.solve(k=16, sigma=0.0, ncv=48, tol=1e-10, cg_tol=1e-12, v0_device=v0.data_ptr(),
+                      evecs_out=Y.data_ptr())
+    info = dict(plan.last_info)
+    exact = syn.grid_eigenvalues(N, 3)[:200]
+    near = exact[np.abs(exact[None, :] - w[:, None]).argmin(1)]
+    assert np.max(np.abs(w - near) / near) < 1e-10, (w, near)
+    distinct = np.unique(np.round(exact / exact[0], 9)) * exact[0]
+    below = distinct[distinct <= w.max() * (1 + 1e-9)]
+    for lam in below:
+        assert np.min(np.abs(w - lam)) <= 1e-9 * lam, (lam, w)
+    AY = torch.empty(n, dtype=torch.float64, device="cuda")
+    for i in range(16):
+        y = Y[:, i].contiguous()
+        plan.matvec_device(y.data_ptr(), AY.data_ptr())
+        assert float(torch.linalg.norm(AY - w[i] * y)) <= 1e-8 * 12.0
+    G = Y.T @ Y
+    assert float((G - torch.eye(16, dtype=torch.float64, device="cuda")).abs().max()) < 1e-9
+    assert info["cg_failures"] == 0 and info["cg_iters"] > 0
+    plan.close()
+
+
+def test_plan_reorder_bfs_keeps_caller_numbering(ge):
+    """LG_PLAN_REORDER_BFS: the plan renumbers the rows by BFS level inside;
+    eigenvalues match ARPACK at 1e-10, the eigenvectors come back in the
+    caller's numbering (residuals against the caller's matrix), matvec maps
+    both ways, and the Lanczos tridiagonal equals the unordered plan's."""
+    import torch
+
+    from gpu_eigsh import synthetic as syn
+    from oracle.irlm import arpack_eigsh
+
+    L, _ = syn.knn_laplacian(20000, k=10, seed=7)
+    v0 = np.random.default_rng(2).standard_normal(L.shape[0])
+    an = anorm1(L)
+    for mixed in (False, True):
+        with ge.EigshPlan(L, max_ncv=40, mixed=mixed, reorder=True) as plan:
+            w, V = plan.solve(k=8, which="LA", ncv=40, tol=1e-10, v0=v0)
+            if not mixed:
+                ws, _ = arpack_eigsh(L, 8, which="LA", ncv=40, tol=1e-10, v0=v0)
+                assert eig_rel_err(w, ws, an) < 1e-10
+                assert _residuals(L, w, V).max() <= 1e-10 * an
+            x = torch.from_numpy(v0).cuda()
+            y = torch.empty_like(x)
+            plan.matvec_device(x.data_ptr(), y.data_ptr())
+            Lx = (L.astype(np.float32).astype(np.float64) if mixed else L) @ v0
+            assert np.abs(y.cpu().numpy() - Lx).max() <= 1e-12 * np.abs(Lx).max()
+            a1, b1 = plan.factorize(v0, 20)
+        with ge.EigshPlan(L, max_ncv=40, mixed=mixed) as plain:
+            a0, b0 = plain.factorize(v0, 20)
+        assert np.abs(a1 - a0).max() < 1e-10 * an and np.abs(b1 - b0).max() < 1e-10 * an

@@ -73,3 +73,16 @@ def test_breakdown_invariant_subspace():
     (w, _), info = oracle_eigsh(A, 4, ncv=20, which="SA", tol=1e-10, v0=v0)
     assert info["breakdowns"] >= 1
     np.testing.assert_allclose(w, [1.0, 2.0, 3.0, 10.0], rtol=1e-10)
+
+
+@pytest.mark.parametrize("N", [1, 2, 5, 16])
+def test_grid3d_device_builder_equals_host_builder(N):
+    """The GPU-side assembly of the configuration-2 matrix (run here with torch
+    on the CPU) gives the host builder's CSR exactly."""
+    n, rp, col, val = syn.grid3d_dirichlet_device(N, device="cpu")
+    B = syn.grid3d_dirichlet(N)
+    B.eliminate_zeros()
+    assert n == N ** 3 and int(rp[-1]) == 7 * n - 6 * N * N
+    np.testing.assert_array_equal(rp.numpy(), B.indptr)
+    np.testing.assert_array_equal(col.numpy(), B.indices)
+    np.testing.assert_array_equal(val.numpy(), B.data)

@@ -1,7 +1,9 @@
 """GPU (2+ devices): the row-partitioned eigsh equals the single-GPU solve.
 
 Two ranks (processes, one GPU each, NCCL) split the rows of a kNN graph
-Laplacian and of an R-MAT normalised Laplacian (configuration 4's family,
+Laplacian (in the generator's order, and renumbered by BFS level so that the
+halos are small: run with the halo exchange and, forced, with the
+all-gather) and of an R-MAT normalised Laplacian (configuration 4's family,
 with rows longer than the row kernels' cut).  Every rank must report the same
 eigenvalues, equal to the single-GPU plan's at 1e-10, and the assembled
 eigenvector rows must satisfy ||A v - lambda v|| <= tol ||A||.  Skipped with
@@ -26,8 +28,19 @@ def _free_port():
 def _matrix(case):
     from gpu_eigsh import synthetic as syn
 
-    if case == "knn":
+    if case.startswith("knn"):
         L, _ = syn.knn_laplacian(60000, k=10, seed=4)
+        if case != "knn":
+            import torch
+
+            from gpu_eigsh.ordering import bfs_order, permute_symmetric
+
+            dev = torch.device("cuda", torch.cuda.current_device())
+            rp = torch.from_numpy(L.indptr.astype(np.int32)).to(dev)
+            ci = torch.from_numpy(L.indices.astype(np.int32)).to(dev)
+            va = torch.from_numpy(L.data).to(dev)
+            rp2, ci2, va2, _ = permute_symmetric(rp, ci, va, bfs_order(rp, ci))
+            L = sp.csr_matrix((va2.cpu().numpy(), ci2.cpu().numpy(), rp2.cpu().numpy()), shape=L.shape)
         return L, dict(k=10, which="LA", ncv=30, tol=1e-10), False
     import torch
 
@@ -59,20 +72,29 @@ def _worker(rank, world, port, case, out_w, out_y):
         col = torch.from_numpy(L.indices[a:b].astype(np.int32)).to(dev)
         val = torch.from_numpy(L.data[a:b].astype(np.float64)).to(dev)
         v0 = np.random.default_rng(0).standard_normal(n)
-        pe = PartitionedEigsh(comm, n, rp, col, val, max_ncv=kw["ncv"])
+        forced = {"knn_bfs_allgather": "allgather"}.get(case, "auto")
+        pe = PartitionedEigsh(comm, n, rp, col, val, max_ncv=kw["ncv"], exchange=forced)
         k = kw.pop("k")
         w, Y = pe.solve(k, v0[r0:r1], **kw)
         torch.cuda.synchronize()
         out_w[rank, :k] = torch.from_numpy(np.asarray(w))
         out_y[r0:r1, :k] = Y.cpu()
+        mode, recv_rows, send_rows = pe.exchange_info
         pe.close()
+        # the BFS numbering leaves a thin boundary between the two row blocks
+        if case == "knn_bfs":
+            assert mode == "halo" and 0 < recv_rows < (r1 - r0) // 4, (mode, recv_rows)
+        if case == "knn_bfs_allgather":
+            assert mode == "allgather"
+        if case == "rmat":
+            assert mode == "allgather", (mode, recv_rows)
     finally:
         comm.close()
         dist.barrier()
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["knn", "rmat"])
+@pytest.mark.parametrize("case", ["knn", "knn_bfs", "knn_bfs_allgather", "rmat"])
 def test_partitioned_equals_single_gpu(case):
     import torch
     import torch.multiprocessing as mp
