@@ -356,6 +356,31 @@ int compute_eigsh_sigma(int n, int nnz, const int* row_ptr, const int* col_idx, 
                         int ncv, int max_iters, double tol, double sigma, int cg_max_iters, double cg_tol,
                         double* out_eigenvalues, double* out_eigenvectors);
 
+/* Backward of eigsh (implicit differentiation, Xie et al. 2020), device
+ * pointers on `stream`.  For every eigenpair i (eigenvalue evals[i],
+ * eigenvector column i of X, n x k row-major) the solution xi_i of
+ *   (A - evals[i] I) xi_i = (I - X X^T) g_evecs[:, i],   xi_i orthogonal to X,
+ * is found by conjugate gradients (relative residual cg_tol, at most
+ * cg_max_iters iterations; the k systems advance together as one block, each
+ * with its own shift and convergence test), and for every stored entry
+ * p = (r, c) of the CSR
+ *   grad_vals[p] = sum_i (g_evals[i] X[r, i] - xi_i[r]) X[c, i].
+ * g_evals (k) and g_evecs (n x k row-major) may be NULL (zero).  cg_iters
+ * (host, k ints, may be NULL) receives the iterations per pair, negative when
+ * a pair stopped at the limit or at a breakdown, as the reference's CG
+ * reports.  1 <= k <= min(n, 128); the CSR is checked on the device first.
+ * Replaces compute_adjoint_eigsh, python/gpu_eigsh/_cuda_eigsh.cu:183-326. */
+int lg_eigsh_adjoint(int n, long long nnz, const int* row_ptr, const int* col_idx, const double* vals, int k,
+                     const double* evals, const double* X, const double* g_evals, const double* g_evecs,
+                     double* grad_vals, int cg_max_iters, double cg_tol, int* cg_iters, void* stream);
+
+/* Reference-compatible form of lg_eigsh_adjoint: host arrays, returns 0 (or a
+ * negative LG_ERR_* status; the reference aborts the process instead).
+ * Same signature as compute_adjoint_eigsh (python/gpu_eigsh/_cuda_eigsh.cu:183-194). */
+int compute_adjoint_eigsh(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals, int k,
+                          const double* eigenvalues, const double* eigenvectors, const double* grad_evals,
+                          const double* grad_evecs, double* grad_vals, int cg_max_iters, double cg_tol);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,15 @@ __global__ void cast_f64_f32_kernel(const double* __restrict__ a, float* __restr
     b[i] = (float)a[i];
 }
 
+// Sets *bad when a column index lies outside [0, ncols) (device-pointer CSR
+// input is checked before any kernel gathers through it).
+__global__ void check_cols_kernel(const int* __restrict__ col, long long nnz, int ncols, int* bad) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nnz; i += (long long)gridDim.x * blockDim.x) {
+    const int c = col[i];
+    if (c < 0 || c >= ncols) *bad = 1;
+  }
+}
+
 __global__ void scale_kernel(double* x, int n, double s) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] *= s;
 }
@@ -239,8 +248,29 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
 
   std::vector<int> hrp((size_t)n + 1);
   if (device_ptrs) {
+    // the same structural checks as for host input: row_ptr on the host,
+    // column indices by a kernel
     LG_TRY(cudaMemcpyAsync(hrp.data(), rowptr, sizeof(int) * hrp.size(), cudaMemcpyDeviceToHost, stream));
+    LG_TRY(cudaMemsetAsync(state, 0, sizeof(int) * ST_WORDS, stream));
+    if (nnz > 0) {
+      check_cols_kernel<<<num_sm * 4, 256, 0, stream>>>(d_col, nnz, n_cols, state);
+      LG_TRY(cudaGetLastError());
+    }
+    LG_TRY(cudaMemcpyAsync(h_state, state, sizeof(int), cudaMemcpyDeviceToHost, stream));
     LG_TRY(cudaStreamSynchronize(stream));
+    if (hrp[0] != 0 || (long long)hrp[n] != nnz) {
+      g_last_error = "row_ptr must start at 0 and end at nnz";
+      return LG_ERR_INVALID;
+    }
+    for (int i = 0; i < n; ++i)
+      if (hrp[i + 1] < hrp[i]) {
+        g_last_error = "row_ptr is not monotone";
+        return LG_ERR_INVALID;
+      }
+    if (h_state[0] != 0) {
+      g_last_error = "column index out of range";
+      return LG_ERR_INVALID;
+    }
   } else {
     std::copy(rowptr, rowptr + n + 1, hrp.begin());
   }

@@ -11,6 +11,8 @@ Drop-in for the reference package of the same name:
 * ``gpu_eigsh.funm_torch`` — ``slq_logdet``, ``funm_apply_kraemer``,
   ``funm_qform_op`` (torch.autograd.Functions).
 * ``gpu_eigsh.imgp`` — ``make_imgp_precision_matvec``.
+* ``differentiable_eigsh`` — eigenpairs as a torch.autograd.Function with the
+  implicit-differentiation backward (``gpu_eigsh.differentiable``).
 
 All arithmetic runs in the CUDA library ``_lib/liblanczos_b200.so``; there is
 no CPU fallback.
@@ -22,7 +24,15 @@ import numpy as np
 from . import _native
 from ._native import LanczosError
 
-__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence"]
+__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence", "differentiable_eigsh"]
+
+
+def differentiable_eigsh(*args, **kwargs):
+    """See gpu_eigsh.differentiable.differentiable_eigsh (imported on first use:
+    it needs torch)."""
+    from .differentiable import differentiable_eigsh as _impl
+
+    return _impl(*args, **kwargs)
 
 try:  # raise scipy's own exception type so existing handlers keep working
     from scipy.sparse.linalg import ArpackNoConvergence
