@@ -545,6 +545,91 @@ def run_knn_partitioned(args, L, v0, dev, world, rank):
             "scaling": "strong"}
 
 
+ADJ_K = 20
+ADJ_WORKLOAD = (f"differentiable_eigsh backward (implicit differentiation, k={ADJ_K} smallest pairs, reference "
+                "defaults ncv=3k maxiter=3000 tol=1e-12, cg_max_iters=500 cg_tol=1e-10) on the n=1e6 kNN graph "
+                "Laplacian, random upstream gradients on all eigenvalues and eigenvectors (seed 0)")
+
+
+def adj_bytes_per_iteration(n, nnz, k):
+    """Algorithmic DRAM bytes of one block-CG iteration of lg_eigsh_adjoint
+    (blocks n x ld doubles, ld = k rounded up to 8): the sparse product reads
+    the CSR and P and writes AP; the update reads P, AP, Xi, R and writes Xi,
+    R; the Gram reads X and R; the deflation reads X, R, P and writes R, P."""
+    blk = 8 * n * ((k + 7) // 8 * 8)
+    return (12 * nnz + 4 * (n + 1) + 2 * blk) + 6 * blk + 2 * blk + 5 * blk
+
+
+def run_adjoint(args, L, dev, with_cpu):
+    """The differentiable eigsh backward on configuration 1: eigenpairs from
+    the forward (outside the timed region), then loss.backward() timed with
+    CUDA events on the stream the adjoint runs on."""
+    import torch
+
+    from gpu_eigsh import differentiable_eigsh
+
+    n = L.shape[0]
+    crow = torch.from_numpy(L.indptr.astype(np.int64)).to(dev)
+    col = torch.from_numpy(L.indices.astype(np.int64)).to(dev)
+    rng = np.random.default_rng(0)
+    ge = torch.from_numpy(rng.standard_normal(ADJ_K)).to(dev)
+    gv = torch.from_numpy(rng.standard_normal((n, ADJ_K))).to(dev)
+    times, info = [], None
+    for rep in range(2):
+        vals = torch.from_numpy(L.data.astype(np.float64)).to(dev).requires_grad_(True)
+        A = torch.sparse_csr_tensor(crow, col, vals, L.shape, check_invariants=False)
+        t0 = time.perf_counter()
+        w, V = differentiable_eigsh(A, k=ADJ_K)
+        fwd_s = time.perf_counter() - t0
+        loss = (w * ge).sum() + (V * gv).sum()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        loss.backward()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+        if rep == 0:
+            # the iteration counts of the pairs, from the autograd node
+            node = w.grad_fn
+            info = {"cg_iters": list(getattr(node, "cg_iters", [])), "forward_s": fwd_s,
+                    "eigenvalues": [float(x) for x in w.detach().cpu()[:4]]}
+    ms = times[-1]
+    iters = max(abs(i) for i in info["cg_iters"]) if info["cg_iters"] else 0
+    peak, peak_kind = measured_peaks()
+    bpi = adj_bytes_per_iteration(n, L.nnz, ADJ_K)
+    ach = bpi * iters / (ms / 1000.0) / 1e9 if iters else None
+    out = {"workload": ADJ_WORKLOAD, "metric": "adjoint_backward_s", "value": ms / 1000.0, "unit": "s",
+           "higher_is_better": False, "k": ADJ_K, "block_cg_iterations": iters,
+           "cg_iterations_per_pair": info["cg_iters"], "forward_s": round(info["forward_s"], 3),
+           "roofline": {"bound": "hbm", "kernel": "block CG iteration (adj_spmm, adj_update, adj_gram, adj_deflate)",
+                        "achieved": ach, "peak": peak, "unit": "GB/s", "frac": (ach / peak) if ach else None,
+                        "peak_source": peak_kind, "algorithmic_bytes_per_iteration": bpi,
+                        "note": "whole backward time (incl. setup and the gradient SDDMM) / iterations"},
+           "parallelism": "1 GPU"}
+    if with_cpu:
+        out["cpu_baseline"] = adjoint_cpu_baseline(L, w.detach().cpu().numpy(), V.detach().cpu().numpy(),
+                                                    gv[:, 0].cpu().numpy(), max(iters, 1))
+    return out
+
+
+def adjoint_cpu_baseline(L, w, X, g0, iters_gpu, sample_iters=30):
+    """The oracle (the reference's per-pair deflated CG, numpy/scipy on the host)
+    on a bounded sample: one pair, `sample_iters` CG iterations, scaled to k
+    pairs x the GPU's iteration count."""
+    from oracle import adjoint as OA
+
+    rhs = OA.deflate(g0.copy(), X)
+    OA.cg_deflated(L, float(w[0]), rhs, X, tol=0.0, max_iters=2)   # warm
+    t0 = time.perf_counter()
+    OA.cg_deflated(L, float(w[0]), rhs, X, tol=0.0, max_iters=sample_iters)
+    el = time.perf_counter() - t0
+    per_it = el / sample_iters
+    return {"value": per_it * iters_gpu * ADJ_K, "unit": "s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample_iters} deflated-CG iterations of one pair in {el:.2f} s, scaled to {ADJ_K} pairs x "
+                      f"{iters_gpu} iterations (scipy sparse matvec + numpy deflation, host BLAS threads)"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -601,6 +686,16 @@ def run_ours(args):
 
     if args.only_rmat:
         out = run_rmat(args, torch.device("cuda", local), world=world, rank=rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return 0
+    if args.only_adjoint:
+        L, _, _ = build_workload()
+        out = run_adjoint(args, L, torch.device("cuda", local), with_cpu=not args.no_cpu_baseline) if rank == 0 \
+            else None
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -732,6 +827,8 @@ def run_ours(args):
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(L, v0)
     plan.close()
+    if world == 1 and not args.no_adjoint:
+        line["adjoint"] = run_adjoint(args, L, dev, with_cpu=not args.no_cpu_baseline)
     if world > 1 and not args.no_partitioned:
         line["partitioned"] = run_knn_partitioned(args, L, v0, dev, world, rank)
     del L
@@ -769,6 +866,8 @@ def main():
     ap.add_argument("--rmat-scale", type=int, default=RMAT_SCALE, help="R-MAT scale (reduced cases for profiling)")
     ap.add_argument("--reorder", action="store_true",
                     help="renumber the rows by BFS level inside the plan (LG_PLAN_REORDER_BFS)")
+    ap.add_argument("--no-adjoint", action="store_true", help="skip the differentiable-eigsh backward leg")
+    ap.add_argument("--only-adjoint", action="store_true", help="run the differentiable-eigsh backward leg alone")
     ap.add_argument("--no-partitioned", action="store_true",
                     help="at N > 1, skip the row-partitioned configuration-1 solve")
     ap.add_argument("--only-sinv", action="store_true", help="run the configuration-2 (shift-invert) leg alone")

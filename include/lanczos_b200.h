@@ -374,6 +374,34 @@ int lg_eigsh_adjoint(int n, long long nnz, const int* row_ptr, const int* col_id
                      const double* evals, const double* X, const double* g_evals, const double* g_evecs,
                      double* grad_vals, int cg_max_iters, double cg_tol, int* cg_iters, void* stream);
 
+/* Matrix functions by m-step Lanczos quadrature (no restart; the steps stop
+ * at an invariant subspace), f = LG_FUNC_LOG / _EXP / _SQRT / _INV:
+ *   mode 1: y = f(A) v ~ ||v|| V S f(Theta) S^T e1   (n doubles)
+ *   mode 0: *value = v^T f(A) v ~ ||v||^2 sum_i S[0, i]^2 f(Theta_i).
+ * v, y: host (io_on_device = 0) or device pointers, in the caller's numbering.
+ * *m_actual receives the depth reached (1 <= m <= min(n, max_ncv)), or the
+ * reference's negative status: -2 f undefined at a Ritz value (log: theta <= 0,
+ * sqrt: theta < 0, inv: theta = 0), -3 zero v (y = 0), -4 tridiagonal
+ * eigensolver failure; the call itself then still returns LG_OK.  Single-GPU
+ * plans only.  Replaces compute_funm_apply / compute_funm_qform
+ * (python/gpu_eigsh/_cuda_funm.cu:40-251, src/matrix_function.cuh:82-274). */
+int lg_eigsh_plan_funm(lg_eigsh_plan* plan, const double* v, int io_on_device, int m, int func, int mode, double* y,
+                       double* value, int* m_actual);
+
+/* Reference-compatible matrix functions with the reference's signatures and
+ * return values (depth reached, or -1 unknown func_name, -2, -3, -4 as above);
+ * failures the reference cannot report return -100 + LG_ERR_*.  m is capped at
+ * min(n, 127).  compute_funm_debug returns the basis (n x m_actual,
+ * column-major), alpha (m_actual) and beta (m_actual + 1; beta[0] = 0,
+ * beta[m_actual] = the final residual norm) as the reference's test hook
+ * (python/gpu_eigsh/_cuda_funm.cu:132-178). */
+int compute_funm_apply(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, const char* func_name, double* out_y);
+int compute_funm_qform(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, const char* func_name, double* out_value);
+int compute_funm_debug(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, double* out_V, double* out_alpha, double* out_beta);
+
 /* Reference-compatible form of lg_eigsh_adjoint: host arrays, returns 0 (or a
  * negative LG_ERR_* status; the reference aborts the process instead).
  * Same signature as compute_adjoint_eigsh (python/gpu_eigsh/_cuda_eigsh.cu:183-194). */

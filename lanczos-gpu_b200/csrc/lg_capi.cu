@@ -91,6 +91,12 @@ int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long*
   return plan->solver.exchange_info(mode, recv_rows, send_rows);
 }
 
+int lg_eigsh_plan_funm(lg_eigsh_plan* plan, const double* v, int io_on_device, int m, int func, int mode, double* y,
+                       double* value, int* m_actual) {
+  if (!plan) return LG_ERR_INVALID;
+  return plan->solver.funm(v, io_on_device, m, func, mode, y, value, m_actual);
+}
+
 int lg_eigsh_plan_run(lg_eigsh_plan* plan, const lg_eigsh_opts* opts, const double* v0, double* evals,
                       double* evecs, int io_on_device, lg_eigsh_info* info) {
   if (!plan || !opts || !evals) {
@@ -201,3 +207,65 @@ int compute_eigsh_sigma(int n, int nnz, const int* row_ptr, const int* col_idx, 
 }
 
 }  // extern "C"
+
+// ---- reference-compatible matrix functions (python/gpu_eigsh/_cuda_funm.cu) --
+// Return values keep the reference's meaning: the depth reached (> 0), or -1
+// unknown function, -2 f undefined at a Ritz value, -3 zero vector, -4
+// tridiagonal eigensolver failure.  Failures the reference cannot report (it
+// exits the process) come back as kFunmLibErr + LG_ERR_* (text in lg_last_error).
+static const int kFunmLibErr = -100;
+
+static int funm_code(const char* name) {
+  if (!name) return -1;
+  if (std::strcmp(name, "log") == 0) return LG_FUNC_LOG;
+  if (std::strcmp(name, "exp") == 0) return LG_FUNC_EXP;
+  if (std::strcmp(name, "sqrt") == 0) return LG_FUNC_SQRT;
+  if (std::strcmp(name, "inv") == 0) return LG_FUNC_INV;
+  return -1;
+}
+
+static int funm_host(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals, const double* v,
+                     int m, const char* func_name, int mode, double* y, double* value) {
+  const int func = funm_code(func_name);
+  if (func < 0) return -1;   // the reference's "unknown func"
+  if (n < 1 || m < 1 || !v) {
+    lg::g_last_error = "compute_funm: invalid arguments";
+    return kFunmLibErr + LG_ERR_INVALID;
+  }
+  lg_eigsh_plan* p = nullptr;
+  int rc = lg_eigsh_plan_create(&p, n, nnz, row_ptr, col_idx, vals, 0, std::min(m, n), 0);
+  if (rc != LG_OK) return kFunmLibErr + rc;
+  int ma = 0;
+  rc = p->solver.funm(v, 0, std::min(m, n), func, mode, y, value, &ma);
+  lg_eigsh_plan_destroy(p);
+  return rc != LG_OK ? kFunmLibErr + rc : ma;
+}
+
+extern "C" {
+
+int compute_funm_apply(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, const char* func_name, double* out_y) {
+  if (!out_y) return kFunmLibErr + LG_ERR_INVALID;
+  return funm_host(n, nnz, row_ptr, col_idx, vals, v_host, m, func_name, 1, out_y, nullptr);
+}
+
+int compute_funm_qform(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, const char* func_name, double* out_value) {
+  if (!out_value) return kFunmLibErr + LG_ERR_INVALID;
+  return funm_host(n, nnz, row_ptr, col_idx, vals, v_host, m, func_name, 0, nullptr, out_value);
+}
+
+int compute_funm_debug(int n, int nnz, const int* row_ptr, const int* col_idx, const double* vals,
+                       const double* v_host, int m, double* out_V, double* out_alpha, double* out_beta) {
+  if (n < 1 || m < 1 || !v_host || !out_V || !out_alpha || !out_beta) return kFunmLibErr + LG_ERR_INVALID;
+  lg_eigsh_plan* p = nullptr;
+  int rc = lg_eigsh_plan_create(&p, n, nnz, row_ptr, col_idx, vals, 0, std::min(m, n), 0);
+  if (rc != LG_OK) return kFunmLibErr + rc;
+  int ma = 0;
+  rc = p->solver.funm_debug(v_host, std::min(m, n), out_V, out_alpha, out_beta, &ma);
+  lg_eigsh_plan_destroy(p);
+  return rc != LG_OK ? kFunmLibErr + rc : ma;
+}
+
+}  // extern "C"
+

@@ -80,9 +80,11 @@ void Solver::release() {
   }
   if (red) cudaFree(red);
   red = nullptr;
-  for (void* p : {(void*)d_send_idx, (void*)d_recv_pos, (void*)d_send_buf, (void*)d_recv_buf, (void*)d_perm})
+  for (void* p : {(void*)d_send_idx, (void*)d_recv_pos, (void*)d_send_buf, (void*)d_recv_buf, (void*)d_perm,
+                  (void*)funm_ws})
     if (p) cudaFree(p);
   d_perm = nullptr;
+  funm_ws = nullptr;
   d_send_idx = d_recv_pos = nullptr;
   d_send_buf = d_recv_buf = nullptr;
   send_off.clear();

@@ -27,6 +27,11 @@ class Solver {
   int factorize(const double* v0, int m, double* alpha_out, double* beta_out);
   // Partitioned runs: how the residual reaches the other ranks before each
   // sparse product (LG_EXCHANGE_*); the same mode on every rank.
+  // m-step Lanczos quadrature of f(A) v (mode 1) or v^T f(A) v (mode 0), no
+  // restart (lg_funm.cu); *m_actual: depth reached, or the reference's
+  // negative status (-2 f undefined at a Ritz value, -3 zero v, -4 T failed)
+  int funm(const double* v, int io_on_device, int m, int func, int mode, double* y, double* value, int* m_actual);
+  int funm_debug(const double* v, int m, double* V_out, double* alpha_out, double* beta_out, int* m_actual);
   int set_exchange(int mode);
   int exchange_info(int* mode, long long* recv_rows, long long* send_rows) const;
 
@@ -42,6 +47,7 @@ class Solver {
   int gather_residual();
   int setup_halo();
   int build_long_rows(const int* host_rowptr);
+  int funm_factor(const double* v, int io_on_device, int m, int* m_actual, double* vnorm);
   int sync_state();
   int clear_status();
   int apply_step(int j, int beta_mode);
@@ -87,6 +93,7 @@ class Solver {
   int* d_long = nullptr;          // long-row tables (rows, chunk ranges, chunk bounds)
   int* d_classes = nullptr;       // row lists of the row-length classes
   int* d_perm = nullptr;          // reordered plans: plan row -> caller row
+  double* funm_ws = nullptr;      // funm small side: Z, inverse-iteration scratch, q, scalars
   double* d_chunk_sum = nullptr;  // one partial per long-row chunk
 
   double* V = nullptr;      // n x ldv, row-major (ldv >= max_ncv + 1)

@@ -13,6 +13,8 @@ Drop-in for the reference package of the same name:
 * ``gpu_eigsh.imgp`` — ``make_imgp_precision_matvec``.
 * ``differentiable_eigsh`` — eigenpairs as a torch.autograd.Function with the
   implicit-differentiation backward (``gpu_eigsh.differentiable``).
+* ``funm_apply`` / ``funm_qform`` — f(A) v and v^T f(A) v by m-step Lanczos
+  quadrature (numpy in, numpy out).
 
 All arithmetic runs in the CUDA library ``_lib/liblanczos_b200.so``; there is
 no CPU fallback.
@@ -24,7 +26,58 @@ import numpy as np
 from . import _native
 from ._native import LanczosError
 
-__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence", "differentiable_eigsh"]
+__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence", "differentiable_eigsh", "funm_apply",
+           "funm_qform"]
+
+_FUNM_MSG = {-1: "unknown func", -2: "invalid eigenvalue for func", -3: "zero input vector",
+             -4: "tridiag eigensolver failure"}
+
+
+def _funm(A, v, m, func, mode, name):
+    import scipy.sparse as sp
+
+    if not sp.issparse(A):
+        raise TypeError("A must be a scipy sparse matrix")
+    if A.shape[0] != A.shape[1]:
+        raise ValueError(f"Matrix must be square, got {A.shape}")
+    n = A.shape[0]
+    vv = np.ascontiguousarray(v, dtype=np.float64).reshape(-1)
+    if vv.shape[0] != n:
+        raise ValueError(f"v must have length {n}, got {vv.shape[0]}")
+    code = _native.FUNCS.get(func)
+    if code is None:
+        raise RuntimeError(f"{name} failed: {_FUNM_MSG[-1]}")
+    m = min(int(m), n)
+    if m < 1 or m > 127:
+        raise ValueError("m must be between 1 and 127 (the Lanczos depth of one plan)")
+    y = np.zeros(n) if mode == 1 else None
+    val = _native.C.c_double(0.0)
+    ma = _native.C.c_int(0)
+    with EigshPlan(A, max_ncv=m) as plan:
+        _native.check(_native.lib.lg_eigsh_plan_funm(plan._plan, _native.ptr(vv), 0, m, code, mode,
+                                                     _native.ptr(y) if y is not None else None,
+                                                     _native.C.byref(val), _native.C.byref(ma)))
+    rc = int(ma.value)
+    if rc < 0:
+        raise RuntimeError(f"{name} failed: {_FUNM_MSG.get(rc, rc)}")
+    return (y if mode == 1 else float(val.value)), rc
+
+
+def funm_apply(A, v, m=50, func="log"):
+    """y ~ f(A) v by m-step Lanczos quadrature (f in log, exp, sqrt, inv).
+
+    A: scipy sparse symmetric (n x n); v: (n,).  Returns (y, m_actual),
+    m_actual < m when the Krylov space is exhausted.  Raises RuntimeError with
+    the reference's messages (unknown func, invalid eigenvalue for func, zero
+    input vector).  Same call as the reference's gpu_eigsh.funm_apply
+    (python/gpu_eigsh/__init__.py:72-115); m <= 127 here.
+    """
+    return _funm(A, v, m, func, 1, "funm_apply")
+
+
+def funm_qform(A, v, m=50, func="log"):
+    """v^T f(A) v by m-step Lanczos quadrature; returns (value, m_actual)."""
+    return _funm(A, v, m, func, 0, "funm_qform")
 
 
 def differentiable_eigsh(*args, **kwargs):

@@ -147,6 +147,10 @@ SIGNATURES = {
     "lg_outer_accumulate": (_I, [_I, _I, _V, _V, _I, _V, _V]),
     "lg_eigsh_adjoint": (_I, [_I, C.c_longlong, _V, _V, _V, _I, _V, _V, _V, _V, _V, _I, C.c_double, _PI, _V]),
     "compute_adjoint_eigsh": (_I, [_I, _I, _PI, _PI, _PD, _I, _PD, _PD, _PD, _PD, _PD, _I, C.c_double]),
+    "lg_eigsh_plan_funm": (_I, [_V, _V, _I, _I, _I, _I, _V, _PD, _PI]),
+    "compute_funm_apply": (_I, [_I, _I, _PI, _PI, _PD, _PD, _I, C.c_char_p, _PD]),
+    "compute_funm_qform": (_I, [_I, _I, _PI, _PI, _PD, _PD, _I, C.c_char_p, _PD]),
+    "compute_funm_debug": (_I, [_I, _I, _PI, _PI, _PD, _PD, _I, _PD, _PD, _PD]),
     "lg_status_string": (C.c_char_p, [C.c_int]),
     "lg_last_error": (C.c_int, [C.c_char_p, C.c_int]),
     "compute_eigsh": (C.c_int, [C.c_int, C.c_int, _PI, _PI, _PD, C.c_int, C.c_int, C.c_int, C.c_double, _PD,

@@ -96,6 +96,27 @@ class _DifferentiableEigsh(torch.autograd.Function):
         return (grad.to(ctx.vdev, ctx.vdtype), None, None, None, None, None, None, None, None, None, None)
 
 
+def _direct_values(A: torch.Tensor) -> torch.Tensor:
+    """A.values(), connected to the autograd graph past the sparse constructor.
+
+    torch's backward of torch.sparse_csr_tensor(crow, col, values) forms the
+    gradient of A densely (n x n: 8 TB at n = 1e6) before sampling it at the
+    stored entries.  When A comes straight from that constructor, its saved
+    `values` input is returned instead, so the gradient flows to it entry by
+    entry; otherwise (or if this torch build names things differently) A.values().
+    """
+    vals = A.values()
+    node = A.grad_fn
+    if node is not None and type(node).__name__.startswith("SparseCompressedTensorBackward"):
+        try:
+            saved = node._saved_values
+        except (AttributeError, RuntimeError):
+            return vals
+        if isinstance(saved, torch.Tensor) and saved.shape == vals.shape and saved.data_ptr() == vals.data_ptr():
+            return saved
+    return vals
+
+
 def differentiable_eigsh(A, k=20, ncv=0, maxiter=3000, tol=1e-12, sigma=None, cg_max_iters=500, cg_tol=1e-10):
     """k eigenpairs of a symmetric sparse matrix with gradients to its values.
 
@@ -109,7 +130,7 @@ def differentiable_eigsh(A, k=20, ncv=0, maxiter=3000, tol=1e-12, sigma=None, cg
     """
     if isinstance(A, torch.Tensor):
         if A.layout == torch.sparse_csr:
-            crow, col, values = A.crow_indices(), A.col_indices(), A.values()
+            crow, col, values = A.crow_indices(), A.col_indices(), _direct_values(A)
         elif A.is_sparse:
             Acsr = A.coalesce().to_sparse_csr()
             crow, col, values = Acsr.crow_indices(), Acsr.col_indices(), Acsr.values()

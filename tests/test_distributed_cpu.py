@@ -135,3 +135,26 @@ def test_permute_symmetric_matches_scipy():
     np.testing.assert_array_equal(ci.numpy(), P.indices)
     np.testing.assert_array_equal(va.numpy(), P.data)
     np.testing.assert_array_equal(pos.numpy()[perm.numpy()], np.arange(L.shape[0]))
+
+
+def test_differentiable_values_bypass_dense_gradient():
+    """The values of a torch sparse CSR tensor reach differentiable_eigsh
+    without torch's dense n x n gradient of the sparse constructor (checked on
+    CPU: the routing only, no eigensolve)."""
+    import warnings
+
+    from gpu_eigsh.differentiable import _direct_values
+
+    warnings.filterwarnings("ignore")
+    n = 50
+    crow = torch.arange(0, n + 1)
+    col = torch.arange(n)
+    leaf = torch.ones(n, dtype=torch.float64, requires_grad=True)
+    vals = leaf * 3.0
+    A = torch.sparse_csr_tensor(crow, col, vals, (n, n))
+    v = _direct_values(A)
+    assert v is vals
+    (v * 2.0).sum().backward()
+    assert torch.equal(leaf.grad, torch.full((n,), 6.0, dtype=torch.float64))
+    B = torch.sparse_csr_tensor(crow, col, torch.ones(n, dtype=torch.float64), (n, n))
+    assert torch.equal(_direct_values(B), B.values())
