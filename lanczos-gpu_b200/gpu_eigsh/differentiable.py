@@ -46,6 +46,13 @@ def _cuda_device(t: torch.Tensor) -> torch.device:
     return t.device if t.is_cuda else torch.device("cuda", torch.cuda.current_device())
 
 
+# From this many rows on, the matrix is renumbered by BFS level for the
+# solve and the backward: the block of k gathered columns (n x k doubles) no
+# longer fits in L2, and in a random vertex order every gather of the sparse
+# products would go to DRAM.
+REORDER_MIN_ROWS = 1 << 16
+
+
 class _DifferentiableEigsh(torch.autograd.Function):
     @staticmethod
     def forward(ctx, values, crow, col, n, k, ncv, maxiter, tol, sigma, cg_max_iters, cg_tol):
@@ -56,6 +63,18 @@ class _DifferentiableEigsh(torch.autograd.Function):
         ci = col.detach().to(dev, torch.int32).contiguous()
         va = values.detach().to(dev, torch.float64).contiguous()
         nnz = int(ci.numel())
+        perm = order = pos = None
+        if int(n) >= REORDER_MIN_ROWS and nnz > 0:
+            # the renumbering walks the graph: check the CSR first (the plan
+            # checks it again on its own)
+            if (rp.numel() != int(n) + 1 or int(rp[0]) != 0 or int(rp[-1]) != nnz or bool((rp[1:] < rp[:-1]).any())
+                    or int(ci.min()) < 0 or int(ci.max()) >= int(n)):
+                raise ValueError("malformed CSR (row pointers or column indices)")
+            from .ordering import bfs_order, permute_symmetric
+
+            with torch.cuda.device(dev):
+                perm = bfs_order(rp, ci)
+                rp, ci, va, pos, order = permute_symmetric(rp, ci, va, perm, return_order=True)
         with torch.cuda.device(dev):
             torch.cuda.current_stream(dev).synchronize()   # the plan copies the CSR on its own stream
             plan = EigshPlan(None, max_ncv=max(int(ncv), 2),
@@ -73,9 +92,11 @@ class _DifferentiableEigsh(torch.autograd.Function):
                 plan.close()
         evals = torch.from_numpy(np.ascontiguousarray(w)).to(dev)
         ctx.save_for_backward(evals, Y, va, rp, ci)
+        ctx.perm, ctx.order = perm, order
         ctx.n, ctx.k, ctx.cg = int(n), int(k), (int(cg_max_iters), float(cg_tol))
         ctx.vdev, ctx.vdtype = values.device, values.dtype
-        return evals.to(values.device), Y.to(values.device)
+        Yc = Y if pos is None else Y.index_select(0, pos)   # rows back in the caller's numbering
+        return evals.to(values.device), Yc.to(values.device)
 
     @staticmethod
     def backward(ctx, g_evals, g_evecs):
@@ -83,7 +104,10 @@ class _DifferentiableEigsh(torch.autograd.Function):
         dev = va.device
         n, k = ctx.n, ctx.k
         ge = None if g_evals is None else g_evals.detach().to(dev, torch.float64).contiguous()
-        gv = None if g_evecs is None else g_evecs.detach().to(dev, torch.float64).contiguous()
+        gv = None if g_evecs is None else g_evecs.detach().to(dev, torch.float64)
+        if gv is not None and ctx.perm is not None:
+            gv = gv.index_select(0, ctx.perm)   # into the solve's numbering
+        gv = None if gv is None else gv.contiguous()
         grad = torch.empty(va.numel(), dtype=torch.float64, device=dev)
         iters = (C.c_int * k)()
         with torch.cuda.device(dev):
@@ -93,6 +117,10 @@ class _DifferentiableEigsh(torch.autograd.Function):
                 ge.data_ptr() if ge is not None else None, gv.data_ptr() if gv is not None else None,
                 grad.data_ptr(), ctx.cg[0], ctx.cg[1], iters, stream))
         ctx.cg_iters = list(iters)
+        if ctx.order is not None:   # entries back in the caller's storage order
+            g2 = torch.empty_like(grad)
+            g2[ctx.order] = grad
+            grad = g2
         return (grad.to(ctx.vdev, ctx.vdtype), None, None, None, None, None, None, None, None, None, None)
 
 

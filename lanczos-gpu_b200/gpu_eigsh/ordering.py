@@ -53,10 +53,12 @@ def bfs_order(rowptr: torch.Tensor, col: torch.Tensor) -> torch.Tensor:
     return torch.argsort(level * n + torch.arange(n, device=rowptr.device))
 
 
-def permute_symmetric(rowptr: torch.Tensor, col: torch.Tensor, val: torch.Tensor, perm: torch.Tensor):
+def permute_symmetric(rowptr: torch.Tensor, col: torch.Tensor, val: torch.Tensor, perm: torch.Tensor,
+                      return_order: bool = False):
     """P A P^T of a CSR (row i of the result = row perm[i] of A, columns
     renumbered by pos = perm^-1 and sorted).  Returns (rowptr int32, col
-    int32, val, pos int64) on the device of the inputs."""
+    int32, val, pos int64) on the device of the inputs, and with return_order
+    also `order` (int64): entry j of the result is entry order[j] of A."""
     n = rowptr.numel() - 1
     dev = rowptr.device
     perm = perm.to(dev, torch.int64)
@@ -71,4 +73,5 @@ def permute_symmetric(rowptr: torch.Tensor, col: torch.Tensor, val: torch.Tensor
     new_counts = counts[perm]
     out_rp = torch.zeros(n + 1, dtype=torch.int32, device=dev)
     out_rp[1:] = torch.cumsum(new_counts, 0).to(torch.int32)
-    return out_rp, c_new[order].to(torch.int32).contiguous(), val[order].contiguous(), pos
+    out = (out_rp, c_new[order].to(torch.int32).contiguous(), val[order].contiguous(), pos)
+    return out + (order,) if return_order else out
