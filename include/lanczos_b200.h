@@ -99,14 +99,15 @@ int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* 
                          int mixed);
 
 /* lg_eigsh_plan_create with flags.  LG_PLAN_REORDER_BFS renumbers the rows
- * inside the plan by breadth-first level from a pseudo-peripheral vertex
- * (the matrix pattern must be symmetric), so that the gathers of the sparse
- * product stay in L2 for graphs whose input numbering has no locality (the
- * kNN graph of randomly ordered points).  The caller sees its own numbering
- * everywhere: v0, the eigenvectors and lg_eigsh_plan_matvec are mapped
- * through the permutation; the eigenvalues are those of the same matrix.
- * Creation costs two BFS sweeps (a few tens of ms at n = 1e6), so the flag
- * pays off for plans that solve more than once. */
+ * inside the plan in Cuthill-McKee order (BFS levels from a
+ * pseudo-peripheral vertex, each level in the order of the vertices that found
+ * it; the matrix pattern must be symmetric), so that the gathers of the sparse
+ * product stay in L1 / L2 for graphs whose input numbering has no locality
+ * (the kNN graph of randomly ordered points).  The caller sees its own
+ * numbering everywhere: v0, the eigenvectors and lg_eigsh_plan_matvec are
+ * mapped through the permutation; the eigenvalues are those of the same
+ * matrix.  Creation computes the order on the host (a few hundred ms at
+ * n = 1e6), so the flag pays off for plans that solve more than once. */
 #define LG_PLAN_REORDER_BFS 1
 int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr,
                             const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
@@ -328,6 +329,14 @@ int lg_imgp_laplacian(int n, long long nnz, const int* rowptr, const int* col, i
  * which keeps the caller's order). */
 int lg_graph_bfs_levels(int n, const int* rowptr, const int* col, int start, int* level, int* work, int* nlevels,
                         void* stream);
+
+/* Cuthill-McKee order of the graph of a HOST CSR (every edge stored both
+ * ways): perm[new] = old, n ints.  Each connected component starts from a
+ * pseudo-peripheral vertex; inside a BFS level the vertices follow the order
+ * of their discoverers, unvisited neighbours by increasing degree.  Orders the
+ * rows of the SLQ operator and of large differentiable-eigsh matrices so that
+ * consecutive rows gather neighbouring rows (no counterpart in the reference). */
+int lg_graph_cm_order(int n, const int* rowptr, const int* col, int* perm);
 
 /* y = A x for a dense row-major n x n A (vectors with element strides ldx, ldy),
  * and gA += lam x^T (fp64 gA, vectors with element stride ld): the dense-matrix

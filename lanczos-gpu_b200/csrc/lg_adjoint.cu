@@ -274,159 +274,6 @@ adj_gram_kernel(int n, int ld, const double* __restrict__ X, const double* __res
   for (int i = t; i < kGramChunk; i += kDT) part[(size_t)blockIdx.x * kGramChunk + i] = red[i];
 }
 
-// ---------------------------------------------------------------------------
-// ld <= 32: the Gram and the deflation in the row-lane layout (16 lanes per
-// row, lane l owning columns 2l and 2l + 1, 16-byte accesses as the other
-// row kernels).  The X row is broadcast across its 16 lanes by shuffles
-// (X[row, a] lives in lane a / 2), so every lane forms its two columns of
-// X^T R (Gram) or of X D (deflation) with D's two columns in registers.
-// ---------------------------------------------------------------------------
-constexpr int kRlLanes = 16;
-constexpr int kRlMaxLd = 24;   // D's columns in registers: 2 x ld doubles per lane (ld = 32 spills)
-
-template <int KA>
-__global__ void __launch_bounds__(kT, 1)
-adj_gram_rl_kernel(int n, const double* __restrict__ X, const double* __restrict__ B, double* __restrict__ part,
-                   const int* __restrict__ active) {
-  if (active && *active == 0) return;
-  using G = RowLanes<double, kRlLanes>;
-  __shared__ double red[KA * KA];
-  const G g;
-  const int t = threadIdx.x, warp = t >> 5;
-  const int c0 = 2 * g.l;
-  const bool mine = c0 < KA;
-  const int base = g.lane - g.l;
-  for (int i = t; i < KA * KA; i += kT) red[i] = 0.0;
-  double acc0[KA], acc1[KA];   // D[a][c0], D[a][c0 + 1]
-#pragma unroll
-  for (int a = 0; a < KA; ++a) acc0[a] = acc1[a] = 0.0;
-  for (long long wrow = g.first_warp_row(); wrow < n; wrow += G::stride()) {
-    const long long row = wrow + g.sub;
-    double2 xv = make_double2(0.0, 0.0), bv = make_double2(0.0, 0.0);
-    if (row < n && mine) {
-      xv = __ldg(reinterpret_cast<const double2*>(X + row * KA + c0));
-      bv = *reinterpret_cast<const double2*>(B + row * KA + c0);
-    }
-#pragma unroll
-    for (int a = 0; a < KA; a += 2) {
-      const double xa = __shfl_sync(kFull, xv.x, base + a / 2);
-      const double xb = __shfl_sync(kFull, xv.y, base + a / 2);
-      acc0[a] += xa * bv.x;
-      acc1[a] += xa * bv.y;
-      acc0[a + 1] += xb * bv.x;
-      acc1[a + 1] += xb * bv.y;
-    }
-  }
-  // the two row groups of the warp, then the warps in order
-#pragma unroll
-  for (int a = 0; a < KA; ++a) {
-    acc0[a] += __shfl_xor_sync(kFull, acc0[a], kRlLanes);
-    acc1[a] += __shfl_xor_sync(kFull, acc1[a], kRlLanes);
-  }
-  __syncthreads();
-  for (int w = 0; w < kW; ++w) {
-    if (warp == w && g.sub == 0 && mine) {
-#pragma unroll
-      for (int a = 0; a < KA; ++a) {
-        red[a * KA + c0] += acc0[a];
-        red[a * KA + c0 + 1] += acc1[a];
-      }
-    }
-    __syncthreads();
-  }
-  for (int i = t; i < KA * KA; i += kT)
-    part[(size_t)blockIdx.x * kGramChunk + (i / KA) * kGramTile + (i % KA)] = red[i];
-}
-
-// MODE 0: R -= X D with the convergence prologue and P = R + beta P;
-// MODE 1: B -= X D.  (As adj_deflate_kernel, in the row-lane layout.)
-template <int MODE, int KA>
-__global__ void __launch_bounds__(kT, 1)
-adj_deflate_rl_kernel(int n, int k, int it, int max_iters, const double* __restrict__ X, double* __restrict__ B,
-                      double* __restrict__ P, State s) {
-  if (*s.active == 0) return;
-  using G = RowLanes<double, kRlLanes>;
-  __shared__ double s_beta[kMaxB];
-  __shared__ int s_upd[kMaxB];
-  __shared__ int s_run;
-  const G g;
-  const int t = threadIdx.x;
-  if (MODE == 0) {
-    if (t == 0) s_run = 0;
-    __syncthreads();
-    for (int c = t; c < KA; c += kT) {
-      double beta = 0.0;
-      int upd = 0;
-      if (c < k && s.done[c] == 0) {
-        double dn = 0.0;
-        for (int a = 0; a < k; ++a) {
-          const double d = s.D[(size_t)a * kDStride + c];
-          dn += d * d;
-        }
-        const double rr_new = fmax(s.rraw[c] - dn, 0.0);
-        if (rr_new < s.tol2[c]) {
-          if (blockIdx.x == 0) {
-            s.done[c] = 1;
-            s.iters[c] = it + 1;
-          }
-        } else if (it + 1 >= max_iters) {
-          if (blockIdx.x == 0) {
-            s.done[c] = 2;
-            s.iters[c] = -max_iters;
-          }
-        } else {
-          beta = rr_new / s.rr[(it & 1) * kMaxB + c];
-          upd = 1;
-          if (blockIdx.x == 0) s.rr[((it + 1) & 1) * kMaxB + c] = rr_new;
-          atomicAdd(&s_run, 1);
-        }
-      }
-      s_beta[c] = beta;
-      s_upd[c] = upd;
-    }
-  }
-  __syncthreads();
-  if (MODE == 0 && blockIdx.x == 0 && t == 0) *s.active = s_run;
-  const int c0 = 2 * g.l;
-  const bool mine = c0 < KA;
-  const int base = g.lane - g.l;
-  double d0[KA], d1[KA];
-#pragma unroll
-  for (int a = 0; a < KA; ++a) {
-    d0[a] = mine ? s.D[(size_t)a * kDStride + c0] : 0.0;
-    d1[a] = mine ? s.D[(size_t)a * kDStride + c0 + 1] : 0.0;
-  }
-  const double be0 = (MODE == 0 && mine) ? s_beta[c0] : 0.0, be1 = (MODE == 0 && mine) ? s_beta[c0 + 1] : 0.0;
-  const bool up0 = MODE == 0 && mine && s_upd[c0], up1 = MODE == 0 && mine && s_upd[c0 + 1];
-  for (long long wrow = g.first_warp_row(); wrow < n; wrow += G::stride()) {
-    const long long row = wrow + g.sub;
-    const bool ok = row < n && mine;
-    double2 xv = make_double2(0.0, 0.0);
-    if (ok) xv = __ldg(reinterpret_cast<const double2*>(X + row * KA + c0));
-    double y0 = 0.0, y1 = 0.0;
-#pragma unroll
-    for (int a = 0; a < KA; a += 2) {
-      const double xa = __shfl_sync(kFull, xv.x, base + a / 2);
-      const double xb = __shfl_sync(kFull, xv.y, base + a / 2);
-      y0 += xa * d0[a] + xb * d0[a + 1];
-      y1 += xa * d1[a] + xb * d1[a + 1];
-    }
-    if (!ok) continue;
-    double2* bp = reinterpret_cast<double2*>(B + row * KA + c0);
-    double2 v = *bp;
-    v.x -= y0;
-    v.y -= y1;
-    *bp = v;
-    if (MODE == 0) {
-      double2* pp = reinterpret_cast<double2*>(P + row * KA + c0);
-      double2 pv = *pp;
-      if (up0) pv.x = v.x + be0 * pv.x;
-      if (up1) pv.y = v.y + be1 * pv.y;
-      *pp = pv;
-    }
-  }
-}
-
 // D[a0 + a][b0 + b] = sum over the CTA rows of part, in CTA order: one warp
 // per entry (lanes take every 32nd row, then a fixed shuffle tree).
 __global__ void adj_gram_reduce_kernel(const double* __restrict__ part, int nparts, int a0, int na, int b0, int nb,
@@ -690,7 +537,7 @@ cudaError_t pool_for(int dev, cudaMemPool_t* out) {
 }
 
 struct Work {
-  int n, k, ld, grid_rl, grid_rl1, grid_gram, grid_defl;   // grid_rl1: one CTA of 512 per SM
+  int n, k, ld, grid_rl, grid_gram, grid_defl;
   double *X, *P, *AP, *Xi, *R;
   double* part;          // max(grid_rl * kRowStride, grid_gram * kGramChunk)
   ColSum cs_pap, cs_rr, cs_nrm;
@@ -737,18 +584,6 @@ size_t carve(char* base, Work& w) {
 
 template <int MODE>
 cudaError_t launch_deflate(const Work& w, int it, int max_iters, double* B, cudaStream_t st) {
-  if (w.ld <= kRlMaxLd) {
-    constexpr int M = MODE == 0 ? 0 : 1;
-#define LG_DRL(KA) \
-  adj_deflate_rl_kernel<M, KA><<<w.grid_rl1, kT, 0, st>>>(w.n, w.k, it, max_iters, w.X, B, w.P, w.s)
-    switch (w.ld) {
-      case 8: LG_DRL(8); break;
-      case 16: LG_DRL(16); break;
-      default: LG_DRL(24); break;
-    }
-#undef LG_DRL
-    return cudaGetLastError();
-  }
   const size_t smem = sizeof(double) * (size_t)w.ld * w.ld;
   static bool attr = false;
   if (!attr) {
@@ -763,17 +598,6 @@ cudaError_t launch_deflate(const Work& w, int it, int max_iters, double* B, cuda
 
 // D = X^T B over every 32 x 32 chunk of (ld x ld).
 cudaError_t gram(const Work& w, const double* B, const int* active, cudaStream_t st) {
-  if (w.ld <= kRlMaxLd) {
-    switch (w.ld) {
-      case 8: adj_gram_rl_kernel<8><<<w.grid_rl1, kT, 0, st>>>(w.n, w.X, B, w.part, active); break;
-      case 16: adj_gram_rl_kernel<16><<<w.grid_rl1, kT, 0, st>>>(w.n, w.X, B, w.part, active); break;
-      default: adj_gram_rl_kernel<24><<<w.grid_rl1, kT, 0, st>>>(w.n, w.X, B, w.part, active); break;
-    }
-    const int entries = w.ld * w.ld;
-    adj_gram_reduce_kernel<<<(entries * 32 + 255) / 256, 256, 0, st>>>(w.part, w.grid_rl1, 0, w.ld, 0, w.ld, w.s.D,
-                                                                       active);
-    return cudaGetLastError();
-  }
   for (int a0 = 0; a0 < w.ld; a0 += kGramTile) {
     const int ta = std::min(4, (w.ld - a0) / 8);
     for (int b0 = 0; b0 < w.ld; b0 += kGramTile) {
@@ -878,7 +702,6 @@ extern "C" int lg_eigsh_adjoint(int n, long long nnz, const int* rowptr, const i
   w.ld = (k + 7) / 8 * 8;
   w.grid_rl = 2 * sms;   // the row kernels are built for 2 CTAs of 512 threads per SM
   w.grid_gram = 2 * sms;
-  w.grid_rl1 = sms;
   w.grid_defl = 4 * sms;
   void* base = nullptr;
   cudaMemPool_t pool = nullptr;

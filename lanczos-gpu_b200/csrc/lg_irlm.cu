@@ -330,51 +330,30 @@ __global__ void scatter_perm_kernel(double* __restrict__ out, const double* __re
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[perm[i]] = in[i];
 }
 
-// Renumbers the rows by breadth-first level from a pseudo-peripheral vertex
-// (two sweeps of lg_graph_bfs_levels; ties by index, unreachable vertices
-// last) so that neighbouring rows get nearby numbers and the gathers of the
-// sparse product hit L2.  The plan keeps perm (plan row -> caller row): v0 is
+// Renumbers the rows in Cuthill-McKee order (BFS levels from a
+// pseudo-peripheral vertex, each level in the order of the vertices that
+// found it; lg_graph_cm_order on the host) so that neighbouring rows get
+// nearby numbers and the gathers of the sparse product hit L1 / L2.  The plan keeps perm (plan row -> caller row): v0 is
 // gathered through it and the Ritz vectors are written through it, so the
 // caller sees its own numbering.  hrp (host row pointer) becomes the new one.
 int Solver::reorder_bfs(std::vector<int>& hrp) {
-  int* d_level = nullptr;
-  int* d_work = nullptr;
-  LG_TRY(cudaMalloc(&d_level, sizeof(int) * (size_t)n));
-  cudaError_t e = cudaMalloc(&d_work, sizeof(int) * (2 * (size_t)n + 2));
-  if (e != cudaSuccess) {
-    cudaFree(d_level);
-    LG_TRY(e);
+  // Cuthill-McKee order on the host (lg_graph_cm_order) from the column
+  // indices already on the device
+  std::vector<int> hcol((size_t)std::max<long long>(nnz, 1));
+  if (nnz > 0) {
+    LG_TRY(cudaMemcpyAsync(hcol.data(), d_col, sizeof(int) * (size_t)nnz, cudaMemcpyDeviceToHost, stream));
+    LG_TRY(cudaStreamSynchronize(stream));
   }
-  std::vector<int> lev((size_t)n);
-  int start = 0, rounds = 0, rc = LG_OK;
-  for (int sweep = 0; sweep < 2 && rc == LG_OK; ++sweep) {
-    rc = lg_graph_bfs_levels(n, d_rowptr, d_col, start, d_level, d_work, &rounds, stream);
-    if (rc != LG_OK) break;
-    e = cudaMemcpyAsync(lev.data(), d_level, sizeof(int) * (size_t)n, cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) {
-      set_error("CUDA error %s at lg_irlm.cu:%d", cudaGetErrorString(e), __LINE__);
-      rc = LG_ERR_CUDA;
-      break;
-    }
-    if (sweep == 0) start = (int)(std::max_element(lev.begin(), lev.end()) - lev.begin());
-  }
-  cudaFree(d_level);
-  cudaFree(d_work);
-  if (rc != LG_OK) return rc;
-  // counting sort by level, stable in the vertex index
-  const int maxl = std::max(0, *std::max_element(lev.begin(), lev.end()));
-  std::vector<long long> bucket((size_t)maxl + 3, 0);
-  for (int v = 0; v < n; ++v) ++bucket[(size_t)(lev[v] < 0 ? maxl + 1 : lev[v]) + 1];
-  for (size_t b = 1; b < bucket.size(); ++b) bucket[b] += bucket[b - 1];
   std::vector<int> perm((size_t)n), pos((size_t)n), nrp((size_t)n + 1);
-  for (int v = 0; v < n; ++v) perm[(size_t)bucket[(size_t)(lev[v] < 0 ? maxl + 1 : lev[v])]++] = v;
+  int rc = lg_graph_cm_order(n, hrp.data(), hcol.data(), perm.data());
+  if (rc != LG_OK) return rc;
   for (int i = 0; i < n; ++i) pos[(size_t)perm[i]] = i;
   nrp[0] = 0;
   for (int i = 0; i < n; ++i) nrp[(size_t)i + 1] = nrp[i] + (hrp[(size_t)perm[i] + 1] - hrp[perm[i]]);
 
   int *d_pos = nullptr, *rp2 = nullptr, *col2 = nullptr;
   double* val2 = nullptr;
+  cudaError_t e = cudaSuccess;
   LG_TRY(cudaMalloc(&d_perm, sizeof(int) * (size_t)n));
   LG_TRY(cudaMalloc(&d_pos, sizeof(int) * (size_t)n));
   e = cudaMalloc(&rp2, sizeof(int) * ((size_t)n + 1));

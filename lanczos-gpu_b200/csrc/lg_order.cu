@@ -99,3 +99,81 @@ extern "C" int lg_graph_bfs_levels(int n, const int* rowptr, const int* col, int
   }
   return LG_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Cuthill-McKee order (host).  Inside every BFS level the vertices follow the
+// order of the vertices that discovered them (neighbours by increasing
+// degree), so consecutive rows have neighbours that are themselves close
+// together: a warp's gathers hit the same L1 lines and the rows of a CTA
+// touch a narrow window of the block.  Each connected component starts from a
+// pseudo-peripheral vertex (the last vertex reached by a BFS from its
+// lowest-numbered vertex); components follow one another in order of that
+// lowest vertex.
+// ---------------------------------------------------------------------------
+#include <algorithm>
+#include <vector>
+
+extern "C" int lg_graph_cm_order(int n, const int* rowptr, const int* col, int* perm) {
+  if (n < 1 || !rowptr || !perm || (rowptr[n] > 0 && !col) || rowptr[0] != 0) {
+    g_last_error = "lg_graph_cm_order: invalid arguments";
+    return LG_ERR_INVALID;
+  }
+  for (int v = 0; v < n; ++v)
+    if (rowptr[v + 1] < rowptr[v]) {
+      g_last_error = "lg_graph_cm_order: row_ptr is not monotone";
+      return LG_ERR_INVALID;
+    }
+  const long long nnz = rowptr[n];
+  for (long long k = 0; k < nnz; ++k)
+    if (col[k] < 0 || col[k] >= n) {
+      g_last_error = "lg_graph_cm_order: column index out of range";
+      return LG_ERR_INVALID;
+    }
+  std::vector<int> stamp((size_t)n, -1);   // BFS of the component search
+  std::vector<char> placed((size_t)n, 0);
+  std::vector<int> queue;
+  queue.reserve((size_t)n);
+  std::vector<int> nb;
+  auto degree = [&](int v) { return rowptr[v + 1] - rowptr[v]; };
+  int pos = 0, comp = 0;
+  for (int root = 0; root < n; ++root) {
+    if (placed[root]) continue;
+    // pseudo-peripheral start: the last vertex a BFS from `root` reaches
+    queue.clear();
+    queue.push_back(root);
+    stamp[root] = comp;
+    for (size_t h = 0; h < queue.size(); ++h) {
+      const int u = queue[h];
+      for (int k = rowptr[u]; k < rowptr[u + 1]; ++k) {
+        const int v = col[k];
+        if (stamp[v] != comp && !placed[v]) {
+          stamp[v] = comp;
+          queue.push_back(v);
+        }
+      }
+    }
+    const int start = queue.back();
+    ++comp;
+    // Cuthill-McKee from `start`
+    const int first = pos;
+    perm[pos++] = start;
+    placed[start] = 1;
+    for (int h = first; h < pos; ++h) {
+      const int u = perm[h];
+      nb.clear();
+      for (int k = rowptr[u]; k < rowptr[u + 1]; ++k) {
+        const int v = col[k];
+        if (!placed[v]) {
+          placed[v] = 1;
+          nb.push_back(v);
+        }
+      }
+      std::sort(nb.begin(), nb.end(), [&](int a, int b) {
+        const int da = degree(a), db = degree(b);
+        return da != db ? da < db : a < b;
+      });
+      for (int v : nb) perm[pos++] = v;
+    }
+  }
+  return pos == n ? LG_OK : LG_ERR_NUMERIC;
+}

@@ -143,6 +143,7 @@ SIGNATURES = {
     "lg_slq_block_start_grad": (_I, [_I, _I, _I, _I, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
     "lg_imgp_laplacian": (_I, [_I, C.c_longlong, _V, _V, _I, _V, C.c_double, _I, _V, _V, _V, _V, _V, _V]),
     "lg_graph_bfs_levels": (_I, [_I, _V, _V, _I, _V, _V, _PI, _V]),
+    "lg_graph_cm_order": (_I, [_I, _PI, _PI, _PI]),
     "lg_dense_matvec": (_I, [_I, _I, _V, _V, _I, _V, _I, _V]),
     "lg_outer_accumulate": (_I, [_I, _I, _V, _V, _I, _V, _V]),
     "lg_eigsh_adjoint": (_I, [_I, C.c_longlong, _V, _V, _V, _I, _V, _V, _V, _V, _V, _I, C.c_double, _PI, _V]),

@@ -46,7 +46,7 @@ def _cuda_device(t: torch.Tensor) -> torch.device:
     return t.device if t.is_cuda else torch.device("cuda", torch.cuda.current_device())
 
 
-# From this many rows on, the matrix is renumbered by BFS level for the
+# From this many rows on, the matrix is renumbered (Cuthill-McKee) for the
 # solve and the backward: the block of k gathered columns (n x k doubles) no
 # longer fits in L2, and in a random vertex order every gather of the sparse
 # products would go to DRAM.
@@ -70,10 +70,10 @@ class _DifferentiableEigsh(torch.autograd.Function):
             if (rp.numel() != int(n) + 1 or int(rp[0]) != 0 or int(rp[-1]) != nnz or bool((rp[1:] < rp[:-1]).any())
                     or int(ci.min()) < 0 or int(ci.max()) >= int(n)):
                 raise ValueError("malformed CSR (row pointers or column indices)")
-            from .ordering import bfs_order, permute_symmetric
+            from .ordering import cm_order, permute_symmetric
 
             with torch.cuda.device(dev):
-                perm = bfs_order(rp, ci)
+                perm = cm_order(rp, ci)
                 rp, ci, va, pos, order = permute_symmetric(rp, ci, va, perm, return_order=True)
         with torch.cuda.device(dev):
             torch.cuda.current_stream(dev).synchronize()   # the plan copies the CSR on its own stream

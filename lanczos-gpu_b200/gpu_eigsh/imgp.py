@@ -73,8 +73,8 @@ class ImgpPrecisionMatvec:
         cols = torch.cat([idx[1], idx[0]])
         eid = torch.arange(M, device=dev).repeat(2)
         self.rowptr, self.col, self.d2 = self._csr(rows, cols, eid, d2)
-        # row order for locality of the neighbour gathers: BFS levels from a
-        # peripheral vertex; perm[new] = old, pos[old] = new
+        # row order for locality of the neighbour gathers: Cuthill-McKee from
+        # a peripheral vertex; perm[new] = old, pos[old] = new
         self.perm = self.pos = None
         if reorder and M:
             perm = self._bfs_order()
@@ -96,11 +96,13 @@ class ImgpPrecisionMatvec:
         return rowptr, cols[order].to(torch.int32).contiguous(), d2[eid[order]].contiguous()
 
     def _bfs_order(self) -> torch.Tensor:
-        """Vertices sorted by (BFS level from a pseudo-peripheral vertex, index);
-        unreachable vertices last."""
-        from .ordering import bfs_order
+        """Cuthill-McKee order of the graph (gpu_eigsh.ordering.cm_order):
+        BFS levels from a pseudo-peripheral vertex, each level in the order of
+        the vertices that found it (8-9 % faster SLQ products at n = 1e6 than
+        the levels alone)."""
+        from .ordering import cm_order
 
-        return bfs_order(self.rowptr, self.col)
+        return cm_order(self.rowptr, self.col)
 
     def to_internal(self, X: torch.Tensor) -> torch.Tensor:
         """Rows of X (caller's vertex order) in the operator's row order."""

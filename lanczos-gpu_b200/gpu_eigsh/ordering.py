@@ -2,8 +2,9 @@
 
 ``bfs_order`` numbers the vertices of the graph of a symmetric CSR by
 breadth-first level from a pseudo-peripheral vertex (two sweeps of
-lg_graph_bfs_levels on the GPU), ties broken by the old index: rows that are
-neighbours in the graph get nearby numbers, so
+lg_graph_bfs_levels on the GPU), ties broken by the old index; ``cm_order``
+(Cuthill-McKee, on the host) also orders each level by the vertices that
+found it.  Rows that are neighbours in the graph get nearby numbers, so
 
 * the sparse products of the SLQ operator gather from rows that a CTA's
   neighbours also read (L2 hits), and
@@ -22,7 +23,7 @@ import torch
 
 from . import _native
 
-__all__ = ["bfs_levels", "bfs_order", "permute_symmetric"]
+__all__ = ["bfs_levels", "bfs_order", "cm_order", "permute_symmetric"]
 
 
 def _stream(device):
@@ -51,6 +52,23 @@ def bfs_order(rowptr: torch.Tensor, col: torch.Tensor) -> torch.Tensor:
     level = bfs_levels(rowptr, col, start).to(torch.int64)
     level = torch.where(level < 0, torch.full_like(level, n), level)
     return torch.argsort(level * n + torch.arange(n, device=rowptr.device))
+
+
+def cm_order(rowptr: torch.Tensor, col: torch.Tensor) -> torch.Tensor:
+    """perm (int64, on rowptr's device): the Cuthill-McKee order of the graph
+    of a symmetric CSR (lg_graph_cm_order, computed on the host): BFS levels
+    as bfs_order, and inside a level the order of the vertices that found
+    them, so that consecutive rows also gather neighbouring rows."""
+    import numpy as np
+
+    n = rowptr.numel() - 1
+    rp = np.ascontiguousarray(rowptr.detach().cpu().numpy(), dtype=np.int32)
+    ci = np.ascontiguousarray(col.detach().cpu().numpy(), dtype=np.int32)
+    perm = np.empty(n, dtype=np.int32)
+    PI = _native.C.POINTER(_native.C.c_int)
+    _native.check(_native.lib.lg_graph_cm_order(n, rp.ctypes.data_as(PI), ci.ctypes.data_as(PI),
+                                                perm.ctypes.data_as(PI)))
+    return torch.from_numpy(perm.astype(np.int64)).to(rowptr.device)
 
 
 def permute_symmetric(rowptr: torch.Tensor, col: torch.Tensor, val: torch.Tensor, perm: torch.Tensor,
