@@ -330,6 +330,22 @@ int lg_imgp_laplacian(int n, long long nnz, const int* rowptr, const int* col, i
 int lg_graph_bfs_levels(int n, const int* rowptr, const int* col, int start, int* level, int* work, int* nlevels,
                         void* stream);
 
+/* Matrix Market files (host).  lg_mtx_read parses a `coordinate` file
+ * (real, integer or pattern; general, symmetric or skew-symmetric, mirrored
+ * entries added) on all host cores into a CSR held by the returned handle:
+ * 0-based, columns sorted inside each row, duplicate entries summed;
+ * lg_mtx_copy copies it out (row_ptr: nrows + 1, col and vals: nnz),
+ * lg_mtx_free releases it.  lg_mtx_write writes a CSR as `coordinate real
+ * general` (symmetric = 1: `symmetric`, lower triangle only), every value in
+ * the shortest form that reads back to the same double.  Replaces
+ * load_matrix_market / export_matrix_market (src/main.cu:129-244). */
+typedef struct lg_mtx lg_mtx;
+int lg_mtx_read(const char* path, lg_mtx** out, int* nrows, int* ncols, long long* nnz);
+int lg_mtx_copy(const lg_mtx* m, int* row_ptr, int* col, double* vals);
+int lg_mtx_free(lg_mtx* m);
+int lg_mtx_write(const char* path, int nrows, int ncols, const int* row_ptr, const int* col, const double* vals,
+                 int symmetric);
+
 /* Cuthill-McKee order of the graph of a HOST CSR (every edge stored both
  * ways): perm[new] = old, n ints.  Each connected component starts from a
  * pseudo-peripheral vertex; inside a BFS level the vertices follow the order
@@ -337,6 +353,35 @@ int lg_graph_bfs_levels(int n, const int* rowptr, const int* col, int start, int
  * rows of the SLQ operator and of large differentiable-eigsh matrices so that
  * consecutive rows gather neighbouring rows (no counterpart in the reference). */
 int lg_graph_cm_order(int n, const int* rowptr, const int* col, int* perm);
+
+/* Exact k nearest neighbours of n DEVICE points (row-major n x dim fp64),
+ * self excluded: out_idx (n x k int64) and out_d2 (n x k squared distances,
+ * sums of squared coordinate differences in coordinate order, no fused
+ * multiply-add), each row ascending by (distance, index) — the order of the
+ * reference driver's partial_sort over (dist2, j) pairs (src/main.cu:42-63),
+ * which replaces it, and of cKDTree.query in
+ * benchmark/generate_large_laplacian.py:36-44 up to exact ties.
+ * method: LG_KNN_AUTO (cells for dim <= 3, else brute), LG_KNN_CELLS (uniform
+ * cell grid, dim <= 3), LG_KNN_BRUTE (tiled all-pairs, dim <= 32).
+ * 1 <= k <= min(64, n - 1).  Synchronises `stream` once (coordinate bounds). */
+#define LG_KNN_AUTO 0
+#define LG_KNN_CELLS 1
+#define LG_KNN_BRUTE 2
+int lg_knn(int n, int dim, int k, const double* pts, long long* out_idx, double* out_d2, int method, void* stream);
+
+/* The kNN graph Laplacian L = D - A on the device, in two calls.
+ * A_ij = exp(-d2_ij / denom) for j in i's list or i in j's list (union
+ * symmetrisation: src/main.cu:65-74, the A.maximum(A.T) of
+ * benchmark/generate_large_laplacian.py:58); D_ii = sum_j A_ij summed in
+ * column order.  Rows hold their entries in ascending column order with the
+ * diagonal included (src/main.cu:76-107).  denom = 4 bw^2 gives both
+ * reference builders' weights.
+ * lg_knn_laplacian_rows: row_ptr (device, n + 1) and *nnz (host); checks that
+ *   every list holds distinct indices in [0, n) other than its row.
+ * lg_knn_laplacian_fill: col (nnz int32) and vals (nnz fp64) for that row_ptr. */
+int lg_knn_laplacian_rows(int n, int k, const long long* idx, int* rowptr, long long* nnz, void* stream);
+int lg_knn_laplacian_fill(int n, int k, const long long* idx, const double* d2, double denom, const int* rowptr,
+                          int* col, double* vals, void* stream);
 
 /* y = A x for a dense row-major n x n A (vectors with element strides ldx, ldy),
  * and gA += lam x^T (fp64 gA, vectors with element stride ld): the dense-matrix

@@ -24,6 +24,7 @@ LG_ERR_CG_NOCONV = -6
 WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
 EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
 LG_PLAN_REORDER_BFS = 1
+KNN_METHODS = {"auto": 0, "cells": 1, "brute": 2}
 
 
 class EigshOpts(C.Structure):
@@ -144,6 +145,13 @@ SIGNATURES = {
     "lg_imgp_laplacian": (_I, [_I, C.c_longlong, _V, _V, _I, _V, C.c_double, _I, _V, _V, _V, _V, _V, _V]),
     "lg_graph_bfs_levels": (_I, [_I, _V, _V, _I, _V, _V, _PI, _V]),
     "lg_graph_cm_order": (_I, [_I, _PI, _PI, _PI]),
+    "lg_mtx_read": (_I, [C.c_char_p, C.POINTER(C.c_void_p), _PI, _PI, C.POINTER(C.c_longlong)]),
+    "lg_mtx_copy": (_I, [_V, _PI, _PI, _PD]),
+    "lg_mtx_free": (_I, [_V]),
+    "lg_mtx_write": (_I, [C.c_char_p, _I, _I, _PI, _PI, _PD, _I]),
+    "lg_knn": (_I, [_I, _I, _I, _V, _V, _V, _I, _V]),
+    "lg_knn_laplacian_rows": (_I, [_I, _I, _V, _V, C.POINTER(C.c_longlong), _V]),
+    "lg_knn_laplacian_fill": (_I, [_I, _I, _V, _V, C.c_double, _V, _V, _V, _V]),
     "lg_dense_matvec": (_I, [_I, _I, _V, _V, _I, _V, _I, _V]),
     "lg_outer_accumulate": (_I, [_I, _I, _V, _V, _I, _V, _V]),
     "lg_eigsh_adjoint": (_I, [_I, C.c_longlong, _V, _V, _V, _I, _V, _V, _V, _V, _V, _I, C.c_double, _PI, _V]),
