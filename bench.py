@@ -495,6 +495,70 @@ def run_sinv(args, dev):
     return out
 
 
+GRAPH_N, GRAPH_DIM, GRAPH_K, GRAPH_BW, GRAPH_SEED = 100_000, 10, 15, 0.3, 123
+GRAPH_WORKLOAD = (f"kNN graph Laplacian of benchmark/generate_large_laplacian.py's defaults: n={GRAPH_N:,} points "
+                  f"RandomState({GRAPH_SEED}).random((n, {GRAPH_DIM})), k={GRAPH_K}, weights exp(-d^2/(4 bw^2)) "
+                  f"bw={GRAPH_BW}, A.maximum(A.T), L = D - A (exact neighbours, fp64)")
+
+
+def run_graph(args, dev, with_cpu):
+    """Graph construction on one GPU: lg_knn (all-pairs tiles at dim 10) and
+    the Laplacian assembly, points resident (value) and from host points to a
+    host CSR (e2e); the reference generator's cKDTree path timed on the host
+    as the CPU baseline (oracle/graph.py restates it)."""
+    import torch
+
+    from gpu_eigsh import graph as G
+
+    pts = G.generate_points(GRAPH_N, GRAPH_DIM, GRAPH_SEED)
+    P = torch.from_numpy(pts).to(dev)
+
+    def build():
+        idx, d2 = G.knn(P, GRAPH_K)
+        return G.laplacian_from_knn(idx, d2, GRAPH_BW)
+
+    for _ in range(2):
+        build()
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    reps, t_knn, t_all = 3, [], []
+    for _ in range(reps):
+        e[0].record()
+        idx, d2 = G.knn(P, GRAPH_K)
+        e[1].record()
+        rp, col, val = G.laplacian_from_knn(idx, d2, GRAPH_BW)
+        e[2].record()
+        torch.cuda.synchronize()
+        t_knn.append(e[0].elapsed_time(e[1]))
+        t_all.append(e[0].elapsed_time(e[2]))
+    nnz = int(rp[-1])
+    # end to end: host points in, host scipy CSR out
+    t0 = time.perf_counter()
+    L = G.generate_knn_laplacian(GRAPH_N, GRAPH_DIM, GRAPH_K, GRAPH_BW, GRAPH_SEED)
+    e2e_s = time.perf_counter() - t0
+    knn_ms = min(t_knn)
+    pairs = float(GRAPH_N) * (GRAPH_N - 1)
+    out = {"workload": GRAPH_WORKLOAD, "metric": "graph_build_s", "value": min(t_all) / 1000.0, "unit": "s",
+           "higher_is_better": False, "n": GRAPH_N, "nnz": nnz, "knn_ms": knn_ms,
+           "laplacian_ms": min(t_all) - knn_ms,
+           "knn_search": "all-pairs tiles (dim > 3), fp64, contraction-free distance sums",
+           "distance_pairs_per_s": pairs / (knn_ms / 1000.0),
+           "fp64_ops_per_s": pairs * GRAPH_DIM * 3 / (knn_ms / 1000.0),
+           "e2e": {"value": e2e_s, "unit": "s", "h2d_bytes": pts.nbytes, "d2h_bytes": int(L.data.nbytes +
+                                                                                            L.indices.nbytes +
+                                                                                            L.indptr.nbytes)},
+           "parallelism": "1 GPU"}
+    if with_cpu:
+        from oracle import graph as OG
+
+        t0 = time.perf_counter()
+        OG.generator_laplacian(GRAPH_N, GRAPH_DIM, GRAPH_K, GRAPH_BW, GRAPH_SEED)
+        out["cpu_baseline"] = {"value": time.perf_counter() - t0, "unit": "s", "cores": 1, "kind": "port",
+                               "sample": "the full workload: the generator's cKDTree build and query (one thread, as "
+                                         "the script calls it) and its scipy assembly"}
+    return out
+
+
 def run_knn_partitioned(args, L, v0, dev, world, rank):
     """Configuration 1 with its rows split over the ranks (strong scaling):
     the matrix renumbered by BFS level (gpu_eigsh.ordering) so that the row
@@ -705,6 +769,14 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps(out), flush=True)
         return 0
+    if args.only_graph:
+        out = run_graph(args, torch.device("cuda", local), with_cpu=not args.no_cpu_baseline) if rank == 0 else None
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return 0
     if args.only_sinv:
         out = run_sinv(args, torch.device("cuda", local)) if rank == 0 else None
         if world > 1:
@@ -845,6 +917,8 @@ def run_ours(args):
     if not args.no_sinv and world == 1:
         # the shift-invert path is single-GPU (every rank would repeat it)
         line["sinv"] = run_sinv(args, dev)
+    if not args.no_graph and world == 1:
+        line["graph"] = run_graph(args, dev, with_cpu=not args.no_cpu_baseline)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -877,6 +951,8 @@ def main():
     ap.add_argument("--only-sinv", action="store_true", help="run the configuration-2 (shift-invert) leg alone")
     ap.add_argument("--no-sinv", action="store_true", help="skip the configuration-2 (shift-invert) leg")
     ap.add_argument("--sinv-n", type=int, default=SINV_N, help="grid side of the shift-invert leg (reduced cases)")
+    ap.add_argument("--only-graph", action="store_true", help="run the graph-construction leg alone")
+    ap.add_argument("--no-graph", action="store_true", help="skip the graph-construction leg")
     ap.add_argument("--slq-n", type=int, default=N_POINTS, help="SLQ graph size (reduced cases for profiling)")
     ap.add_argument("--slq-m", type=int, default=SLQ_M, help="SLQ Lanczos depth (reduced cases for profiling)")
     args = ap.parse_args()

@@ -60,9 +60,9 @@ typedef struct lg_eigsh_opts {
 /* Kernel classes of info.kernel_* */
 enum {
   LG_K_SPMV = 0,     /* normalise + SpMV of a Lanczos step */
-  LG_K_PROJECT = 1,  /* Gram-Schmidt pass 1: h = V^T w */
-  LG_K_CORRPROJ = 2, /* pass 2: r = w - V h, s = V^T r */
-  LG_K_CORRECT = 3,  /* pass 3: r -= V s */
+  LG_K_PROJECT = 1,  /* Gram-Schmidt pass 1: h = V^T w (lag steps: s = V^T u, t = V^T z in one stream) */
+  LG_K_CORRPROJ = 2, /* pass 2: r = w - V h, s = V^T r (lag steps: the correction finishing v_j and r1) */
+  LG_K_CORRECT = 3,  /* pass 3: r -= V s (also the delayed pass of an extension's last residual) */
   LG_K_RESTART = 4,  /* one-CTA tridiagonal QR + shifts */
   LG_K_BASIS = 5,    /* V*Q restart update / Ritz vectors */
   LG_K_CG = 6,       /* shift-invert CG iteration kernels */
@@ -109,6 +109,14 @@ int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* 
  * matrix.  Creation computes the order on the host (a few hundred ms at
  * n = 1e6), so the flag pays off for plans that solve more than once. */
 #define LG_PLAN_REORDER_BFS 1
+/* LG_PLAN_CGS2_INLINE keeps both classical Gram-Schmidt passes inside every
+ * Lanczos step (three streams of the basis per step).  By default the second
+ * pass of step j-1 is delayed into step j (two streams per step: the
+ * projection of the new vector and the delayed projection share one read of
+ * V, and so do the two corrections); the basis, alpha and beta agree with the
+ * in-step passes to rounding, and the DGKS and breakdown tests are the same.
+ * Shift-invert solves always use the in-step passes. */
+#define LG_PLAN_CGS2_INLINE 2
 int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr,
                             const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
                             int mixed, int flags);

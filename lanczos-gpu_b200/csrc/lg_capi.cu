@@ -43,7 +43,7 @@ int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const in
                             const double* vals, int device_ptrs, int max_ncv, int mixed, int flags) {
   if (!plan) return LG_ERR_INVALID;
   *plan = nullptr;
-  if (flags & ~LG_PLAN_REORDER_BFS) {
+  if (flags & ~(LG_PLAN_REORDER_BFS | LG_PLAN_CGS2_INLINE)) {
     lg::g_last_error = "unknown plan flags";
     return LG_ERR_INVALID;
   }

@@ -43,6 +43,8 @@ enum Status {
   STATUS_BREAKDOWN = 2,   // invariant subspace found after step ST_STEP
   STATUS_TRIDIAG_FAIL = 3,
   STATUS_TIMEOUT = 4,     // a bounded device-side wait gave up
+  STATUS_PASS3_LAG = 5,   // a delayed second pass (lag step) left too little of the residual of step ST_STEP:
+                          // apply that pass explicitly, then a third, as DGKS does
 };
 
 // Device-side double scalars.
@@ -54,6 +56,7 @@ enum ScalarWord {
   SC_TAU = 4,        // restart: coefficient on V_new[:, nev_use]
   SC_BN = 5,         // residual norm at the last restart check
   SC_BETA_NEXT = 6,  // norm of the residual that will become the next basis vector
+  SC_ALPHA_PREV = 7, // lag step j: alpha_{j-1} before its delayed second-pass term (read by every CTA)
   SC_WORDS = 16
 };
 
@@ -87,6 +90,28 @@ __device__ inline double block_sum(double v, double* scratch) {
   for (int w = 0; w < nw; ++w) t += scratch[w];
   __syncthreads();
   return t;
+}
+
+// Reference: src/lanczos_ops.cuh:264-277 (adaptive_breakdown_tol), evaluated
+// for the step that produced the residual (index jr): eps^(2/3) times the
+// largest absolute row sum of the tridiagonal T[0..jr], with alpha[jr] taken
+// as `alpha_last` when `use_last` (a lag step checks with the corrected value
+// before it is stored).  Called by all 32 lanes of a warp (one row per lane,
+// max-reduced by shuffles: the same value as a serial scan); the result is
+// valid in every lane.
+__device__ inline double breakdown_tol_warp(const double* alpha, const double* beta, int jr, bool use_last = false,
+                                            double alpha_last = 0.0) {
+  double est = 0.0;
+  for (int i = threadIdx.x & 31; i <= jr; i += 32) {
+    double rs = fabs((use_last && i == jr) ? alpha_last : alpha[i]);
+    if (i > 0) rs += fabs(beta[i]);
+    if (i < jr) rs += fabs(beta[i + 1]);
+    est = fmax(est, rs);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) est = fmax(est, __shfl_xor_sync(0xffffffffu, est, o));
+  const double eps23 = 3.6687695461231177e-11;  // DBL_EPSILON^(2/3)
+  return eps23 * fmax(est, kSafeMin);
 }
 
 // ---------------------------------------------------------------------------

@@ -345,6 +345,299 @@ gs_async_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const d
 }
 
 // ---------------------------------------------------------------------------
+// Lag steps: the second Gram-Schmidt pass of step j-1 delayed into step j
+// (the delayed reorthogonalisation of low-synchronisation CGS2, Swirydowicz,
+// Langou, Ananthan, Yang, Thomas 2020; Bielich et al. 2022), two streams of V
+// per Lanczos step instead of three.
+//
+// Entering step j the basis has j finished columns and R holds u, the
+// residual of step j-1 after ONE pass (u = r1).  With rho = ||u||:
+//   spmv (BETA_LAG)   z = A u / rho
+//   gs_lag_project    s = V^T u, t = V^T z, u^T z, ||u||^2     (one read of V)
+//   gs_lag_correct    beta_j = sqrt(||u||^2 - ||s||^2)         (the norm of the
+//                       twice-orthogonalised residual u - V s)
+//                     v_j = (u - V s) / beta_j                 -> V[:, j]
+//                     alpha_{j-1} += s_{j-1}                   (its second-pass term)
+//                     v_j^T z = (u^T z - s.t) / beta_j
+//                     r1 = (rho / beta_j) (z - V t - (v_j^T z) v_j)  -> R
+//                     alpha_j = rho (v_j^T z) / beta_j - s_{j-1}     (first pass)
+// Since A v_j = (rho z - A V s) / beta_j and, by the Lanczos relation,
+// A V s = V T s + beta_j s_{j-1} v_j, the projections of A v_j are
+// V^T A v_j = (rho t - T s) / beta_j and v_j^T A v_j = alpha_j above; r1 is
+// then exactly (rho / beta_j)(z - V t - (v_j^T z) v_j): the T s terms cancel.
+// Only the alpha update uses the relation, through a term of the size of s
+// (a rounding-level quantity), so the basis, alpha and beta agree with the
+// in-step CGS2 to rounding.  The DGKS test of the reference (rnorm after the
+// second pass <= ||r1|| / sqrt(2)) becomes beta_j^2 <= ||u||^2 / 2 and ends the
+// step with STATUS_PASS3_LAG; the breakdown test is the reference's, on beta_j.
+// ---------------------------------------------------------------------------
+constexpr int kLagStageDoubles = 32 * 2 * 2 + 16;   // V chunks, 8 entries of u, 8 of z
+
+size_t gs_lag_smem() { return sizeof(double) * (size_t)kGsWarps * kGsStages * kLagStageDoubles; }
+
+// Both kernels keep gs_async_kernel's layout (LPR lanes per basis row, two
+// 16-byte chunks per lane, a per-warp cp.async ring) with the rows' entries
+// of u and z staged beside the V chunks.
+template <int LPR>
+__global__ void __launch_bounds__(kGsThreads, 1)
+gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ U,
+                      const double* __restrict__ Z, double* __restrict__ partS, double* __restrict__ partT,
+                      int* state) {
+  if (state[ST_STATUS] != STATUS_RUNNING) return;
+  constexpr int CH = 2;
+  constexpr int RW = 32 / LPR;
+  constexpr int COLS = 2 * LPR * CH;
+  static_assert(RW <= 8, "row entries per stage");
+  extern __shared__ __align__(16) double gs_ring[];
+  __shared__ double wsum[kGsWarps][COLS];
+  __shared__ double scr[32];
+
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int sub = lane & (LPR - 1), grp = lane / LPR;
+  bool live[CH], pair[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    const int c0 = ch * 2 * LPR + 2 * sub;
+    live[ch] = c0 < ncols;
+    pair[ch] = c0 + 1 < ncols;
+  }
+  double2 as[CH], at[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    as[ch] = make_double2(0.0, 0.0);
+    at[ch] = make_double2(0.0, 0.0);
+  }
+  double uz = 0.0, uu = 0.0, zz = 0.0;
+
+  const long long rb = (long long)n * blockIdx.x / gridDim.x;
+  const long long re = (long long)n * (blockIdx.x + 1) / gridDim.x;
+  const long long step = (long long)kGsWarps * RW;
+  const long long wfirst = rb + (long long)warp * RW;
+  const long long ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
+  double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
+
+  auto issue = [&](long long gi) {
+    double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
+    const long long r = wfirst + gi * step + grp;
+    const bool ok = gi < ngroups && r < re;
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      const bool go = ok && live[ch];
+      cp_async16(st + (ch * 32 + lane) * 2, go ? V + r * ldv + ch * 2 * LPR + 2 * sub : V, go ? 16 : 0);
+    }
+    if (sub == 0) {
+      cp_async8(st + 128 + grp, ok ? U + r : U, ok ? 8 : 0);
+      cp_async8(st + 136 + grp, ok ? Z + r : Z, ok ? 8 : 0);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < kGsStages - 1; ++s) issue(s);
+  for (long long gi = 0; gi < ngroups; ++gi) {
+    __syncwarp();
+    issue(gi + kGsStages - 1);
+    cp_async_wait<kGsStages - 1>();
+    __syncwarp();
+    const double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
+    const long long r = wfirst + gi * step + grp;
+    const bool ok = r < re;
+    const double xu = st[128 + grp], xz = st[136 + grp];
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      double2 v = *reinterpret_cast<const double2*>(st + (ch * 32 + lane) * 2);
+      if (!pair[ch]) v.y = 0.0;
+      as[ch].x += v.x * xu;
+      as[ch].y += v.y * xu;
+      at[ch].x += v.x * xz;
+      at[ch].y += v.y * xz;
+    }
+    if (ok && sub == 0) {
+      uz += xu * xz;
+      uu += xu * xu;
+      zz += xz * xz;
+    }
+  }
+  cp_async_wait<0>();
+
+  // column sums: s through wsum first, then t
+  for (int pass = 0; pass < 2; ++pass) {
+    double2* acc = pass == 0 ? as : at;
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+#pragma unroll
+      for (int o = 16; o >= LPR; o >>= 1) {
+        acc[ch].x += __shfl_xor_sync(0xffffffffu, acc[ch].x, o);
+        acc[ch].y += __shfl_xor_sync(0xffffffffu, acc[ch].y, o);
+      }
+      if (grp == 0) {
+        const int c0 = ch * 2 * LPR + 2 * sub;
+        wsum[warp][c0] = acc[ch].x;
+        wsum[warp][c0 + 1] = acc[ch].y;
+      }
+    }
+    __syncthreads();
+    double* prow = (pass == 0 ? partS : partT) + (size_t)blockIdx.x * kPartStride;
+    if (t < ncols) {
+      double sum = 0.0;
+      for (int w = 0; w < kGsWarps; ++w) sum += wsum[w][t];
+      prow[t] = sum;
+    }
+    __syncthreads();
+  }
+  const double tuz = block_sum(uz, scr);
+  const double tuu = block_sum(uu, scr);
+  const double tzz = block_sum(zz, scr);
+  if (t == 0) {
+    partS[(size_t)blockIdx.x * kPartStride + ncols] = tuu;
+    partS[(size_t)blockIdx.x * kPartStride + kPartScalar] = tuz;
+    partT[(size_t)blockIdx.x * kPartStride + kPartScalar] = tzz;
+  }
+}
+
+template <int LPR>
+__global__ void __launch_bounds__(kGsThreads, 1)
+gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const double* __restrict__ Z,
+                      const double* __restrict__ partS, const double* __restrict__ partT, int nrows_in,
+                      double* __restrict__ part_out, double* scal, double* alpha, double* beta, int* state) {
+  if (state[ST_STATUS] != STATUS_RUNNING) return;
+  constexpr int CH = 2;
+  constexpr int RW = 32 / LPR;
+  static_assert(RW <= 8, "row entries per stage");
+  extern __shared__ __align__(16) double gs_ring[];
+  __shared__ double cs[kMaxCols], ct[kMaxCols];
+  __shared__ double red[kGsThreads];
+  __shared__ double scr[32];
+  __shared__ double sh_b1, sh_b2, sh_rb, sh_vjz;
+  __shared__ int sh_stop;
+
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int sub = lane & (LPR - 1), grp = lane / LPR;
+  const int j = ncols;   // the column this step finishes
+
+  if (t < kMaxCols) {
+    cs[t] = 0.0;
+    ct[t] = 0.0;
+  }
+  __syncthreads();
+  double uz, zz;
+  reduce_partials(partS, nrows_in, ncols + 1, cs, &uz, red);   // cs[j] = ||u||^2
+  reduce_partials(partT, nrows_in, ncols, ct, &zz, red);
+  if (t < 32) {
+    double ss = 0.0, st = 0.0;
+    for (int i = t; i < ncols; i += 32) {
+      ss += cs[i] * cs[i];
+      st += cs[i] * ct[i];
+    }
+    ss = warp_sum(ss);
+    st = warp_sum(st);
+    const double uu = cs[j];
+    const double aprev = scal[SC_ALPHA_PREV] + cs[j - 1];
+    const double btol = breakdown_tol_warp(alpha, beta, j - 1, true, aprev);
+    if (t == 0) {
+      const double b2 = uu - ss;
+      const double b = b2 > 0.0 ? sqrt(b2) : 0.0;
+      int stop = STATUS_RUNNING;
+      if (!(b2 > 0.5 * uu)) stop = STATUS_PASS3_LAG;
+      else if (b < btol) stop = STATUS_BREAKDOWN;
+      double s1 = 1.0, s2 = 1.0;
+      safe_inv(b, s1, s2);
+      const double rho = scal[SC_BETA_NEXT];
+      const double vjz = ((uz - st) * s1) * s2;
+      sh_b1 = s1;
+      sh_b2 = s2;
+      sh_rb = ((rho * s1) * s2);
+      sh_vjz = vjz;
+      sh_stop = stop;
+      if (blockIdx.x == 0) {
+        if (stop != STATUS_RUNNING) {
+          state[ST_STEP] = j - 1;
+          state[ST_STATUS] = stop;
+        } else {
+          alpha[j - 1] = aprev;
+          beta[j] = b;
+          alpha[j] = ((rho * vjz) * s1) * s2 - cs[j - 1];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (sh_stop != STATUS_RUNNING) return;
+  const double b1 = sh_b1, b2s = sh_b2, rb = sh_rb, vjz = sh_vjz;
+
+  double2 c1[CH], c2[CH];
+  bool live[CH], pair[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    const int c0 = ch * 2 * LPR + 2 * sub;
+    live[ch] = c0 < ncols;
+    pair[ch] = c0 + 1 < ncols;
+    c1[ch] = make_double2(c0 < ncols ? cs[c0] : 0.0, c0 + 1 < ncols ? cs[c0 + 1] : 0.0);
+    c2[ch] = make_double2(c0 < ncols ? ct[c0] : 0.0, c0 + 1 < ncols ? ct[c0 + 1] : 0.0);
+  }
+  double nrm = 0.0;
+
+  const long long rb0 = (long long)n * blockIdx.x / gridDim.x;
+  const long long re = (long long)n * (blockIdx.x + 1) / gridDim.x;
+  const long long step = (long long)kGsWarps * RW;
+  const long long wfirst = rb0 + (long long)warp * RW;
+  const long long ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
+  double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
+
+  auto issue = [&](long long gi) {
+    double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
+    const long long r = wfirst + gi * step + grp;
+    const bool ok = gi < ngroups && r < re;
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      const bool go = ok && live[ch];
+      cp_async16(st + (ch * 32 + lane) * 2, go ? V + r * ldv + ch * 2 * LPR + 2 * sub : V, go ? 16 : 0);
+    }
+    if (sub == 0) {
+      cp_async8(st + 128 + grp, ok ? R + r : R, ok ? 8 : 0);
+      cp_async8(st + 136 + grp, ok ? Z + r : Z, ok ? 8 : 0);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < kGsStages - 1; ++s) issue(s);
+  for (long long gi = 0; gi < ngroups; ++gi) {
+    __syncwarp();
+    issue(gi + kGsStages - 1);
+    cp_async_wait<kGsStages - 1>();
+    __syncwarp();
+    const double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
+    const long long r = wfirst + gi * step + grp;
+    const bool ok = r < re;
+    double d1 = 0.0, d2 = 0.0;
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      double2 v = *reinterpret_cast<const double2*>(st + (ch * 32 + lane) * 2);
+      if (!pair[ch]) v.y = 0.0;
+      d1 += v.x * c1[ch].x + v.y * c1[ch].y;
+      d2 += v.x * c2[ch].x + v.y * c2[ch].y;
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) {
+      d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+      d2 += __shfl_xor_sync(0xffffffffu, d2, o);
+    }
+    if (ok && sub == 0) {
+      const double xu = st[128 + grp], xz = st[136 + grp];
+      const double vj = ((xu - d1) * b1) * b2s;
+      const double r1 = rb * (xz - d2 - vjz * vj);
+      V[r * ldv + j] = vj;
+      R[r] = r1;
+      nrm += r1 * r1;
+    }
+  }
+  cp_async_wait<0>();
+  const double tot = block_sum(nrm, scr);
+  if (t == 0) part_out[(size_t)blockIdx.x * kPartStride + kPartScalar] = tot;
+}
+
+// ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
 GsPlan gs_plan(int n, int ncols, int grid) {
@@ -420,6 +713,58 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld
                        int j, int alpha_mode, int* state) {
   return launch_mode<3>(p, st, V, ldv, ncols, n, nullptr, R, part_in, nrows_in, part_out, scal, alpha, j,
                         alpha_mode, state);
+}
+
+
+template <int LP>
+static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+                                  const double* U, const double* Z, double* partS, double* partT, int* state) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gs_lag_project_kernel<LP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gs_lag_smem());
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  gs_lag_project_kernel<LP><<<p.grid, kGsThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, U, Z, partS, partT, state);
+  return cudaGetLastError();
+}
+
+template <int LP>
+static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+                                  const double* Z, const double* partS, const double* partT, int nrows_in,
+                                  double* part_out, double* scal, double* alpha, double* beta, int* state) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gs_lag_correct_kernel<LP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gs_lag_smem());
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  gs_lag_correct_kernel<LP><<<p.grid, kGsThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, R, Z, partS, partT,
+                                                                       nrows_in, part_out, scal, alpha, beta, state);
+  return cudaGetLastError();
+}
+
+cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+                           const double* U, const double* Z, double* partS, double* partT, int* state) {
+  if (p.lpr == 4) return lag_project_lp<4>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  if (p.lpr == 8) return lag_project_lp<8>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  if (p.lpr == 16) return lag_project_lp<16>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  return lag_project_lp<32>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+}
+
+cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+                           const double* Z, const double* partS, const double* partT, int nrows_in,
+                           double* part_out, double* scal, double* alpha, double* beta, int* state) {
+  if (p.lpr == 4)
+    return lag_correct_lp<4>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+  if (p.lpr == 8)
+    return lag_correct_lp<8>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+  if (p.lpr == 16)
+    return lag_correct_lp<16>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta,
+                              state);
+  return lag_correct_lp<32>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
 }
 
 }  // namespace lg

@@ -276,6 +276,7 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   } else {
     std::copy(rowptr, rowptr + n + 1, hrp.begin());
   }
+  lag_steps = !(flags & LG_PLAN_CGS2_INLINE);
   if ((flags & LG_PLAN_REORDER_BFS) && !comm) {
     int rc = reorder_bfs(hrp);
     if (rc != LG_OK) return rc;
@@ -681,8 +682,19 @@ int Solver::apply_step(int j, int beta_mode) {
   return apply_shift_invert(j, beta_mode);
 }
 
-int Solver::extend(int j0, int j1, int first_mode) {
+int Solver::extend(int j0, int j1, int first_mode, bool lag) {
+  bool last_lag = false;
   for (int j = j0; j < j1; ++j) {
+    // a lag step needs a previous column and a residual whose coupling is
+    // its norm (not after a fresh start, an explicit third pass or a random
+    // restart, whose first step keeps the in-step passes and their checks)
+    if (lag && j > 0 && (j > j0 || first_mode == BETA_RESTART)) {
+      int rc = lag_step(j);
+      if (rc != LG_OK) return rc;
+      last_lag = true;
+      continue;
+    }
+    last_lag = false;
     int rc = apply_step(j, j == j0 ? first_mode : BETA_STEP);
     if (rc != LG_OK) return rc;
     const int ncols = j + 1;
@@ -705,7 +717,57 @@ int Solver::extend(int j0, int j1, int first_mode) {
     rc = reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
     if (rc != LG_OK) return rc;
   }
+  if (last_lag) return finish_lag(j1 - 1);
   return LG_OK;
+}
+
+// Lag step j: z = A u / ||u|| from the once-orthogonalised residual u of step
+// j-1, then one stream of V for s = V^T u and t = V^T z, and one that
+// finishes v_j = (u - V s) / beta_j and forms the next once-orthogonalised
+// residual (lg_gs.cu, gs_lag_project / gs_lag_correct).
+int Solver::lag_step(int j) {
+  const double vb = mixed ? 4.0 : 8.0;
+  const double sbytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 8.0 * n;
+  int rc = gather_residual();
+  if (rc != LG_OK) return rc;
+  const double* Rg = comm ? Rfull : R;
+  LG_TRY(timed(LG_K_SPMV, sbytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
+    return spmv_step(A, stream, grid_spmv, Rg, W, nullptr, ldv, inC, nrowsC, j, BETA_LAG, alpha, beta, scal, state,
+                     R);
+  }));
+  const GsPlan p = gs_plan(n, j, grid_gs);
+  const double vbytes = 8.0 * (double)n * j;
+  LG_TRY(timed(LG_K_PROJECT, vbytes + 16.0 * n, 1,
+               [&] { return gs_lag_project(p, stream, V, ldv, j, n, R, W, partA, partB, state); }));
+  const double *inS = nullptr, *inT = nullptr;
+  int nS = 0, nT = 0;
+  rc = reduce_partials_all(partA, p.grid, 0, &inS, &nS);
+  if (rc != LG_OK) return rc;
+  rc = reduce_partials_all(partB, p.grid, 1, &inT, &nT);
+  if (rc != LG_OK) return rc;
+  LG_TRY(timed(LG_K_CORRPROJ, vbytes + 32.0 * n, 1, [&] {
+    return gs_lag_correct(p, stream, V, ldv, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);
+  }));
+  return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
+}
+
+// The delayed second pass of the last residual of an extension (step s):
+// R -= V[:, 0..s] (V^T R), alpha_s += its coefficient, ||R||^2 partials for
+// the restart (whose DGKS / breakdown tests then read them).
+int Solver::finish_lag(int s) {
+  const int ncols = s + 1;
+  const GsPlan p = gs_plan(n, ncols, grid_gs);
+  const double vbytes = 8.0 * (double)n * ncols;
+  const double* inA = nullptr;
+  int nA = 0;
+  LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
+               [&] { return gs_project(p, stream, V, ldv, ncols, n, R, partA, state); }));
+  int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
+  if (rc != LG_OK) return rc;
+  LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
+    return gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state);
+  }));
+  return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
 
 cudaEvent_t Solver::next_event() {
@@ -839,7 +901,8 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
   }
 
   long long steps = 0;
-  int rc = extend(0, m, BETA_INIT);
+  const bool lag = lag_steps && !o.use_sigma;
+  int rc = extend(0, m, BETA_INIT, lag);
   if (rc != LG_OK) return rc;
   steps += m;
 
@@ -881,7 +944,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
       g_last_error = "tridiagonal QR iteration did not converge (non-finite values?)";
       return LG_ERR_NUMERIC;
     }
-    if (status == STATUS_PASS3 || status == STATUS_BREAKDOWN) {
+    if (status == STATUS_PASS3 || status == STATUS_BREAKDOWN || status == STATUS_PASS3_LAG) {
       const int s = h_state[ST_STEP];
       if (s < 0 || s >= m) {
         g_last_error = "internal: bad step index in device state";
@@ -890,7 +953,13 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
       rc = clear_status();
       if (rc != LG_OK) return rc;
       int next_mode = BETA_STEP;
-      if (status == STATUS_PASS3 && s != last_pass3_step) {
+      if (status == STATUS_PASS3_LAG) {
+        // the delayed second pass of step s, applied, then the third pass
+        rc = pass3(s);
+        if (rc == LG_OK) rc = pass3(s);
+        ++pass3_count;
+        last_pass3_step = s;
+      } else if (status == STATUS_PASS3 && s != last_pass3_step) {
         rc = pass3(s);
         ++pass3_count;
         last_pass3_step = s;
@@ -902,7 +971,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
       }
       if (rc != LG_OK) return rc;
       if (s + 1 < m) {
-        rc = extend(s + 1, m, next_mode);
+        rc = extend(s + 1, m, next_mode, lag);
         if (rc != LG_OK) return rc;
         steps += m - (s + 1);
       } else if (next_mode == BETA_ZERO) {
@@ -941,7 +1010,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + nev_use) + 16.0 * n, 1, [&] { return basis_update(bp, ba, stream); }));
     rc = reduce_partials_all(partC, bp.grid, 2, &inC, &nrowsC);
     if (rc != LG_OK) return rc;
-    rc = extend(nev_use, m, BETA_RESTART);
+    rc = extend(nev_use, m, BETA_RESTART, lag);
     if (rc != LG_OK) return rc;
     steps += m - nev_use;
     ++iter;

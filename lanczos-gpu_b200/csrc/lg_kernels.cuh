@@ -26,12 +26,28 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state);
 
+// Lag step j (second Gram-Schmidt pass of step j-1 delayed into step j; V has
+// j finished columns, R = u the once-orthogonalised residual of step j-1,
+// W = z = A u / ||u||):
+//   gs_lag_project: partS rows = [V^T u | ||u||^2 in column j], scalar u^T z;
+//                   partT rows = [V^T z], scalar ||z||^2
+//   gs_lag_correct: DGKS / breakdown checks, alpha_{j-1} += s_{j-1},
+//                   beta[j], v_j = (u - V s) / beta_j into V[:, j],
+//                   R = (rho / beta_j) (z - V t - (v_j^T z) v_j), alpha[j]
+//                   (first pass); part_out: ||R||^2.
+cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+                           const double* U, const double* Z, double* partS, double* partT, int* state);
+cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+                           const double* Z, const double* partS, const double* partT, int nrows_in,
+                           double* part_out, double* scal, double* alpha, double* beta, int* state);
+
 // SpMV step (lg_spmv.cu).  beta_mode says what the norm of R means.
 enum BetaMode {
   BETA_INIT = 0,      // starting vector: normalise only
   BETA_STEP = 1,      // residual of step j-1: store beta[j], run the DGKS / breakdown checks
   BETA_RESTART = 2,   // residual after an implicit restart: store beta[j], breakdown check only
   BETA_ZERO = 3,      // fresh vector after an invariant subspace: beta[j] = 0
+  BETA_LAG = 4,       // lag step: w = A r / ||r|| only (V[:, j] and beta[j] come from gs_lag_correct)
 };
 
 struct CsrDev {

@@ -51,7 +51,13 @@ class Solver {
   int sync_state();
   int clear_status();
   int apply_step(int j, int beta_mode);
-  int extend(int j0, int j1, int first_mode);
+  // Lanczos steps j0 .. j1-1.  lag: steps after the first take the second
+  // Gram-Schmidt pass delayed into the next step (lag_step), and the last
+  // residual gets that pass at the end (finish_lag).
+  int extend(int j0, int j1, int first_mode, bool lag = false);
+  int lag_step(int j);
+  int finish_lag(int s);
+  bool lag_steps = true;   // false: LG_PLAN_CGS2_INLINE (both passes inside every step)
   int pass3(int s);
   int random_restart(int s);
   // shift-invert (lg_cg.cu)

@@ -5,7 +5,9 @@
 // src/cast_kernels.cu:7-15).  Here:
 //   * one kernel per step does  beta_j = ||r||, v_j = r / beta_j,
 //     w = A v_j  — the normalisation of the previous residual is folded into
-//     the SpMV (w = (A r) / beta_j), so no separate scale/copy launches;
+//     the SpMV (w = (A r) / beta_j), so no separate scale/copy launches; in a
+//     lag step (BETA_LAG, Vj null) only w = A r / ||r|| (v_j is finished by
+//     the delayed second Gram-Schmidt pass, lg_gs.cu);
 //   * the fp32-value variant keeps x and the accumulator in fp64
 //     (fp32 values halve the value stream; accuracy stays fp64);
 //   * rows are handled by a group of L lanes (vector-per-row, L picked from
@@ -17,26 +19,6 @@
 #include <cmath>
 
 namespace lg {
-
-// Reference: src/lanczos_ops.cuh:264-277 (adaptive_breakdown_tol), evaluated
-// for the step that produced the residual (index jr): eps^(2/3) times the
-// largest absolute row sum of the tridiagonal T[0..jr].  Called by all 32
-// lanes of a warp (one row per lane, max-reduced by shuffles: the same value
-// as a serial scan, without a serial chain of loads in front of the kernel);
-// the result is valid in every lane.
-__device__ double breakdown_tol_warp(const double* alpha, const double* beta, int jr) {
-  double est = 0.0;
-  for (int i = threadIdx.x & 31; i <= jr; i += 32) {
-    double rs = fabs(alpha[i]);
-    if (i > 0) rs += fabs(beta[i]);
-    if (i < jr) rs += fabs(beta[i + 1]);
-    est = fmax(est, rs);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) est = fmax(est, __shfl_xor_sync(0xffffffffu, est, o));
-  const double eps23 = 3.6687695461231177e-11;  // DBL_EPSILON^(2/3)
-  return eps23 * fmax(est, kSafeMin);
-}
 
 // Prologue shared by the SpMV step and the normalise-only step: reduce the
 // norm partials of R, run the DGKS / breakdown checks, store beta_j.  Every
@@ -74,6 +56,7 @@ __device__ int step_prologue(const double* __restrict__ part_in, int nrows_in, i
         } else {
           if (beta_mode == BETA_STEP || beta_mode == BETA_RESTART) beta[j] = bn;
           else if (beta_mode == BETA_ZERO) beta[j] = 0.0;
+          else if (beta_mode == BETA_LAG) scal[SC_ALPHA_PREV] = alpha[j - 1];
           scal[SC_BETA_NEXT] = bn;
         }
       }
@@ -127,11 +110,11 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
     if (lane == 0) {
       if (okA) {
         W[rowA] = (accA * s1) * s2;
-        Vj[(size_t)rowA * ldv] = (R_own[rowA] * s1) * s2;
+        if (Vj) Vj[(size_t)rowA * ldv] = (R_own[rowA] * s1) * s2;
       }
       if (okB) {
         W[rowB] = (accB * s1) * s2;
-        Vj[(size_t)rowB * ldv] = (R_own[rowB] * s1) * s2;
+        if (Vj) Vj[(size_t)rowB * ldv] = (R_own[rowB] * s1) * s2;
       }
     }
   }

@@ -129,15 +129,19 @@ class EigshPlan:
     same keywords as :func:`gpu_eigsh`.  ``reorder=True`` renumbers the rows
     inside the plan by BFS level (LG_PLAN_REORDER_BFS) for locality of the
     sparse product; v0, eigenvectors and ``matvec_device`` keep the caller's
-    numbering.
+    numbering.  ``cgs2_inline=True`` keeps both Gram-Schmidt passes inside
+    every Lanczos step (LG_PLAN_CGS2_INLINE) instead of delaying the second
+    pass into the next step's stream of the basis (same results to rounding).
     """
 
     def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None,
-                 reorder: bool = False):
+                 reorder: bool = False, cgs2_inline: bool = False):
         self._plan = None
-        flags = _native.LG_PLAN_REORDER_BFS if reorder else 0
+        flags = (_native.LG_PLAN_REORDER_BFS if reorder else 0) | (_native.LG_PLAN_CGS2_INLINE if cgs2_inline else 0)
         if reorder and comm is not None:
             raise ValueError("reorder a partitioned matrix before splitting it (gpu_eigsh.ordering)")
+        if cgs2_inline and comm is not None:
+            raise ValueError("cgs2_inline is a single-GPU plan option")
         h = _native.C.c_void_p()
         if comm is not None:
             # row-partitioned: device_csr holds this rank's rows (global column indices)

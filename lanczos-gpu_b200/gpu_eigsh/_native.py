@@ -24,6 +24,7 @@ LG_ERR_CG_NOCONV = -6
 WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
 EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
 LG_PLAN_REORDER_BFS = 1
+LG_PLAN_CGS2_INLINE = 2
 KNN_METHODS = {"auto": 0, "cells": 1, "brute": 2}
 
 

@@ -322,3 +322,48 @@ def test_plan_reorder_bfs_keeps_caller_numbering(ge):
         with ge.EigshPlan(L, max_ncv=40, mixed=mixed) as plain:
             a0, b0 = plain.factorize(v0, 20)
         assert np.abs(a1 - a0).max() < 1e-10 * an and np.abs(b1 - b0).max() < 1e-10 * an
+
+
+@pytest.mark.parametrize("case", ["knn_LA", "knn_SA", "grid_SA", "mixed_LA", "breakdown"])
+def test_lag_steps_match_inline_cgs2(ge, case):
+    """Delayed second Gram-Schmidt pass (the default) against both passes
+    inside every step (LG_PLAN_CGS2_INLINE): the same eigenvalues to 1e-11
+    relative, both at ARPACK's to 1e-10, residuals within tol * ||A||, an
+    orthonormal Ritz basis, and the same restart count (to one restart)."""
+    from gpu_eigsh import synthetic as syn
+    from oracle.irlm import arpack_eigsh
+
+    mixed = case == "mixed_LA"
+    if case.startswith("knn") or mixed:
+        A, _ = syn.knn_laplacian(20000, k=10, seed=11)
+        k, which, ncv = 8, case.split("_")[1], 40
+    elif case == "grid_SA":
+        A, k, which, ncv = syn.grid2d_dirichlet(60), 10, "SA", 40
+    else:
+        A = sp.block_diag([sp.diags([1.0, 2.0, 3.0]), sp.diags(np.linspace(10, 20, 200))]).tocsr()
+        k, which, ncv = 4, "SA", 20
+    n = A.shape[0]
+    v0 = np.random.default_rng(3).standard_normal(n)
+    if case == "breakdown":
+        v0[3:] = 0.0
+    an = anorm1(A)
+    out = {}
+    for inline in (False, True):
+        with ge.EigshPlan(A, max_ncv=ncv, mixed=mixed, cgs2_inline=inline) as plan:
+            w, V = plan.solve(k=k, which=which, ncv=ncv, tol=1e-10, v0=v0)
+            out[inline] = (w, V, dict(plan.last_info))
+    (w0, V0, i0), (w1, V1, i1) = out[False], out[True]
+    assert eig_rel_err(w0, w1, an) < 1e-11
+    # the same Krylov spaces to rounding; a borderline convergence test may flip by one restart
+    assert abs(i0["restarts"] - i1["restarts"]) <= 1
+    Aref = A.astype(np.float32).astype(np.float64) if mixed else A
+    assert _residuals(Aref, w0, V0).max() <= 1e-10 * an
+    np.testing.assert_allclose(V0.T @ V0, np.eye(k), atol=1e-10)
+    if not mixed:
+        ws, _ = arpack_eigsh(A, k, which=which, ncv=ncv, tol=1e-10, v0=v0)
+        assert eig_rel_err(w0, ws, an) < 1e-10
+    if case == "breakdown":
+        assert i0["breakdowns"] >= 1
+        np.testing.assert_allclose(w0, [1.0, 2.0, 3.0, 10.0], rtol=1e-10)
+    else:
+        assert i0["launches"] < i1["launches"]   # one stream of the basis fewer per step
