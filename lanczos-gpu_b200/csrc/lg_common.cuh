@@ -120,20 +120,35 @@ __device__ inline double breakdown_tol_warp(const double* alpha, const double* b
 // Reduce `nrows` partial rows: columns [0, nc) into out[0..nc), the scalar
 // slot into *scal_out.  Every thread of the block gets the same values.
 // `red` needs blockDim.x doubles; blockDim.x must be a multiple of 128.
+// Rows are summed in order r = grp, grp + ngrp, ... by every thread; the loads
+// go out eight at a time (independent), the adds keep that order, so the
+// result does not depend on the batching.
+__device__ __forceinline__ double sum_rows_strided(const double* __restrict__ part, int nrows, int first, int stride,
+                                                   int slot) {
+  double acc = 0.0;
+  int r = first;
+  for (; r + 7 * stride < nrows; r += 8 * stride) {
+    double v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = part[(size_t)(r + u * stride) * kPartStride + slot];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc += v[u];
+  }
+  for (; r < nrows; r += stride) acc += part[(size_t)r * kPartStride + slot];
+  return acc;
+}
+
 __device__ inline void reduce_partials(const double* __restrict__ part, int nrows, int nc, double* out,
                                 double* scal_out, double* red) {
   const int t = threadIdx.x;
   const int ngrp = blockDim.x >> 7;
   const int slot = t & 127, grp = t >> 7;
   double acc = 0.0;
-  if (slot < nc) {
-#pragma unroll 4
-    for (int r = grp; r < nrows; r += ngrp) acc += part[(size_t)r * kPartStride + slot];
-  }
+  if (slot < nc) acc = sum_rows_strided(part, nrows, grp, ngrp, slot);
   red[grp * 128 + slot] = acc;
   double sc = 0.0;
   if (t < 32) {
-    for (int r = t; r < nrows; r += 32) sc += part[(size_t)r * kPartStride + kPartScalar];
+    sc = sum_rows_strided(part, nrows, t, 32, kPartScalar);
     sc = warp_sum(sc);
   }
   __syncthreads();
@@ -143,6 +158,43 @@ __device__ inline void reduce_partials(const double* __restrict__ part, int nrow
     out[t] = s;
   }
   if (t == 0) *scal_out = sc;
+  __syncthreads();
+}
+
+// reduce_partials of two tables with the same row count in one pass (their
+// loads in flight together); same values as two separate calls.  `red`
+// needs 2 * blockDim.x doubles.
+__device__ inline void reduce_partials2(const double* __restrict__ pa, const double* __restrict__ pb, int nrows,
+                                        int nca, int ncb, double* outa, double* outb, double* sca_out,
+                                        double* scb_out, double* red) {
+  const int t = threadIdx.x;
+  const int ngrp = blockDim.x >> 7;
+  const int slot = t & 127, grp = t >> 7;
+  double acca = 0.0, accb = 0.0;
+  if (slot < nca) acca = sum_rows_strided(pa, nrows, grp, ngrp, slot);
+  if (slot < ncb) accb = sum_rows_strided(pb, nrows, grp, ngrp, slot);
+  red[grp * 128 + slot] = acca;
+  red[blockDim.x + grp * 128 + slot] = accb;
+  double sca = 0.0, scb = 0.0;
+  if (t < 32) {
+    sca = warp_sum(sum_rows_strided(pa, nrows, t, 32, kPartScalar));
+    scb = warp_sum(sum_rows_strided(pb, nrows, t, 32, kPartScalar));
+  }
+  __syncthreads();
+  if (t < nca) {
+    double s = 0.0;
+    for (int g = 0; g < ngrp; ++g) s += red[g * 128 + t];
+    outa[t] = s;
+  }
+  if (t < ncb) {
+    double s = 0.0;
+    for (int g = 0; g < ngrp; ++g) s += red[blockDim.x + g * 128 + t];
+    outb[t] = s;
+  }
+  if (t == 0) {
+    *sca_out = sca;
+    *scb_out = scb;
+  }
   __syncthreads();
 }
 

@@ -371,25 +371,31 @@ gs_async_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const d
 // second pass <= ||r1|| / sqrt(2)) becomes beta_j^2 <= ||u||^2 / 2 and ends the
 // step with STATUS_PASS3_LAG; the breakdown test is the reference's, on beta_j.
 // ---------------------------------------------------------------------------
-constexpr int kLagStageDoubles = 32 * 2 * 2 + 16;   // V chunks, 8 entries of u, 8 of z
+// Layout: 16 warps per CTA (512 threads, so the coefficient and chunk
+// registers of four 16-byte chunks per lane fit without spills), LPR lanes
+// per basis row, each lane holding four 16-byte chunks (8 columns), so a
+// warp iteration covers 32/LPR rows: LPR = 4, 8, 16 for up to 32, 64, 128
+// live columns, 8, 4, 2 rows per iteration.  A per-warp cp.async ring stages
+// the V chunks and the rows' entries of u and z.
+constexpr int kLagWarps = 16;
+constexpr int kLagThreads = kLagWarps * 32;
+constexpr int kLagCH = 4;
+constexpr int kLagStageDoubles = 32 * kLagCH * 2 + 16;   // V chunks, 8 entries of u, 8 of z
 
-size_t gs_lag_smem() { return sizeof(double) * (size_t)kGsWarps * kGsStages * kLagStageDoubles; }
+size_t gs_lag_smem() { return sizeof(double) * (size_t)kLagWarps * kGsStages * kLagStageDoubles; }
 
-// Both kernels keep gs_async_kernel's layout (LPR lanes per basis row, two
-// 16-byte chunks per lane, a per-warp cp.async ring) with the rows' entries
-// of u and z staged beside the V chunks.
 template <int LPR>
-__global__ void __launch_bounds__(kGsThreads, 1)
+__global__ void __launch_bounds__(kLagThreads, 1)
 gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ U,
                       const double* __restrict__ Z, double* __restrict__ partS, double* __restrict__ partT,
                       int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
-  constexpr int CH = 2;
+  constexpr int CH = kLagCH;
   constexpr int RW = 32 / LPR;
   constexpr int COLS = 2 * LPR * CH;
   static_assert(RW <= 8, "row entries per stage");
   extern __shared__ __align__(16) double gs_ring[];
-  __shared__ double wsum[kGsWarps][COLS];
+  __shared__ double wsum[kLagWarps][COLS];
   __shared__ double scr[32];
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -409,40 +415,41 @@ gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, c
   }
   double uz = 0.0, uu = 0.0, zz = 0.0;
 
-  const long long rb = (long long)n * blockIdx.x / gridDim.x;
-  const long long re = (long long)n * (blockIdx.x + 1) / gridDim.x;
-  const long long step = (long long)kGsWarps * RW;
-  const long long wfirst = rb + (long long)warp * RW;
-  const long long ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
+  const int rb = (int)((long long)n * blockIdx.x / gridDim.x);
+  const int re = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
+  constexpr int step = kLagWarps * RW;
+  const int wfirst = rb + warp * RW;
+  const int ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
   double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
 
-  auto issue = [&](long long gi) {
-    double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
-    const long long r = wfirst + gi * step + grp;
+  auto issue = [&](int gi) {
+    double* st = ring + (gi % kGsStages) * kLagStageDoubles;
+    const int r = wfirst + gi * step + grp;
     const bool ok = gi < ngroups && r < re;
+    const double* row = V + (size_t)r * ldv + 2 * sub;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? V + r * ldv + ch * 2 * LPR + 2 * sub : V, go ? 16 : 0);
+      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
     }
     if (sub == 0) {
-      cp_async8(st + 128 + grp, ok ? U + r : U, ok ? 8 : 0);
-      cp_async8(st + 136 + grp, ok ? Z + r : Z, ok ? 8 : 0);
+      cp_async8(st + 32 * CH * 2 + grp, ok ? U + r : U, ok ? 8 : 0);
+      cp_async8(st + 32 * CH * 2 + 8 + grp, ok ? Z + r : Z, ok ? 8 : 0);
     }
     cp_async_commit();
   };
 
 #pragma unroll
   for (int s = 0; s < kGsStages - 1; ++s) issue(s);
-  for (long long gi = 0; gi < ngroups; ++gi) {
+  for (int gi = 0; gi < ngroups; ++gi) {
     __syncwarp();
     issue(gi + kGsStages - 1);
     cp_async_wait<kGsStages - 1>();
     __syncwarp();
-    const double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
-    const long long r = wfirst + gi * step + grp;
+    const double* st = ring + (gi % kGsStages) * kLagStageDoubles;
+    const int r = wfirst + gi * step + grp;
     const bool ok = r < re;
-    const double xu = st[128 + grp], xz = st[136 + grp];
+    const double xu = st[32 * CH * 2 + grp], xz = st[32 * CH * 2 + 8 + grp];
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       double2 v = *reinterpret_cast<const double2*>(st + (ch * 32 + lane) * 2);
@@ -480,7 +487,7 @@ gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, c
     double* prow = (pass == 0 ? partS : partT) + (size_t)blockIdx.x * kPartStride;
     if (t < ncols) {
       double sum = 0.0;
-      for (int w = 0; w < kGsWarps; ++w) sum += wsum[w][t];
+      for (int w = 0; w < kLagWarps; ++w) sum += wsum[w][t];
       prow[t] = sum;
     }
     __syncthreads();
@@ -496,17 +503,17 @@ gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, c
 }
 
 template <int LPR>
-__global__ void __launch_bounds__(kGsThreads, 1)
+__global__ void __launch_bounds__(kLagThreads, 1)
 gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const double* __restrict__ Z,
                       const double* __restrict__ partS, const double* __restrict__ partT, int nrows_in,
                       double* __restrict__ part_out, double* scal, double* alpha, double* beta, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
-  constexpr int CH = 2;
+  constexpr int CH = kLagCH;
   constexpr int RW = 32 / LPR;
   static_assert(RW <= 8, "row entries per stage");
   extern __shared__ __align__(16) double gs_ring[];
   __shared__ double cs[kMaxCols], ct[kMaxCols];
-  __shared__ double red[kGsThreads];
+  __shared__ double red[2 * kLagThreads];
   __shared__ double scr[32];
   __shared__ double sh_b1, sh_b2, sh_rb, sh_vjz;
   __shared__ int sh_stop;
@@ -521,8 +528,7 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
   }
   __syncthreads();
   double uz, zz;
-  reduce_partials(partS, nrows_in, ncols + 1, cs, &uz, red);   // cs[j] = ||u||^2
-  reduce_partials(partT, nrows_in, ncols, ct, &zz, red);
+  reduce_partials2(partS, partT, nrows_in, ncols + 1, ncols, cs, ct, &uz, &zz, red);   // cs[j] = ||u||^2
   if (t < 32) {
     double ss = 0.0, st = 0.0;
     for (int i = t; i < ncols; i += 32) {
@@ -577,39 +583,39 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
   }
   double nrm = 0.0;
 
-  const long long rb0 = (long long)n * blockIdx.x / gridDim.x;
-  const long long re = (long long)n * (blockIdx.x + 1) / gridDim.x;
-  const long long step = (long long)kGsWarps * RW;
-  const long long wfirst = rb0 + (long long)warp * RW;
-  const long long ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
+  const int rb0 = (int)((long long)n * blockIdx.x / gridDim.x);
+  const int re = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
+  constexpr int step = kLagWarps * RW;
+  const int wfirst = rb0 + warp * RW;
+  const int ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
   double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
 
-  auto issue = [&](long long gi) {
-    double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
-    const long long r = wfirst + gi * step + grp;
+  auto issue = [&](int gi) {
+    double* st = ring + (gi % kGsStages) * kLagStageDoubles;
+    const int r = wfirst + gi * step + grp;
     const bool ok = gi < ngroups && r < re;
+    const double* row = V + (size_t)r * ldv + 2 * sub;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? V + r * ldv + ch * 2 * LPR + 2 * sub : V, go ? 16 : 0);
+      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
     }
     if (sub == 0) {
-      cp_async8(st + 128 + grp, ok ? R + r : R, ok ? 8 : 0);
-      cp_async8(st + 136 + grp, ok ? Z + r : Z, ok ? 8 : 0);
+      cp_async8(st + 32 * CH * 2 + grp, ok ? R + r : R, ok ? 8 : 0);
+      cp_async8(st + 32 * CH * 2 + 8 + grp, ok ? Z + r : Z, ok ? 8 : 0);
     }
     cp_async_commit();
   };
 
 #pragma unroll
   for (int s = 0; s < kGsStages - 1; ++s) issue(s);
-  for (long long gi = 0; gi < ngroups; ++gi) {
+  for (int gi = 0; gi < ngroups; ++gi) {
     __syncwarp();
     issue(gi + kGsStages - 1);
     cp_async_wait<kGsStages - 1>();
     __syncwarp();
-    const double* st = ring + (int)(gi % kGsStages) * kLagStageDoubles;
-    const long long r = wfirst + gi * step + grp;
-    const bool ok = r < re;
+    const double* st = ring + (gi % kGsStages) * kLagStageDoubles;
+    const int r = wfirst + gi * step + grp;
     double d1 = 0.0, d2 = 0.0;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
@@ -623,11 +629,11 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
       d1 += __shfl_xor_sync(0xffffffffu, d1, o);
       d2 += __shfl_xor_sync(0xffffffffu, d2, o);
     }
-    if (ok && sub == 0) {
-      const double xu = st[128 + grp], xz = st[136 + grp];
+    if (r < re && sub == 0) {
+      const double xu = st[32 * CH * 2 + grp], xz = st[32 * CH * 2 + 8 + grp];
       const double vj = ((xu - d1) * b1) * b2s;
       const double r1 = rb * (xz - d2 - vjz * vj);
-      V[r * ldv + j] = vj;
+      V[(size_t)r * ldv + j] = vj;
       R[r] = r1;
       nrm += r1 * r1;
     }
@@ -726,7 +732,7 @@ static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gs_lag_project_kernel<LP><<<p.grid, kGsThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, U, Z, partS, partT, state);
+  gs_lag_project_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, U, Z, partS, partT, state);
   return cudaGetLastError();
 }
 
@@ -741,30 +747,26 @@ static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, i
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gs_lag_correct_kernel<LP><<<p.grid, kGsThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, R, Z, partS, partT,
-                                                                       nrows_in, part_out, scal, alpha, beta, state);
+  gs_lag_correct_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, R, Z, partS, partT,
+                                                                        nrows_in, part_out, scal, alpha, beta, state);
   return cudaGetLastError();
 }
 
 cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                            const double* U, const double* Z, double* partS, double* partT, int* state) {
-  if (p.lpr == 4) return lag_project_lp<4>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
-  if (p.lpr == 8) return lag_project_lp<8>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
-  if (p.lpr == 16) return lag_project_lp<16>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
-  return lag_project_lp<32>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  if (ncols <= 32) return lag_project_lp<4>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  if (ncols <= 64) return lag_project_lp<8>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  return lag_project_lp<16>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
 }
 
 cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
                            const double* Z, const double* partS, const double* partT, int nrows_in,
                            double* part_out, double* scal, double* alpha, double* beta, int* state) {
-  if (p.lpr == 4)
+  if (ncols <= 32)
     return lag_correct_lp<4>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
-  if (p.lpr == 8)
+  if (ncols <= 64)
     return lag_correct_lp<8>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
-  if (p.lpr == 16)
-    return lag_correct_lp<16>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta,
-                              state);
-  return lag_correct_lp<32>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+  return lag_correct_lp<16>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
 }
 
 }  // namespace lg

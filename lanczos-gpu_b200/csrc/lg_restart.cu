@@ -36,6 +36,7 @@ namespace lg {
 namespace {
 
 constexpr int kRsThreads = 128;
+constexpr int kRsSmemM = 72;   // m <= 72: M and the 4 m^2 inverse-iteration factors (5 m^2 doubles) fit in shared memory
 constexpr double kUnit = 1.1102230246251565e-16;        // 2^-53
 constexpr double kEps23Arpack = 2.3112508282095347e-11;  // (2^-53)^(2/3)
 
@@ -137,8 +138,12 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   if (sh_stop != STATUS_RUNNING) return;
   const double bn = sh_bn;
 
-  // ---- 2./3. Ritz values (bisection) and eigenvectors of T (inverse iteration)
-  if (!tridiag_eigen_cta<kRsThreads>(d, e, e2, m, th, M, a.scratch, cl, &sh_onenrm)) {
+  // ---- 2./3. Ritz values (bisection) and eigenvectors of T (inverse iteration);
+  // the LU factors of the inverse iterations in shared memory behind M when
+  // they fit (their loads sit on the iterations' dependent chains)
+  const bool f_smem = m <= kRsSmemM;
+  if (!tridiag_eigen_cta<kRsThreads>(d, e, e2, m, th, M, f_smem ? M + (size_t)m * m : a.scratch, cl, &sh_onenrm,
+                                     f_smem ? m : 0)) {
     if (t == 0) {
       state[ST_ERRINFO] = 1;
       state[ST_STATUS] = STATUS_TRIDIAG_FAIL;
@@ -307,7 +312,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
 size_t restart_scratch_doubles() { return (size_t)4 * kMaxCols * kRsThreads; }
 
 cudaError_t restart_step(const RestartArgs& a, cudaStream_t st) {
-  const size_t smem = (size_t)a.m * a.m * sizeof(double);
+  const size_t smem = (size_t)a.m * a.m * sizeof(double) * (a.m <= kRsSmemM ? 5 : 1);
   cudaError_t e = cudaFuncSetAttribute(restart_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   restart_kernel<<<1, kRsThreads, smem, st>>>(a);

@@ -43,23 +43,23 @@ __device__ inline int sturm_count(const double* d, const double* e2, int m, doub
 }
 
 // Inverse iteration for eigenvalue lam of the tridiagonal (d, e): a pivoted
-// LU of T - lam I (factors in the thread's slice of F, stride NT), three
-// solves from a pseudo-random start, each followed by re-orthogonalisation
-// against the `nprev` finished vectors Z[:, c0 .. c0+nprev) of the same
-// cluster and normalisation.  Result in column `col` of Z (m x m, col-major).
-template <int NT>
-__device__ void inverse_iteration(const double* d, const double* e, int m, double lam, double pivtiny, double* F,
-                                  double* Z, int col, int c0, int nprev) {
+// LU of T - lam I (factors in the thread's slice of F: four planes of
+// `fplane` doubles, entry k of thread t at k * fs + t), three solves from a
+// pseudo-random start, each followed by re-orthogonalisation against the
+// `nprev` finished vectors Z[:, c0 .. c0+nprev) of the same cluster and
+// normalisation.  Result in column `col` of Z (m x m, col-major).
+__device__ inline void inverse_iteration(const double* d, const double* e, int m, double lam, double pivtiny,
+                                         double* F, int fs, int fplane, double* Z, int col, int c0, int nprev) {
   const int t = threadIdx.x;
-  double* u1 = F;                                  // [k * NT + t]
-  double* u2 = F + kMaxCols * NT;
-  double* u3 = F + 2 * kMaxCols * NT;
-  double* L = F + 3 * kMaxCols * NT;
+  double* u1 = F;                                  // [k * fs + t]
+  double* u2 = F + fplane;
+  double* u3 = F + 2 * fplane;
+  double* L = F + 3 * fplane;
   uint64_t piv[2] = {0ull, 0ull};
   double a = d[0] - lam, c = (m > 1) ? e[0] : 0.0;
   for (int k = 0; k < m - 1; ++k) {
     const double b = e[k], a1 = d[k + 1] - lam, c1 = (k + 1 < m - 1) ? e[k + 1] : 0.0;
-    const size_t ix = (size_t)k * NT + t;
+    const size_t ix = (size_t)k * fs + t;
     if (fabs(a) >= fabs(b)) {
       const double l = (a != 0.0) ? b / a : 0.0;
       u1[ix] = a; u2[ix] = c; u3[ix] = 0.0; L[ix] = l;
@@ -73,14 +73,14 @@ __device__ void inverse_iteration(const double* d, const double* e, int m, doubl
       c = -l * c1;
     }
   }
-  u1[(size_t)(m - 1) * NT + t] = a;
+  u1[(size_t)(m - 1) * fs + t] = a;
 
   double* x = Z + (size_t)col * m;
   for (int k = 0; k < m; ++k) x[k] = uniform_centered(0x9E3779B97F4A7C15ull + col, (uint64_t)k) * 2.0;
   for (int it = 0; it < 3; ++it) {
     // forward: row interchanges and L
     for (int k = 0; k < m - 1; ++k) {
-      const size_t ix = (size_t)k * NT + t;
+      const size_t ix = (size_t)k * fs + t;
       if ((piv[k >> 6] >> (k & 63)) & 1ull) {
         const double tmp = x[k];
         x[k] = x[k + 1];
@@ -90,7 +90,7 @@ __device__ void inverse_iteration(const double* d, const double* e, int m, doubl
     }
     // back substitution with U (diagonal perturbed away from zero)
     for (int k = m - 1; k >= 0; --k) {
-      const size_t ix = (size_t)k * NT + t;
+      const size_t ix = (size_t)k * fs + t;
       double p = u1[ix];
       if (fabs(p) < pivtiny) p = (p < 0.0) ? -pivtiny : pivtiny;
       double r = x[k];
@@ -123,12 +123,14 @@ __device__ void inverse_iteration(const double* d, const double* e, int m, doubl
 // bisection on Sturm counts (one thread each, accurate to ~eps*||T||), then
 // eigenvectors (columns of the m x m column-major Z) by inverse iteration,
 // clusters (gap <= 1e-3 ||T||_1) handled in rounds with re-orthogonalisation.
-// F: 4 * kMaxCols * NT doubles of global scratch; cl: kMaxCols ints of shared
-// memory; *onenrm (shared) receives ||T||_1.  Returns false (block-uniform)
-// when T has non-finite entries.  Must be called by all threads of the CTA.
+// F: inverse-iteration scratch, 4 * kMaxCols * NT doubles of global memory
+// (fs = 0), or 4 m^2 doubles of shared memory with fs = m (entry stride m,
+// planes of m * m); cl: kMaxCols ints of shared memory; *onenrm (shared)
+// receives ||T||_1.  Returns false (block-uniform) when T has non-finite
+// entries.  Must be called by all threads of the CTA.
 template <int NT>
 __device__ bool tridiag_eigen_cta(const double* d, const double* e, const double* e2, int m, double* th, double* Z,
-                                  double* F, int* cl, double* onenrm) {
+                                  double* F, int* cl, double* onenrm, int fs = 0) {
   __shared__ double sh_glo, sh_ghi, sh_pivmin;
   __shared__ int sh_rounds;
   const int t = threadIdx.x;
@@ -176,7 +178,10 @@ __device__ bool tridiag_eigen_cta(const double* d, const double* e, const double
   __syncthreads();
   const double pivtiny = kUnitRoundoff * fmax(*onenrm, kSafeMin);
   for (int r = 0; r < sh_rounds; ++r) {
-    if (t < m && t - cl[t] == r) inverse_iteration<NT>(d, e, m, th[t], pivtiny, F, Z, t, cl[t], r);
+    if (t < m && t - cl[t] == r) {
+      if (fs > 0) inverse_iteration(d, e, m, th[t], pivtiny, F, fs, m * fs, Z, t, cl[t], r);
+      else inverse_iteration(d, e, m, th[t], pivtiny, F, NT, kMaxCols * NT, Z, t, cl[t], r);
+    }
     __syncthreads();
   }
   return true;
