@@ -17,12 +17,14 @@
 #include "lg_csr.cuh"
 #include "lg_kernels.cuh"
 #include "lg_solver.h"
+#include "lg_staging.h"
 
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace lg {
@@ -173,8 +175,22 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
         g_last_error = "row_ptr is not monotone";
         return LG_ERR_INVALID;
       }
-    for (long long k = 0; k < nnz_; ++k)
-      if (col[k] < 0 || col[k] >= n_cols) {
+    // column range on all host cores (tens of millions of entries)
+    const int nth = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<char> bad((size_t)nth, 0);
+    std::vector<std::thread> pool;
+    for (int w = 0; w < nth; ++w)
+      pool.emplace_back([&, w] {
+        const long long b = nnz_ * w / nth, e = nnz_ * (w + 1) / nth;
+        for (long long k = b; k < e; ++k)
+          if (col[k] < 0 || col[k] >= n_cols) {
+            bad[w] = 1;
+            return;
+          }
+      });
+    for (std::thread& th : pool) th.join();
+    for (char b : bad)
+      if (b) {
         g_last_error = "column index out of range";
         return LG_ERR_INVALID;
       }
@@ -202,11 +218,18 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   LG_TRY(cudaMalloc(&d_rowptr, sizeof(int) * (size_t)(n + 1)));
   LG_TRY(cudaMalloc(&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
   LG_TRY(cudaMalloc(&d_val64, sizeof(double) * (size_t)std::max<long long>(nnz, 1)));
-  const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-  LG_TRY(cudaMemcpyAsync(d_rowptr, rowptr, sizeof(int) * (size_t)(n + 1), kind, stream));
-  if (nnz > 0) {
-    LG_TRY(cudaMemcpyAsync(d_col, col, sizeof(int) * (size_t)nnz, kind, stream));
-    LG_TRY(cudaMemcpyAsync(d_val64, vals, sizeof(double) * (size_t)nnz, kind, stream));
+  if (device_ptrs) {
+    LG_TRY(cudaMemcpyAsync(d_rowptr, rowptr, sizeof(int) * (size_t)(n + 1), cudaMemcpyDeviceToDevice, stream));
+    if (nnz > 0) {
+      LG_TRY(cudaMemcpyAsync(d_col, col, sizeof(int) * (size_t)nnz, cudaMemcpyDeviceToDevice, stream));
+      LG_TRY(cudaMemcpyAsync(d_val64, vals, sizeof(double) * (size_t)nnz, cudaMemcpyDeviceToDevice, stream));
+    }
+  } else {   // pageable host arrays: through the pinned staging pool
+    LG_TRY(staged_h2d(d_rowptr, rowptr, sizeof(int) * (size_t)(n + 1), stream));
+    if (nnz > 0) {
+      LG_TRY(staged_h2d(d_col, col, sizeof(int) * (size_t)nnz, stream));
+      LG_TRY(staged_h2d(d_val64, vals, sizeof(double) * (size_t)nnz, stream));
+    }
   }
 
   LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
@@ -1072,8 +1095,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     ba.state = state;
     const BasisPlan bp = basis_plan(n, m, ksel, grid_basis);
     LG_TRY(timed(LG_K_BASIS, 8.0 * n * (m + ksel), 1, [&] { return basis_update(bp, ba, stream); }));
-    if (!io_on_device)
-      LG_TRY(cudaMemcpyAsync(evecs, Ytmp, sizeof(double) * (size_t)n * ksel, cudaMemcpyDeviceToHost, stream));
+    if (!io_on_device) LG_TRY(staged_d2h(evecs, Ytmp, sizeof(double) * (size_t)n * ksel, stream));
   }
   LG_TRY(cudaEventRecord(ev1, stream));
   LG_TRY(cudaStreamSynchronize(stream));

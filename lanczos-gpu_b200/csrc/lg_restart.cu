@@ -8,7 +8,7 @@
 //
 //   1. beta_m = ||r|| from the partial sums of the last Gram-Schmidt pass,
 //      DGKS / breakdown checks for the last step;
-//   2. Ritz values: bisection on Sturm counts, one thread per eigenvalue
+//   2. Ritz values: multisection on Sturm counts, a few lanes per eigenvalue
 //      (all eigenvalues to ~eps*||T|| absolute accuracy, the accuracy of QR);
 //   3. eigenvectors of T: inverse iteration with a pivoted tridiagonal LU,
 //      one thread per eigenvalue, vectors of eigenvalue clusters
@@ -21,8 +21,8 @@
 //   5. either the wanted pairs are selected (finished), or the np exact shifts
 //      are applied by bulge chasing.  Up to 32 bulges run at once, one lane
 //      each, three rows apart (rotations of neighbouring bulges then touch
-//      disjoint entries), and every thread applies the step's rotations to its
-//      own row of Q.  The result equals the shift-after-shift chase of the
+//      disjoint entries), and the step's rotations are applied to Q by several
+//      threads per row, each taking a share of them.  The result equals the shift-after-shift chase of the
 //      reference; the deflation splitting of ARPACK's dsapps is not done
 //      (a negligible coupling just makes the chase pass identity rotations).
 #include "lg_common.cuh"
@@ -35,7 +35,7 @@ namespace lg {
 
 namespace {
 
-constexpr int kRsThreads = 128;
+constexpr int kRsThreads = 512;   // bisection lanes per eigenvalue and Q-update threads per row scale with it
 constexpr int kRsSmemM = 72;   // m <= 72: M and the 4 m^2 inverse-iteration factors (5 m^2 doubles) fit in shared memory
 constexpr double kUnit = 1.1102230246251565e-16;        // 2^-53
 constexpr double kEps23Arpack = 2.3112508282095347e-11;  // (2^-53)^(2/3)
@@ -221,6 +221,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   // every unreduced block.  Couplings that become negligible during the
   // chases are left alone (the bulge then just passes identity rotations).
   const int np = sh_np, nev = sh_nev;
+  int tpr = 1;   // threads per row of Q in the rotation updates
+  while (tpr < 32 && 2 * tpr * m <= kRsThreads) tpr *= 2;
   __shared__ int blk_lo[kMaxCols], blk_hi[kMaxCols];
   __shared__ int sh_nblk;
   __syncthreads();   // M (eigenvectors) no longer needed
@@ -273,14 +275,17 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
           rot_k[lane] = kk;
         }
         __syncthreads();
-        if (t < m) {
-          for (int s = 0; s < nb; ++s) {
+        // the step's rotations touch disjoint column pairs (bulges three
+        // rows apart), so the tpr threads of a row split them freely
+        if (t < tpr * m) {
+          const int row = t / tpr;
+          for (int s = t % tpr; s < nb; s += tpr) {
             const int k = rot_k[s];
             if (k < 0) continue;
             const double c = rot_c[s], sn = rot_s[s];
-            const double x0 = M[t + (size_t)k * m], x1 = M[t + (size_t)(k + 1) * m];
-            M[t + (size_t)k * m] = c * x0 - sn * x1;
-            M[t + (size_t)(k + 1) * m] = sn * x0 + c * x1;
+            const double x0 = M[row + (size_t)k * m], x1 = M[row + (size_t)(k + 1) * m];
+            M[row + (size_t)k * m] = c * x0 - sn * x1;
+            M[row + (size_t)(k + 1) * m] = sn * x0 + c * x1;
           }
         }
         __syncthreads();

@@ -42,6 +42,29 @@ __device__ inline int sturm_count(const double* d, const double* e2, int m, doub
   return cnt;
 }
 
+// Sturm counts at P points at once: P independent LDL^T pivot chains
+// interleaved, so their divisions overlap.  Same recurrence as sturm_count.
+constexpr int kSturmP = 4;
+template <int P>
+__device__ __forceinline__ void sturm_counts(const double* d, const double* e2, int m, const double* x,
+                                             double pivmin, int* cnt) {
+  double q[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    q[p] = d[0] - x[p];
+    cnt[p] = q[p] < 0.0;
+  }
+  for (int k = 1; k < m; ++k) {
+    const double dk = d[k], ek = e2[k - 1];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      if (fabs(q[p]) < pivmin) q[p] = -pivmin;
+      q[p] = (dk - x[p]) - ek / q[p];
+      cnt[p] += q[p] < 0.0;
+    }
+  }
+}
+
 // Inverse iteration for eigenvalue lam of the tridiagonal (d, e): a pivoted
 // LU of T - lam I (factors in the thread's slice of F: four planes of
 // `fplane` doubles, entry k of thread t at k * fs + t), three solves from a
@@ -120,7 +143,7 @@ __device__ inline void inverse_iteration(const double* d, const double* e, int m
 
 // All eigenpairs of the symmetric tridiagonal (d, e) (e[i] couples i, i+1;
 // e2 = e^2), computed by one CTA of NT >= m threads: eigenvalues ascending by
-// bisection on Sturm counts (one thread each, accurate to ~eps*||T||), then
+// multisection on Sturm counts (up to 8 lanes each, accurate to ~eps*||T||), then
 // eigenvectors (columns of the m x m column-major Z) by inverse iteration,
 // clusters (gap <= 1e-3 ||T||_1) handled in rounds with re-orthogonalisation.
 // F: inverse-iteration scratch, 4 * kMaxCols * NT doubles of global memory
@@ -153,16 +176,50 @@ __device__ bool tridiag_eigen_cta(const double* d, const double* e, const double
   }
   __syncthreads();
   if (!(*onenrm >= 0.0)) return false;
-  if (t < m) {
-    double lo = sh_glo, hi = sh_ghi;
-    for (int it = 0; it < 128; ++it) {
-      const double mid = 0.5 * (lo + hi);
-      if (hi - lo <= 2.0 * kUnitRoundoff * fmax(fabs(lo), fabs(hi)) + 4.0 * sh_pivmin || mid <= lo || mid >= hi)
-        break;
-      if (sturm_count(d, e2, m, mid, sh_pivmin) > t) hi = mid;
-      else lo = mid;
+  // Multisection: eigenvalue i belongs to G consecutive lanes (G a power of
+  // two, G m <= NT, at most 8), each evaluating kSturmP interior points per
+  // round with interleaved Sturm chains (their divisions overlap), so a round
+  // cuts the bracket into G kSturmP + 1 pieces.  All G lanes hold the same
+  // bracket, updated from the first point whose count exceeds i.
+  {
+    int G = 1;
+    while (G < 8 && 2 * G * m <= NT) G *= 2;
+    const int i = t / G, g = t % G;
+    const int np = G * kSturmP;
+    const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << ((t & 31) & ~(G - 1)));
+    if (i < m) {
+      double lo = sh_glo, hi = sh_ghi;
+      for (int it = 0; it < 128; ++it) {
+        // The stop test must be the same in every lane of the group (they
+        // shuffle below): it reads only the bracket and the round's first and
+        // last points, which every lane computes with the same arithmetic,
+        // and the group votes on it as well.
+        const double x0 = lo + (hi - lo) * (1.0 / (double)(np + 1));
+        const double xl = lo + (hi - lo) * ((double)np / (double)(np + 1));
+        bool stop = hi - lo <= 2.0 * kUnitRoundoff * fmax(fabs(lo), fabs(hi)) + 4.0 * sh_pivmin || x0 <= lo ||
+                    xl >= hi;
+        stop = __any_sync(gmask, stop);
+        if (stop) break;
+        double x[kSturmP];
+#pragma unroll
+        for (int q = 0; q < kSturmP; ++q) x[q] = lo + (hi - lo) * ((double)(g * kSturmP + q + 1) / (double)(np + 1));
+        int cnt[kSturmP];
+        sturm_counts<kSturmP>(d, e2, m, x, sh_pivmin, cnt);
+        int first = kSturmP;   // the group-local index of this lane's first point with count > i
+#pragma unroll
+        for (int q = kSturmP - 1; q >= 0; --q)
+          if (cnt[q] > i) first = q;
+        int f = g * kSturmP + first;   // global index; np when none of this lane's points qualifies
+        if (first == kSturmP) f = np;
+        for (int o = 1; o < G; o <<= 1) f = min(f, __shfl_xor_sync(gmask, f, o));
+        // the bracket's new ends: points f-1 and f of the round (lo / hi at the ends)
+        const double nlo = f == 0 ? lo : lo + (hi - lo) * ((double)f / (double)(np + 1));
+        const double nhi = f == np ? hi : lo + (hi - lo) * ((double)(f + 1) / (double)(np + 1));
+        lo = nlo;
+        hi = nhi;
+      }
+      if (g == 0) th[i] = 0.5 * (lo + hi);
     }
-    th[t] = 0.5 * (lo + hi);
   }
   __syncthreads();
   if (t == 0) {

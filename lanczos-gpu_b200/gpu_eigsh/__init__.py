@@ -109,7 +109,8 @@ def _as_csr(A):
         raise TypeError("A must be a scipy sparse matrix or a 2-D numpy array")
     if M.shape[0] != M.shape[1]:
         raise ValueError(f"Matrix must be square, got {M.shape}")
-    M.sum_duplicates()
+    # duplicate or unsorted entries need no pass here: the sparse products sum
+    # every stored entry, which is the matrix scipy means
     indptr = np.ascontiguousarray(M.indptr, dtype=np.int32)
     indices = np.ascontiguousarray(M.indices, dtype=np.int32)
     data = np.ascontiguousarray(M.data, dtype=np.float64)
