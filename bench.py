@@ -64,10 +64,12 @@ WORKLOAD = (f"eigsh k={K_EIG} which=LA ncv={NCV} tol={TOL:g} on the n=1e6 kNN gr
 
 
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) over the
-# algorithmic bytes of the same launch, from the captures summarised under
-# profiles/ (captured on the configuration-1 / reduced configuration-3
-# workloads); `traffic` = ratio x the bench's algorithmic bytes per launch.
-TRAFFIC_RATIO = {"spmv": 1.27, "gs_project": 1.056, "gs_correct_project": 1.044, "gs_correct": 1.049,
+# algorithmic bytes of the same launch, per kernel class of the headline plan
+# (lag steps: the SpMV without the column write, the lag projection and
+# correction, the extension-end passes) and of the SLQ phases, from the
+# committed ncu summaries (configuration-1 / reduced configuration-3
+# captures); `traffic` = ratio x the bench's algorithmic bytes per launch.
+TRAFFIC_RATIO = {"spmv": 0.975, "gs_project": 1.008, "gs_correct_project": 1.03, "gs_correct": 1.049,
                  "basis": 1.035, "slq_forward": 0.955, "slq_backward": 0.96}
 
 
@@ -312,7 +314,7 @@ def run_slq(args, dev, with_e2e, with_cpu, world=1, rank=0):
     out["roofline"] = {"bound": "hbm", "kernel": dom[0], "achieved": dom[1], "peak": peak, "unit": "GB/s",
                        "frac": dom[1] / peak, "peak_source": peak_kind,
                        "traffic": TRAFFIC_RATIO[dom[0]] * dom[3], "traffic_unit": "bytes per phase (all steps)",
-                       "traffic_source": "ncu ratio (profiles/slq_products_knn6e5.md) x algorithmic bytes",
+                       "traffic_source": "ncu DRAM/algorithmic ratio of the phase (committed ncu summary) x algorithmic bytes",
                        "algorithmic_bytes_per_launch": dom[3], "avg_launch_ms": dom[2]}
     out["phases"] = {"forward_ms": f_ms, "forward_GBs": fa, "forward_frac": fa / peak, "forward_bytes": fwd_b,
                      "backward_ms": b_ms, "backward_GBs": ba, "backward_frac": ba / peak, "backward_bytes": bwd_b}
@@ -876,7 +878,7 @@ def run_ours(args):
                      "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
                      "traffic": (TRAFFIC_RATIO[dom] * kbytes[dom] / max(1, kcalls[dom])) if dom in TRAFFIC_RATIO
                      else None,
-                     "traffic_source": "ncu DRAM/algorithmic ratio of this kernel (profiles/) x algorithmic bytes",
+                     "traffic_source": "ncu DRAM/algorithmic ratio of this kernel (committed ncu summary) x algorithmic bytes",
                      "avg_launch_us": 1000.0 * kms[dom] / max(1, kcalls[dom]),
                      "algorithmic_bytes_per_launch": kbytes[dom] / max(1, kcalls[dom])},
         "step_roofline": {"kernels": step_cls, "achieved": step_ach, "peak": peak, "unit": "GB/s",
