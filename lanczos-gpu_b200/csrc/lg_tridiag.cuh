@@ -97,6 +97,14 @@ __device__ inline void inverse_iteration(const double* d, const double* e, int m
     }
   }
   u1[(size_t)(m - 1) * fs + t] = a;
+  // the back substitutions multiply by the reciprocals of the pivots (each
+  // perturbed away from zero): u1 holds 1 / pivot from here on
+  for (int k = 0; k < m; ++k) {
+    const size_t ix = (size_t)k * fs + t;
+    double pv = u1[ix];
+    if (fabs(pv) < pivtiny) pv = (pv < 0.0) ? -pivtiny : pivtiny;
+    u1[ix] = 1.0 / pv;
+  }
 
   double* x = Z + (size_t)col * m;
   for (int k = 0; k < m; ++k) x[k] = uniform_centered(0x9E3779B97F4A7C15ull + col, (uint64_t)k) * 2.0;
@@ -111,15 +119,13 @@ __device__ inline void inverse_iteration(const double* d, const double* e, int m
       }
       x[k + 1] -= L[ix] * x[k];
     }
-    // back substitution with U (diagonal perturbed away from zero)
+    // back substitution with U (reciprocal pivots)
     for (int k = m - 1; k >= 0; --k) {
       const size_t ix = (size_t)k * fs + t;
-      double p = u1[ix];
-      if (fabs(p) < pivtiny) p = (p < 0.0) ? -pivtiny : pivtiny;
       double r = x[k];
       if (k + 1 < m) r -= u2[ix] * x[k + 1];
       if (k + 2 < m) r -= u3[ix] * x[k + 2];
-      x[k] = r / p;
+      x[k] = r * u1[ix];
     }
     // re-orthogonalise against the cluster's finished vectors, normalise
     for (int q = 0; q < nprev; ++q) {
@@ -131,9 +137,10 @@ __device__ inline void inverse_iteration(const double* d, const double* e, int m
     double mx = 0.0;
     for (int k = 0; k < m; ++k) mx = fmax(mx, fabs(x[k]));
     if (!(mx > 0.0)) mx = 1.0;
+    const double rmx = 1.0 / mx;
     double s2 = 0.0;
     for (int k = 0; k < m; ++k) {
-      x[k] /= mx;
+      x[k] *= rmx;
       s2 += x[k] * x[k];
     }
     const double inv = 1.0 / sqrt(s2);
