@@ -6,7 +6,7 @@
 // Differences in structure (same mathematics):
 //  * all vectors, alpha/beta, the restart logic and the convergence test stay
 //    on the device; the host enqueues a whole Lanczos extension
-//    (4 kernels per step) without waiting and synchronises once per
+//    (3 kernels per lag step, 4 with in-step CGS2) without waiting and synchronises once per
 //    restart to read a 16-word state record;
 //  * rare events (a third DGKS pass, an invariant subspace) are detected on
 //    the device, which then turns the rest of the queued work into no-ops;
