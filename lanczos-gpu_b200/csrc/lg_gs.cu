@@ -590,10 +590,13 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
   const int ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
   double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
 
+  // The warp walks its row groups last to first: the projection just streamed
+  // them first to last, so the correction starts on the rows that are still
+  // in L2 (measured 29.2 against 29.9 ms per configuration-1 solve).
   auto issue = [&](int gi) {
     double* st = ring + (gi % kGsStages) * kLagStageDoubles;
-    const int r = wfirst + gi * step + grp;
-    const bool ok = gi < ngroups && r < re;
+    const int r = gi < ngroups ? wfirst + (ngroups - 1 - gi) * step + grp : re;
+    const bool ok = r < re;
     const double* row = V + (size_t)r * ldv + 2 * sub;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
@@ -615,7 +618,7 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
     cp_async_wait<kGsStages - 1>();
     __syncwarp();
     const double* st = ring + (gi % kGsStages) * kLagStageDoubles;
-    const int r = wfirst + gi * step + grp;
+    const int r = wfirst + (ngroups - 1 - gi) * step + grp;
     double d1 = 0.0, d2 = 0.0;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
