@@ -81,20 +81,25 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
 
   // Each lane group works on two rows at once so the dependent load chains
-  // (row_ptr -> col -> x gather) of the two rows overlap.
+  // (row_ptr -> col -> x gather) of the two rows overlap; the row bounds of
+  // the next trip are loaded while this trip's gathers are in flight.
   const int lane = threadIdx.x & (L - 1);
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
   const int rows_per_warp = 32 / L;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; (long long)w * rows_per_warp * 2 < count;
-       w += warps_total) {
-    const int iA = w * rows_per_warp * 2 + ((threadIdx.x & 31) / L);
-    const int iB = iA + rows_per_warp;
+  const int gl = (threadIdx.x & 31) / L;
+  auto bounds = [&](int w, int& rowA, int& rowB, int& kA, int& eA, int& kB, int& eB) {
+    const int iA = w * rows_per_warp * 2 + gl, iB = iA + rows_per_warp;
     const bool okA = iA < count, okB = iB < count;
-    const int rowA = okA ? (list ? __ldg(list + iA) : iA) : 0;
-    const int rowB = okB ? (list ? __ldg(list + iB) : iB) : 0;
-    int kA = 0, eA = 0, kB = 0, eB = 0;
+    rowA = okA ? (list ? __ldg(list + iA) : iA) : -1;
+    rowB = okB ? (list ? __ldg(list + iB) : iB) : -1;
+    kA = eA = kB = eB = 0;
     if (okA) { kA = __ldg(rowptr + rowA); eA = min(__ldg(rowptr + rowA + 1), kA + kLongRow); kA += lane; }
     if (okB) { kB = __ldg(rowptr + rowB); eB = min(__ldg(rowptr + rowB + 1), kB + kLongRow); kB += lane; }
+  };
+  int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int rowA, rowB, kA, eA, kB, eB;
+  if ((long long)w * rows_per_warp * 2 < count) bounds(w, rowA, rowB, kA, eA, kB, eB);
+  for (; (long long)w * rows_per_warp * 2 < count; w += warps_total) {
     double accA = 0.0, accB = 0.0;
     while (kA < eA || kB < eB) {
       if (kA < eA) accA += (double)__ldg(val + kA) * __ldg(R + __ldg(col + kA));
@@ -102,19 +107,22 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
       kA += L;
       kB += L;
     }
+    const int curA = rowA, curB = rowB;
+    const int wn = w + warps_total;
+    if ((long long)wn * rows_per_warp * 2 < count) bounds(wn, rowA, rowB, kA, eA, kB, eB);
 #pragma unroll
     for (int o = L / 2; o > 0; o >>= 1) {
       accA += __shfl_xor_sync(0xffffffffu, accA, o);
       accB += __shfl_xor_sync(0xffffffffu, accB, o);
     }
     if (lane == 0) {
-      if (okA) {
-        W[rowA] = (accA * s1) * s2;
-        if (Vj) Vj[(size_t)rowA * ldv] = (R_own[rowA] * s1) * s2;
+      if (curA >= 0) {
+        W[curA] = (accA * s1) * s2;
+        if (Vj) Vj[(size_t)curA * ldv] = (R_own[curA] * s1) * s2;
       }
-      if (okB) {
-        W[rowB] = (accB * s1) * s2;
-        if (Vj) Vj[(size_t)rowB * ldv] = (R_own[rowB] * s1) * s2;
+      if (curB >= 0) {
+        W[curB] = (accB * s1) * s2;
+        if (Vj) Vj[(size_t)curB * ldv] = (R_own[curB] * s1) * s2;
       }
     }
   }
