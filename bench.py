@@ -17,8 +17,13 @@ solves; `ms_per_step` is the time to converge.
 The Krylov basis (n x 61 fp64 = 488 MB) is larger than L2, so no L2 flush is
 needed between steps.
 
-With N GPUs (torchrun), every rank solves its own copy (replicas, weak
-scaling); value = all ranks' Lanczos steps / max-over-ranks time.
+With N GPUs (torchrun), the same solve runs with the rows of the matrix
+split over the ranks (Cuthill-McKee order, then N row blocks; halo exchange
+before each sparse product, one reduction of the Gram-Schmidt sums per pass):
+strong scaling, value = the solve's Lanczos steps / max-over-ranks time.
+A "mixed" object times the same solve in the mixed mode (fp32 matrix values,
+fp64 accumulation and basis), and a "summary" object at the end of the line
+repeats every leg's headline number.
 
 The same line carries an "slq" object for the second half of the metric,
 "SLQ logdet+grad sec" (configuration 3): slq_logdet of the IMGP precision
@@ -35,9 +40,12 @@ values; rows partitioned over the ranks at N > 1) and "sinv" (configuration
 inner CG to 1e-12; one GPU, N = 1 only).
 
 --impl reference times the reference's algorithm on the host cores: the CPU
-oracle (C restatement of the reference IRLM, OpenMP over all cores) running
-the initial 60-step Lanczos factorisation of the same matrix per step, and the
-reference's torch SLQ algorithm (oracle/slq.py) on a bounded sample.
+oracle (C restatement of the reference IRLM, OpenMP over every core the
+process may use, whatever OMP_NUM_THREADS a launcher set) running the initial
+60-step Lanczos factorisation of the same matrix per step, and the
+reference's torch SLQ algorithm (oracle/slq.py) on a bounded sample.  It
+builds its matrix with the seeded generators loaded by file path and never
+loads the CUDA library.
 """
 from __future__ import annotations
 
@@ -137,8 +145,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _synthetic():
+    """gpu_eigsh/synthetic.py (numpy / scipy generators only), loaded by file
+    path: importing it through the package would map the CUDA library, which
+    the reference arm must not load."""
+    import importlib.util
+
+    name = "lg_synthetic_bench"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, ROOT / "lanczos-gpu_b200" / "gpu_eigsh" / "synthetic.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        sys.modules[name] = mod
+    return sys.modules[name]
+
+
+def host_cores() -> int:
+    """Cores this process may run on.  torchrun exports OMP_NUM_THREADS=1 to
+    every rank; the CPU legs set their thread counts from this instead."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def build_workload():
-    from gpu_eigsh import synthetic as syn
+    syn = _synthetic()
 
     t0 = time.time()
     L, info = syn.knn_laplacian(N_POINTS, k=10, seed=1)
@@ -150,8 +182,9 @@ def build_workload():
 def cpu_baseline(L, v0, budget_s=20.0):
     """The oracle (reference algorithm, C, all host cores) on a bounded sample:
     repeated 60-step Lanczos factorisations of the same matrix."""
-    from oracle.irlm import num_threads, oracle_lanczos_steps
+    from oracle.irlm import num_threads, oracle_lanczos_steps, set_num_threads
 
+    set_num_threads(host_cores())
     oracle_lanczos_steps(L, 4, v0, cgs2=False)  # warm (page in, thread pool)
     steps, t0 = 0, time.perf_counter()
     while True:
@@ -188,9 +221,7 @@ def slq_bytes(n, nnz, B, nu, m, es):
 
 
 def slq_edges(n=N_POINTS):
-    from gpu_eigsh import synthetic as syn
-
-    return syn.knn_edge_list(n, k=10, seed=1)
+    return _synthetic().knn_edge_list(n, k=10, seed=1)
 
 
 def slq_cpu_baseline(idx, d2, n=N_POINTS, m_full=SLQ_M):
@@ -201,7 +232,7 @@ def slq_cpu_baseline(idx, d2, n=N_POINTS, m_full=SLQ_M):
     import torch
     from oracle import slq as oslq
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(host_cores())
     it, dt = torch.from_numpy(idx), torch.from_numpy(d2).to(torch.float32)
     t = []
     for m in (1, 2):
@@ -561,57 +592,126 @@ def run_graph(args, dev, with_cpu):
     return out
 
 
-def run_knn_partitioned(args, L, v0, dev, world, rank):
-    """Configuration 1 with its rows split over the ranks (strong scaling):
-    the matrix renumbered by BFS level (gpu_eigsh.ordering) so that the row
-    blocks touch only their neighbours, then the halo exchange carries the
-    boundary rows before each sparse product.  Complete solves timed with CUDA
-    events, max over ranks."""
+class HeadlineSolver:
+    """The configuration-1 solve of the headline.
+
+    One GPU: an EigshPlan on the device CSR that renumbers the rows in
+    Cuthill-McKee order inside the plan (LG_PLAN_REORDER_BFS).  N GPUs: the
+    same Cuthill-McKee order applied before the split (gpu_eigsh.ordering),
+    rows in N blocks (gpu_eigsh.distributed.PartitionedEigsh), the halo of
+    boundary rows exchanged before each sparse product, one solve shared by
+    all ranks (strong scaling).  solve(profile) -> (eigenvalues, info)."""
+
+    def __init__(self, L, v0, dev, world, rank, mixed=False, reorder=True):
+        import torch
+
+        import gpu_eigsh
+
+        self.world, self.n = world, L.shape[0]
+        n = self.n
+        rp = torch.from_numpy(L.indptr.astype(np.int32)).to(dev)
+        ci = torch.from_numpy(L.indices.astype(np.int32)).to(dev)
+        va = torch.from_numpy(L.data.astype(np.float64)).to(dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        if world == 1:
+            self.comm = None
+            self.plan = gpu_eigsh.EigshPlan(None, max_ncv=NCV, mixed=mixed, reorder=reorder,
+                                            device_csr=(n, L.nnz, rp.data_ptr(), ci.data_ptr(), va.data_ptr()))
+            self.v0 = torch.from_numpy(v0).to(dev)
+            self.Y = torch.empty((n, K_EIG), dtype=torch.float64, device=dev)
+            self.exchange = None
+        else:
+            from gpu_eigsh.distributed import Communicator, PartitionedEigsh, partition_rows
+            from gpu_eigsh.ordering import cm_order, permute_symmetric
+
+            perm = cm_order(rp, ci)
+            self.perm = perm.cpu().numpy()
+            rp, ci, va, _ = permute_symmetric(rp, ci, va, perm)
+            r0, r1 = partition_rows(n, world, rank)
+            a, b = int(rp[r0]), int(rp[r1])
+            lrp = (rp[r0:r1 + 1] - a).contiguous()
+            lci, lva = ci[a:b].contiguous(), va[a:b].contiguous()
+            self.v0 = torch.from_numpy(v0).to(dev)[perm][r0:r1].contiguous()
+            self.comm = Communicator()
+            self.pe = PartitionedEigsh(self.comm, n, lrp, lci, lva, max_ncv=NCV, mixed=mixed)
+            self.plan = self.pe.plan
+            self.Y = torch.empty((r1 - r0, K_EIG), dtype=torch.float64, device=dev)
+            self.exchange = self.pe.exchange_info
+            self.rows = (r0, r1)
+        torch.cuda.synchronize()
+        self.plan_s = time.perf_counter() - t0
+
+    def solve(self, profile=False):
+        w, _ = self.plan.solve(k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0_device=self.v0.data_ptr(),
+                               evecs_out=self.Y.data_ptr(), profile=profile)
+        return w, dict(self.plan.last_info)
+
+    def close(self):
+        self.plan.close()
+        if self.comm is not None:
+            self.comm.close()
+
+
+def max_over_ranks(x, dev, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def e2e_partitioned(args, L, v0, dev, world, rank):
+    """End to end at N GPUs through the public API: each rank copies its
+    slice of the (already renumbered) host CSR and v0 from pinned host memory,
+    builds the partitioned plan (a collective: halo lists), solves, and
+    copies its rows of the eigenvectors back to the host.  Wall time per
+    call, max over ranks."""
     import torch
     import torch.distributed as dist
 
     from gpu_eigsh.distributed import Communicator, PartitionedEigsh, partition_rows
-    from gpu_eigsh.ordering import bfs_order, permute_symmetric
 
     n = L.shape[0]
-    rp = torch.from_numpy(L.indptr.astype(np.int32)).to(dev)
-    ci = torch.from_numpy(L.indices.astype(np.int32)).to(dev)
-    va = torch.from_numpy(L.data.astype(np.float64)).to(dev)
-    perm = bfs_order(rp, ci)
-    rp, ci, va, _ = permute_symmetric(rp, ci, va, perm)
+    rp = torch.from_numpy(L.indptr.astype(np.int32))
+    ci = torch.from_numpy(L.indices.astype(np.int32))
     r0, r1 = partition_rows(n, world, rank)
     a, b = int(rp[r0]), int(rp[r1])
-    lrp = (rp[r0:r1 + 1] - a).contiguous()
-    lci, lva = ci[a:b].contiguous(), va[a:b].contiguous()
-    v0l = torch.from_numpy(v0).to(dev)[perm][r0:r1].contiguous()
-    del rp, ci, va
+    h_rp = (rp[r0:r1 + 1] - a).pin_memory()
+    h_ci = ci[a:b].pin_memory()
+    h_va = torch.from_numpy(L.data[a:b].astype(np.float64)).pin_memory()
+    h_v0 = torch.from_numpy(v0[r0:r1].copy()).pin_memory()
     comm = Communicator()
-    pe = PartitionedEigsh(comm, n, lrp, lci, lva, max_ncv=NCV)
-    kw = dict(which="LA", ncv=NCV, tol=TOL)
-    pe.solve(K_EIG, v0l, **kw)
-    torch.cuda.synchronize()
+
+    def call():
+        d_rp, d_ci = h_rp.to(dev, non_blocking=True), h_ci.to(dev, non_blocking=True)
+        d_va, d_v0 = h_va.to(dev, non_blocking=True), h_v0.to(dev, non_blocking=True)
+        pe = PartitionedEigsh(comm, n, d_rp, d_ci, d_va, max_ncv=NCV)
+        w, Y = pe.solve(K_EIG, d_v0, which="LA", ncv=NCV, tol=TOL)
+        Yh = Y.cpu()
+        steps = pe.last_info["steps"]
+        pe.close()
+        return w, Yh, steps
+
+    call()
+    reps = max(1, min(args.steps, 2))
     dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(1, min(args.steps, 3))
-    ev0.record()
+    t0 = time.perf_counter()
+    steps = 0
     for _ in range(reps):
-        w, _ = pe.solve(K_EIG, v0l, **kw)
-    ev1.record()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / reps
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    info = dict(pe.last_info)
-    mode, recv_rows, send_rows = pe.exchange_info
-    pe.close()
+        _, _, st = call()
+        steps += st
+    dist.barrier()
+    el = max_over_ranks(time.perf_counter() - t0, dev, world)
     comm.close()
-    return {"workload": WORKLOAD + "; rows renumbered by BFS level, then split in equal blocks",
-            "metric": "time_to_converge_s", "value": ms / 1000.0, "unit": "s", "higher_is_better": False,
-            "lanczos_steps_per_solve": info["steps"], "steps_per_sec": info["steps"] / (ms / 1000.0),
-            "exchange": mode, "halo_rows_received_rank0": recv_rows, "halo_rows_sent_rank0": send_rows,
-            "top_eigenvalues": [float(x) for x in w[-4:]], "parallelism": f"rows partitioned over {world} GPUs",
-            "scaling": "strong"}
+    h2d = int(h_rp.numel() * 4 + h_ci.numel() * 4 + h_va.numel() * 8 + h_v0.numel() * 8)
+    d2h = int((r1 - r0) * K_EIG * 8)
+    return {"value": steps / el, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_solve": 1000.0 * el / reps,
+            "note": "rank 0's bytes; every rank copies its own CSR slice and eigenvector rows"}
 
 
 ADJ_K = 20
@@ -694,7 +794,7 @@ def adjoint_cpu_baseline(L, w, X, g0, iters_gpu, sample_iters=30):
     OA.cg_deflated(L, float(w[0]), rhs, X, tol=0.0, max_iters=sample_iters)
     el = time.perf_counter() - t0
     per_it = el / sample_iters
-    return {"value": per_it * iters_gpu * ADJ_K, "unit": "s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": per_it * iters_gpu * ADJ_K, "unit": "s", "cores": host_cores(), "kind": "port",
             "sample": f"{sample_iters} deflated-CG iterations of one pair in {el:.2f} s, scaled to {ADJ_K} pairs x "
                       f"{iters_gpu} iterations (scipy sparse matvec + numpy deflation, host BLAS threads)"}
 
@@ -704,8 +804,9 @@ def run_reference(args):
     if rank != 0:
         return 0
     L, v0, winfo = build_workload()
-    from oracle.irlm import num_threads, oracle_lanczos_steps
+    from oracle.irlm import num_threads, oracle_lanczos_steps, set_num_threads
 
+    set_num_threads(host_cores())
     for _ in range(args.warmup):
         oracle_lanczos_steps(L, 8, v0, cgs2=False)
     times = []
@@ -798,24 +899,10 @@ def run_ours(args):
     L, v0, winfo = build_workload()
     n = L.shape[0]
     dev = torch.device("cuda", local)
-    rp = torch.from_numpy(L.indptr.astype(np.int32)).to(dev)
-    ci = torch.from_numpy(L.indices.astype(np.int32)).to(dev)
-    va = torch.from_numpy(L.data.astype(np.float64)).to(dev)
-    v0d = torch.from_numpy(v0).to(dev)
-    Y = torch.empty((n, K_EIG), dtype=torch.float64, device=dev)
-    torch.cuda.synchronize()
-    t_plan = time.perf_counter()
-    plan = gpu_eigsh.EigshPlan(None, max_ncv=NCV, mixed=args.mixed, reorder=args.reorder,
-                               device_csr=(n, L.nnz, rp.data_ptr(), ci.data_ptr(), va.data_ptr()))
-    plan_s = time.perf_counter() - t_plan
-
-    def solve(profile=False):
-        w, _ = plan.solve(k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0_device=v0d.data_ptr(), evecs_out=Y.data_ptr(),
-                          profile=profile)
-        return w, dict(plan.last_info)
+    hs = HeadlineSolver(L, v0, dev, world, rank, mixed=args.mixed, reorder=args.reorder)
 
     for _ in range(args.warmup):
-        solve()
+        hs.solve()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -826,28 +913,23 @@ def run_ours(args):
     ev0.record()
     timed_infos = []
     for _ in range(args.steps):
-        w, info = solve()
+        w, info = hs.solve()
         timed_infos.append(info)
     ev1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dev, world)
+    # one solve shared by all ranks: its Lanczos steps (the same on every rank)
     steps_total = sum(i["steps"] for i in timed_infos)
+    value = steps_total / (ms / 1000.0)
     # the same solves again with a CUDA event pair around every launch (the
     # per-kernel times of the roofline); recording ~1800 events adds ~15 % to
     # a solve, so the timed solves above run without them
-    infos = [solve(profile=True)[1] for _ in range(args.steps)]
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        s = torch.tensor([float(steps_total)], device=dev, dtype=torch.float64)
-        dist.all_reduce(s, op=dist.ReduceOp.SUM)
-        steps_total = int(s.item())
-    value = steps_total / (ms / 1000.0)
+    infos = [hs.solve(profile=True)[1] for _ in range(args.steps)]
 
     # roofline of the dominant kernel class, from the live per-kernel events
+    # (rank 0's rows at N > 1)
     classes = infos[0]["kernel_ms"].keys()
     kms = {c: sum(i["kernel_ms"][c] for i in infos) for c in classes}
     kcalls = {c: sum(i["kernel_calls"][c] for i in infos) for c in classes}
@@ -860,19 +942,23 @@ def run_ours(args):
     step_bytes = sum(kbytes[c] for c in step_cls)
     step_ach = step_bytes / (step_ms / 1000.0) / 1e9 if step_ms > 0 else None
     launches = sum(i["launches"] for i in timed_infos)
+    if world > 1:
+        par = f"rows partitioned over {world} GPUs (Cuthill-McKee order, {hs.exchange[0]} exchange)"
+    else:
+        par = "1 GPU"
 
     line = {
         "metric": "lanczos_steps_per_sec", "value": value, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": WORKLOAD + (" (fp32 values, fp64 accumulation)" if args.mixed else "")
-                   + ("; rows renumbered in Cuthill-McKee order inside the plan at creation (outside the timed "
-                      "solves; v0 and eigenvectors in the caller's numbering)" if args.reorder else ""),
-                   "n": n, "nnz": int(L.nnz), "edges": winfo["edges"], "parallelism": f"replicas{world}",
+                   + ("; rows renumbered in Cuthill-McKee order at plan creation (outside the timed solves; v0 "
+                      "and eigenvectors in the caller's numbering)" if args.reorder or world > 1 else ""),
+                   "n": n, "nnz": int(L.nnz), "edges": winfo["edges"], "parallelism": par,
                    "l2": "inputs larger than L2 (basis 488 MB), no flush"},
-        "time_to_converge_s": ms / args.steps / 1000.0, "plan_create_s": plan_s,
+        "time_to_converge_s": ms / args.steps / 1000.0, "plan_create_s": hs.plan_s,
         "lanczos_steps_per_solve": timed_infos[0]["steps"], "restarts_per_solve": timed_infos[0]["restarts"],
-        "nconv": timed_infos[0]["nconv"],
+        "nconv": timed_infos[0]["nconv"], "top_eigenvalues": [float(x) for x in w[-4:]],
         "kernel_times": "per-kernel CUDA events in a second pass of the same solves (profile mode)",
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
@@ -887,32 +973,41 @@ def run_ours(args):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if world > 1:
+        line["exchange"] = {"mode": hs.exchange[0], "halo_rows_received_rank0": hs.exchange[1],
+                            "halo_rows_sent_rank0": hs.exchange[2], "rows_rank0": list(hs.rows)}
+    perm = getattr(hs, "perm", None)
+    hs.close()
 
-    if rank == 0 and not args.no_e2e:
-        # end to end through the public API with host buffers: CSR upload,
-        # allocation, solve, eigenvectors back to the host
-        gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0)  # warm
-        e_steps, t0 = 0, time.perf_counter()
-        reps = max(1, min(args.steps, 2))
-        for _ in range(reps):
-            (we, Ve), inf = gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0, return_info=True)
-            e_steps += inf["steps"]
-        el = time.perf_counter() - t0
-        h2d = 4 * (n + 1) + 12 * L.nnz + 8 * n
-        d2h = 8 * n * K_EIG + 8 * K_EIG
-        line["e2e"] = {"value": e_steps / el, "unit": "steps/s", "h2d_bytes_per_step": h2d,
-                       "d2h_bytes_per_step": d2h, "ms_per_solve": 1000.0 * el / reps}
-        from scipy.sparse.linalg import norm as spnorm  # noqa: F401
-
-        res = np.linalg.norm(L @ Ve - Ve * we, axis=0).max()
-        line["max_residual_over_normA"] = float(res / abs(L).sum(axis=1).max())
+    if not args.no_e2e:
+        if world == 1:
+            # end to end through the public API with host buffers: CSR upload,
+            # allocation, solve, eigenvectors back to the host
+            gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0)  # warm
+            e_steps, t0 = 0, time.perf_counter()
+            reps = max(1, min(args.steps, 2))
+            for _ in range(reps):
+                (we, Ve), inf = gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0,
+                                                   return_info=True)
+                e_steps += inf["steps"]
+            el = time.perf_counter() - t0
+            h2d = 4 * (n + 1) + 12 * L.nnz + 8 * n
+            d2h = 8 * n * K_EIG + 8 * K_EIG
+            line["e2e"] = {"value": e_steps / el, "unit": "steps/s", "h2d_bytes_per_step": h2d,
+                           "d2h_bytes_per_step": d2h, "ms_per_solve": 1000.0 * el / reps}
+            res = np.linalg.norm(L @ Ve - Ve * we, axis=0).max()
+            line["max_residual_over_normA"] = float(res / abs(L).sum(axis=1).max())
+        else:
+            Lp = L[perm][:, perm].tocsr()
+            Lp.sort_indices()
+            line["e2e"] = e2e_partitioned(args, Lp, v0[perm], dev, world, rank)
+            del Lp
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(L, v0)
-    plan.close()
+    if world == 1 and not args.no_mixed:
+        line["mixed"] = run_mixed(args, L, v0, dev)
     if world == 1 and not args.no_adjoint:
         line["adjoint"] = run_adjoint(args, L, dev, with_cpu=not args.no_cpu_baseline)
-    if world > 1 and not args.no_partitioned:
-        line["partitioned"] = run_knn_partitioned(args, L, v0, dev, world, rank)
     del L
     if not args.no_slq:
         # with N > 1 every rank takes part in the sharded e2e steps (collectives)
@@ -926,12 +1021,58 @@ def run_ours(args):
         line["sinv"] = run_sinv(args, dev)
     if not args.no_graph and world == 1:
         line["graph"] = run_graph(args, dev, with_cpu=not args.no_cpu_baseline)
+    line["summary"] = summary(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
+
+
+def run_mixed(args, L, v0, dev):
+    """Configuration 1 in the mixed mode (fp32 matrix values, fp64
+    accumulation and basis), one GPU: complete solves timed with CUDA events."""
+    import torch
+
+    hs = HeadlineSolver(L, v0, dev, 1, 0, mixed=True, reorder=args.reorder)
+    hs.solve()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, min(args.steps, 5))
+    ev0.record()
+    infos = [hs.solve() for _ in range(reps)]
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / reps
+    w, info = infos[-1]
+    prof = hs.solve(profile=True)[1]
+    hs.close()
+    return {"workload": WORKLOAD + " (fp32 values, fp64 accumulation and basis)", "metric": "lanczos_steps_per_sec",
+            "value": info["steps"] / (ms / 1000.0), "unit": "steps/s", "time_to_converge_s": ms / 1000.0,
+            "lanczos_steps_per_solve": info["steps"], "restarts_per_solve": info["restarts"],
+            "nconv": info["nconv"], "top_eigenvalues": [float(x) for x in w[-4:]],
+            "kernel_ms_per_solve": dict(prof["kernel_ms"]), "parallelism": "1 GPU"}
+
+
+def summary(line):
+    """The headline figures of every leg in a few keys, last on the line."""
+    def g(obj, *keys):
+        for k in keys:
+            if not isinstance(obj, dict) or k not in obj:
+                return None
+            obj = obj[k]
+        return obj
+
+    out = {"eigsh_steps_per_s": line["value"], "eigsh_s": line["time_to_converge_s"],
+           "eigsh_e2e_steps_per_s": g(line, "e2e", "value"), "eigsh_step_frac": g(line, "step_roofline", "frac"),
+           "eigsh_cpu_steps_per_s": g(line, "cpu_baseline", "value"),
+           "mixed_s": g(line, "mixed", "time_to_converge_s"),
+           "slq_s": g(line, "slq", "value"), "slq_e2e_s": g(line, "slq", "e2e", "value"),
+           "slq_cpu_s": g(line, "slq", "cpu_baseline", "value"),
+           "rmat_s": g(line, "rmat", "value"), "sinv_s": g(line, "sinv", "value"),
+           "adjoint_s": g(line, "adjoint", "value"), "graph_s": g(line, "graph", "value")}
+    return {k: (round(v, 6) if isinstance(v, float) else v) for k, v in out.items() if v is not None}
 
 
 def main():
@@ -953,8 +1094,7 @@ def main():
                          "renumbering inside the plan, LG_PLAN_REORDER_BFS, done at plan creation)")
     ap.add_argument("--no-adjoint", action="store_true", help="skip the differentiable-eigsh backward leg")
     ap.add_argument("--only-adjoint", action="store_true", help="run the differentiable-eigsh backward leg alone")
-    ap.add_argument("--no-partitioned", action="store_true",
-                    help="at N > 1, skip the row-partitioned configuration-1 solve")
+    ap.add_argument("--no-mixed", action="store_true", help="skip the configuration-1 mixed-precision leg")
     ap.add_argument("--only-sinv", action="store_true", help="run the configuration-2 (shift-invert) leg alone")
     ap.add_argument("--no-sinv", action="store_true", help="skip the configuration-2 (shift-invert) leg")
     ap.add_argument("--sinv-n", type=int, default=SINV_N, help="grid side of the shift-invert leg (reduced cases)")

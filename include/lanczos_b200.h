@@ -121,6 +121,35 @@ int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const in
                             const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
                             int mixed, int flags);
 
+/* ---- matrix-free operators ---------------------------------------------
+ *
+ * A plan whose operator is the caller's function y = A x instead of a CSR
+ * matrix (A symmetric, n x n).  Replaces FunctionOperator
+ * (src/matvec_operator.cuh:149-163), whose callback type lg_matvec_fn keeps:
+ * x and y are n doubles, `user` is passed through untouched.  Three kinds:
+ *   LG_OP_DEVICE  fn gets device pointers.  The plan's stream is drained
+ *                 before each call and the whole device after it, so fn may
+ *                 use any stream (the reference's contract).
+ *   LG_OP_HOST    fn gets host pointers (pinned copies made by the plan):
+ *                 operators that live on the host, e.g. a Python
+ *                 scipy.sparse.linalg.LinearOperator.
+ *   LG_OP_STREAM  sfn gets device pointers and the plan's cudaStream_t; it
+ *                 enqueues y = A x on that stream and returns without
+ *                 waiting, so the solve keeps its one host wait per restart.
+ * fn / sfn run on the thread that calls lg_eigsh_plan_run (or _matvec,
+ * _factorize, _funm), once per Lanczos step.  The Lanczos steps keep both
+ * Gram-Schmidt passes inside every step (the delayed second pass of CSR plans
+ * folds 1/||r|| into the sparse product).  Shift-invert needs a CSR plan. */
+typedef void (*lg_matvec_fn)(const double* x, double* y, int n, void* user);
+typedef void (*lg_matvec_stream_fn)(const double* x, double* y, int n, void* user, void* stream);
+#define LG_OP_DEVICE 0
+#define LG_OP_HOST 1
+#define LG_OP_STREAM 2
+/* kind LG_OP_DEVICE / LG_OP_HOST: fn set, sfn NULL; LG_OP_STREAM: sfn set,
+ * fn NULL.  n >= 2; workspace for up to max_ncv basis vectors. */
+int lg_eigsh_plan_create_op(lg_eigsh_plan** plan, int n, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn,
+                            void* user, int max_ncv);
+
 /* Solve.  evals: host, k doubles, ascending.  evecs: n x k per opts layout.
  * io_on_device = 1: v0 and evecs are device pointers.  v0 may be NULL. */
 int lg_eigsh_plan_run(lg_eigsh_plan* plan, const lg_eigsh_opts* opts, const double* v0, double* evals,
@@ -172,6 +201,25 @@ int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global,
 int lg_eigsh_plan_set_exchange(lg_eigsh_plan* plan, int mode);
 int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long* recv_rows, long long* send_rows);
 
+/* Host-side halo planning of a partitioned plan (the steps
+ * lg_eigsh_plan_create_dist runs between its collectives), callable without a
+ * GPU so that the plan can be checked on CPU ranks.  No counterpart in the
+ * reference (single device).
+ * lg_halo_recv_list: the global rows of other ranks that this rank's columns
+ *   (host array col, nnz entries, global indices) name, grouped by owner
+ *   (ascending owner, then row) into recv_pos (capacity entries); recv_cnt
+ *   (nranks) the count per owner, *total the list length (also when the
+ *   capacity is too small, which returns LG_ERR_INVALID).
+ * lg_halo_send_plan: from the all-reduced count matrix counts (nranks x
+ *   nranks doubles, row r = rows rank r receives from each rank) this rank's
+ *   rows sent to each peer (send_cnt, nranks) and the exchange mode
+ *   (LG_EXCHANGE_HALO or LG_EXCHANGE_ALLGATHER) every rank derives alike.
+ * The rows a rank sends to peer p are p's receive positions owned by this
+ * rank, in p's order; the receiver writes them at the same global positions. */
+int lg_halo_recv_list(int n_global, int nranks, int rank, long long nnz, const int* col, int* recv_pos,
+                      long long capacity, long long* recv_cnt, long long* total);
+int lg_halo_send_plan(int n_global, int nranks, int rank, const double* counts, long long* send_cnt, int* mode);
+
 /* m Lanczos steps (CGS2) from the host vector v0 without restarts: alpha
  * (m doubles) and beta (m+1 doubles; beta[0] = 0, beta[m] = final residual
  * norm) of the tridiagonal, copied to the host.  A test and debugging hook
@@ -199,9 +247,14 @@ int lg_cgs2_orthogonalize(const double* V, int ldv, int n, int ncols, const doub
  * start-up): no cudaMalloc/cudaFree or other allocating call is made.  The
  * workspace is a fixed 0.5 MiB device array inside the library that every GPU
  * loading it keeps until exit; 1 <= ncols <= 128.  The first call on a device
- * resolves the array's address (make it before capturing any stream).  All
- * calls share the array: calls that overlap on the GPU race, so order them on
- * one stream.  This entry point has no counterpart in the reference. */
+ * resolves the array's address and caches it.  With CUDA's lazy module
+ * loading that first call is also when the library's device code is loaded
+ * on the device, which takes driver memory: make the first call on each
+ * device outside the no-allocation context (at start-up, for example), and
+ * before capturing any stream.  The cached address does not survive a
+ * cudaDeviceReset of that device; do not call this entry point after one.
+ * All calls share the array: calls that overlap on the GPU race, so order
+ * them on one stream.  This entry point has no counterpart in the reference. */
 int lg_cgs2_orthogonalize_noalloc(const double* V, int ldv, int n, int ncols, const double* w, double* r,
                                   double* coef, double* norms, void* stream);
 

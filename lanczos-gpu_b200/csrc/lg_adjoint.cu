@@ -585,13 +585,9 @@ size_t carve(char* base, Work& w) {
 template <int MODE>
 cudaError_t launch_deflate(const Work& w, int it, int max_iters, double* B, cudaStream_t st) {
   const size_t smem = sizeof(double) * (size_t)w.ld * w.ld;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(adj_deflate_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(double) * kMaxB * kMaxB));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = smem_attr_once(attr, (const void*)adj_deflate_kernel<MODE>, (int)(sizeof(double) * kMaxB * kMaxB));
+  if (e != cudaSuccess) return e;
   adj_deflate_kernel<MODE><<<w.grid_defl, kDT, smem, st>>>(w.n, w.k, w.ld, it, max_iters, w.X, B, w.P, w.s);
   return cudaGetLastError();
 }

@@ -58,6 +58,21 @@ int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const in
   return LG_OK;
 }
 
+int lg_eigsh_plan_create_op(lg_eigsh_plan** plan, int n, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn,
+                            void* user, int max_ncv) {
+  if (!plan) return LG_ERR_INVALID;
+  *plan = nullptr;
+  lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();
+  if (!p) return LG_ERR_NOMEM;
+  const int rc = p->solver.create_op(n, kind, fn, sfn, user, max_ncv);
+  if (rc != LG_OK) {
+    delete p;
+    return rc;
+  }
+  *plan = p;
+  return LG_OK;
+}
+
 int lg_partition_block(int n, int nranks) {
   if (n < 1 || nranks < 1) return 0;
   const long long per = ((long long)n + nranks - 1) / nranks;

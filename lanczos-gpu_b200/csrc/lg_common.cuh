@@ -7,6 +7,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <cfloat>
 
@@ -223,6 +224,23 @@ __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __host__ __device__ __forceinline__ double uniform_centered(uint64_t seed, uint64_t i) {
   uint64_t r = mix64(seed * 0x100000001B3ull + mix64(i));
   return (double)(r >> 11) * (1.0 / 9007199254740992.0) - 0.5;
+}
+
+// ---------------------------------------------------------------------------
+// Dynamic shared memory above the 48 KB default must be opted into per kernel
+// and per device.  `done` is the caller's bit set of devices (ids 0..63) on
+// which the attribute is already set; devices beyond 63 set it on every call.
+// Two threads racing on a first call both set it, which is harmless.
+// ---------------------------------------------------------------------------
+inline cudaError_t smem_attr_once(std::atomic<unsigned long long>& done, const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 }  // namespace lg

@@ -676,13 +676,9 @@ static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V
   if ((MODE == 1 && kGsAsync1) || (MODE == 2 && kGsAsync2) || (MODE == 3 && kGsAsync3)) {
 #define LG_GSA(LP)                                                                                              \
   do {                                                                                                          \
-    static bool attr = false;                                                                                   \
-    if (!attr) {                                                                                                \
-      cudaError_t e = cudaFuncSetAttribute(gs_async_kernel<MODE, LP>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                           (int)gs_async_smem());                                              \
-      if (e != cudaSuccess) return e;                                                                           \
-      attr = true;                                                                                              \
-    }                                                                                                           \
+    static std::atomic<unsigned long long> attr{0};                                                             \
+    cudaError_t e = smem_attr_once(attr, (const void*)gs_async_kernel<MODE, LP>, (int)gs_async_smem());         \
+    if (e != cudaSuccess) return e;                                                                             \
     gs_async_kernel<MODE, LP><<<p.grid, kGsThreads, gs_async_smem(), st>>>(V, ldv, ncols, n, vec, Rout, part_in,  \
                                                                           nrows_in, part_out, scal, alpha, j,   \
                                                                           alpha_mode, state);                   \
@@ -728,13 +724,9 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld
 template <int LP>
 static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
                                   const double* U, const double* Z, double* partS, double* partT, int* state) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gs_lag_project_kernel<LP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gs_lag_smem());
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP>, (int)gs_lag_smem());
+  if (e != cudaSuccess) return e;
   gs_lag_project_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, U, Z, partS, partT, state);
   return cudaGetLastError();
 }
@@ -743,13 +735,9 @@ template <int LP>
 static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
                                   const double* Z, const double* partS, const double* partT, int nrows_in,
                                   double* part_out, double* scal, double* alpha, double* beta, int* state) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gs_lag_correct_kernel<LP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gs_lag_smem());
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_correct_kernel<LP>, (int)gs_lag_smem());
+  if (e != cudaSuccess) return e;
   gs_lag_correct_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, R, Z, partS, partT,
                                                                         nrows_in, part_out, scal, alpha, beta, state);
   return cudaGetLastError();

@@ -15,6 +15,7 @@
 //    allocated inside the iteration.
 #include "lg_common.cuh"
 #include "lg_csr.cuh"
+#include "lg_halo.h"
 #include "lg_kernels.cuh"
 #include "lg_solver.h"
 #include "lg_staging.h"
@@ -109,6 +110,11 @@ void Solver::release() {
   cg_part = cg_scal = nullptr;
   cg_counter = nullptr;
   conv = state = cg_flags = nullptr;
+  if (op_x) cudaFree(op_x);
+  op_x = nullptr;
+  if (h_op_x) cudaFreeHost(h_op_x);
+  if (h_op_y) cudaFreeHost(h_op_y);
+  h_op_x = h_op_y = nullptr;
   if (h_state) cudaFreeHost(h_state);
   if (h_cg_flags) cudaFreeHost(h_cg_flags);
   h_state = h_cg_flags = nullptr;
@@ -119,6 +125,141 @@ void Solver::release() {
   ev0 = ev1 = nullptr;
   if (stream) cudaStreamDestroy(stream);
   stream = nullptr;
+}
+
+int Solver::init_device() {
+  LG_TRY(cudaGetDevice(&device));
+  LG_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, device));
+  int smem_optin = 0;
+  LG_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  smem_budget = (size_t)smem_optin;
+  LG_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  LG_TRY(cudaEventCreate(&ev0));
+  LG_TRY(cudaEventCreate(&ev1));
+
+  grid_gs = num_sm;
+  grid_spmv = num_sm * 8;
+  grid_basis = num_sm * 4;
+  return LG_OK;
+}
+
+// The Krylov basis, the operator output and residual, the partial-sum rows,
+// the tridiagonal and the restart state (n, ld, ldv and the stream are set).
+int Solver::alloc_workspace() {
+  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
+  LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
+  if (comm) {
+    LG_TRY(cudaMalloc(&Rfull, sizeof(double) * (size_t)ld * nranks));
+    LG_TRY(cudaMemsetAsync(Rfull, 0, sizeof(double) * (size_t)ld * nranks, stream));
+    R = Rfull + (size_t)rank * ld;
+    LG_TRY(cudaMalloc(&red, sizeof(double) * 3 * kPartStride));
+    LG_TRY(cudaMemsetAsync(red, 0, sizeof(double) * 3 * kPartStride, stream));
+  } else {
+    LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
+    LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+  }
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
+  LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
+  const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
+  for (double** p : {&partA, &partB, &partC}) {
+    LG_TRY(cudaMalloc(p, sizeof(double) * (size_t)prow * kPartStride));
+    LG_TRY(cudaMemsetAsync(*p, 0, sizeof(double) * (size_t)prow * kPartStride, stream));
+  }
+  LG_TRY(cudaMalloc(&alpha, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(cudaMalloc(&beta, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(cudaMalloc(&scal, sizeof(double) * SC_WORDS));
+  LG_TRY(cudaMalloc(&ritz, sizeof(double) * kMaxCols));
+  LG_TRY(cudaMalloc(&bounds, sizeof(double) * kMaxCols));
+  LG_TRY(cudaMalloc(&zsel, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(cudaMalloc(&Q, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(cudaMalloc(&rs_scratch, sizeof(double) * restart_scratch_doubles()));
+  LG_TRY(cudaMalloc(&conv, sizeof(int) * kMaxCols));
+  LG_TRY(cudaMalloc(&state, sizeof(int) * ST_WORDS));
+  LG_TRY(cudaMallocHost(&h_state, sizeof(int) * ST_WORDS));
+  return LG_OK;
+}
+
+int Solver::create_op(int n_, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn, void* user, int max_ncv_) {
+  if (n_ < 2) {
+    g_last_error = "matrix-free plan: n must be at least 2";
+    return LG_ERR_INVALID;
+  }
+  if (kind != LG_OP_DEVICE && kind != LG_OP_HOST && kind != LG_OP_STREAM) {
+    g_last_error = "matrix-free plan: kind must be LG_OP_DEVICE, LG_OP_HOST or LG_OP_STREAM";
+    return LG_ERR_INVALID;
+  }
+  if ((kind == LG_OP_STREAM) != (sfn != nullptr) || (kind != LG_OP_STREAM) != (fn != nullptr)) {
+    g_last_error = "matrix-free plan: LG_OP_STREAM takes sfn only, LG_OP_DEVICE / LG_OP_HOST take fn only";
+    return LG_ERR_INVALID;
+  }
+  comm = nullptr;
+  n_global = n_;
+  row0 = 0;
+  nranks = 1;
+  rank = 0;
+  n = n_;
+  nnz = 0;
+  mixed = 0;
+  op_kind = kind;
+  op_fn = fn;
+  op_sfn = sfn;
+  op_user = user;
+  max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
+  ld = round_up(n, kRowAlign);
+  ldv = round_up(max_ncv + 1, 4);
+  int rc = init_device();
+  if (rc != LG_OK) return rc;
+  rc = alloc_workspace();
+  if (rc != LG_OK) return rc;
+  LG_TRY(cudaMalloc(&op_x, sizeof(double) * (size_t)ld));
+  LG_TRY(cudaMemsetAsync(op_x, 0, sizeof(double) * (size_t)ld, stream));
+  if (kind == LG_OP_HOST) {
+    LG_TRY(cudaMallocHost(&h_op_x, sizeof(double) * (size_t)n));
+    LG_TRY(cudaMallocHost(&h_op_y, sizeof(double) * (size_t)n));
+  }
+  lag_steps = false;   // the lag steps fold 1/||u|| into the sparse product; a callback gets v_j itself
+  LG_TRY(cudaStreamSynchronize(stream));
+  return LG_OK;
+}
+
+// y = OP(x) by the caller's callback (x, y: device vectors of n doubles).
+//  LG_OP_STREAM: the callback enqueues its work on the plan's stream.
+//  LG_OP_DEVICE: the callback may use any stream; the plan's stream is
+//    drained before the call and the whole device after it.
+//  LG_OP_HOST:   x goes to pinned host memory, the callback runs on host
+//    vectors, y comes back.
+int Solver::call_user_op(const double* x, double* y) {
+  const size_t bytes = sizeof(double) * (size_t)n;
+  if (op_kind == LG_OP_STREAM) {
+    op_sfn(x, y, n, op_user, (void*)stream);
+    LG_TRY(cudaGetLastError());
+    return LG_OK;
+  }
+  if (op_kind == LG_OP_HOST) {
+    LG_TRY(cudaMemcpyAsync(h_op_x, x, bytes, cudaMemcpyDeviceToHost, stream));
+    LG_TRY(cudaStreamSynchronize(stream));
+    op_fn(h_op_x, h_op_y, n, op_user);
+    LG_TRY(cudaMemcpyAsync(y, h_op_y, bytes, cudaMemcpyHostToDevice, stream));
+    // h_op_y is rewritten by the next call: wait for this copy
+    LG_TRY(cudaStreamSynchronize(stream));
+    return LG_OK;
+  }
+  LG_TRY(cudaStreamSynchronize(stream));
+  op_fn(x, y, n, op_user);
+  LG_TRY(cudaGetLastError());
+  LG_TRY(cudaDeviceSynchronize());
+  return LG_OK;
+}
+
+// Matrix-free step j: v_j = R / beta_j into V[:, j] and op_x (the same DGKS /
+// breakdown checks as the sparse step), then W = OP(v_j).
+int Solver::apply_user_op(int j, int beta_mode) {
+  double* Vj = V + j;
+  LG_TRY(timed(LG_K_OTHER, 24.0 * n, 1, [&] {
+    return normalize_step(stream, num_sm * 8, n, R, Vj, ldv, op_x, inC, nrowsC, j, beta_mode, alpha, beta, scal,
+                          state);
+  }));
+  return call_user_op(op_x, W);
 }
 
 int Solver::create(int n_, long long nnz_, const int* rowptr, const int* col, const double* vals, int device_ptrs,
@@ -202,18 +343,10 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   ld = comm ? lg_partition_block(n_global, nranks) : round_up(n, kRowAlign);
   ldv = round_up(max_ncv + 1, 4);
 
-  LG_TRY(cudaGetDevice(&device));
-  LG_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, device));
-  int smem_optin = 0;
-  LG_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-  smem_budget = (size_t)smem_optin;
-  LG_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  LG_TRY(cudaEventCreate(&ev0));
-  LG_TRY(cudaEventCreate(&ev1));
-
-  grid_gs = num_sm;
-  grid_spmv = num_sm * 8;
-  grid_basis = num_sm * 4;
+  {
+    int rc = init_device();
+    if (rc != LG_OK) return rc;
+  }
 
   LG_TRY(cudaMalloc(&d_rowptr, sizeof(int) * (size_t)(n + 1)));
   LG_TRY(cudaMalloc(&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
@@ -232,36 +365,10 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
     }
   }
 
-  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
-  LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
-  if (comm) {
-    LG_TRY(cudaMalloc(&Rfull, sizeof(double) * (size_t)ld * nranks));
-    LG_TRY(cudaMemsetAsync(Rfull, 0, sizeof(double) * (size_t)ld * nranks, stream));
-    R = Rfull + (size_t)rank * ld;
-    LG_TRY(cudaMalloc(&red, sizeof(double) * 3 * kPartStride));
-    LG_TRY(cudaMemsetAsync(red, 0, sizeof(double) * 3 * kPartStride, stream));
-  } else {
-    LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
-    LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
+  {
+    int rc = alloc_workspace();
+    if (rc != LG_OK) return rc;
   }
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
-  LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
-  const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
-  for (double** p : {&partA, &partB, &partC}) {
-    LG_TRY(cudaMalloc(p, sizeof(double) * (size_t)prow * kPartStride));
-    LG_TRY(cudaMemsetAsync(*p, 0, sizeof(double) * (size_t)prow * kPartStride, stream));
-  }
-  LG_TRY(cudaMalloc(&alpha, sizeof(double) * (kMaxCols + 2)));
-  LG_TRY(cudaMalloc(&beta, sizeof(double) * (kMaxCols + 2)));
-  LG_TRY(cudaMalloc(&scal, sizeof(double) * SC_WORDS));
-  LG_TRY(cudaMalloc(&ritz, sizeof(double) * kMaxCols));
-  LG_TRY(cudaMalloc(&bounds, sizeof(double) * kMaxCols));
-  LG_TRY(cudaMalloc(&zsel, sizeof(double) * kMaxCols * kMaxCols));
-  LG_TRY(cudaMalloc(&Q, sizeof(double) * kMaxCols * kMaxCols));
-  LG_TRY(cudaMalloc(&rs_scratch, sizeof(double) * restart_scratch_doubles()));
-  LG_TRY(cudaMalloc(&conv, sizeof(int) * kMaxCols));
-  LG_TRY(cudaMalloc(&state, sizeof(int) * ST_WORDS));
-  LG_TRY(cudaMallocHost(&h_state, sizeof(int) * ST_WORDS));
 
   A.n = n;
   A.nnz = nnz;
@@ -437,7 +544,7 @@ __global__ void halo_unpack_kernel(const double* __restrict__ in, const int* __r
 }
 
 // Halo lists of a partitioned plan (collective: every rank calls it once, at
-// creation).  The columns of this rank's rows that other ranks own, grouped by
+// creation; the host steps are lg_halo.cu's halo_recv_lists / halo_send_plan).  The columns of this rank's rows that other ranks own, grouped by
 // owner in ascending order, are the rows it receives; one all-reduce of the
 // ranks x ranks count matrix tells every rank what it sends to whom, and one
 // grouped exchange hands each owner the positions it must pack.  Halo mode is
@@ -460,24 +567,7 @@ int Solver::setup_halo() {
   LG_TRY(e);
 
   std::vector<int> pos;
-  recv_off.assign(nranks, 0);
-  recv_cnt.assign(nranks, 0);
-  send_off.assign(nranks, 0);
-  send_cnt.assign(nranks, 0);
-  for (int o = 0; o < nranks; ++o) {
-    recv_off[o] = (long long)pos.size();
-    if (o == rank) continue;
-    const long long lo = (long long)o * ld, hi = std::min<long long>((long long)(o + 1) * ld, n_global);
-    for (long long c = lo; c < hi; ++c) {
-      const unsigned w = bits[(size_t)(c >> 5)];
-      if (w == 0u) {   // skip the rest of an empty word (block starts are multiples of 32)
-        c |= 31;
-        continue;
-      }
-      if ((w >> (c & 31)) & 1u) pos.push_back((int)c);
-    }
-    recv_cnt[o] = (long long)pos.size() - recv_off[o];
-  }
+  halo_recv_lists(bits.data(), ld, nranks, rank, n_global, pos, recv_off, recv_cnt);
   halo_recv = (long long)pos.size();
 
   // count matrix: row r = the rows rank r receives from each rank
@@ -495,18 +585,7 @@ int Solver::setup_halo() {
   cudaFree(d_cnt);
   if (rc != LG_OK) return rc;
   LG_TRY(e);
-  long long off = 0;
-  bool small = true;
-  for (int p = 0; p < nranks; ++p) {
-    send_off[p] = off;
-    send_cnt[p] = p == rank ? 0 : (long long)cnt[(size_t)p * nranks + rank];
-    off += send_cnt[p];
-    double recv_p = 0.0;
-    for (int o = 0; o < nranks; ++o) recv_p += cnt[(size_t)p * nranks + o];
-    if (2.0 * recv_p > (double)(nranks - 1) * (double)ld) small = false;
-  }
-  halo_send = off;
-  exchange_auto = small ? LG_EXCHANGE_HALO : LG_EXCHANGE_ALLGATHER;
+  exchange_auto = halo_send_plan(cnt.data(), nranks, rank, ld, send_off, send_cnt, &halo_send);
   exchange = exchange_auto;
 
   LG_TRY(cudaMalloc(&d_recv_pos, sizeof(int) * (size_t)std::max<long long>(halo_recv, 1)));
@@ -688,6 +767,7 @@ int Solver::clear_status() {
 
 // w = OP(v_j) preceded by the normalisation of R into V[:, j].
 int Solver::apply_step(int j, int beta_mode) {
+  if (op_kind >= 0) return apply_user_op(j, beta_mode);
   double* Vj = V + j;   // column j of the row-major basis
   if (!opts.use_sigma) {
     // CSR stream + x gather (counted once) + v_j and w written
@@ -886,6 +966,10 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
 
   if (comm && o.use_sigma) {
     g_last_error = "shift-invert is not available with a row-partitioned plan";
+    return LG_ERR_INVALID;
+  }
+  if (op_kind >= 0 && o.use_sigma) {
+    g_last_error = "shift-invert needs a CSR plan (its inner CG multiplies by the matrix)";
     return LG_ERR_INVALID;
   }
   if (o.use_sigma) {
@@ -1195,6 +1279,12 @@ int Solver::matvec(const double* x, double* y) {
   if (comm) {
     g_last_error = "matvec is not available with a row-partitioned plan";
     return LG_ERR_INVALID;
+  }
+  if (op_kind >= 0) {
+    int rc = call_user_op(x, y);
+    if (rc != LG_OK) return rc;
+    LG_TRY(cudaStreamSynchronize(stream));
+    return LG_OK;
   }
   if (d_perm) {   // y = A x in the caller's numbering: gather x, product, scatter y
     gather_perm_kernel<<<num_sm * 4, 256, 0, stream>>>(R, x, d_perm, n);

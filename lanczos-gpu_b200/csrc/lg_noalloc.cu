@@ -15,7 +15,10 @@
 // must not pass its name to a kernel (in host code it is only a stand-in, not
 // a device address): the first call on each device resolves the real address
 // with cudaGetSymbolAddress while that device is current, checks the result
-// and caches it.  Make that first call before capturing any stream.
+// and caches it.  Under CUDA's lazy module loading that first call is also
+// when this library's device code is loaded on the device (driver memory is
+// taken then), so it belongs outside the no-allocation context, and before
+// any stream capture.  A cudaDeviceReset invalidates the cached address.
 //
 // Every call on a device shares the one array, and the array keeps whatever
 // the previous call left in it: the status words are cleared at the start of

@@ -18,6 +18,10 @@ class Solver {
   ~Solver();
   int create(int n, long long nnz, const int* rowptr, const int* col, const double* vals, int device_ptrs,
              int max_ncv, int mixed, int flags);
+  // Matrix-free plan: the operator is the caller's callback (LG_OP_DEVICE /
+  // LG_OP_HOST: fn; LG_OP_STREAM: sfn), no CSR.  Shift-invert is not
+  // available (its inner CG multiplies by the CSR).
+  int create_op(int n, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn, void* user, int max_ncv);
   // Row-partitioned solver: this rank's n_local rows of an n_global x n_global matrix.
   int create_dist(lg_comm* comm, int n_global, int n_local, long long nnz, const int* rowptr, const int* col,
                   const double* vals, int device_ptrs, int max_ncv, int mixed);
@@ -37,6 +41,8 @@ class Solver {
 
  private:
   void release();
+  int init_device();
+  int alloc_workspace();
   int create_impl(int n_rows, int n_cols, long long nnz, const int* rowptr, const int* col, const double* vals,
                   int device_ptrs, int max_ncv, int mixed, int flags);
   int reorder_bfs(std::vector<int>& host_rowptr);
@@ -51,6 +57,10 @@ class Solver {
   int sync_state();
   int clear_status();
   int apply_step(int j, int beta_mode);
+  // Matrix-free plans: normalise R into V[:, j] and op_x, then y = OP(op_x)
+  // by the caller's callback.
+  int apply_user_op(int j, int beta_mode);
+  int call_user_op(const double* x, double* y);
   // Lanczos steps j0 .. j1-1.  lag: steps after the first take the second
   // Gram-Schmidt pass delayed into the next step (lag_step), and the last
   // residual gets that pass at the end (finish_lag).
@@ -66,6 +76,16 @@ class Solver {
   int cg_solve(const double* b, double* x);
 
   int n = 0, ld = 0, ldv = 0, max_ncv = 0, mixed = 0;   // ld: vector length padding; ldv: basis row stride
+  // matrix-free plans: LG_OP_* (-1: the plan owns a CSR), the callback and
+  // its argument; op_x: the contiguous operand; host operators: pinned
+  // copies of x and y
+  int op_kind = -1;
+  lg_matvec_fn op_fn = nullptr;
+  lg_matvec_stream_fn op_sfn = nullptr;
+  void* op_user = nullptr;
+  double* op_x = nullptr;
+  double* h_op_x = nullptr;
+  double* h_op_y = nullptr;
   // row partition (comm set): this rank owns global rows [row0, row0 + n); the
   // residuals of all ranks live in Rfull (nranks blocks of ld = nb doubles)
   // and R is this rank's block, so global column indices address Rfull.

@@ -24,10 +24,12 @@ from __future__ import annotations
 import numpy as np
 
 from . import _native
+from . import operators as _operators
 from ._native import LanczosError
+from .operators import CudaOperator
 
-__all__ = ["gpu_eigsh", "EigshPlan", "LanczosError", "ArpackNoConvergence", "differentiable_eigsh", "funm_apply",
-           "funm_qform"]
+__all__ = ["gpu_eigsh", "EigshPlan", "CudaOperator", "LanczosError", "ArpackNoConvergence", "differentiable_eigsh",
+           "funm_apply", "funm_qform"]
 
 _FUNM_MSG = {-1: "unknown func", -2: "invalid eigenvalue for func", -3: "zero input vector",
              -4: "tridiag eigensolver failure"}
@@ -136,8 +138,22 @@ class EigshPlan:
     """
 
     def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None,
-                 reorder: bool = False, cgs2_inline: bool = False):
+                 reorder: bool = False, cgs2_inline: bool = False, callback=None):
         self._plan = None
+        self._cb = None
+        if callback is not None or (A is not None and device_csr is None and _operators.is_operator(A)):
+            # matrix-free: A is a LinearOperator / CudaOperator (or a raw
+            # device callback with A giving the size)
+            if mixed or reorder or comm is not None:
+                raise ValueError("mixed, reorder and comm need a sparse matrix, not an operator")
+            n = int(A.shape[0]) if hasattr(A, "shape") else int(A)
+            if hasattr(A, "shape") and (len(A.shape) != 2 or A.shape[0] != A.shape[1]):
+                raise ValueError(f"operator must be square, got shape {A.shape}")
+            self._cb = callback if callback is not None else _operators.Callback(A)
+            self._plan = self._cb.create_plan(n, max_ncv)
+            self.n, self.nnz, self.mixed, self.max_ncv = n, 0, False, int(max_ncv)
+            self.last_info = {}
+            return
         flags = (_native.LG_PLAN_REORDER_BFS if reorder else 0) | (_native.LG_PLAN_CGS2_INLINE if cgs2_inline else 0)
         if reorder and comm is not None:
             raise ValueError("reorder a partitioned matrix before splitting it (gpu_eigsh.ordering)")
@@ -194,13 +210,18 @@ class EigshPlan:
         a = np.zeros(int(m))
         b = np.zeros(int(m) + 1)
         P = _native.C.POINTER(_native.C.c_double)
-        _native.check(_native.lib.lg_eigsh_plan_factorize(self._plan, v0a.ctypes.data_as(P), int(m),
-                                                          a.ctypes.data_as(P), b.ctypes.data_as(P)))
+        rc = _native.lib.lg_eigsh_plan_factorize(self._plan, v0a.ctypes.data_as(P), int(m), a.ctypes.data_as(P),
+                                                 b.ctypes.data_as(P))
+        if self._cb is not None:
+            self._cb.raise_pending()
+        _native.check(rc)
         return a, b
 
     def matvec_device(self, x_ptr: int, y_ptr: int):
         """y = A x on device buffers (raw CUDA pointers, n doubles each)."""
         _native.check(_native.lib.lg_eigsh_plan_matvec(self._plan, int(x_ptr), int(y_ptr)))
+        if self._cb is not None:
+            self._cb.raise_pending()
 
     def solve(self, k=6, ncv=None, maxiter=None, tol=0.0, which="LM", sigma=None, cg_max_iters=None,
               cg_tol=1e-12, *, v0=None, return_eigenvectors=True, max_steps=None, seed=42,
@@ -267,6 +288,8 @@ class EigshPlan:
                                            evals.ctypes.data_as(_native.C.POINTER(_native.C.c_double)),
                                            evp or None, io_dev, _native.C.byref(info))
         self.last_info = info.as_dict()
+        if self._cb is not None:
+            self._cb.raise_pending()   # an exception of the caller's matvec comes first
         if rc == _native.LG_ERR_CG_NOCONV:
             raise LanczosError(rc, _native.last_error() + "; increase cg_max_iters or cg_tol")
         _native.check(rc)
@@ -287,7 +310,12 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
               return_info=False, M=None, mode="normal", reorder=False):
     """Compute k eigenvalues (and eigenvectors) of a sparse symmetric matrix on the GPU.
 
-    Semantics follow ``scipy.sparse.linalg.eigsh``:
+    Semantics follow ``scipy.sparse.linalg.eigsh``.  ``A`` is a scipy sparse
+    matrix or dense array (uploaded as CSR), a
+    ``scipy.sparse.linalg.LinearOperator`` (its ``matvec`` runs on the host,
+    once per Lanczos step), or a :class:`CudaOperator` (a torch function of a
+    CUDA vector, run on the solver's stream): the reference's
+    FunctionOperator (src/matvec_operator.cuh:149-163).
 
     k : number of eigenpairs (1 <= k < n).
     ncv : Lanczos basis size; None or 0 -> min(n, max(2k+1, 20)).
@@ -312,6 +340,12 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
     """
     if M is not None or mode != "normal":
         raise NotImplementedError("generalized problems (M) and non-normal shift-invert modes are not supported")
+    if _operators.is_operator(A):
+        if sigma is not None:
+            raise NotImplementedError("shift-invert needs a sparse matrix (its inner CG multiplies by A); "
+                                      "an operator has no such form")
+        if mixed or reorder:
+            raise ValueError("mixed and reorder need a sparse matrix, not an operator")
     n = A.shape[0]
     if k is not None and int(k) >= n:
         import scipy.sparse as sp

@@ -25,6 +25,10 @@ WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
 EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
 LG_PLAN_REORDER_BFS = 1
 LG_PLAN_CGS2_INLINE = 2
+LG_OP_DEVICE, LG_OP_HOST, LG_OP_STREAM = 0, 1, 2
+# callback types of lg_eigsh_plan_create_op (include/lanczos_b200.h)
+MATVEC_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)
+MATVEC_STREAM_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p)
 KNN_METHODS = {"auto": 0, "cells": 1, "brute": 2}
 
 
@@ -113,6 +117,8 @@ SIGNATURES = {
                                        C.c_void_p, C.c_int, C.c_int, C.c_int]),
     "lg_eigsh_plan_create_ex": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_void_p, C.c_void_p,
                                           C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "lg_eigsh_plan_create_op": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_int]),
     "lg_eigsh_plan_run": (C.c_int, [C.c_void_p, C.POINTER(EigshOpts), C.c_void_p, _PD, C.c_void_p, C.c_int,
                                     C.POINTER(EigshInfo)]),
     "lg_eigsh_plan_destroy": (C.c_int, [C.c_void_p]),
@@ -123,6 +129,9 @@ SIGNATURES = {
     "lg_eigsh_plan_create_dist": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_longlong,
                                             C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
     "lg_eigsh_plan_set_exchange": (C.c_int, [C.c_void_p, C.c_int]),
+    "lg_halo_recv_list": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_longlong, _PI, _PI, C.c_longlong,
+                                    C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
+    "lg_halo_send_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, _PD, C.POINTER(C.c_longlong), _PI]),
     "lg_eigsh_plan_exchange_info": (C.c_int, [C.c_void_p, _PI, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "lg_eigsh_plan_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "lg_eigsh_plan_factorize": (C.c_int, [C.c_void_p, _PD, C.c_int, _PD, _PD]),

@@ -11,6 +11,7 @@ benchmark/scipy_reference.py:30).
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 import numpy as np
@@ -33,6 +34,8 @@ def lib():
         L.oracle_lanczos_steps.restype = C.c_longlong
         L.oracle_lanczos_steps.argtypes = [C.c_int, PI, PI, PD, C.c_int, PD, C.c_int, PD, PD]
         L.oracle_num_threads.restype = C.c_int
+        L.oracle_set_num_threads.restype = C.c_int
+        L.oracle_set_num_threads.argtypes = [C.c_int]
         _lib = L
     return _lib
 
@@ -89,6 +92,21 @@ def oracle_lanczos_steps(A, m, v0, cgs2=True):
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def host_cores() -> int:
+    """Cores this process may run on (its affinity mask), not what a launcher
+    put into OMP_NUM_THREADS."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def set_num_threads(nth: int | None = None) -> int:
+    """Threads of the oracle's parallel loops (default: every host core);
+    returns the count in effect."""
+    return int(lib().oracle_set_num_threads(int(nth or host_cores())))
 
 
 def arpack_eigsh(A, k, **kw):

@@ -479,3 +479,16 @@ int oracle_num_threads(void) {
   return 1;
 #endif
 }
+
+/* Threads of the parallel loops started by the calling thread (all host cores
+ * by default; a launcher may have set OMP_NUM_THREADS=1).  Returns the count
+ * now in effect. */
+int oracle_set_num_threads(int nth) {
+#ifdef _OPENMP
+  if (nth > 0) omp_set_num_threads(nth);
+  return omp_get_max_threads();
+#else
+  (void)nth;
+  return 1;
+#endif
+}

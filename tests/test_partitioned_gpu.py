@@ -5,7 +5,7 @@ Laplacian (in the generator's order, and renumbered by BFS level so that the
 halos are small: run with the halo exchange and, forced, with the
 all-gather) and of an R-MAT normalised Laplacian (configuration 4's family,
 with rows longer than the row kernels' cut).  Every rank must report the same
-eigenvalues, equal to the single-GPU plan's at 1e-10, and the assembled
+eigenvalues, equal to the single-GPU plan's and to scipy ARPACK's at 1e-10, and the assembled
 eigenvector rows must satisfy ||A v - lambda v|| <= tol ||A||.  Skipped with
 fewer than two GPUs.
 """
@@ -114,6 +114,14 @@ def test_partitioned_equals_single_gpu(case):
     ref = gpu_eigsh.gpu_eigsh(L, v0=v0, return_eigenvectors=False, **kw)
     w = out_w[0].numpy()
     assert np.max(np.abs(w - np.sort(ref)) / np.maximum(np.abs(ref), 1e-300)) < 1e-10
+    # and the ground truth itself: scipy's ARPACK with the same arguments
+    from oracle.irlm import arpack_eigsh
+
+    from _parity import anorm1, eig_rel_err
+
+    kw_a = {key: kw[key] for key in ("which", "ncv", "tol")}
+    ws, _ = arpack_eigsh(L, k, v0=v0, **kw_a)
+    assert eig_rel_err(w, ws, anorm1(L)) < 1e-10
     Y = out_y.numpy()
     res = np.linalg.norm(L @ Y - Y * w, axis=0).max()
     assert res <= kw["tol"] * abs(L).sum(axis=1).max()

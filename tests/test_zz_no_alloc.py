@@ -51,6 +51,41 @@ def test_noalloc_matches_allocating_entry_point_twice():
             assert ((a - b).norm() / b.norm()).item() < 1e-12, f"call {call}"
 
 
+def test_noalloc_call_takes_no_device_memory():
+    """After the first call on the device (which loads the module and
+    resolves the array), a call changes neither the device's free memory nor
+    torch's allocations: the outputs are the caller's, the workspace is the
+    library's fixed array."""
+    import torch
+    from gpu_eigsh import _native
+
+    n, ncols = 150000, 40
+    g = torch.Generator(device="cuda").manual_seed(9)
+    Q, _ = torch.linalg.qr(torch.randn(n, ncols, generator=g, device="cuda", dtype=torch.float64))
+    V = torch.zeros(n, ncols, device="cuda", dtype=torch.float64)
+    V[:, :ncols] = Q
+    w = torch.randn(n, generator=g, device="cuda", dtype=torch.float64)
+    r = torch.empty_like(w)
+    coef = torch.empty(ncols, dtype=torch.float64, device="cuda")
+    norms = torch.empty(3, dtype=torch.float64, device="cuda")
+    fn = _native.lib.lg_cgs2_orthogonalize_noalloc
+    args = (ctypes.c_void_p(V.data_ptr()), ncols, n, ncols, ctypes.c_void_p(w.data_ptr()),
+            ctypes.c_void_p(r.data_ptr()), ctypes.c_void_p(coef.data_ptr()), ctypes.c_void_p(norms.data_ptr()),
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert fn(*args) == 0          # first call: module load and symbol address
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    stats0 = torch.cuda.memory_stats()
+    for _ in range(3):
+        assert fn(*args) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    stats1 = torch.cuda.memory_stats()
+    assert free1 == free0, (free0, free1)
+    assert stats1.get("allocation.all.allocated", 0) == stats0.get("allocation.all.allocated", 0)
+    assert float(norms[2]) > 0.0
+
+
 def test_noalloc_rejects_too_many_columns():
     import torch
     from gpu_eigsh import _native
