@@ -201,6 +201,25 @@ int lg_eigsh_plan_create_dist(lg_eigsh_plan** plan, lg_comm* comm, int n_global,
 int lg_eigsh_plan_set_exchange(lg_eigsh_plan* plan, int mode);
 int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long* recv_rows, long long* send_rows);
 
+/* Transport of a partitioned plan's reductions and residual exchange.
+ * LG_TRANSPORT_PEER: each reduction and each exchange is one kernel that
+ * stores straight into the other ranks' memory over NVLink (buffers mapped
+ * with CUDA IPC at plan creation) and waits, bounded, on flags the other
+ * ranks raise; every rank adds the ranks' partial rows in rank order, so all
+ * ranks hold bitwise the same sums.  LG_TRANSPORT_NCCL: NCCL all-reduce and
+ * grouped send/receive (or all-gather).  lg_eigsh_plan_create_dist picks the
+ * peer transport when every rank has its own GPU and every mapping opens
+ * (environment LG_PEER_TRANSPORT=0 keeps NCCL), identically on every rank;
+ * set_transport overrides it (every rank must pass the same mode before its
+ * next run; LG_TRANSPORT_PEER fails where the mappings are missing).  A wait
+ * that gives up (about ten seconds) ends the run with LG_ERR_TIMEOUT.
+ * No counterpart in the reference (single device). */
+#define LG_TRANSPORT_AUTO 0
+#define LG_TRANSPORT_NCCL 1
+#define LG_TRANSPORT_PEER 2
+int lg_eigsh_plan_set_transport(lg_eigsh_plan* plan, int mode);
+int lg_eigsh_plan_transport(const lg_eigsh_plan* plan, int* mode);
+
 /* Host-side halo planning of a partitioned plan (the steps
  * lg_eigsh_plan_create_dist runs between its collectives), callable without a
  * GPU so that the plan can be checked on CPU ranks.  No counterpart in the

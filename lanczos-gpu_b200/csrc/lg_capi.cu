@@ -106,6 +106,17 @@ int lg_eigsh_plan_exchange_info(const lg_eigsh_plan* plan, int* mode, long long*
   return plan->solver.exchange_info(mode, recv_rows, send_rows);
 }
 
+int lg_eigsh_plan_set_transport(lg_eigsh_plan* plan, int mode) {
+  if (!plan) return LG_ERR_INVALID;
+  return plan->solver.set_transport(mode);
+}
+
+int lg_eigsh_plan_transport(const lg_eigsh_plan* plan, int* mode) {
+  if (!plan || !mode) return LG_ERR_INVALID;
+  *mode = plan->solver.transport_mode();
+  return LG_OK;
+}
+
 int lg_eigsh_plan_funm(lg_eigsh_plan* plan, const double* v, int io_on_device, int m, int func, int mode, double* y,
                        double* value, int* m_actual) {
   if (!plan) return LG_ERR_INVALID;

@@ -102,6 +102,14 @@ int comm_allgather_inplace(const lg_comm* c, double* full, size_t count_per_rank
   return r == ncclSuccess ? LG_OK : nccl_fail("ncclAllGather", r);
 }
 
+int comm_allgather_bytes(const lg_comm* c, void* full, size_t bytes_per_rank, cudaStream_t st) {
+  const CommImpl* ci = reinterpret_cast<const CommImpl*>(c);
+  char* base = static_cast<char*>(full);
+  ncclResult_t r = g_nccl.AllGather(base + (size_t)ci->rank * bytes_per_rank, base, bytes_per_rank, ncclChar,
+                                    ci->comm, st);
+  return r == ncclSuccess ? LG_OK : nccl_fail("ncclAllGather", r);
+}
+
 int comm_sendrecv(const lg_comm* c, int elem_bytes, const void* sendbuf, const long long* send_off,
                   const long long* send_cnt, void* recvbuf, const long long* recv_off, const long long* recv_cnt,
                   cudaStream_t st) {

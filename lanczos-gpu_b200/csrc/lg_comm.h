@@ -14,6 +14,9 @@ int comm_allreduce_sum(const lg_comm* c, double* buf, size_t count, cudaStream_t
 // full holds nranks blocks of count_per_rank doubles; this rank's block is
 // already in place; afterwards every rank holds all blocks.
 int comm_allgather_inplace(const lg_comm* c, double* full, size_t count_per_rank, cudaStream_t st);
+// full holds nranks blocks of bytes_per_rank bytes (this rank's in place);
+// afterwards every rank holds all blocks.
+int comm_allgather_bytes(const lg_comm* c, void* full, size_t bytes_per_rank, cudaStream_t st);
 // One grouped exchange: to every other rank p, send_cnt[p] elements from
 // sendbuf + send_off[p]; from p, recv_cnt[p] elements into recvbuf +
 // recv_off[p] (offsets and counts in elements, host arrays of nranks entries;

@@ -76,6 +76,7 @@ __global__ void scale_kernel(double* x, int n, double s) {
 Solver::~Solver() { release(); }
 
 void Solver::release() {
+  release_peer();
   if (Rfull) {
     cudaFree(Rfull);
     Rfull = nullptr;
@@ -424,6 +425,8 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   if (comm) {
     int rc = setup_halo();
     if (rc != LG_OK) return rc;
+    rc = setup_peer();
+    if (rc != LG_OK) return rc;
   }
 
   LG_TRY(cudaStreamSynchronize(stream));
@@ -715,6 +718,13 @@ int Solver::reduce_partials_all(double* part, int nrows, int slot, const double*
     return LG_OK;
   }
   double* row = red + (size_t)slot * kPartStride;
+  if (transport == LG_TRANSPORT_PEER) {
+    int rc = peer_reduce(part, nullptr, nrows, 1, slot);
+    if (rc != LG_OK) return rc;
+    *in = row;
+    *nin = 1;
+    return LG_OK;
+  }
   sum_rows_kernel<<<1, 160, 0, stream>>>(part, nrows, row);
   LG_TRY(cudaGetLastError());
   launches += 2;
@@ -725,12 +735,31 @@ int Solver::reduce_partials_all(double* part, int nrows, int slot, const double*
   return LG_OK;
 }
 
+int Solver::reduce_partials_all2(double* pa, double* pb, int nrows, int slot, const double** ina,
+                                 const double** inb, int* nin) {
+  if (comm && transport == LG_TRANSPORT_PEER) {
+    int rc = peer_reduce(pa, pb, nrows, 2, slot);
+    if (rc != LG_OK) return rc;
+    *ina = red + (size_t)slot * kPartStride;
+    *inb = red + (size_t)(slot + 1) * kPartStride;
+    *nin = 1;
+    return LG_OK;
+  }
+  int na = 0, nb = 0;
+  int rc = reduce_partials_all(pa, nrows, slot, ina, &na);
+  if (rc != LG_OK) return rc;
+  rc = reduce_partials_all(pb, nrows, slot + 1, inb, &nb);
+  *nin = na;
+  return rc;
+}
+
 // Before a sparse product: the other ranks' residual rows that this rank's
 // columns name into Rfull, by the halo exchange (pack the rows others read,
 // grouped sends and receives, unpack at their global positions) or by an
 // in-place all-gather of every block.
 int Solver::gather_residual() {
   if (!comm) return LG_OK;
+  if (transport == LG_TRANSPORT_PEER) return peer_exchange();
   if (exchange == LG_EXCHANGE_HALO) {
     if (halo_send > 0) {
       const int g = (int)std::min<long long>((long long)num_sm * 4, (halo_send + 255) / 256);
@@ -843,10 +872,8 @@ int Solver::lag_step(int j) {
   LG_TRY(timed(LG_K_PROJECT, vbytes + 16.0 * n, 1,
                [&] { return gs_lag_project(p, stream, V, ldv, j, n, R, W, partA, partB, state); }));
   const double *inS = nullptr, *inT = nullptr;
-  int nS = 0, nT = 0;
-  rc = reduce_partials_all(partA, p.grid, 0, &inS, &nS);
-  if (rc != LG_OK) return rc;
-  rc = reduce_partials_all(partB, p.grid, 1, &inT, &nT);
+  int nS = 0;
+  rc = reduce_partials_all2(partA, partB, p.grid, 0, &inS, &inT, &nS);
   if (rc != LG_OK) return rc;
   LG_TRY(timed(LG_K_CORRPROJ, vbytes + 32.0 * n, 1, [&] {
     return gs_lag_correct(p, stream, V, ldv, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);

@@ -13,6 +13,16 @@ namespace lg {
 
 extern thread_local std::string g_last_error;
 
+// Peer-memory transport of partitioned plans (lg_peer.cu): every rank's
+// exchange buffer (mailbox, then flag words) and residual buffer, as this
+// rank addresses them (its own, or mapped with CUDA IPC).
+constexpr int kMaxPeerRanks = 16;
+struct PeerPtrs {
+  double* mail[kMaxPeerRanks];
+  unsigned long long* flags[kMaxPeerRanks];
+  double* R[kMaxPeerRanks];
+};
+
 class Solver {
  public:
   ~Solver();
@@ -37,6 +47,9 @@ class Solver {
   int funm(const double* v, int io_on_device, int m, int func, int mode, double* y, double* value, int* m_actual);
   int funm_debug(const double* v, int m, double* V_out, double* alpha_out, double* beta_out, int* m_actual);
   int set_exchange(int mode);
+  // Partitioned runs: LG_TRANSPORT_* of the reductions and the exchange.
+  int set_transport(int mode);
+  int transport_mode() const { return transport; }
   int exchange_info(int* mode, long long* recv_rows, long long* send_rows) const;
 
  private:
@@ -52,6 +65,15 @@ class Solver {
   int reduce_partials_all(double* part, int nrows, int slot, const double** in, int* nin);
   int gather_residual();
   int setup_halo();
+  // peer transport (lg_peer.cu)
+  int setup_peer();
+  void release_peer();
+  int peer_reduce(const double* partA, const double* partB, int nrows, int ntables, int slot);
+  int peer_exchange();
+  // reduce_partials_all of two tables of one producer (rows `slot` and
+  // slot + 1 of red): one peer all-reduce, or two NCCL ones.
+  int reduce_partials_all2(double* pa, double* pb, int nrows, int slot, const double** ina, const double** inb,
+                           int* nin);
   int build_long_rows(const int* host_rowptr);
   int funm_factor(const double* v, int io_on_device, int m, int* m_actual, double* vnorm);
   int sync_state();
@@ -101,6 +123,16 @@ class Solver {
   int exchange = LG_EXCHANGE_ALLGATHER, exchange_auto = LG_EXCHANGE_ALLGATHER;
   std::vector<long long> send_off, send_cnt, recv_off, recv_cnt;
   long long halo_send = 0, halo_recv = 0;
+  int transport = LG_TRANSPORT_NCCL;
+  bool peer_ok = false;
+  unsigned long long peer_seq = 0;   // calls of the peer transport (the same sequence on every rank)
+  long long peer_wait_cycles = 0;    // bound of every wait of the peer kernels
+  void* peer_xch = nullptr;          // this rank's mailbox + flags (mapped by the peers)
+  unsigned* peer_counter = nullptr;  // last-CTA counter of the exchange kernel
+  long long* d_peer_send_off = nullptr;
+  void* peer_open_mail[kMaxPeerRanks] = {};
+  void* peer_open_R[kMaxPeerRanks] = {};
+  PeerPtrs peer_ptrs{};
   int* d_send_idx = nullptr;
   int* d_recv_pos = nullptr;
   double* d_send_buf = nullptr;

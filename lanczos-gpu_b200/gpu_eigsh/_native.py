@@ -23,6 +23,7 @@ LG_ERR_CG_NOCONV = -6
 
 WHICH = {"LM": 0, "SM": 1, "LA": 2, "SA": 3, "BE": 4}
 EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
+TRANSPORT = {"auto": 0, "nccl": 1, "peer": 2}
 LG_PLAN_REORDER_BFS = 1
 LG_PLAN_CGS2_INLINE = 2
 LG_OP_DEVICE, LG_OP_HOST, LG_OP_STREAM = 0, 1, 2
@@ -129,6 +130,8 @@ SIGNATURES = {
     "lg_eigsh_plan_create_dist": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_longlong,
                                             C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
     "lg_eigsh_plan_set_exchange": (C.c_int, [C.c_void_p, C.c_int]),
+    "lg_eigsh_plan_set_transport": (C.c_int, [C.c_void_p, C.c_int]),
+    "lg_eigsh_plan_transport": (C.c_int, [C.c_void_p, _PI]),
     "lg_halo_recv_list": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_longlong, _PI, _PI, C.c_longlong,
                                     C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "lg_halo_send_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, _PD, C.POINTER(C.c_longlong), _PI]),

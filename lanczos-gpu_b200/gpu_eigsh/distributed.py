@@ -170,7 +170,7 @@ class PartitionedEigsh:
     the eigenvectors as an (r1 - r0) x k tensor)."""
 
     def __init__(self, comm: Communicator, n_global: int, rowptr, col, vals, max_ncv: int = 127,
-                 mixed: bool = False, exchange: str = "auto"):
+                 mixed: bool = False, exchange: str = "auto", transport: str = "auto"):
         import torch
 
         from . import EigshPlan
@@ -188,6 +188,29 @@ class PartitionedEigsh:
         self.torch = torch
         if exchange != "auto":
             self.set_exchange(exchange)
+        if transport != "auto":
+            self.set_transport(transport)
+
+    def set_transport(self, mode: str):
+        """'auto', 'nccl' or 'peer' (every rank must choose the same): how the
+        partial sums are reduced and the residual rows exchanged — NCCL
+        collectives, or one kernel each that stores into the other ranks'
+        memory over NVLink."""
+        from . import _native
+
+        if mode not in _native.TRANSPORT:
+            raise ValueError("transport must be 'auto', 'nccl' or 'peer'")
+        _native.check(_native.lib.lg_eigsh_plan_set_transport(self.plan._plan, _native.TRANSPORT[mode]))
+
+    @property
+    def transport(self) -> str:
+        import ctypes as C
+
+        from . import _native
+
+        m = C.c_int(0)
+        _native.check(_native.lib.lg_eigsh_plan_transport(self.plan._plan, C.byref(m)))
+        return {v: k for k, v in _native.TRANSPORT.items()}[m.value]
 
     def set_exchange(self, mode: str):
         """'auto', 'allgather' or 'halo' (every rank must choose the same)."""
