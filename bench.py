@@ -460,7 +460,8 @@ def run_rmat(args, dev, world=1, rank=0):
                              "peak": peak, "unit": "GB/s", "peak_source": peak_kind,
                              "frac": (sbytes / (sms / 1000) / 1e9 / peak) if sms else None},
            "gpu_launches_per_solve": infos[0]["launches"],
-           "parallelism": f"rows partitioned over {world} GPUs (NCCL)" if world > 1 else "1 GPU",
+           "parallelism": f"rows partitioned over {world} GPUs ({transport_name(plan)} transport)" if world > 1
+           else "1 GPU",
            "scaling": "strong" if world > 1 else None}
     plan.close()
     if comm is not None:
@@ -651,6 +652,18 @@ class HeadlineSolver:
         self.plan.close()
         if self.comm is not None:
             self.comm.close()
+
+
+def transport_name(plan):
+    """'peer' (reductions and exchanges as kernels over NVLink peer memory) or
+    'nccl', as the partitioned plan chose."""
+    import ctypes as C
+
+    from gpu_eigsh import _native
+
+    m = C.c_int(0)
+    _native.check(_native.lib.lg_eigsh_plan_transport(plan._plan, C.byref(m)))
+    return {v: k for k, v in _native.TRANSPORT.items()}[m.value]
 
 
 def max_over_ranks(x, dev, world):
@@ -943,7 +956,8 @@ def run_ours(args):
     step_ach = step_bytes / (step_ms / 1000.0) / 1e9 if step_ms > 0 else None
     launches = sum(i["launches"] for i in timed_infos)
     if world > 1:
-        par = f"rows partitioned over {world} GPUs (Cuthill-McKee order, {hs.exchange[0]} exchange)"
+        par = (f"rows partitioned over {world} GPUs (Cuthill-McKee order, {hs.exchange[0]} exchange, "
+               f"{transport_name(hs.plan)} transport)")
     else:
         par = "1 GPU"
 
@@ -986,15 +1000,18 @@ def run_ours(args):
             gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0)  # warm
             e_steps, t0 = 0, time.perf_counter()
             reps = max(1, min(args.steps, 2))
+            phases = []
             for _ in range(reps):
                 (we, Ve), inf = gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0,
                                                    return_info=True)
                 e_steps += inf["steps"]
+                phases.append(inf["host_ms"])
             el = time.perf_counter() - t0
             h2d = 4 * (n + 1) + 12 * L.nnz + 8 * n
             d2h = 8 * n * K_EIG + 8 * K_EIG
             line["e2e"] = {"value": e_steps / el, "unit": "steps/s", "h2d_bytes_per_step": h2d,
-                           "d2h_bytes_per_step": d2h, "ms_per_solve": 1000.0 * el / reps}
+                           "d2h_bytes_per_step": d2h, "ms_per_solve": 1000.0 * el / reps,
+                           "host_ms_last_call": {k: round(v, 2) for k, v in phases[-1].items()}}
             res = np.linalg.norm(L @ Ve - Ve * we, axis=0).max()
             line["max_residual_over_normA"] = float(res / abs(L).sum(axis=1).max())
         else:

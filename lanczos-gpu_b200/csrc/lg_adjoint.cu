@@ -29,6 +29,7 @@
 // (SDDMM) over the sparsity pattern on the device.
 #include "../../include/lanczos_b200.h"
 #include "lg_common.cuh"
+#include "lg_pool.h"
 #include "lg_slq.cuh"
 
 #include <cuda_runtime.h>
@@ -508,32 +509,6 @@ int fail(const char* m) {
 int cuda_fail(cudaError_t e) {
   g_last_error = std::string("lg_eigsh_adjoint: ") + cudaGetErrorString(e);
   return e == cudaErrorMemoryAllocation ? LG_ERR_NOMEM : LG_ERR_CUDA;
-}
-
-// The workspace comes from a memory pool of the library's own (one per
-// device) that keeps its memory between calls: a backward pass inside a
-// training loop then maps no memory (the default pool would return ~1 GB at
-// n = 1e6 to the driver at every synchronisation and map it again).
-cudaError_t pool_for(int dev, cudaMemPool_t* out) {
-  static cudaMemPool_t pools[64] = {};
-  static std::mutex mu;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!pools[dev]) {
-    cudaMemPoolProps props = {};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = dev;
-    cudaMemPool_t p = nullptr;
-    cudaError_t e = cudaMemPoolCreate(&p, &props);
-    if (e != cudaSuccess) return e;
-    unsigned long long keep = ~0ull;
-    e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
-    if (e != cudaSuccess) return e;
-    pools[dev] = p;
-  }
-  *out = pools[dev];
-  return cudaSuccess;
 }
 
 struct Work {

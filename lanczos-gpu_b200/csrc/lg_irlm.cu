@@ -16,6 +16,7 @@
 #include "lg_common.cuh"
 #include "lg_csr.cuh"
 #include "lg_halo.h"
+#include "lg_pool.h"
 #include "lg_kernels.cuh"
 #include "lg_solver.h"
 #include "lg_staging.h"
@@ -82,11 +83,11 @@ void Solver::release() {
     Rfull = nullptr;
     R = nullptr;
   }
-  if (red) cudaFree(red);
+  if (red) dfree(red);
   red = nullptr;
   for (void* p : {(void*)d_send_idx, (void*)d_recv_pos, (void*)d_send_buf, (void*)d_recv_buf, (void*)d_perm,
                   (void*)funm_ws})
-    if (p) cudaFree(p);
+    if (p) dfree(p);
   d_perm = nullptr;
   funm_ws = nullptr;
   d_send_idx = d_recv_pos = nullptr;
@@ -99,7 +100,7 @@ void Solver::release() {
   void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, d_long, d_chunk_sum, d_classes, V, W, R, partA, partB, partC, alpha, beta, scal,
                   ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
-    if (p) cudaFree(p);
+    if (p) dfree(p);
   d_rowptr = d_col = nullptr;
   d_val64 = nullptr;
   d_val32 = nullptr;
@@ -111,7 +112,7 @@ void Solver::release() {
   cg_part = cg_scal = nullptr;
   cg_counter = nullptr;
   conv = state = cg_flags = nullptr;
-  if (op_x) cudaFree(op_x);
+  if (op_x) dfree(op_x);
   op_x = nullptr;
   if (h_op_x) cudaFreeHost(h_op_x);
   if (h_op_y) cudaFreeHost(h_op_y);
@@ -126,6 +127,26 @@ void Solver::release() {
   ev0 = ev1 = nullptr;
   if (stream) cudaStreamDestroy(stream);
   stream = nullptr;
+}
+
+// Plan buffers come from the library's device pool (lg_pool.h) on the plan's
+// stream, so creating and destroying plans in a loop maps no memory after the
+// first plan; buffers other ranks map with CUDA IPC stay plain allocations.
+cudaError_t Solver::dalloc(void** p, size_t bytes) {
+  cudaError_t e = pool_alloc(p, bytes, stream);
+  if (e == cudaSuccess) pooled.insert(*p);
+  return e;
+}
+
+void Solver::dfree(void* p) {
+  if (!p) return;
+  auto it = pooled.find(p);
+  if (it != pooled.end()) {
+    pool_free(p, stream);
+    pooled.erase(it);
+  } else {
+    cudaFree(p);
+  }
 }
 
 int Solver::init_device() {
@@ -147,35 +168,35 @@ int Solver::init_device() {
 // The Krylov basis, the operator output and residual, the partial-sum rows,
 // the tridiagonal and the restart state (n, ld, ldv and the stream are set).
 int Solver::alloc_workspace() {
-  LG_TRY(cudaMalloc(&V, sizeof(double) * (size_t)n * ldv));
-  LG_TRY(cudaMalloc(&W, sizeof(double) * (size_t)ld));
+  LG_TRY(dalloc((void**)&V, sizeof(double) * (size_t)n * ldv));
+  LG_TRY(dalloc((void**)&W, sizeof(double) * (size_t)ld));
   if (comm) {
     LG_TRY(cudaMalloc(&Rfull, sizeof(double) * (size_t)ld * nranks));
     LG_TRY(cudaMemsetAsync(Rfull, 0, sizeof(double) * (size_t)ld * nranks, stream));
     R = Rfull + (size_t)rank * ld;
-    LG_TRY(cudaMalloc(&red, sizeof(double) * 3 * kPartStride));
+    LG_TRY(dalloc((void**)&red, sizeof(double) * 3 * kPartStride));
     LG_TRY(cudaMemsetAsync(red, 0, sizeof(double) * 3 * kPartStride, stream));
   } else {
-    LG_TRY(cudaMalloc(&R, sizeof(double) * (size_t)ld));
+    LG_TRY(dalloc((void**)&R, sizeof(double) * (size_t)ld));
     LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   }
   LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
   LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
   const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
   for (double** p : {&partA, &partB, &partC}) {
-    LG_TRY(cudaMalloc(p, sizeof(double) * (size_t)prow * kPartStride));
+    LG_TRY(dalloc((void**)p, sizeof(double) * (size_t)prow * kPartStride));
     LG_TRY(cudaMemsetAsync(*p, 0, sizeof(double) * (size_t)prow * kPartStride, stream));
   }
-  LG_TRY(cudaMalloc(&alpha, sizeof(double) * (kMaxCols + 2)));
-  LG_TRY(cudaMalloc(&beta, sizeof(double) * (kMaxCols + 2)));
-  LG_TRY(cudaMalloc(&scal, sizeof(double) * SC_WORDS));
-  LG_TRY(cudaMalloc(&ritz, sizeof(double) * kMaxCols));
-  LG_TRY(cudaMalloc(&bounds, sizeof(double) * kMaxCols));
-  LG_TRY(cudaMalloc(&zsel, sizeof(double) * kMaxCols * kMaxCols));
-  LG_TRY(cudaMalloc(&Q, sizeof(double) * kMaxCols * kMaxCols));
-  LG_TRY(cudaMalloc(&rs_scratch, sizeof(double) * restart_scratch_doubles()));
-  LG_TRY(cudaMalloc(&conv, sizeof(int) * kMaxCols));
-  LG_TRY(cudaMalloc(&state, sizeof(int) * ST_WORDS));
+  LG_TRY(dalloc((void**)&alpha, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(dalloc((void**)&beta, sizeof(double) * (kMaxCols + 2)));
+  LG_TRY(dalloc((void**)&scal, sizeof(double) * SC_WORDS));
+  LG_TRY(dalloc((void**)&ritz, sizeof(double) * kMaxCols));
+  LG_TRY(dalloc((void**)&bounds, sizeof(double) * kMaxCols));
+  LG_TRY(dalloc((void**)&zsel, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(dalloc((void**)&Q, sizeof(double) * kMaxCols * kMaxCols));
+  LG_TRY(dalloc((void**)&rs_scratch, sizeof(double) * restart_scratch_doubles()));
+  LG_TRY(dalloc((void**)&conv, sizeof(int) * kMaxCols));
+  LG_TRY(dalloc((void**)&state, sizeof(int) * ST_WORDS));
   LG_TRY(cudaMallocHost(&h_state, sizeof(int) * ST_WORDS));
   return LG_OK;
 }
@@ -212,7 +233,7 @@ int Solver::create_op(int n_, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn
   if (rc != LG_OK) return rc;
   rc = alloc_workspace();
   if (rc != LG_OK) return rc;
-  LG_TRY(cudaMalloc(&op_x, sizeof(double) * (size_t)ld));
+  LG_TRY(dalloc((void**)&op_x, sizeof(double) * (size_t)ld));
   LG_TRY(cudaMemsetAsync(op_x, 0, sizeof(double) * (size_t)ld, stream));
   if (kind == LG_OP_HOST) {
     LG_TRY(cudaMallocHost(&h_op_x, sizeof(double) * (size_t)n));
@@ -349,9 +370,9 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
     if (rc != LG_OK) return rc;
   }
 
-  LG_TRY(cudaMalloc(&d_rowptr, sizeof(int) * (size_t)(n + 1)));
-  LG_TRY(cudaMalloc(&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
-  LG_TRY(cudaMalloc(&d_val64, sizeof(double) * (size_t)std::max<long long>(nnz, 1)));
+  LG_TRY(dalloc((void**)&d_rowptr, sizeof(int) * (size_t)(n + 1)));
+  LG_TRY(dalloc((void**)&d_col, sizeof(int) * (size_t)std::max<long long>(nnz, 1)));
+  LG_TRY(dalloc((void**)&d_val64, sizeof(double) * (size_t)std::max<long long>(nnz, 1)));
   if (device_ptrs) {
     LG_TRY(cudaMemcpyAsync(d_rowptr, rowptr, sizeof(int) * (size_t)(n + 1), cudaMemcpyDeviceToDevice, stream));
     if (nnz > 0) {
@@ -413,7 +434,7 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
     if (rc != LG_OK) return rc;
   }
   if (mixed) {
-    LG_TRY(cudaMalloc(&d_val32, sizeof(float) * (size_t)std::max<long long>(nnz, 1)));
+    LG_TRY(dalloc((void**)&d_val32, sizeof(float) * (size_t)std::max<long long>(nnz, 1)));
     cast_f64_f32_kernel<<<num_sm * 4, 256, 0, stream>>>(d_val64, d_val32, nnz);
     LG_TRY(cudaGetLastError());
     A.val32 = d_val32;
@@ -488,11 +509,11 @@ int Solver::reorder_bfs(std::vector<int>& hrp) {
   int *d_pos = nullptr, *rp2 = nullptr, *col2 = nullptr;
   double* val2 = nullptr;
   cudaError_t e = cudaSuccess;
-  LG_TRY(cudaMalloc(&d_perm, sizeof(int) * (size_t)n));
-  LG_TRY(cudaMalloc(&d_pos, sizeof(int) * (size_t)n));
-  e = cudaMalloc(&rp2, sizeof(int) * ((size_t)n + 1));
-  if (e == cudaSuccess) e = cudaMalloc(&col2, sizeof(int) * (size_t)std::max<long long>(nnz, 1));
-  if (e == cudaSuccess) e = cudaMalloc(&val2, sizeof(double) * (size_t)std::max<long long>(nnz, 1));
+  LG_TRY(dalloc((void**)&d_perm, sizeof(int) * (size_t)n));
+  LG_TRY(dalloc((void**)&d_pos, sizeof(int) * (size_t)n));
+  e = dalloc((void**)&rp2, sizeof(int) * ((size_t)n + 1));
+  if (e == cudaSuccess) e = dalloc((void**)&col2, sizeof(int) * (size_t)std::max<long long>(nnz, 1));
+  if (e == cudaSuccess) e = dalloc((void**)&val2, sizeof(double) * (size_t)std::max<long long>(nnz, 1));
   if (e == cudaSuccess) e = cudaMemcpyAsync(d_perm, perm.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(d_pos, pos.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(rp2, nrp.data(), sizeof(int) * ((size_t)n + 1), cudaMemcpyHostToDevice, stream);
@@ -501,16 +522,16 @@ int Solver::reorder_bfs(std::vector<int>& hrp) {
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);   // the host vectors go out of scope
-  cudaFree(d_pos);
+  dfree(d_pos);
   if (e != cudaSuccess) {
-    cudaFree(rp2);
-    cudaFree(col2);
-    cudaFree(val2);
+    dfree(rp2);
+    dfree(col2);
+    dfree(val2);
     LG_TRY(e);
   }
-  cudaFree(d_rowptr);
-  cudaFree(d_col);
-  cudaFree(d_val64);
+  dfree(d_rowptr);
+  dfree(d_col);
+  dfree(d_val64);
   d_rowptr = rp2;
   d_col = col2;
   d_val64 = val2;
@@ -675,7 +696,7 @@ int Solver::build_long_rows(const int* hrp) {
           ++A.nclasses;
         }
       }
-      LG_TRY(cudaMalloc(&d_classes, sizeof(int) * (size_t)n));
+      LG_TRY(dalloc((void**)&d_classes, sizeof(int) * (size_t)n));
       LG_TRY(cudaMemcpyAsync(d_classes, lists.data(), sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, stream));
       LG_TRY(cudaStreamSynchronize(stream));
       for (int c = 0; c < A.nclasses; ++c)
@@ -686,8 +707,8 @@ int Solver::build_long_rows(const int* hrp) {
   A.nchunks = (int)cb.size();
   if (A.nlong == 0) return LG_OK;
   const size_t total = rows.size() + first.size() + cb.size() + ce.size();
-  LG_TRY(cudaMalloc(&d_long, sizeof(int) * total));
-  LG_TRY(cudaMalloc(&d_chunk_sum, sizeof(double) * cb.size()));
+  LG_TRY(dalloc((void**)&d_long, sizeof(int) * total));
+  LG_TRY(dalloc((void**)&d_chunk_sum, sizeof(double) * cb.size()));
   int* p = d_long;
   for (const std::vector<int>* v : {&rows, &first, &cb, &ce}) {
     LG_TRY(cudaMemcpyAsync(p, v->data(), sizeof(int) * v->size(), cudaMemcpyHostToDevice, stream));
@@ -1183,9 +1204,9 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     double* Y = evecs;
     if (!io_on_device) {
       if (!Ytmp || ytmp_elems < (size_t)n * ksel) {
-        if (Ytmp) cudaFree(Ytmp);
+        if (Ytmp) dfree(Ytmp);
         Ytmp = nullptr;
-        LG_TRY(cudaMalloc(&Ytmp, sizeof(double) * (size_t)n * ksel));
+        LG_TRY(dalloc((void**)&Ytmp, sizeof(double) * (size_t)n * ksel));
         ytmp_elems = (size_t)n * ksel;
       }
       Y = Ytmp;

@@ -32,7 +32,7 @@
 // synchronisation, and the other ranks' waits give up the same way.  The
 // transport is only used when every rank sits on its own GPU and every peer
 // mapping opened; otherwise the plan keeps NCCL, decided alike on every rank.
-// No TMA and no multicast: plain stores and loads of peer memory.
+// Only plain stores and loads touch peer memory (no bulk or tensor copies).
 #include "lg_common.cuh"
 #include "lg_comm.h"
 #include "lg_solver.h"
@@ -90,34 +90,37 @@ peer_allreduce_kernel(const double* __restrict__ partA, const double* __restrict
                       double* out, PeerPtrs P, int nranks, int rank, unsigned long long seq, long long wait_cycles,
                       int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
-  constexpr int G = kReduceThreads / kPartStride;   // row groups per table (7)
-  __shared__ double grp[G][kPartStride];
+  constexpr int NW = kReduceThreads / 32;          // 32 warps
+  constexpr int CPL = (kPartStride + 31) / 32;     // columns per lane (5)
+  __shared__ double wsum[NW][kPartStride];
   __shared__ double sums[2][kPartStride];
   __shared__ int sh_fail;
-  const int t = threadIdx.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int par = (int)(seq & 1ull);
-  // 1. this rank's rows, per column: group g sums rows g, g + G, ... in order,
-  //    then the groups in order
+  // 1. this rank's rows: warp w sums rows w, w + 32, ... (every load of a
+  //    lane independent, so they are in flight together), lanes across the
+  //    columns; then the warps' sums in warp order.  A fixed order.
   for (int tb = 0; tb < ntables; ++tb) {
     const double* part = tb == 0 ? partA : partB;
-    if (t < G * kPartStride) {
-      const int g = t / kPartStride, col = t - g * kPartStride;
-      double acc = 0.0;
-      int r = g;
-      for (; r + 3 * G < nrows; r += 4 * G) {
-        double v[4];
+    double acc[CPL];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = __ldcg(part + (size_t)(r + u * G) * kPartStride + col);
+    for (int c = 0; c < CPL; ++c) acc[c] = 0.0;
+    for (int r = warp; r < nrows; r += NW) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc += v[u];
+      for (int c = 0; c < CPL; ++c) {
+        const int col = lane + 32 * c;
+        if (col < kPartStride) acc[c] += __ldcg(part + (size_t)r * kPartStride + col);
       }
-      for (; r < nrows; r += G) acc += __ldcg(part + (size_t)r * kPartStride + col);
-      grp[g][col] = acc;
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const int col = lane + 32 * c;
+      if (col < kPartStride) wsum[warp][col] = acc[c];
     }
     __syncthreads();
     if (t < kPartStride) {
       double s = 0.0;
-      for (int g = 0; g < G; ++g) s += grp[g][t];
+      for (int w = 0; w < NW; ++w) s += wsum[w][t];
       sums[tb][t] = s;
     }
     __syncthreads();

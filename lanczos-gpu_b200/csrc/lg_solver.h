@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <string>
+#include <unordered_set>
 #include <vector>
 
 #include "../../include/lanczos_b200.h"
@@ -54,6 +55,9 @@ class Solver {
 
  private:
   void release();
+  cudaError_t dalloc(void** p, size_t bytes);
+  void dfree(void* p);
+  std::unordered_set<void*> pooled;   // buffers from the device pool
   int init_device();
   int alloc_workspace();
   int create_impl(int n_rows, int n_cols, long long nnz, const int* rowptr, const int* col, const double* vals,

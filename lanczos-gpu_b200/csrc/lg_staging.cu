@@ -12,7 +12,9 @@
 #include "lg_staging.h"
 
 #include <algorithm>
+#include <condition_variable>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -29,22 +31,85 @@ void* g_slot[2] = {nullptr, nullptr};
 cudaEvent_t g_ev[2] = {nullptr, nullptr};
 int g_stage_dev = -1;
 
+// Host workers kept for the process (started on first use, never joined: the
+// pool outlives every caller), so a copy of a few chunks does not pay for
+// creating and joining a dozen threads per chunk.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool* p = new CopyPool();   // intentionally never destroyed
+    return *p;
+  }
+  int size() const { return (int)workers_.size() + 1; }
+  // Runs fn(0 .. parts-1) on the workers and the calling thread; returns when
+  // all parts are done.  One job at a time (callers hold g_stage_mu).
+  void run(int parts, const std::function<void(int)>& fn) {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      job_ = &fn;
+      parts_ = parts;
+      next_ = 1;   // part 0 is the caller's
+      done_ = 0;
+      ++gen_;
+    }
+    cv_.notify_all();
+    fn(0);
+    std::unique_lock<std::mutex> lk(mu_);
+    ++done_;
+    for (;;) {   // help with parts no worker has taken yet
+      if (next_ >= parts_) break;
+      const int part = next_++;
+      lk.unlock();
+      fn(part);
+      lk.lock();
+      ++done_;
+    }
+    cv_done_.wait(lk, [&] { return done_ == parts_; });
+    job_ = nullptr;
+  }
+
+ private:
+  CopyPool() {
+    const int nth = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency())) - 1;
+    for (int w = 0; w < nth; ++w) workers_.emplace_back([this] { loop(); });
+    for (std::thread& t : workers_) t.detach();
+  }
+  void loop() {
+    unsigned long long seen = 0;
+    std::unique_lock<std::mutex> lk(mu_);
+    for (;;) {
+      cv_.wait(lk, [&] { return gen_ != seen && job_ != nullptr && next_ < parts_; });
+      seen = gen_;
+      while (job_ && next_ < parts_) {
+        const int part = next_++;
+        const std::function<void(int)>* f = job_;
+        lk.unlock();
+        (*f)(part);
+        lk.lock();
+        if (++done_ == parts_) cv_done_.notify_all();
+      }
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, cv_done_;
+  const std::function<void(int)>* job_ = nullptr;
+  int parts_ = 0, next_ = 0, done_ = 0;
+  unsigned long long gen_ = 0;
+};
+
 void parallel_copy(void* dst, const void* src, size_t bytes) {
   const size_t per = size_t(2) << 20;
-  const int nth = (int)std::max<size_t>(1, std::min<size_t>({16, std::thread::hardware_concurrency(),
-                                                             (bytes + per - 1) / per}));
+  CopyPool& pool = CopyPool::get();
+  const int nth = (int)std::max<size_t>(1, std::min<size_t>((size_t)pool.size(), (bytes + per - 1) / per));
   if (nth <= 1) {
     std::memcpy(dst, src, bytes);
     return;
   }
-  std::vector<std::thread> pool;
-  pool.reserve(nth);
-  for (int w = 0; w < nth; ++w)
-    pool.emplace_back([=] {
-      const size_t b = bytes * w / nth, e = bytes * (w + 1) / nth;
-      std::memcpy(static_cast<char*>(dst) + b, static_cast<const char*>(src) + b, e - b);
-    });
-  for (std::thread& t : pool) t.join();
+  pool.run(nth, [=](int w) {
+    const size_t b = bytes * w / nth, e = bytes * (w + 1) / nth;
+    std::memcpy(static_cast<char*>(dst) + b, static_cast<const char*>(src) + b, e - b);
+  });
 }
 
 // Slots of the current device (re-created when the caller's device changes).

@@ -21,6 +21,8 @@ no CPU fallback.
 """
 from __future__ import annotations
 
+import time
+
 import numpy as np
 
 from . import _native
@@ -353,7 +355,9 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
             raise TypeError("Cannot use scipy.linalg.eigh for sparse A with k >= N. "
                             "Use scipy.linalg.eigh(A.toarray()) or reduce k.")
     ncv_eff = _default_ncv(n, int(k)) if (ncv is None or int(ncv) <= 0) else min(int(ncv), n)
+    t0 = time.perf_counter()
     plan = EigshPlan(A, max_ncv=max(ncv_eff, 2), mixed=mixed, reorder=reorder)
+    t1 = time.perf_counter()
     try:
         try:
             out = plan.solve(k=k, ncv=ncv_eff, maxiter=maxiter, tol=tol, which=which, sigma=sigma,
@@ -362,8 +366,14 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
         except ArpackNoConvergence as exc:
             exc.info = plan.last_info
             raise
-        if return_info:
-            return out, plan.last_info
-        return out
+        t2 = time.perf_counter()
     finally:
         plan.close()
+    if return_info:
+        info = dict(plan.last_info)
+        # host wall time of the three phases: plan (CSR upload and checks,
+        # workspace), solve (v0 up, iterations, eigenvectors down), close
+        info["host_ms"] = {"plan": 1e3 * (t1 - t0), "solve": 1e3 * (t2 - t1),
+                           "close": 1e3 * (time.perf_counter() - t2)}
+        return out, info
+    return out
