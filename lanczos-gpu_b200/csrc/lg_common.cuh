@@ -227,6 +227,36 @@ __host__ __device__ __forceinline__ double uniform_centered(uint64_t seed, uint6
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (the Lanczos step kernels).  A kernel launched
+// with launch_pdl may start while the kernel before it on the stream is still
+// finishing; griddep_wait() blocks until that kernel has completed and its
+// memory is visible, so everything the previous kernel writes is read after
+// it.  griddep_launch_dependents() lets the next kernel of the stream start
+// early (its own griddep_wait still waits for this one to complete).  Both
+// are no-ops in a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // Dynamic shared memory above the 48 KB default must be opted into per kernel
 // and per device.  `done` is the caller's bit set of devices (ids 0..63) on
 // which the attribute is already set; devices beyond 63 set it on every call.

@@ -389,6 +389,8 @@ __global__ void __launch_bounds__(kLagThreads, 1)
 gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ U,
                       const double* __restrict__ Z, double* __restrict__ partS, double* __restrict__ partT,
                       int* state) {
+  griddep_wait();   // Z comes from the sparse product just before
+  griddep_launch_dependents();
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   constexpr int CH = kLagCH;
   constexpr int RW = 32 / LPR;
@@ -507,28 +509,116 @@ __global__ void __launch_bounds__(kLagThreads, 1)
 gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const double* __restrict__ Z,
                       const double* __restrict__ partS, const double* __restrict__ partT, int nrows_in,
                       double* __restrict__ part_out, double* scal, double* alpha, double* beta, int* state) {
-  if (state[ST_STATUS] != STATUS_RUNNING) return;
   constexpr int CH = kLagCH;
   constexpr int RW = 32 / LPR;
   static_assert(RW <= 8, "row entries per stage");
   extern __shared__ __align__(16) double gs_ring[];
-  __shared__ double cs[kMaxCols], ct[kMaxCols];
-  __shared__ double red[2 * kLagThreads];
+  __shared__ double cs[kMaxCols + 1], ct[kMaxCols + 1];
+  __shared__ double wred[2][8][kMaxCols + 2];
   __shared__ double scr[32];
-  __shared__ double sh_b1, sh_b2, sh_rb, sh_vjz;
+  __shared__ double sh_b1, sh_b2, sh_rb, sh_vjz, sh_uz, sh_zz;
   __shared__ int sh_stop;
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int sub = lane & (LPR - 1), grp = lane / LPR;
   const int j = ncols;   // the column this step finishes
 
-  if (t < kMaxCols) {
-    cs[t] = 0.0;
-    ct[t] = 0.0;
+  bool live[CH], pair[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    const int c0 = ch * 2 * LPR + 2 * sub;
+    live[ch] = c0 < ncols;
+    pair[ch] = c0 + 1 < ncols;
+  }
+  const int rb0 = (int)((long long)n * blockIdx.x / gridDim.x);
+  const int re = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
+  constexpr int step = kLagWarps * RW;
+  const int wfirst = rb0 + warp * RW;
+  const int ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
+  double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
+  auto issue = [&](int gi) {
+    double* st = ring + (gi % kGsStages) * kLagStageDoubles;
+    const int r = gi < ngroups ? wfirst + (ngroups - 1 - gi) * step + grp : re;
+    const bool ok = r < re;
+    const double* row = V + (size_t)r * ldv + 2 * sub;
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      const bool go = ok && live[ch];
+      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
+    }
+    if (sub == 0) {
+      cp_async8(st + 32 * CH * 2 + grp, ok ? R + r : R, ok ? 8 : 0);
+      cp_async8(st + 32 * CH * 2 + 8 + grp, ok ? Z + r : Z, ok ? 8 : 0);
+    }
+    cp_async_commit();
+  };
+  // The first row groups are in flight while the partial sums are reduced.
+  // V's live columns, u and z were final before the projection started, so
+  // these copies may run before this kernel waits for the projection; its
+  // partial sums and the state word are read after the wait.
+#pragma unroll
+  for (int s = 0; s < kGsStages - 1; ++s) issue(s);
+  griddep_wait();
+  griddep_launch_dependents();
+  if (state[ST_STATUS] != STATUS_RUNNING) {
+    cp_async_wait<0>();   // no copy may still target shared memory when the CTA exits
+    return;
+  }
+
+  // partial-sum tables: threads [0, 256) table S (columns 0..j, scalar u^T z),
+  // [256, 512) table T (columns 0..j-1, scalar ||z||^2); warp w of a half sums
+  // rows w, w + 8, ... in order (all loads of a lane independent), then the
+  // eight warps in order
+  {
+    const int half = t >> 8, w8 = (t >> 5) & 7;
+    const double* part = half == 0 ? partS : partT;
+    const int nc = half == 0 ? ncols + 1 : ncols;   // columns, then the scalar slot as entry nc
+    double acc[5] = {0.0, 0.0, 0.0, 0.0, 0.0};
+    int colx[5];
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+      const int i = lane + 32 * q;
+      colx[q] = i < nc ? i : (i == nc ? kPartScalar : -1);
+    }
+    int r = w8;
+    for (; r + 24 < nrows_in; r += 32) {
+#pragma unroll
+      for (int q = 0; q < 5; ++q) {
+        if (colx[q] < 0) continue;
+        const double* pc = part + colx[q];
+        const double a0 = __ldcg(pc + (size_t)r * kPartStride), a1 = __ldcg(pc + (size_t)(r + 8) * kPartStride);
+        const double a2 = __ldcg(pc + (size_t)(r + 16) * kPartStride), a3 = __ldcg(pc + (size_t)(r + 24) * kPartStride);
+        acc[q] += a0;
+        acc[q] += a1;
+        acc[q] += a2;
+        acc[q] += a3;
+      }
+    }
+    for (; r < nrows_in; r += 8) {
+#pragma unroll
+      for (int q = 0; q < 5; ++q)
+        if (colx[q] >= 0) acc[q] += __ldcg(part + (size_t)r * kPartStride + colx[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+      const int i = lane + 32 * q;
+      if (i <= nc) wred[half][w8][i] = acc[q];
+    }
   }
   __syncthreads();
-  double uz, zz;
-  reduce_partials2(partS, partT, nrows_in, ncols + 1, ncols, cs, ct, &uz, &zz, red);   // cs[j] = ||u||^2
+  if (t < 2 * (kMaxCols + 2)) {
+    const int half = t >= kMaxCols + 2 ? 1 : 0, i = t - half * (kMaxCols + 2);
+    const int nc = half == 0 ? ncols + 1 : ncols;
+    if (i <= nc) {
+      double s = 0.0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) s += wred[half][w][i];
+      if (i < nc) (half == 0 ? cs : ct)[i] = s;
+      else if (half == 0) sh_uz = s;
+      else sh_zz = s;
+    }
+  }
+  __syncthreads();
   if (t < 32) {
     double ss = 0.0, st = 0.0;
     for (int i = t; i < ncols; i += 32) {
@@ -541,6 +631,7 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
     const double aprev = scal[SC_ALPHA_PREV] + cs[j - 1];
     const double btol = breakdown_tol_warp(alpha, beta, j - 1, true, aprev);
     if (t == 0) {
+      const double uz = sh_uz;
       const double b2 = uu - ss;
       const double b = b2 > 0.0 ? sqrt(b2) : 0.0;
       int stop = STATUS_RUNNING;
@@ -568,50 +659,21 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
     }
   }
   __syncthreads();
-  if (sh_stop != STATUS_RUNNING) return;
+  if (sh_stop != STATUS_RUNNING) {
+    cp_async_wait<0>();   // no copy may still target shared memory when the CTA exits
+    return;
+  }
   const double b1 = sh_b1, b2s = sh_b2, rb = sh_rb, vjz = sh_vjz;
 
   double2 c1[CH], c2[CH];
-  bool live[CH], pair[CH];
 #pragma unroll
   for (int ch = 0; ch < CH; ++ch) {
     const int c0 = ch * 2 * LPR + 2 * sub;
-    live[ch] = c0 < ncols;
-    pair[ch] = c0 + 1 < ncols;
     c1[ch] = make_double2(c0 < ncols ? cs[c0] : 0.0, c0 + 1 < ncols ? cs[c0 + 1] : 0.0);
     c2[ch] = make_double2(c0 < ncols ? ct[c0] : 0.0, c0 + 1 < ncols ? ct[c0 + 1] : 0.0);
   }
   double nrm = 0.0;
 
-  const int rb0 = (int)((long long)n * blockIdx.x / gridDim.x);
-  const int re = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
-  constexpr int step = kLagWarps * RW;
-  const int wfirst = rb0 + warp * RW;
-  const int ngroups = wfirst < re ? (re - wfirst + step - 1) / step : 0;   // warp-uniform
-  double* ring = gs_ring + (size_t)warp * kGsStages * kLagStageDoubles;
-
-  // The warp walks its row groups last to first: the projection just streamed
-  // them first to last, so the correction starts on the rows that are still
-  // in L2 (measured 29.2 against 29.9 ms per configuration-1 solve).
-  auto issue = [&](int gi) {
-    double* st = ring + (gi % kGsStages) * kLagStageDoubles;
-    const int r = gi < ngroups ? wfirst + (ngroups - 1 - gi) * step + grp : re;
-    const bool ok = r < re;
-    const double* row = V + (size_t)r * ldv + 2 * sub;
-#pragma unroll
-    for (int ch = 0; ch < CH; ++ch) {
-      const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
-    }
-    if (sub == 0) {
-      cp_async8(st + 32 * CH * 2 + grp, ok ? R + r : R, ok ? 8 : 0);
-      cp_async8(st + 32 * CH * 2 + 8 + grp, ok ? Z + r : Z, ok ? 8 : 0);
-    }
-    cp_async_commit();
-  };
-
-#pragma unroll
-  for (int s = 0; s < kGsStages - 1; ++s) issue(s);
   for (int gi = 0; gi < ngroups; ++gi) {
     __syncwarp();
     issue(gi + kGsStages - 1);
@@ -727,8 +789,8 @@ static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP>, (int)gs_lag_smem());
   if (e != cudaSuccess) return e;
-  gs_lag_project_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, U, Z, partS, partT, state);
-  return cudaGetLastError();
+  return launch_pdl(gs_lag_project_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, ldv, ncols, n, U,
+                    Z, partS, partT, state);
 }
 
 template <int LP>
@@ -738,9 +800,8 @@ static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, i
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_correct_kernel<LP>, (int)gs_lag_smem());
   if (e != cudaSuccess) return e;
-  gs_lag_correct_kernel<LP><<<p.grid, kLagThreads, gs_lag_smem(), st>>>(V, ldv, ncols, n, R, Z, partS, partT,
-                                                                        nrows_in, part_out, scal, alpha, beta, state);
-  return cudaGetLastError();
+  return launch_pdl(gs_lag_correct_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, ldv, ncols, n, R,
+                    Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
 }
 
 cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,

@@ -76,6 +76,8 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
                  const double* __restrict__ R_own, double* __restrict__ W, double* __restrict__ Vj, int ldv,
                  const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
                  double* beta, double* scal, int* state) {
+  griddep_wait();   // R and the partial sums come from the previous kernel
+  griddep_launch_dependents();
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   double s1, s2;
   if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
@@ -218,9 +220,13 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
                                const double* R_own, double* W, double* Vj, int ldv, const double* part_in,
                                int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
                                int* state) {
-#define LG_STEP(LN, CNT, LIST)                                                                          \
-  spmv_step_kernel<VT, LN><<<grid, 256, 0, st>>>(CNT, LIST, A.rowptr, A.col, val, R, R_own, W, Vj, ldv, part_in, \
-                                                 nrows_in, j, beta_mode, alpha, beta, scal, state)
+#define LG_STEP(LN, CNT, LIST)                                                                              \
+  do {                                                                                                      \
+    cudaError_t e_ = launch_pdl(spmv_step_kernel<VT, LN>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr,  \
+                                A.col, val, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, \
+                                scal, state);                                                                \
+    if (e_ != cudaSuccess) return e_;                                                                       \
+  } while (0)
   const int ncls = A.nclasses > 0 ? A.nclasses : 1;
   for (int c = 0; c < ncls; ++c) {
     const int lanes = A.nclasses > 0 ? A.class_lanes[c] : A.lanes;
