@@ -66,7 +66,8 @@ basis_kernel(BasisArgs a) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   extern __shared__ __align__(16) double sm[];
   __shared__ double scr[32];
-  const int m = a.m, kq = a.kq, n = a.n, ldv = a.ldv;
+  const int m = a.m, kq = a.kq, n = a.n;
+  const VLayout vl = a.vl;
   const BsGeom g(m, kq);
   double* Qs = sm;                              // kqp columns x sq (column-major, zero padded)
   double* Vs = sm + (size_t)g.kqp * g.sq;       // kTR rows x sv (row-major, zero padded)
@@ -89,10 +90,14 @@ basis_kernel(BasisArgs a) {
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const long long row0 = (long long)tile * kTR;
     __syncthreads();   // previous tile consumed; Qs ready on the first pass
-    for (int i = t; i < kTR * g.mp; i += kBsThreads) {
-      const int rr = i / g.mp, c = i % g.mp;
+    // eight columns of a row at a time (one panel row of the solver's basis:
+    // 64 contiguous bytes; consecutive threads take consecutive rows)
+    for (int i = t; i < kTR * (g.mp >> 2); i += kBsThreads) {
+      const int rr = i % kTR, c = (i / kTR) * 4;
       const long long row = row0 + rr;
-      Vs[rr * g.sv + c] = (row < n && c < m) ? a.V[row * ldv + c] : 0.0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        Vs[rr * g.sv + c + q] = (row < n && c + q < m) ? a.V[vidx(vl, row, c + q)] : 0.0;
     }
     __syncthreads();
     double acc[NOB][2];
@@ -120,7 +125,7 @@ basis_kernel(BasisArgs a) {
       for (int i = t; i < kTR * kv; i += kBsThreads) {
         const int rr = i / kv, k = i % kv;
         const long long row = row0 + rr;
-        if (row < n) a.V[row * ldv + k] = Vs[rr * g.sv + k];
+        if (row < n) a.V[vidx(vl, row, k)] = Vs[rr * g.sv + k];
       }
       if (t < kTR) {
         const long long row = row0 + t;

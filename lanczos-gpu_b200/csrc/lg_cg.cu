@@ -275,10 +275,10 @@ int Solver::cg_solve(const double* b, double* x) {
 }
 
 int Solver::apply_shift_invert(int j, int beta_mode) {
-  double* Vj = V + j;                    // column j of the row-major basis
+  double* Vj = V + vidx(vl, 0, j);       // column j of the basis
   double* b = cg_ws + 4 * (size_t)ld;    // the same vector, contiguous (CG right-hand side)
   LG_TRY(timed(LG_K_OTHER, 24.0 * n, 1, [&] {
-    return normalize_step(stream, num_sm * 8, n, R, Vj, ldv, b, partC, nrowsC, j, beta_mode, alpha, beta, scal,
+    return normalize_step(stream, num_sm * 8, n, R, Vj, (int)vl.rs, b, partC, nrowsC, j, beta_mode, alpha, beta, scal,
                           state);
   }));
   return cg_solve(b, W);

@@ -126,7 +126,7 @@ int Solver::funm_factor(const double* v, int io_on_device, int m, int* m_actual,
   LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
   LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * vsize(), stream));
   LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   const cudaMemcpyKind kind = io_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   if (d_perm) {
@@ -245,7 +245,7 @@ int Solver::funm(const double* v, int io_on_device, int m, int func, int mode, d
   }
   BasisArgs ba;
   ba.V = V;
-  ba.ldv = ldv;
+  ba.vl = vl;
   ba.n = n;
   ba.m = ma;
   ba.kq = 1;
@@ -283,7 +283,7 @@ int Solver::funm_debug(const double* v, int m, double* V_out, double* alpha_out,
   if (e == cudaSuccess) {
     BasisArgs ba;
     ba.V = V;
-    ba.ldv = ldv;
+    ba.vl = vl;
     ba.n = n;
     ba.m = ma;
     ba.kq = ma;

@@ -8,8 +8,10 @@
 //   pass 2 : r1 = w - V h  and  s = V^T r1, ||r1||^2      gs_correct_project
 //   pass 3 : r2 = r1 - V s, ||r2||^2, alpha_j = h_j + s_j gs_correct
 //
-// V is stored ROW-major (n x ldv): a basis row is contiguous, so a warp
-// streams rows with its lanes spread over the columns.  In pass 2 the lanes
+// V has the layout L (lg_kernels.cuh): the solver keeps it in panels of 8
+// columns, the caller of lg_cgs2_orthogonalize row-major; either way a lane
+// loads 16-byte chunks of two adjacent columns of a row, and a warp streams
+// rows with its lanes spread over the columns.  In pass 2 the lanes
 // hold one row of V in registers, reduce the row dot V[row,:]·h across the
 // lanes (shuffles), form r1[row], and immediately accumulate V[row,:]*r1[row]
 // into per-lane column sums — the two halves of the pass share one read of
@@ -45,7 +47,7 @@ __device__ __forceinline__ double2 ld_stream(const double* p) {
 // vec and Rout never alias (MODE 3 reads and writes R through Rout only).
 template <int MODE, int LPR, int CH>
 __global__ void __launch_bounds__(kGsThreads, 1)
-gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ vec,
+gs_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const double* __restrict__ vec,
           double* __restrict__ Rout, const double* __restrict__ part_in, int nrows_in,
           double* __restrict__ part_out, double* scal, double* alpha, int j, int alpha_mode, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
@@ -105,10 +107,9 @@ gs_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double*
     for (int u = 0; u < U; ++u) {
       const long long r = r0 + u * step;
       const bool ok = r < re;
-      const double* row = V + r * ldv;
 #pragma unroll
       for (int ch = 0; ch < CH; ++ch) {
-        v[u][ch] = (ok && live[ch]) ? ld_stream(row + ch * 2 * LPR + 2 * sub) : make_double2(0.0, 0.0);
+        v[u][ch] = (ok && live[ch]) ? ld_stream(V + vidx(L, r, ch * 2 * LPR + 2 * sub)) : make_double2(0.0, 0.0);
         if (!pair[ch]) v[u][ch].y = 0.0;   // padding column: never let its contents in
       }
       x[u] = ok ? (MODE == 3 ? Rout[r] : vec[r]) : 0.0;
@@ -203,7 +204,7 @@ size_t gs_async_smem() { return sizeof(double) * (size_t)kGsWarps * kGsStages * 
 
 template <int MODE, int LPR>
 __global__ void __launch_bounds__(kGsThreads, 1)
-gs_async_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ vec,
+gs_async_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const double* __restrict__ vec,
                 double* __restrict__ Rout, const double* __restrict__ part_in, int nrows_in,
                 double* __restrict__ part_out, double* scal, double* alpha, int j, int alpha_mode, int* state) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
@@ -266,7 +267,7 @@ gs_async_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const d
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? V + r * ldv + ch * 2 * LPR + 2 * sub : V, go ? 16 : 0);
+      cp_async16(st + (ch * 32 + lane) * 2, go ? V + vidx(L, r, ch * 2 * LPR + 2 * sub) : V, go ? 16 : 0);
     }
     if (sub == 0) cp_async8(st + 128 + grp, ok ? xsrc + r : xsrc, ok ? 8 : 0);
     cp_async_commit();
@@ -386,7 +387,7 @@ size_t gs_lag_smem() { return sizeof(double) * (size_t)kLagWarps * kGsStages * k
 
 template <int LPR>
 __global__ void __launch_bounds__(kLagThreads, 1)
-gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, const double* __restrict__ U,
+gs_lag_project_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const double* __restrict__ U,
                       const double* __restrict__ Z, double* __restrict__ partS, double* __restrict__ partT,
                       int* state) {
   griddep_wait();   // Z comes from the sparse product just before
@@ -428,11 +429,10 @@ gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, c
     double* st = ring + (gi % kGsStages) * kLagStageDoubles;
     const int r = wfirst + gi * step + grp;
     const bool ok = gi < ngroups && r < re;
-    const double* row = V + (size_t)r * ldv + 2 * sub;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
+      cp_async16(st + (ch * 32 + lane) * 2, go ? V + vidx(L, r, ch * 2 * LPR + 2 * sub) : V, go ? 16 : 0);
     }
     if (sub == 0) {
       cp_async8(st + 32 * CH * 2 + grp, ok ? U + r : U, ok ? 8 : 0);
@@ -506,7 +506,7 @@ gs_lag_project_kernel(const double* __restrict__ V, int ldv, int ncols, int n, c
 
 template <int LPR>
 __global__ void __launch_bounds__(kLagThreads, 1)
-gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const double* __restrict__ Z,
+gs_lag_correct_kernel(double* V, VLayout L, int ncols, int n, double* R, const double* __restrict__ Z,
                       const double* __restrict__ partS, const double* __restrict__ partT, int nrows_in,
                       double* __restrict__ part_out, double* scal, double* alpha, double* beta, int* state) {
   constexpr int CH = kLagCH;
@@ -540,11 +540,10 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
     double* st = ring + (gi % kGsStages) * kLagStageDoubles;
     const int r = gi < ngroups ? wfirst + (ngroups - 1 - gi) * step + grp : re;
     const bool ok = r < re;
-    const double* row = V + (size_t)r * ldv + 2 * sub;
 #pragma unroll
     for (int ch = 0; ch < CH; ++ch) {
       const bool go = ok && live[ch];
-      cp_async16(st + (ch * 32 + lane) * 2, go ? row + ch * 2 * LPR : V, go ? 16 : 0);
+      cp_async16(st + (ch * 32 + lane) * 2, go ? V + vidx(L, r, ch * 2 * LPR + 2 * sub) : V, go ? 16 : 0);
     }
     if (sub == 0) {
       cp_async8(st + 32 * CH * 2 + grp, ok ? R + r : R, ok ? 8 : 0);
@@ -698,7 +697,7 @@ gs_lag_correct_kernel(double* V, int ldv, int ncols, int n, double* R, const dou
       const double xu = st[32 * CH * 2 + grp], xz = st[32 * CH * 2 + 8 + grp];
       const double vj = ((xu - d1) * b1) * b2s;
       const double r1 = rb * (xz - d2 - vjz * vj);
-      V[(size_t)r * ldv + j] = vj;
+      V[vidx(L, r, j)] = vj;
       R[r] = r1;
       nrm += r1 * r1;
     }
@@ -732,7 +731,7 @@ GsPlan gs_plan(int n, int ncols, int grid) {
 constexpr bool kGsAsync2 = true, kGsAsync3 = true, kGsAsync1 = false;
 
 template <int MODE>
-static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                const double* vec, double* Rout, const double* part_in, int nrows_in,
                                double* part_out, double* scal, double* alpha, int j, int alpha_mode, int* state) {
   if ((MODE == 1 && kGsAsync1) || (MODE == 2 && kGsAsync2) || (MODE == 3 && kGsAsync3)) {
@@ -741,7 +740,7 @@ static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V
     static std::atomic<unsigned long long> attr{0};                                                             \
     cudaError_t e = smem_attr_once(attr, (const void*)gs_async_kernel<MODE, LP>, (int)gs_async_smem());         \
     if (e != cudaSuccess) return e;                                                                             \
-    gs_async_kernel<MODE, LP><<<p.grid, kGsThreads, gs_async_smem(), st>>>(V, ldv, ncols, n, vec, Rout, part_in,  \
+    gs_async_kernel<MODE, LP><<<p.grid, kGsThreads, gs_async_smem(), st>>>(V, L, ncols, n, vec, Rout, part_in,    \
                                                                           nrows_in, part_out, scal, alpha, j,   \
                                                                           alpha_mode, state);                   \
   } while (0)
@@ -753,7 +752,7 @@ static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V
     return cudaGetLastError();
   }
 #define LG_GS(LP, C)                                                                                          \
-  gs_kernel<MODE, LP, C><<<p.grid, kGsThreads, 0, st>>>(V, ldv, ncols, n, vec, Rout, part_in, nrows_in,      \
+  gs_kernel<MODE, LP, C><<<p.grid, kGsThreads, 0, st>>>(V, L, ncols, n, vec, Rout, part_in, nrows_in,        \
                                                         part_out, scal, alpha, j, alpha_mode, state)
   if (p.lpr == 4) LG_GS(4, 2);
   else if (p.lpr == 8) LG_GS(8, 2);
@@ -763,62 +762,62 @@ static cudaError_t launch_mode(const GsPlan& p, cudaStream_t st, const double* V
   return cudaGetLastError();
 }
 
-cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                        const double* vec, double* part_out, int* state) {
-  return launch_mode<1>(p, st, V, ldv, ncols, n, vec, nullptr, nullptr, 0, part_out, nullptr, nullptr, 0, 0,
+  return launch_mode<1>(p, st, V, L, ncols, n, vec, nullptr, nullptr, 0, part_out, nullptr, nullptr, 0, 0,
                         state);
 }
 
-cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                const double* W, double* R, const double* part_in, int nrows_in,
                                double* part_out, double* scal, int* state) {
-  return launch_mode<2>(p, st, V, ldv, ncols, n, W, R, part_in, nrows_in, part_out, scal, nullptr, 0, 0, state);
+  return launch_mode<2>(p, st, V, L, ncols, n, W, R, part_in, nrows_in, part_out, scal, nullptr, 0, 0, state);
 }
 
-cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n, double* R,
+cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n, double* R,
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state) {
-  return launch_mode<3>(p, st, V, ldv, ncols, n, nullptr, R, part_in, nrows_in, part_out, scal, alpha, j,
+  return launch_mode<3>(p, st, V, L, ncols, n, nullptr, R, part_in, nrows_in, part_out, scal, alpha, j,
                         alpha_mode, state);
 }
 
 
 template <int LP>
-static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                   const double* U, const double* Z, double* partS, double* partT, int* state) {
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP>, (int)gs_lag_smem());
   if (e != cudaSuccess) return e;
-  return launch_pdl(gs_lag_project_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, ldv, ncols, n, U,
+  return launch_pdl(gs_lag_project_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols, n, U,
                     Z, partS, partT, state);
 }
 
 template <int LP>
-static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, VLayout L, int ncols, int n, double* R,
                                   const double* Z, const double* partS, const double* partT, int nrows_in,
                                   double* part_out, double* scal, double* alpha, double* beta, int* state) {
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_correct_kernel<LP>, (int)gs_lag_smem());
   if (e != cudaSuccess) return e;
-  return launch_pdl(gs_lag_correct_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, ldv, ncols, n, R,
+  return launch_pdl(gs_lag_correct_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols, n, R,
                     Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
 }
 
-cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                            const double* U, const double* Z, double* partS, double* partT, int* state) {
-  if (ncols <= 32) return lag_project_lp<4>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
-  if (ncols <= 64) return lag_project_lp<8>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
-  return lag_project_lp<16>(p, st, V, ldv, ncols, n, U, Z, partS, partT, state);
+  if (ncols <= 32) return lag_project_lp<4>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
+  if (ncols <= 64) return lag_project_lp<8>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
+  return lag_project_lp<16>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
 }
 
-cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, VLayout L, int ncols, int n, double* R,
                            const double* Z, const double* partS, const double* partT, int nrows_in,
                            double* part_out, double* scal, double* alpha, double* beta, int* state) {
   if (ncols <= 32)
-    return lag_correct_lp<4>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+    return lag_correct_lp<4>(p, st, V, L, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
   if (ncols <= 64)
-    return lag_correct_lp<8>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
-  return lag_correct_lp<16>(p, st, V, ldv, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+    return lag_correct_lp<8>(p, st, V, L, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
+  return lag_correct_lp<16>(p, st, V, L, ncols, n, R, Z, partS, partT, nrows_in, part_out, scal, alpha, beta, state);
 }
 
 }  // namespace lg

@@ -168,7 +168,7 @@ int Solver::init_device() {
 // The Krylov basis, the operator output and residual, the partial-sum rows,
 // the tridiagonal and the restart state (n, ld, ldv and the stream are set).
 int Solver::alloc_workspace() {
-  LG_TRY(dalloc((void**)&V, sizeof(double) * (size_t)n * ldv));
+  LG_TRY(dalloc((void**)&V, sizeof(double) * vsize()));
   LG_TRY(dalloc((void**)&W, sizeof(double) * (size_t)ld));
   if (comm) {
     LG_TRY(cudaMalloc(&Rfull, sizeof(double) * (size_t)ld * nranks));
@@ -180,7 +180,7 @@ int Solver::alloc_workspace() {
     LG_TRY(dalloc((void**)&R, sizeof(double) * (size_t)ld));
     LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   }
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * vsize(), stream));
   LG_TRY(cudaMemsetAsync(W, 0, sizeof(double) * (size_t)ld, stream));
   const int prow = std::max(grid_gs, std::max(grid_basis, num_sm)) ;
   for (double** p : {&partA, &partB, &partC}) {
@@ -228,7 +228,9 @@ int Solver::create_op(int n_, int kind, lg_matvec_fn fn, lg_matvec_stream_fn sfn
   op_user = user;
   max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
   ld = round_up(n, kRowAlign);
-  ldv = round_up(max_ncv + 1, 4);
+  ldv = round_up(max_ncv + 1, 8);
+  vl.rs = 8;
+  vl.ps = 8ll * round_up(n, 8);
   int rc = init_device();
   if (rc != LG_OK) return rc;
   rc = alloc_workspace();
@@ -276,9 +278,9 @@ int Solver::call_user_op(const double* x, double* y) {
 // Matrix-free step j: v_j = R / beta_j into V[:, j] and op_x (the same DGKS /
 // breakdown checks as the sparse step), then W = OP(v_j).
 int Solver::apply_user_op(int j, int beta_mode) {
-  double* Vj = V + j;
+  double* Vj = V + vidx(vl, 0, j);
   LG_TRY(timed(LG_K_OTHER, 24.0 * n, 1, [&] {
-    return normalize_step(stream, num_sm * 8, n, R, Vj, ldv, op_x, inC, nrowsC, j, beta_mode, alpha, beta, scal,
+    return normalize_step(stream, num_sm * 8, n, R, Vj, (int)vl.rs, op_x, inC, nrowsC, j, beta_mode, alpha, beta, scal,
                           state);
   }));
   return call_user_op(op_x, W);
@@ -363,7 +365,9 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   mixed = mixed_;
   max_ncv = std::max(2, std::min(max_ncv_ > 0 ? max_ncv_ : kMaxCols - 1, kMaxCols - 1));
   ld = comm ? lg_partition_block(n_global, nranks) : round_up(n, kRowAlign);
-  ldv = round_up(max_ncv + 1, 4);
+  ldv = round_up(max_ncv + 1, 8);
+  vl.rs = 8;
+  vl.ps = 8ll * round_up(n, 8);
 
   {
     int rc = init_device();
@@ -818,7 +822,7 @@ int Solver::clear_status() {
 // w = OP(v_j) preceded by the normalisation of R into V[:, j].
 int Solver::apply_step(int j, int beta_mode) {
   if (op_kind >= 0) return apply_user_op(j, beta_mode);
-  double* Vj = V + j;   // column j of the row-major basis
+  double* Vj = V + vidx(vl, 0, j);   // column j of the basis
   if (!opts.use_sigma) {
     // CSR stream + x gather (counted once) + v_j and w written
     const double vb = mixed ? 4.0 : 8.0;
@@ -827,7 +831,7 @@ int Solver::apply_step(int j, int beta_mode) {
     if (rc != LG_OK) return rc;
     const double* Rg = comm ? Rfull : R;
     LG_TRY(timed(LG_K_SPMV, bytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
-      return spmv_step(A, stream, grid_spmv, Rg, W, Vj, ldv, inC, nrowsC, j, beta_mode, alpha, beta, scal, state,
+      return spmv_step(A, stream, grid_spmv, Rg, W, Vj, (int)vl.rs, inC, nrowsC, j, beta_mode, alpha, beta, scal, state,
                        R);
     }));
     return LG_OK;
@@ -856,16 +860,16 @@ int Solver::extend(int j0, int j1, int first_mode, bool lag) {
     const double *inA = nullptr, *inB = nullptr;
     int nA = 0, nB = 0;
     LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
-                 [&] { return gs_project(p, stream, V, ldv, ncols, n, W, partA, state); }));
+                 [&] { return gs_project(p, stream, V, vl, ncols, n, W, partA, state); }));
     rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
     if (rc != LG_OK) return rc;
     LG_TRY(timed(LG_K_CORRPROJ, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct_project(p, stream, V, ldv, ncols, n, W, R, inA, nA, partB, scal, state);
+      return gs_correct_project(p, stream, V, vl, ncols, n, W, R, inA, nA, partB, scal, state);
     }));
     rc = reduce_partials_all(partB, p.grid, 1, &inB, &nB);
     if (rc != LG_OK) return rc;
     LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
-      return gs_correct(p, stream, V, ldv, ncols, n, R, inB, nB, partC, scal, alpha, j, 1, state);
+      return gs_correct(p, stream, V, vl, ncols, n, R, inB, nB, partC, scal, alpha, j, 1, state);
     }));
     rc = reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
     if (rc != LG_OK) return rc;
@@ -885,19 +889,19 @@ int Solver::lag_step(int j) {
   if (rc != LG_OK) return rc;
   const double* Rg = comm ? Rfull : R;
   LG_TRY(timed(LG_K_SPMV, sbytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
-    return spmv_step(A, stream, grid_spmv, Rg, W, nullptr, ldv, inC, nrowsC, j, BETA_LAG, alpha, beta, scal, state,
+    return spmv_step(A, stream, grid_spmv, Rg, W, nullptr, (int)vl.rs, inC, nrowsC, j, BETA_LAG, alpha, beta, scal, state,
                      R);
   }));
   const GsPlan p = gs_plan(n, j, grid_gs);
   const double vbytes = 8.0 * (double)n * j;
   LG_TRY(timed(LG_K_PROJECT, vbytes + 16.0 * n, 1,
-               [&] { return gs_lag_project(p, stream, V, ldv, j, n, R, W, partA, partB, state); }));
+               [&] { return gs_lag_project(p, stream, V, vl, j, n, R, W, partA, partB, state); }));
   const double *inS = nullptr, *inT = nullptr;
   int nS = 0;
   rc = reduce_partials_all2(partA, partB, p.grid, 0, &inS, &inT, &nS);
   if (rc != LG_OK) return rc;
   LG_TRY(timed(LG_K_CORRPROJ, vbytes + 32.0 * n, 1, [&] {
-    return gs_lag_correct(p, stream, V, ldv, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);
+    return gs_lag_correct(p, stream, V, vl, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);
   }));
   return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
@@ -912,11 +916,11 @@ int Solver::finish_lag(int s) {
   const double* inA = nullptr;
   int nA = 0;
   LG_TRY(timed(LG_K_PROJECT, vbytes + 8.0 * n, 1,
-               [&] { return gs_project(p, stream, V, ldv, ncols, n, R, partA, state); }));
+               [&] { return gs_project(p, stream, V, vl, ncols, n, R, partA, state); }));
   int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
   if (rc != LG_OK) return rc;
   LG_TRY(timed(LG_K_CORRECT, vbytes + 16.0 * n, 1, [&] {
-    return gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state);
+    return gs_correct(p, stream, V, vl, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state);
   }));
   return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
@@ -951,10 +955,10 @@ int Solver::pass3(int s) {
   launches += 2;
   const double* inA = nullptr;
   int nA = 0;
-  LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
+  LG_TRY(gs_project(p, stream, V, vl, ncols, n, R, partA, state));
   int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
   if (rc != LG_OK) return rc;
-  LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state));
+  LG_TRY(gs_correct(p, stream, V, vl, ncols, n, R, inA, nA, partC, scal, alpha, s, 2, state));
   return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
 
@@ -972,10 +976,10 @@ int Solver::random_restart(int s) {
   for (int pass = 0; pass < 2; ++pass) {
     const double* inA = nullptr;
     int nA = 0;
-    LG_TRY(gs_project(p, stream, V, ldv, ncols, n, R, partA, state));
+    LG_TRY(gs_project(p, stream, V, vl, ncols, n, R, partA, state));
     int rc = reduce_partials_all(partA, p.grid, 0, &inA, &nA);
     if (rc != LG_OK) return rc;
-    LG_TRY(gs_correct(p, stream, V, ldv, ncols, n, R, inA, nA, partC, scal, alpha, s, 0, state));
+    LG_TRY(gs_correct(p, stream, V, vl, ncols, n, R, inA, nA, partC, scal, alpha, s, 0, state));
     rc = reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
     if (rc != LG_OK) return rc;
   }
@@ -1030,7 +1034,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
   LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
   LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * vsize(), stream));
 
   // Starting vector into R.
   if (v0) {
@@ -1150,7 +1154,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     }
     BasisArgs ba;
     ba.V = V;
-    ba.ldv = ldv;
+    ba.vl = vl;
     ba.n = n;
     ba.m = m;
     ba.kq = nev_use + 1;
@@ -1213,7 +1217,7 @@ int Solver::run(const lg_eigsh_opts& o, const double* v0, double* evals, double*
     }
     BasisArgs ba;
     ba.V = V;
-    ba.ldv = ldv;
+    ba.vl = vl;
     ba.n = n;
     ba.m = m;
     ba.kq = ksel;
@@ -1293,7 +1297,7 @@ int Solver::factorize(const double* v0, int m, double* alpha_out, double* beta_o
   LG_TRY(cudaMemsetAsync(scal, 0, sizeof(double) * SC_WORDS, stream));
   LG_TRY(cudaMemsetAsync(alpha, 0, sizeof(double) * (kMaxCols + 2), stream));
   LG_TRY(cudaMemsetAsync(beta, 0, sizeof(double) * (kMaxCols + 2), stream));
-  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * (size_t)n * ldv, stream));
+  LG_TRY(cudaMemsetAsync(V, 0, sizeof(double) * vsize(), stream));
   LG_TRY(cudaMemsetAsync(R, 0, sizeof(double) * (size_t)ld, stream));
   if (d_perm) {
     LG_TRY(cudaMemcpyAsync(W, v0, sizeof(double) * (size_t)n, cudaMemcpyHostToDevice, stream));

@@ -7,8 +7,23 @@
 
 namespace lg {
 
-// Launch geometry of the Gram-Schmidt pass kernels (lg_gs.cu).  V is
-// row-major n x ldv; `ncols` live columns.
+// Layout of a basis: element (r, c) is at V + (c >> 3) * ps + r * rs + (c & 7).
+//  * the solver's panel layout: columns in panels of 8, each panel an
+//    n_pad x 8 row-major block (rs = 8, ps = 8 n_pad).  Reading c live
+//    columns streams ceil(c / 8) contiguous panels, and a new column lands 8
+//    bytes every 64 (a row's entry of one panel), not every row stride;
+//  * a row-major n x ld array (the caller's basis of lg_cgs2_orthogonalize):
+//    rs = ld, ps = 8.
+// A 16-byte chunk of two columns (c even) never straddles a panel.
+struct VLayout {
+  long long rs = 0, ps = 0;
+};
+__host__ __device__ __forceinline__ long long vidx(const VLayout& L, long long r, int c) {
+  return (long long)(c >> 3) * L.ps + r * L.rs + (c & 7);
+}
+
+// Launch geometry of the Gram-Schmidt pass kernels (lg_gs.cu).  V has the
+// layout L; `ncols` live columns.
 struct GsPlan {
   int lpr = 32;      // lanes per basis row
   int ch = 1;        // 2*lpr-column chunks per row
@@ -17,12 +32,12 @@ struct GsPlan {
 
 GsPlan gs_plan(int n, int ncols, int grid);
 
-cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                        const double* vec, double* part_out, int* state);
-cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_correct_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                const double* W, double* R, const double* part_in, int nrows_in,
                                double* part_out, double* scal, int* state);
-cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n, double* R,
+cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n, double* R,
                        const double* part_in, int nrows_in, double* part_out, double* scal, double* alpha,
                        int j, int alpha_mode, int* state);
 
@@ -35,9 +50,9 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, int ld
 //                   beta[j], v_j = (u - V s) / beta_j into V[:, j],
 //                   R = (rho / beta_j) (z - V t - (v_j^T z) v_j), alpha[j]
 //                   (first pass); part_out: ||R||^2.
-cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, int ldv, int ncols, int n,
+cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                            const double* U, const double* Z, double* partS, double* partT, int* state);
-cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, int ldv, int ncols, int n, double* R,
+cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, VLayout L, int ncols, int n, double* R,
                            const double* Z, const double* partS, const double* partT, int nrows_in,
                            double* part_out, double* scal, double* alpha, double* beta, int* state);
 
@@ -76,7 +91,7 @@ struct CsrDev {
   const int* class_rows[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
-// Vj points at column j of the row-major basis (stride ldv).
+// Vj points at column j of the basis, its rows ldv doubles apart (the layout's rs).
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,
                       int ldv, const double* part_in, int nrows_in, int j, int beta_mode, double* alpha,
                       double* beta, double* scal, int* state, const double* R_own = nullptr);
@@ -123,13 +138,13 @@ enum Which { WHICH_LM = 0, WHICH_SM = 1, WHICH_LA = 2, WHICH_SA = 3, WHICH_BE = 
 size_t restart_scratch_doubles();
 cudaError_t restart_step(const RestartArgs& a, cudaStream_t st);
 
-// Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq], V row-major n x ldv.
+// Basis update (lg_basis.cu): out = V[:, 0:m] * Q[:, 0:kq], V with layout vl.
 //  restart mode: V[:, 0:kq-1] <- out[:, 0:kq-1] in place;
 //                R <- rcoef * R + tau * out[:, kq-1];  norm partials of R.
 //  ritz mode   : Y[:, 0:kq] = out (column-major ldy, or row-major when rowmajor).
 struct BasisArgs {
   double* V = nullptr;
-  int ldv = 0;
+  VLayout vl;
   int n = 0;
   int m = 0;            // columns of V used
   int kq = 0;           // columns of Q used

@@ -44,15 +44,18 @@ size_t cgs2_workspace_doubles(int grid) { return (size_t)3 * grid * kPartStride 
 int cgs2_run(const double* V, int ldv, int n, int ncols, const double* w, double* r, double* coef, double* norms,
              cudaStream_t st, int grid, double* ws, int* state) {
   const GsPlan p = gs_plan(n, ncols, grid);
+  VLayout L;   // the caller's row-major basis
+  L.rs = ldv;
+  L.ps = 8;
   double* partA = ws;
   double* partB = ws + (size_t)grid * kPartStride;
   double* partC = ws + (size_t)2 * grid * kPartStride;
   double* scal = ws + (size_t)3 * grid * kPartStride;
   cudaError_t e = cudaMemsetAsync(state, 0, sizeof(int) * ST_WORDS, st);
-  if (e == cudaSuccess) e = gs_project(p, st, V, ldv, ncols, n, w, partA, state);
-  if (e == cudaSuccess) e = gs_correct_project(p, st, V, ldv, ncols, n, w, r, partA, p.grid, partB, scal, state);
+  if (e == cudaSuccess) e = gs_project(p, st, V, L, ncols, n, w, partA, state);
+  if (e == cudaSuccess) e = gs_correct_project(p, st, V, L, ncols, n, w, r, partA, p.grid, partB, scal, state);
   if (e == cudaSuccess)
-    e = gs_correct(p, st, V, ldv, ncols, n, r, partB, p.grid, partC, scal, nullptr, 0, 0, state);
+    e = gs_correct(p, st, V, L, ncols, n, r, partB, p.grid, partC, scal, nullptr, 0, 0, state);
   if (e == cudaSuccess) {
     cgs2_finalize_kernel<<<1, kGsThreads, 0, st>>>(partA, partB, partC, p.grid, ncols, coef, norms, state);
     e = cudaGetLastError();

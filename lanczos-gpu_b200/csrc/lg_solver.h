@@ -101,7 +101,9 @@ class Solver {
   int apply_shift_invert(int j, int beta_mode);
   int cg_solve(const double* b, double* x);
 
-  int n = 0, ld = 0, ldv = 0, max_ncv = 0, mixed = 0;   // ld: vector length padding; ldv: basis row stride
+  int n = 0, ld = 0, ldv = 0, max_ncv = 0, mixed = 0;   // ld: vector length padding; ldv: basis columns (a multiple of 8)
+  VLayout vl;   // the basis in panels of 8 columns (lg_kernels.cuh): rs = 8, ps = 8 * round_up(n, 8)
+  size_t vsize() const { return (size_t)vl.ps * (size_t)(ldv / 8); }   // doubles of the basis
   // matrix-free plans: LG_OP_* (-1: the plan owns a CSR), the callback and
   // its argument; op_x: the contiguous operand; host operators: pinned
   // copies of x and y
@@ -158,7 +160,7 @@ class Solver {
   double* funm_ws = nullptr;      // funm small side: Z, inverse-iteration scratch, q, scalars
   double* d_chunk_sum = nullptr;  // one partial per long-row chunk
 
-  double* V = nullptr;      // n x ldv, row-major (ldv >= max_ncv + 1)
+  double* V = nullptr;      // basis, ldv columns in panels of 8 (vl), ldv >= max_ncv + 1
   double* W = nullptr;      // operator output
   double* R = nullptr;      // residual (unnormalised next basis vector)
   double* partA = nullptr;  // partial sums: pass 1
