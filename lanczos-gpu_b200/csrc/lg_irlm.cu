@@ -97,10 +97,6 @@ void Solver::release() {
   recv_off.clear();
   recv_cnt.clear();
   halo_send = halo_recv = 0;
-  for (void*& p : sell_arrays) {
-    if (p) dfree(p);
-    p = nullptr;
-  }
   void* ptrs[] = {d_rowptr, d_col, d_val64, d_val32, d_long, d_chunk_sum, d_classes, V, W, R, partA, partB, partC, alpha, beta, scal,
                   ritz, bounds, zsel, Q, rs_scratch, conv, state, Ytmp, cg_ws, cg_part, cg_scal, cg_counter, cg_flags};
   for (void* p : ptrs)
@@ -450,8 +446,6 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   {
     int rc = build_long_rows(hrp.data());
     if (rc != LG_OK) return rc;
-    rc = build_sell(hrp.data());
-    if (rc != LG_OK) return rc;
   }
   if (comm) {
     int rc = setup_halo();
@@ -730,103 +724,6 @@ int Solver::build_long_rows(const int* hrp) {
   A.chunk_begin = A.long_first + first.size();
   A.chunk_end = A.chunk_begin + cb.size();
   A.chunk_sum = d_chunk_sum;
-  return LG_OK;
-}
-
-// Entries of the sliced copy: one warp per slice, lane = slot; the row's k-th
-// entry, or padding (the row's first column, or column 0 for an empty row or
-// slot, with value 0).
-template <typename VT>
-__global__ void sell_fill_kernel(int nslices, const int* __restrict__ srow, const long long* __restrict__ sptr,
-                                 const int* __restrict__ rowptr, const int* __restrict__ col,
-                                 const VT* __restrict__ val, int* __restrict__ scol, VT* __restrict__ sval) {
-  const int lane = threadIdx.x & 31;
-  const int warps_total = (gridDim.x * blockDim.x) >> 5;
-  for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < nslices; s += warps_total) {
-    const long long b = sptr[s], len = (sptr[s + 1] - b) / 32;
-    const int row = srow[(size_t)s * 32 + lane];
-    const int rb = row >= 0 ? rowptr[row] : 0, rl = row >= 0 ? rowptr[row + 1] - rb : 0;
-    const int pad = rl > 0 ? col[rb] : 0;
-    for (long long k = 0; k < len; ++k) {
-      const long long d = b + k * 32 + lane;
-      if (k < rl) {
-        scol[d] = col[rb + k];
-        sval[d] = val[rb + k];
-      } else {
-        scol[d] = pad;
-        sval[d] = (VT)0;
-      }
-    }
-  }
-}
-
-// The sliced copy of the matrix for the step product (CsrDev::sell_*), built
-// when the rows are narrow (no long rows, no length classes) and the padding
-// adds at most a fifth to the entries; rows are sorted by length (longest
-// first, then by index) inside windows of kSellWindow rows, which keeps the
-// gathers of a slice among neighbouring rows.
-int Solver::build_sell(const int* hrp) {
-  A.nslices = 0;
-  if (A.nclasses > 0 || A.nlong > 0 || nnz == 0 || n < 32) return LG_OK;
-  const int nslices = (n + 31) / 32;
-  std::vector<int> srow((size_t)nslices * 32, -1);
-  std::vector<long long> sptr((size_t)nslices + 1, 0);
-  std::vector<int> cnt;
-  for (int w0 = 0; w0 < n; w0 += kSellWindow) {
-    const int w1 = std::min(n, w0 + kSellWindow);
-    int maxlen = 0;
-    for (int i = w0; i < w1; ++i) maxlen = std::max(maxlen, hrp[i + 1] - hrp[i]);
-    cnt.assign((size_t)maxlen + 2, 0);
-    for (int i = w0; i < w1; ++i) ++cnt[(size_t)(maxlen - (hrp[i + 1] - hrp[i]))];   // longest first
-    int acc = 0;
-    for (size_t q = 0; q < cnt.size(); ++q) {
-      const int c = cnt[q];
-      cnt[q] = acc;
-      acc += c;
-    }
-    for (int i = w0; i < w1; ++i) srow[(size_t)w0 + cnt[(size_t)(maxlen - (hrp[i + 1] - hrp[i]))]++] = i;
-  }
-  for (int s = 0; s < nslices; ++s) {
-    int len = 0;
-    for (int l = 0; l < 32; ++l) {
-      const int r = srow[(size_t)s * 32 + l];
-      if (r >= 0) len = std::max(len, hrp[r + 1] - hrp[r]);
-    }
-    sptr[(size_t)s + 1] = sptr[s] + 32ll * len;
-  }
-  const long long total = sptr[nslices];
-  if ((double)total > 1.2 * (double)nnz) return LG_OK;   // too much padding: keep the CSR kernels
-  int *d_srow = nullptr, *d_scol = nullptr;
-  long long* d_sptr = nullptr;
-  LG_TRY(dalloc((void**)&d_srow, sizeof(int) * srow.size()));
-  LG_TRY(dalloc((void**)&d_sptr, sizeof(long long) * sptr.size()));
-  LG_TRY(dalloc((void**)&d_scol, sizeof(int) * (size_t)total));
-  sell_arrays[0] = d_srow;
-  sell_arrays[1] = d_sptr;
-  sell_arrays[2] = d_scol;
-  LG_TRY(cudaMemcpyAsync(d_srow, srow.data(), sizeof(int) * srow.size(), cudaMemcpyHostToDevice, stream));
-  LG_TRY(cudaMemcpyAsync(d_sptr, sptr.data(), sizeof(long long) * sptr.size(), cudaMemcpyHostToDevice, stream));
-  const int grid = num_sm * 8;
-  if (d_val32) {
-    float* d_sv = nullptr;
-    LG_TRY(dalloc((void**)&d_sv, sizeof(float) * (size_t)total));
-    sell_arrays[3] = d_sv;
-    sell_fill_kernel<float><<<grid, 256, 0, stream>>>(nslices, d_srow, d_sptr, d_rowptr, d_col, d_val32, d_scol, d_sv);
-    A.sell_val32 = d_sv;
-  } else {
-    double* d_sv = nullptr;
-    LG_TRY(dalloc((void**)&d_sv, sizeof(double) * (size_t)total));
-    sell_arrays[3] = d_sv;
-    sell_fill_kernel<double><<<grid, 256, 0, stream>>>(nslices, d_srow, d_sptr, d_rowptr, d_col, d_val64, d_scol,
-                                                       d_sv);
-    A.sell_val64 = d_sv;
-  }
-  LG_TRY(cudaGetLastError());
-  LG_TRY(cudaStreamSynchronize(stream));   // the host vectors go out of scope
-  A.sell_row = d_srow;
-  A.sell_ptr = d_sptr;
-  A.sell_col = d_scol;
-  A.nslices = nslices;
   return LG_OK;
 }
 

@@ -89,22 +89,7 @@ struct CsrDev {
   int class_lanes[5] = {0, 0, 0, 0, 0};
   int class_count[5] = {0, 0, 0, 0, 0};
   const int* class_rows[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-  // Sliced copy for the Lanczos step's product when the row lengths are
-  // narrow (kNN graphs, stencils): rows sorted by length inside windows of
-  // kSellWindow rows, cut in slices of 32 rows, each slice padded to its
-  // longest row (padding: the row's own first column with value 0) and stored
-  // entry-major, so entry k of the 32 rows of a slice is 32 consecutive
-  // words.  One lane per row: the column and value loads of a warp are
-  // single coalesced lines, with no row pointer on the dependent chain.
-  // nslices == 0: no sliced copy (the CSR kernels run).
-  int nslices = 0;
-  const int* sell_row = nullptr;         // nslices * 32: the row of each slot (-1: empty slot)
-  const long long* sell_ptr = nullptr;   // nslices + 1: first entry of each slice (32 entries per row position)
-  const int* sell_col = nullptr;
-  const double* sell_val64 = nullptr;
-  const float* sell_val32 = nullptr;
 };
-constexpr int kSellWindow = 4096;   // rows sorted by length within windows of this many rows
 
 // Vj points at column j of the basis, its rows ldv doubles apart (the layout's rs).
 cudaError_t spmv_step(const CsrDev& A, cudaStream_t st, int grid, const double* R, double* W, double* Vj,

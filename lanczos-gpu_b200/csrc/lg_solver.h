@@ -79,8 +79,6 @@ class Solver {
   int reduce_partials_all2(double* pa, double* pb, int nrows, int slot, const double** ina, const double** inb,
                            int* nin);
   int build_long_rows(const int* host_rowptr);
-  int build_sell(const int* host_rowptr);
-  void* sell_arrays[4] = {nullptr, nullptr, nullptr, nullptr};   // sliced copy: rows, slice offsets, columns, values
   int funm_factor(const double* v, int io_on_device, int m, int* m_actual, double* vnorm);
   int sync_state();
   int clear_status();

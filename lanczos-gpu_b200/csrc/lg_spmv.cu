@@ -130,46 +130,6 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
   }
 }
 
-// The step product on the sliced copy (CsrDev::sell_*): one warp per slice
-// of 32 rows, one lane per row, entries summed in order (padding entries add
-// 0); four entries of a row in flight at a time.
-template <typename VT>
-__global__ void __launch_bounds__(256)
-sell_step_kernel(int nslices, const int* __restrict__ srow, const long long* __restrict__ sptr,
-                 const int* __restrict__ scol, const VT* __restrict__ sval, const double* __restrict__ R,
-                 const double* __restrict__ R_own, double* __restrict__ W, double* __restrict__ Vj, int ldv,
-                 const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
-                 double* beta, double* scal, int* state) {
-  griddep_wait();   // R and the partial sums come from the previous kernel
-  griddep_launch_dependents();
-  if (state[ST_STATUS] != STATUS_RUNNING) return;
-  double s1, s2;
-  if (step_prologue(part_in, nrows_in, j, beta_mode, alpha, beta, scal, state, s1, s2) != STATUS_RUNNING) return;
-  const int lane = threadIdx.x & 31;
-  const int warps_total = (gridDim.x * blockDim.x) >> 5;
-  for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < nslices; s += warps_total) {
-    const long long b = __ldg(sptr + s), e = __ldg(sptr + s + 1);
-    const int row = __ldg(srow + (size_t)s * 32 + lane);
-    double acc = 0.0;
-    long long k = b + lane;
-    for (; k + 96 < e; k += 128) {
-      const int c0 = __ldg(scol + k), c1 = __ldg(scol + k + 32), c2 = __ldg(scol + k + 64), c3 = __ldg(scol + k + 96);
-      const double v0 = (double)__ldg(sval + k), v1 = (double)__ldg(sval + k + 32);
-      const double v2 = (double)__ldg(sval + k + 64), v3 = (double)__ldg(sval + k + 96);
-      const double x0 = __ldg(R + c0), x1 = __ldg(R + c1), x2 = __ldg(R + c2), x3 = __ldg(R + c3);
-      acc += v0 * x0;
-      acc += v1 * x1;
-      acc += v2 * x2;
-      acc += v3 * x3;
-    }
-    for (; k < e; k += 32) acc += (double)__ldg(sval + k) * __ldg(R + __ldg(scol + k));
-    if (row >= 0) {
-      W[row] = (acc * s1) * s2;
-      if (Vj) Vj[(size_t)row * ldv] = (R_own[row] * s1) * s2;
-    }
-  }
-}
-
 __global__ void __launch_bounds__(256)
 normalize_step_kernel(int n, const double* __restrict__ R, double* __restrict__ Vj, int ldv, double* __restrict__ out,
                       const double* __restrict__ part_in, int nrows_in, int j, int beta_mode, double* alpha,
@@ -260,14 +220,6 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
                                const double* R_own, double* W, double* Vj, int ldv, const double* part_in,
                                int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
                                int* state) {
-  if (A.nslices > 0) {
-    const VT* sval;
-    if constexpr (sizeof(VT) == 4) sval = A.sell_val32;
-    else sval = A.sell_val64;
-    return launch_pdl(sell_step_kernel<VT>, dim3(grid), dim3(256), 0, st, A.nslices, A.sell_row, A.sell_ptr,
-                      A.sell_col, sval, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, scal,
-                      state);
-  }
 #define LG_STEP(LN, CNT, LIST)                                                                              \
   do {                                                                                                      \
     cudaError_t e_ = launch_pdl(spmv_step_kernel<VT, LN>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr,  \
