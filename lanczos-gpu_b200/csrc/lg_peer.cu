@@ -89,6 +89,10 @@ __global__ void __launch_bounds__(kReduceThreads)
 peer_allreduce_kernel(const double* __restrict__ partA, const double* __restrict__ partB, int nrows, int ntables,
                       double* out, PeerPtrs P, int nranks, int rank, unsigned long long seq, long long wait_cycles,
                       int* state) {
+  griddep_wait();   // the partial rows come from the kernel just before
+  // the next kernel (the correction) may start prefetching its basis rows
+  // while this one waits for the other ranks; it waits for this kernel's sums
+  griddep_launch_dependents();
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   constexpr int NW = kReduceThreads / 32;          // 32 warps
   constexpr int CPL = (kPartStride + 31) / 32;     // columns per lane (5)
@@ -163,6 +167,7 @@ peer_exchange_kernel(const double* __restrict__ Rfull, const int* __restrict__ s
                      const long long* __restrict__ send_off, long long total, int row0, int n_local, PeerPtrs P,
                      int nranks, int rank, unsigned long long seq, long long wait_cycles, unsigned* counter,
                      int* state) {
+  griddep_wait();   // the residual rows come from the kernel just before
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   __shared__ int sh_last, sh_fail;
   const int t = threadIdx.x;
@@ -380,9 +385,8 @@ int Solver::peer_reduce(const double* partA, const double* partB, int nrows, int
   double* out = red + (size_t)slot * kPartStride;
   ++peer_seq;
   ++launches;
-  peer_allreduce_kernel<<<1, kReduceThreads, 0, stream>>>(partA, partB, nrows, ntables, out, peer_ptrs, nranks, rank,
-                                                          peer_seq, peer_wait_cycles, state);
-  LG_PTRY(cudaGetLastError());
+  LG_PTRY(launch_pdl(peer_allreduce_kernel, dim3(1), dim3(kReduceThreads), 0, stream, partA, partB, nrows, ntables, out,
+                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, state));
   return LG_OK;
 }
 
@@ -393,10 +397,9 @@ int Solver::peer_exchange() {
   const long long work = halo ? halo_send : (long long)(nranks - 1) * ((n + 1) / 2);
   const int grid = (int)std::max<long long>(1, std::min<long long>((long long)num_sm * 4,
                                                                     (work + kExchangeThreads - 1) / kExchangeThreads));
-  peer_exchange_kernel<<<grid, kExchangeThreads, 0, stream>>>(Rfull, d_send_idx, halo ? d_peer_send_off : nullptr,
-                                                              halo_send, row0, n, peer_ptrs, nranks, rank, peer_seq,
-                                                              peer_wait_cycles, peer_counter, state);
-  LG_PTRY(cudaGetLastError());
+  LG_PTRY(launch_pdl(peer_exchange_kernel, dim3(grid), dim3(kExchangeThreads), 0, stream, (const double*)Rfull,
+                     (const int*)d_send_idx, (const long long*)(halo ? d_peer_send_off : nullptr), halo_send, row0, n,
+                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, peer_counter, state));
   return LG_OK;
 }
 
