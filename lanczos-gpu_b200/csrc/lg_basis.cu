@@ -27,6 +27,7 @@ namespace {
 constexpr int kBsThreads = 256;
 constexpr int kTR = 64;                      // basis rows per tile (8 warps x 8 rows)
 constexpr int kMaxOB = kMaxCols / 8;         // output blocks of 8 columns
+constexpr size_t kBsSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 
 __host__ __device__ inline int pad_stride(int x) {   // x multiple of 4 -> stride = 4 or 12 (mod 16)
   return (x % 16 == 0 || x % 16 == 8) ? x + 4 : x;
@@ -40,7 +41,7 @@ struct BsGeom {
     sv = pad_stride(mp > kqp ? mp : kqp);
     sq = pad_stride(mp);
   }
-  __host__ __device__ size_t smem_doubles() const { return (size_t)kqp * sq + (size_t)kTR * sv; }
+  __host__ __device__ size_t smem_doubles(int nbuf) const { return (size_t)kqp * sq + (size_t)nbuf * kTR * sv; }
 };
 
 __device__ __forceinline__ void dmma(double& c0, double& c1, double a, double b) {
@@ -48,6 +49,15 @@ __device__ __forceinline__ void dmma(double& c0, double& c1, double a, double b)
                : "+d"(c0), "+d"(c1)
                : "d"(a), "d"(b));
 }
+
+// 16-byte asynchronous copy global -> shared; `bytes` < 16 zero-fills the rest
+__device__ __forceinline__ void bs_cp16(void* smem, const void* gmem, int bytes) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bs_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bs_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 }  // namespace
 
 BasisPlan basis_plan(int n, int m, int kq, int grid) {
@@ -55,10 +65,17 @@ BasisPlan basis_plan(int n, int m, int kq, int grid) {
   p.TR = kTR;
   const int ntiles = (n + kTR - 1) / kTR;
   p.grid = grid < ntiles ? grid : ntiles;
-  p.smem = BsGeom(m, kq).smem_doubles() * sizeof(double);
+  const BsGeom g(m, kq);
+  p.nbuf = g.smem_doubles(2) * sizeof(double) <= kBsSmemLimit ? 2 : 1;
+  p.smem = g.smem_doubles(p.nbuf) * sizeof(double);
   return p;
 }
 
+// One tile of kTR basis rows: out = V[rows, 0:m] Q[0:m, 0:kq] on the FP64
+// tensor cores.  The tile's rows of V arrive in shared memory by asynchronous
+// 16-byte copies, two columns at a time (in the solver's panel layout the 64
+// rows of a panel are 4 KB of contiguous memory); with two buffers the copies
+// of the next tile are in flight while this one is contracted and written.
 template <int NOB>
 __global__ void __launch_bounds__(kBsThreads)
 basis_kernel(BasisArgs a) {
@@ -70,7 +87,7 @@ basis_kernel(BasisArgs a) {
   const VLayout vl = a.vl;
   const BsGeom g(m, kq);
   double* Qs = sm;                              // kqp columns x sq (column-major, zero padded)
-  double* Vs = sm + (size_t)g.kqp * g.sq;       // kTR rows x sv (row-major, zero padded)
+  double* Vbuf[2] = {sm + (size_t)g.kqp * g.sq, sm + (size_t)g.kqp * g.sq + (size_t)(a.nbuf - 1) * kTR * g.sv};
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int gid = lane >> 2, tig = lane & 3;
 
@@ -86,20 +103,37 @@ basis_kernel(BasisArgs a) {
   double nrm = 0.0;
   const int ntiles = (n + kTR - 1) / kTR;
   const int nob = g.kqp / 8;
+  const int npanels = (g.mp + 7) / 8;
 
+  // copies of one tile: index i -> (panel, row, pair of columns), consecutive
+  // threads on consecutive pairs of a panel row, then the next rows
+  auto issue = [&](int tile, double* buf) {
+    const long long row0 = (long long)tile * kTR;
+    for (int i = t; i < kTR * npanels * 4; i += kBsThreads) {
+      const int c = (i / (kTR * 4)) * 8 + 2 * (i & 3);
+      const int rr = (i >> 2) % kTR;
+      if (c >= g.mp) continue;
+      const long long row = row0 + rr;
+      const int bytes = (row < n && c < m) ? (c + 1 < m ? 16 : 8) : 0;
+      bs_cp16(buf + rr * g.sv + c, bytes ? a.V + vidx(vl, row, c) : a.V, bytes);
+    }
+  };
+
+  int cur = 0;
+  if ((int)blockIdx.x < ntiles) issue(blockIdx.x, Vbuf[0]);
+  bs_commit();
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const long long row0 = (long long)tile * kTR;
-    __syncthreads();   // previous tile consumed; Qs ready on the first pass
-    // eight columns of a row at a time (one panel row of the solver's basis:
-    // 64 contiguous bytes; consecutive threads take consecutive rows)
-    for (int i = t; i < kTR * (g.mp >> 2); i += kBsThreads) {
-      const int rr = i % kTR, c = (i / kTR) * 4;
-      const long long row = row0 + rr;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        Vs[rr * g.sv + c + q] = (row < n && c + q < m) ? a.V[vidx(vl, row, c + q)] : 0.0;
+    const int next = tile + gridDim.x;
+    if (a.nbuf == 2) {
+      if (next < ntiles) issue(next, Vbuf[cur ^ 1]);
+      bs_commit();
+      bs_wait<1>();    // this thread's copies of the current tile have landed
+    } else {
+      bs_wait<0>();
     }
-    __syncthreads();
+    __syncthreads();   // every thread's copies (and Qs on the first pass)
+    double* Vs = Vbuf[cur];
     double acc[NOB][2];
 #pragma unroll
     for (int ob = 0; ob < NOB; ++ob) acc[ob][0] = acc[ob][1] = 0.0;
@@ -121,11 +155,13 @@ basis_kernel(BasisArgs a) {
       }
     __syncthreads();
     if (a.restart) {
-      const int kv = kq - 1;   // columns written back into V
-      for (int i = t; i < kTR * kv; i += kBsThreads) {
-        const int rr = i / kv, k = i % kv;
+      const int kv = kq - 1;   // columns written back into V, panel by panel (64 contiguous bytes per row)
+      const int kpan = (kv + 7) / 8;
+      for (int i = t; i < kTR * kpan * 8; i += kBsThreads) {
+        const int c = (i / (kTR * 8)) * 8 + (i & 7);
+        const int rr = (i >> 3) % kTR;
         const long long row = row0 + rr;
-        if (row < n) a.V[vidx(vl, row, k)] = Vs[rr * g.sv + k];
+        if (row < n && c < kv) a.V[vidx(vl, row, c)] = Vs[rr * g.sv + c];
       }
       if (t < kTR) {
         const long long row = row0 + t;
@@ -148,14 +184,23 @@ basis_kernel(BasisArgs a) {
         if (row < n) a.Y[(a.ymap ? (long long)a.ymap[row] : row) + (long long)k * a.ldy] = Vs[rr * g.sv + k];
       }
     }
+    __syncthreads();   // the outputs are read out of Vs before Vs receives copies again
+    if (a.nbuf == 1 && next < ntiles) {
+      issue(next, Vbuf[0]);
+      bs_commit();
+    }
+    cur ^= (a.nbuf - 1);
   }
+  bs_wait<0>();
   if (a.restart) {
     const double tot = block_sum(nrm, scr);
     if (t == 0) a.part_out[(size_t)blockIdx.x * kPartStride + kPartScalar] = tot;
   }
 }
 
-cudaError_t basis_update(const BasisPlan& p, const BasisArgs& a, cudaStream_t st) {
+cudaError_t basis_update(const BasisPlan& p, const BasisArgs& a_in, cudaStream_t st) {
+  BasisArgs a = a_in;
+  a.nbuf = p.nbuf;
   const int nob = ((a.kq + 7) & ~7) / 8;
 #define LG_BS(N)                                                                                     \
   do {                                                                                               \

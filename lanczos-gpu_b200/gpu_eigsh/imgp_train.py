@@ -48,9 +48,11 @@ class TrainResult:
     diverged_at_iter: Optional[int] = None
 
     def summary_line(self) -> str:
-        tag = " [DIVERGED]" if self.diverged else ""
-        return (f"{self.method:>16s}: loss={self.final_loss:>8.3f} theta={self.final_lengthscale:>6.3f} "
-                f"kappa={self.final_graphbandwidth:>6.3f}{tag}")
+        """One line: method, final loss and parameters, and whether training
+        stopped early."""
+        state = f"stopped at step {self.diverged_at_iter}" if self.diverged else "completed"
+        return (f"{self.method}: final loss {self.final_loss:.4f}, lengthscale {self.final_lengthscale:.4f}, "
+                f"graphbandwidth {self.final_graphbandwidth:.4f} ({state}, {len(self.iter_losses)} steps)")
 
 
 def _inv_quad(matvec, y, lengthscale, graphbandwidth):
@@ -110,19 +112,19 @@ def _train(method: str, logdet_fn: Callable, matvec, y: torch.Tensor, lengthscal
         except RuntimeError as e:
             res.diverged, res.diverged_at_iter = True, it
             if verbose:
-                print(f"  [{method}] iter {it} forward exception: {e}")
+                print(f"  {method}: step {it}: the loss could not be evaluated ({e}); stopping")
             break
         lv = float(loss.detach())
         if not math.isfinite(lv) or abs(lv) > divergence_loss_threshold:
             res.diverged, res.diverged_at_iter = True, it
             if verbose:
-                print(f"  [{method}] iter {it} loss not finite or above threshold ({lv})")
+                print(f"  {method}: step {it}: loss {lv} is non-finite or beyond the divergence bound; stopping")
             break
         loss.backward()
         if not all(bool(torch.isfinite(p.grad).all()) for p in (theta, kappa) if p.grad is not None):
             res.diverged, res.diverged_at_iter = True, it
             if verbose:
-                print(f"  [{method}] iter {it} NaN/Inf in gradient")
+                print(f"  {method}: step {it}: a gradient is non-finite; stopping")
             break
         opt.step()
         with torch.no_grad():

@@ -1,9 +1,9 @@
 """Generate golden vectors for the SLQ / Kraemer / IMGP path from the reference's
 own torch code.
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
-REFERENCE_ROOT defaults to /root/reference.  The reference modules
+REFERENCE_ROOT is the root of a checkout of the reference.  The reference modules
 python/gpu_eigsh/funm_torch.py and imgp.py are loaded by file path (the
 package __init__ would import the CUDA extension, which is not built here).
 Outputs small .npz files next to this script; they are committed, and the
@@ -169,4 +169,6 @@ def main(root: Path):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_ROOT")
+    main(Path(sys.argv[1]))

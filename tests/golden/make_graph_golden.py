@@ -1,8 +1,8 @@
 """Generate golden kNN Laplacians with the reference's own generator script.
 
-    python tests/golden/make_graph_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_graph_golden.py REFERENCE_ROOT
 
-REFERENCE_ROOT defaults to /root/reference.  Runs
+REFERENCE_ROOT is the root of a checkout of the reference.  Runs
 benchmark/generate_large_laplacian.py unmodified (its own argument parser,
 cKDTree, scipy assembly and mmwrite) into a temporary directory for a few
 small configurations, reads each laplacian.mtx back with scipy.io.mmread and
@@ -28,7 +28,7 @@ HERE = Path(__file__).resolve().parent
 CASES = [(250, 10, 15, 0.3, 123), (400, 2, 10, 0.05, 7), (300, 3, 8, 0.1, 11)]
 
 
-def main(root: str = "/root/reference") -> None:
+def main(root: str) -> None:
     script = Path(root) / "benchmark" / "generate_large_laplacian.py"
     out = {}
     for c, (n, dim, k, bw, seed) in enumerate(CASES):
@@ -47,4 +47,6 @@ def main(root: str = "/root/reference") -> None:
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_graph_golden.py REFERENCE_ROOT")
+    main(sys.argv[1])
