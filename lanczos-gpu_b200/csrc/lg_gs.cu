@@ -29,6 +29,10 @@
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
 
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
+
 namespace lg {
 
 constexpr int kGsWarps = kGsThreads / 32;
@@ -379,13 +383,14 @@ gs_async_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const
 // live columns, 8, 4, 2 rows per iteration.  A per-warp cp.async ring stages
 // the V chunks and the rows' entries of u and z.
 constexpr int kLagWarps = 16;
+constexpr int kLagCluster = 4;   // CTAs of the projection that add their partial rows into one
 constexpr int kLagThreads = kLagWarps * 32;
 constexpr int kLagCH = 4;
 constexpr int kLagStageDoubles = 32 * kLagCH * 2 + 16;   // V chunks, 8 entries of u, 8 of z
 
 size_t gs_lag_smem() { return sizeof(double) * (size_t)kLagWarps * kGsStages * kLagStageDoubles; }
 
-template <int LPR>
+template <int LPR, int CL>
 __global__ void __launch_bounds__(kLagThreads, 1)
 gs_lag_project_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const double* __restrict__ U,
                       const double* __restrict__ Z, double* __restrict__ partS, double* __restrict__ partT,
@@ -469,7 +474,8 @@ gs_lag_project_kernel(const double* __restrict__ V, VLayout L, int ncols, int n,
   }
   cp_async_wait<0>();
 
-  // column sums: s through wsum first, then t
+  // column sums into this CTA's rows: s through wsum first, then t
+  __shared__ double rowS[kPartStride], rowT[kPartStride];
   for (int pass = 0; pass < 2; ++pass) {
     double2* acc = pass == 0 ? as : at;
 #pragma unroll
@@ -486,11 +492,11 @@ gs_lag_project_kernel(const double* __restrict__ V, VLayout L, int ncols, int n,
       }
     }
     __syncthreads();
-    double* prow = (pass == 0 ? partS : partT) + (size_t)blockIdx.x * kPartStride;
+    double* row = pass == 0 ? rowS : rowT;
     if (t < ncols) {
       double sum = 0.0;
       for (int w = 0; w < kLagWarps; ++w) sum += wsum[w][t];
-      prow[t] = sum;
+      row[t] = sum;
     }
     __syncthreads();
   }
@@ -498,9 +504,39 @@ gs_lag_project_kernel(const double* __restrict__ V, VLayout L, int ncols, int n,
   const double tuu = block_sum(uu, scr);
   const double tzz = block_sum(zz, scr);
   if (t == 0) {
-    partS[(size_t)blockIdx.x * kPartStride + ncols] = tuu;
-    partS[(size_t)blockIdx.x * kPartStride + kPartScalar] = tuz;
-    partT[(size_t)blockIdx.x * kPartStride + kPartScalar] = tzz;
+    rowS[ncols] = tuu;
+    rowS[kPartScalar] = tuz;
+    rowT[kPartScalar] = tzz;
+  }
+  if (CL == 1) {
+    __syncthreads();
+    double* ps = partS + (size_t)blockIdx.x * kPartStride;
+    double* pt = partT + (size_t)blockIdx.x * kPartStride;
+    if (t <= ncols) ps[t] = rowS[t];
+    if (t < ncols) pt[t] = rowT[t];
+    if (t == 0) {
+      ps[kPartScalar] = tuz;
+      pt[kPartScalar] = tzz;
+    }
+  } else {
+    // the CL CTAs of a cluster add their rows (ranks in order, through
+    // distributed shared memory) into one row: the correction reduces CL
+    // times fewer rows in its prologue
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+      const int slot = t < kPartStride ? t : t - kPartStride;   // threads [0, 136): S, [136, 272): T
+      const bool isT = t >= kPartStride;
+      const bool used = t < 2 * kPartStride &&
+                        (isT ? (slot < ncols || slot == kPartScalar) : (slot <= ncols || slot == kPartScalar));
+      if (used) {
+        double sum = 0.0;
+#pragma unroll
+        for (int q = 0; q < CL; ++q) sum += cluster.map_shared_rank(isT ? rowT : rowS, q)[slot];
+        (isT ? partT : partS)[(size_t)(blockIdx.x / CL) * kPartStride + slot] = sum;
+      }
+    }
+    cluster.sync();   // the other CTAs' rows stay alive until they are read
   }
 }
 
@@ -782,14 +818,63 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, VLayou
 }
 
 
+static cudaError_t smem_attr_once_cluster_probe() {
+  static std::atomic<unsigned long long> attr{0};
+  return smem_attr_once(attr, (const void*)gs_lag_project_kernel<8, kLagCluster>, (int)gs_lag_smem());
+}
+
+// Clusters of kLagCluster CTAs only when every cluster of the grid can be
+// resident at once (GPCs whose SM count is not a multiple of the cluster size
+// leave SMs out; a second wave would cost more than the prologue saves).
+// Decided once per device from the occupancy query.
+static bool lag_cluster_fits(int grid) {
+  static std::atomic<int> verdict[64];   // 0 unknown, 1 no, 2 yes (per device)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  int v = verdict[dev].load();
+  if (v == 0) {
+    cudaError_t e = smem_attr_once_cluster_probe();
+    int active = 0;
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(grid);
+      cfg.blockDim = dim3(kLagThreads);
+      cfg.dynamicSmemBytes = gs_lag_smem();
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kLagCluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&active, (const void*)gs_lag_project_kernel<8, kLagCluster>, &cfg);
+    }
+    if (e != cudaSuccess) cudaGetLastError();
+    v = (e == cudaSuccess && (long long)active * kLagCluster >= grid) ? 2 : 1;
+    verdict[dev].store(v);
+  }
+  return v == 2;
+}
+
 template <int LP>
 static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                   const double* U, const double* Z, double* partS, double* partT, int* state) {
+  if (gs_lag_rows(p) != p.grid) {
+    static std::atomic<unsigned long long> attr{0};
+    cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP, kLagCluster>, (int)gs_lag_smem());
+    if (e != cudaSuccess) return e;
+    return launch_pdl_cluster(gs_lag_project_kernel<LP, kLagCluster>, dim3(p.grid), dim3(kLagThreads), kLagCluster,
+                              gs_lag_smem(), st, V, L, ncols, n, U, Z, partS, partT, state);
+  }
   static std::atomic<unsigned long long> attr{0};
-  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP>, (int)gs_lag_smem());
+  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP, 1>, (int)gs_lag_smem());
   if (e != cudaSuccess) return e;
-  return launch_pdl(gs_lag_project_kernel<LP>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols, n, U,
-                    Z, partS, partT, state);
+  return launch_pdl(gs_lag_project_kernel<LP, 1>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols, n,
+                    U, Z, partS, partT, state);
+}
+
+int gs_lag_rows(const GsPlan& p) {
+  return (p.grid % kLagCluster == 0 && lag_cluster_fits(p.grid)) ? p.grid / kLagCluster : p.grid;
 }
 
 template <int LP>

@@ -898,7 +898,7 @@ int Solver::lag_step(int j) {
                [&] { return gs_lag_project(p, stream, V, vl, j, n, R, W, partA, partB, state); }));
   const double *inS = nullptr, *inT = nullptr;
   int nS = 0;
-  rc = reduce_partials_all2(partA, partB, p.grid, 0, &inS, &inT, &nS);
+  rc = reduce_partials_all2(partA, partB, gs_lag_rows(p), 0, &inS, &inT, &nS);
   if (rc != LG_OK) return rc;
   LG_TRY(timed(LG_K_CORRPROJ, vbytes + 32.0 * n, 1, [&] {
     return gs_lag_correct(p, stream, V, vl, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);

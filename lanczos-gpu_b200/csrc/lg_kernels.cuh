@@ -52,6 +52,9 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, VLayou
 //                   (first pass); part_out: ||R||^2.
 cudaError_t gs_lag_project(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                            const double* U, const double* Z, double* partS, double* partT, int* state);
+// Partial-sum rows gs_lag_project writes per table (the CTAs of a cluster
+// combine theirs into one row when the grid allows it).
+int gs_lag_rows(const GsPlan& p);
 cudaError_t gs_lag_correct(const GsPlan& p, cudaStream_t st, double* V, VLayout L, int ncols, int n, double* R,
                            const double* Z, const double* partS, const double* partT, int nrows_in,
                            double* part_out, double* scal, double* alpha, double* beta, int* state);
