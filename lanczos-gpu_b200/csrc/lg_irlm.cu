@@ -678,14 +678,14 @@ int Solver::build_long_rows(const int* hrp) {
   // (power-law graphs), each class gets its own launch over its row list.
   {
     static const int kLanes[5] = {2, 4, 8, 16, 32};
-    std::vector<int> cls(n);
+    // class of a row: the index of pick_lanes(len) in kLanes (len < 3, < 8,
+    // < 16, < 32, else), one byte per row
+    std::vector<unsigned char> cls((size_t)n);
     int hist[5] = {0, 0, 0, 0, 0};
     for (int i = 0; i < n; ++i) {
-      const int len = std::min(hrp[i + 1] - hrp[i], kLongRow);
-      const int l = pick_lanes((double)len);
-      int c = 0;
-      while (kLanes[c] != l) ++c;
-      cls[i] = c;
+      const int len = hrp[i + 1] - hrp[i];
+      const int c = len < 3 ? 0 : len < 8 ? 1 : len < 16 ? 2 : len < 32 ? 3 : 4;
+      cls[(size_t)i] = (unsigned char)c;
       ++hist[c];
     }
     const int top = *std::max_element(hist, hist + 5);
