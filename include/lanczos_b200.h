@@ -92,7 +92,10 @@ int lg_eigsh_opts_default(lg_eigsh_opts* o);
 
 /* Own a device copy of the CSR matrix (int32 indices, fp64 values, n x n,
  * symmetric) plus the solver workspace for up to `max_ncv` basis vectors.
- * device_ptrs = 1: the three arrays are device pointers (copied on device).
+ * device_ptrs = 1: the three arrays are device pointers (copied on device, on
+ * the plan's own non-blocking stream: the caller makes sure the work that
+ * writes them has finished; the same holds for device v0 / evecs buffers
+ * passed to lg_eigsh_plan_run).
  * mixed = 1 also keeps an fp32 copy of the values (made on the device). */
 int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr,
                          const int* col_idx, const double* vals, int device_ptrs, int max_ncv,

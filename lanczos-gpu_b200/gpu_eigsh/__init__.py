@@ -121,6 +121,18 @@ def _as_csr(A):
     return M.shape[0], indptr, indices, data
 
 
+def _sync_caller_stream():
+    """Device pointers handed to the library are read on the library's own
+    non-blocking stream, which does not wait for the caller's: finish the
+    work queued on torch's current stream first (a no-op without torch or
+    without CUDA)."""
+    import sys
+
+    torch = sys.modules.get("torch")
+    if torch is not None and torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.current_stream().synchronize()
+
+
 def _default_ncv(n: int, k: int) -> int:
     # scipy.sparse.linalg._eigen.arpack.choose_ncv: max(2k+1, 20), capped at n
     return min(n, max(2 * k + 1, 20))
@@ -162,6 +174,10 @@ class EigshPlan:
         if cgs2_inline and comm is not None:
             raise ValueError("cgs2_inline is a single-GPU plan option")
         h = _native.C.c_void_p()
+        if device_csr is not None:
+            # the library copies the arrays on its own stream: work still queued
+            # on the caller's stream (the kernels that produced them) must be done
+            _sync_caller_stream()
         if comm is not None:
             # row-partitioned: device_csr holds this rank's rows (global column indices)
             n, nnz, rp, ci, vals = device_csr
@@ -221,6 +237,7 @@ class EigshPlan:
 
     def matvec_device(self, x_ptr: int, y_ptr: int):
         """y = A x on device buffers (raw CUDA pointers, n doubles each)."""
+        _sync_caller_stream()
         _native.check(_native.lib.lg_eigsh_plan_matvec(self._plan, int(x_ptr), int(y_ptr)))
         if self._cb is not None:
             self._cb.raise_pending()
@@ -286,6 +303,8 @@ class EigshPlan:
                 evecs = np.zeros(shape, dtype=np.float64)
                 evp = _native.ptr(evecs)
         info = _native.EigshInfo()
+        if io_dev:
+            _sync_caller_stream()   # v0 / the output buffer may come from the caller's queued work
         rc = _native.lib.lg_eigsh_plan_run(self._plan, _native.C.byref(o), v0p or None,
                                            evals.ctypes.data_as(_native.C.POINTER(_native.C.c_double)),
                                            evp or None, io_dev, _native.C.byref(info))
