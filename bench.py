@@ -67,6 +67,7 @@ import numpy as np  # noqa: E402
 
 N_POINTS = 1_000_000
 K_EIG, NCV, TOL = 20, 60, 1e-10
+MAXITER = 300   # implicit restarts allowed per solve (configuration 1 needs 7, R-MAT 11): a bound, not a target
 WORKLOAD = (f"eigsh k={K_EIG} which=LA ncv={NCV} tol={TOL:g} on the n=1e6 kNN graph Laplacian "
             "(2-D uniform points seed 1, k=10, union-symmetrised, exp(-d^2/2h^2)), fp64 CSR")
 
@@ -420,7 +421,7 @@ def run_rmat(args, dev, world=1, rank=0):
     Y = torch.empty((r1 - r0, RMAT_K), dtype=torch.float64, device=dev)
 
     def solve(profile=False):
-        w, _ = plan.solve(k=RMAT_K, which="LA", ncv=RMAT_NCV, tol=RMAT_TOL, v0_device=v0.data_ptr(),
+        w, _ = plan.solve(k=RMAT_K, which="LA", ncv=RMAT_NCV, tol=RMAT_TOL, maxiter=MAXITER, v0_device=v0.data_ptr(),
                           evecs_out=Y.data_ptr(), profile=profile)
         return w, dict(plan.last_info)
 
@@ -644,7 +645,7 @@ class HeadlineSolver:
         self.plan_s = time.perf_counter() - t0
 
     def solve(self, profile=False):
-        w, _ = self.plan.solve(k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0_device=self.v0.data_ptr(),
+        w, _ = self.plan.solve(k=K_EIG, which="LA", ncv=NCV, tol=TOL, maxiter=MAXITER, v0_device=self.v0.data_ptr(),
                                evecs_out=self.Y.data_ptr(), profile=profile)
         return w, dict(self.plan.last_info)
 
@@ -703,7 +704,7 @@ def e2e_partitioned(args, L, v0, dev, world, rank):
         d_rp, d_ci = h_rp.to(dev, non_blocking=True), h_ci.to(dev, non_blocking=True)
         d_va, d_v0 = h_va.to(dev, non_blocking=True), h_v0.to(dev, non_blocking=True)
         pe = PartitionedEigsh(comm, n, d_rp, d_ci, d_va, max_ncv=NCV)
-        w, Y = pe.solve(K_EIG, d_v0, which="LA", ncv=NCV, tol=TOL)
+        w, Y = pe.solve(K_EIG, d_v0, which="LA", ncv=NCV, tol=TOL, maxiter=MAXITER)
         Yh = Y.cpu()
         steps = pe.last_info["steps"]
         pe.close()
@@ -997,13 +998,13 @@ def run_ours(args):
         if world == 1:
             # end to end through the public API with host buffers: CSR upload,
             # allocation, solve, eigenvectors back to the host
-            gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0)  # warm
+            gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, maxiter=MAXITER, v0=v0)  # warm
             e_steps, t0 = 0, time.perf_counter()
             reps = max(1, min(args.steps, 2))
             phases = []
             for _ in range(reps):
-                (we, Ve), inf = gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, v0=v0,
-                                                   return_info=True)
+                (we, Ve), inf = gpu_eigsh.gpu_eigsh(L, k=K_EIG, which="LA", ncv=NCV, tol=TOL, maxiter=MAXITER,
+                                                   v0=v0, return_info=True)
                 e_steps += inf["steps"]
                 phases.append(inf["host_ms"])
             el = time.perf_counter() - t0
