@@ -446,11 +446,6 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
   {
     int rc = build_long_rows(hrp.data());
     if (rc != LG_OK) return rc;
-    // the gathered vector (all ranks' rows) against L2: above a quarter of
-    // it, the CSR stream is read evict-first so the gathers keep hitting L2
-    int l2 = 0;
-    LG_TRY(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device));
-    A.stream_csr = 8.0 * (double)n_global > 0.25 * (double)l2;
   }
   if (comm) {
     int rc = setup_halo();

@@ -92,9 +92,6 @@ struct CsrDev {
   int class_lanes[5] = {0, 0, 0, 0, 0};
   int class_count[5] = {0, 0, 0, 0, 0};
   const int* class_rows[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-  // Streaming (evict-first) loads of columns and values in the step product:
-  // set when the gathered vector takes a large share of L2.
-  bool stream_csr = false;
 };
 
 // Vj points at column j of the basis, its rows ldv doubles apart (the layout's rs).

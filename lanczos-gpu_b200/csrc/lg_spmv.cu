@@ -68,18 +68,8 @@ __device__ int step_prologue(const double* __restrict__ part_in, int nrows_in, i
   return sh_stop;
 }
 
-// Column and value loads: read-only path, or (STREAM) streaming loads that
-// L2 evicts first, for matrices whose gathered vector is a large share of L2
-// (power-law graphs: the gathers then keep finding x in L2 instead of the
-// CSR stream pushing it out).
-template <bool STREAM, typename T>
-__device__ __forceinline__ T ld_csr(const T* p) {
-  if constexpr (STREAM) return __ldcs(p);
-  else return __ldg(p);
-}
-
 // `list` (optional, `count` entries): the rows to process, else rows 0..count-1.
-template <typename VT, int L, bool STREAM>
+template <typename VT, int L>
 __global__ void __launch_bounds__(256)
 spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict__ rowptr,
                  const int* __restrict__ col, const VT* __restrict__ val, const double* __restrict__ R,
@@ -114,8 +104,8 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
   for (; (long long)w * rows_per_warp * 2 < count; w += warps_total) {
     double accA = 0.0, accB = 0.0;
     while (kA < eA || kB < eB) {
-      if (kA < eA) accA += (double)ld_csr<STREAM>(val + kA) * __ldg(R + ld_csr<STREAM>(col + kA));
-      if (kB < eB) accB += (double)ld_csr<STREAM>(val + kB) * __ldg(R + ld_csr<STREAM>(col + kB));
+      if (kA < eA) accA += (double)__ldg(val + kA) * __ldg(R + __ldg(col + kA));
+      if (kB < eB) accB += (double)__ldg(val + kB) * __ldg(R + __ldg(col + kB));
       kA += L;
       kB += L;
     }
@@ -182,7 +172,7 @@ spmv_plain_kernel(int n, const int* __restrict__ rowptr, const int* __restrict__
 }
 
 // Remainders of the long rows: one warp per chunk of kLongRow nonzeros.
-template <typename VT, bool STREAM>
+template <typename VT>
 __global__ void __launch_bounds__(256)
 long_chunk_kernel(int nchunks, const int* __restrict__ cb, const int* __restrict__ ce, const int* __restrict__ col,
                   const VT* __restrict__ val, const double* __restrict__ x, double* __restrict__ csum,
@@ -191,8 +181,7 @@ long_chunk_kernel(int nchunks, const int* __restrict__ cb, const int* __restrict
   const int lane = threadIdx.x & 31;
   for (int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks; c += (gridDim.x * blockDim.x) >> 5) {
     double acc = 0.0;
-    for (int k = cb[c] + lane; k < ce[c]; k += 32)
-      acc += (double)ld_csr<STREAM>(val + k) * __ldg(x + ld_csr<STREAM>(col + k));
+    for (int k = cb[c] + lane; k < ce[c]; k += 32) acc += (double)__ldg(val + k) * __ldg(x + __ldg(col + k));
     acc = warp_sum(acc);
     if (lane == 0) csum[c] = acc;
   }
@@ -219,12 +208,8 @@ static cudaError_t long_rows_finish(const CsrDev& A, const VT* val, cudaStream_t
   if (A.nlong == 0) return cudaSuccess;
   int grid = (A.nchunks * 32 + 255) / 256;
   if (grid > 4096) grid = 4096;
-  if (A.stream_csr)
-    long_chunk_kernel<VT, true><<<grid, 256, 0, st>>>(A.nchunks, A.chunk_begin, A.chunk_end, A.col, val, x,
-                                                      A.chunk_sum, state);
-  else
-    long_chunk_kernel<VT, false><<<grid, 256, 0, st>>>(A.nchunks, A.chunk_begin, A.chunk_end, A.col, val, x,
-                                                       A.chunk_sum, state);
+  long_chunk_kernel<VT><<<grid, 256, 0, st>>>(A.nchunks, A.chunk_begin, A.chunk_end, A.col, val, x, A.chunk_sum,
+                                              state);
   long_combine_kernel<<<(A.nlong + 255) / 256, 256, 0, st>>>(A.nlong, A.long_rows, A.long_first, A.chunk_sum, y,
                                                              scal, state);
   return cudaGetLastError();
@@ -237,11 +222,9 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
                                int* state) {
 #define LG_STEP(LN, CNT, LIST)                                                                              \
   do {                                                                                                      \
-    cudaError_t e_ = A.stream_csr                                                                          \
-        ? launch_pdl(spmv_step_kernel<VT, LN, true>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr, A.col, \
-                     val, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, scal, state)     \
-        : launch_pdl(spmv_step_kernel<VT, LN, false>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr, A.col,\
-                     val, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, scal, state);    \
+    cudaError_t e_ = launch_pdl(spmv_step_kernel<VT, LN>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr,  \
+                                A.col, val, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, \
+                                scal, state);                                                                \
     if (e_ != cudaSuccess) return e_;                                                                       \
   } while (0)
   const int ncls = A.nclasses > 0 ? A.nclasses : 1;
