@@ -383,7 +383,6 @@ gs_async_kernel(const double* __restrict__ V, VLayout L, int ncols, int n, const
 // live columns, 8, 4, 2 rows per iteration.  A per-warp cp.async ring stages
 // the V chunks and the rows' entries of u and z.
 constexpr int kLagWarps = 16;
-constexpr int kLagCluster = 4;   // CTAs of the projection that add their partial rows into one
 constexpr int kLagThreads = kLagWarps * 32;
 constexpr int kLagCH = 4;
 constexpr int kLagStageDoubles = 32 * kLagCH * 2 + 16;   // V chunks, 8 entries of u, 8 of z
@@ -818,64 +817,70 @@ cudaError_t gs_correct(const GsPlan& p, cudaStream_t st, const double* V, VLayou
 }
 
 
-static cudaError_t smem_attr_once_cluster_probe() {
+// Cluster size of the projection: the largest of 4 and 2 that divides the grid
+// and lets every cluster be resident at once (GPCs whose SM count is not a
+// multiple of the cluster size leave SMs out, and a second wave would cost
+// more than the shorter prologue saves), else 1.  Decided once per device
+// and grid from the occupancy query.
+template <int CL>
+static bool cluster_fits(int grid) {
   static std::atomic<unsigned long long> attr{0};
-  return smem_attr_once(attr, (const void*)gs_lag_project_kernel<8, kLagCluster>, (int)gs_lag_smem());
+  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<8, CL>, (int)gs_lag_smem());
+  int active = 0;
+  if (e == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLagThreads);
+    cfg.dynamicSmemBytes = gs_lag_smem();
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CL;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&active, (const void*)gs_lag_project_kernel<8, CL>, &cfg);
+  }
+  if (e != cudaSuccess) cudaGetLastError();
+  return e == cudaSuccess && (long long)active * CL >= grid;
 }
 
-// Clusters of kLagCluster CTAs only when every cluster of the grid can be
-// resident at once (GPCs whose SM count is not a multiple of the cluster size
-// leave SMs out; a second wave would cost more than the prologue saves).
-// Decided once per device from the occupancy query.
-static bool lag_cluster_fits(int grid) {
-  static std::atomic<int> verdict[64];   // 0 unknown, 1 no, 2 yes (per device)
+static int lag_cluster(int grid) {
+  static std::atomic<long long> cache[64];   // per device: (grid << 8) | cluster, 0 unknown
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  int v = verdict[dev].load();
-  if (v == 0) {
-    cudaError_t e = smem_attr_once_cluster_probe();
-    int active = 0;
-    if (e == cudaSuccess) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(grid);
-      cfg.blockDim = dim3(kLagThreads);
-      cfg.dynamicSmemBytes = gs_lag_smem();
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = kLagCluster;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      e = cudaOccupancyMaxActiveClusters(&active, (const void*)gs_lag_project_kernel<8, kLagCluster>, &cfg);
-    }
-    if (e != cudaSuccess) cudaGetLastError();
-    v = (e == cudaSuccess && (long long)active * kLagCluster >= grid) ? 2 : 1;
-    verdict[dev].store(v);
-  }
-  return v == 2;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  const long long c = cache[dev].load();
+  if (c != 0 && (c >> 8) == grid) return (int)(c & 0xff);
+  int cl = 1;
+  if (grid % 4 == 0 && cluster_fits<4>(grid)) cl = 4;
+  else if (grid % 2 == 0 && cluster_fits<2>(grid)) cl = 2;
+  cache[dev].store(((long long)grid << 8) | cl);
+  return cl;
+}
+
+template <int LP, int CL>
+static cudaError_t lag_project_cl(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
+                                  const double* U, const double* Z, double* partS, double* partT, int* state) {
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP, CL>, (int)gs_lag_smem());
+  if (e != cudaSuccess) return e;
+  if (CL == 1)
+    return launch_pdl(gs_lag_project_kernel<LP, CL>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols,
+                      n, U, Z, partS, partT, state);
+  return launch_pdl_cluster(gs_lag_project_kernel<LP, CL>, dim3(p.grid), dim3(kLagThreads), CL, gs_lag_smem(), st, V,
+                            L, ncols, n, U, Z, partS, partT, state);
 }
 
 template <int LP>
 static cudaError_t lag_project_lp(const GsPlan& p, cudaStream_t st, const double* V, VLayout L, int ncols, int n,
                                   const double* U, const double* Z, double* partS, double* partT, int* state) {
-  if (gs_lag_rows(p) != p.grid) {
-    static std::atomic<unsigned long long> attr{0};
-    cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP, kLagCluster>, (int)gs_lag_smem());
-    if (e != cudaSuccess) return e;
-    return launch_pdl_cluster(gs_lag_project_kernel<LP, kLagCluster>, dim3(p.grid), dim3(kLagThreads), kLagCluster,
-                              gs_lag_smem(), st, V, L, ncols, n, U, Z, partS, partT, state);
-  }
-  static std::atomic<unsigned long long> attr{0};
-  cudaError_t e = smem_attr_once(attr, (const void*)gs_lag_project_kernel<LP, 1>, (int)gs_lag_smem());
-  if (e != cudaSuccess) return e;
-  return launch_pdl(gs_lag_project_kernel<LP, 1>, dim3(p.grid), dim3(kLagThreads), gs_lag_smem(), st, V, L, ncols, n,
-                    U, Z, partS, partT, state);
+  const int cl = lag_cluster(p.grid);
+  if (cl == 4) return lag_project_cl<LP, 4>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
+  if (cl == 2) return lag_project_cl<LP, 2>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
+  return lag_project_cl<LP, 1>(p, st, V, L, ncols, n, U, Z, partS, partT, state);
 }
 
-int gs_lag_rows(const GsPlan& p) {
-  return (p.grid % kLagCluster == 0 && lag_cluster_fits(p.grid)) ? p.grid / kLagCluster : p.grid;
-}
+int gs_lag_rows(const GsPlan& p) { return p.grid / lag_cluster(p.grid); }
 
 template <int LP>
 static cudaError_t lag_correct_lp(const GsPlan& p, cudaStream_t st, double* V, VLayout L, int ncols, int n, double* R,

@@ -30,6 +30,20 @@ __device__ __forceinline__ void givens(double a, double b, double& c, double& s)
   s = -sg * b * rh;
 }
 
+// 1 / q for |q| >= DBL_MIN: the hardware's approximate reciprocal, refined by
+// two Newton-Raphson steps r <- r + r (1 - q r) (each roughly doubles the
+// correct bits), to within a couple of units in the last place.  The Sturm
+// counts below only need the signs of the pivots; an fp64 division is a long
+// instruction sequence, and these counts are the restart's inner loop.
+__device__ __forceinline__ double recip_nr(double q) {
+  double r;
+  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(q));
+  double e = fma(-q, r, 1.0);
+  r = fma(r, e, r);
+  e = fma(-q, r, 1.0);
+  return fma(r, e, r);
+}
+
 // Number of eigenvalues of T below x (Sturm sequence of the LDL^T pivots).
 __device__ inline int sturm_count(const double* d, const double* e2, int m, double x, double pivmin) {
   double q = d[0] - x;
@@ -43,7 +57,8 @@ __device__ inline int sturm_count(const double* d, const double* e2, int m, doub
 }
 
 // Sturm counts at P points at once: P independent LDL^T pivot chains
-// interleaved, so their divisions overlap.  Same recurrence as sturm_count.
+// interleaved, so their reciprocals overlap.  Same recurrence as sturm_count,
+// with e2 / q formed as e2 * recip_nr(q).
 constexpr int kSturmP = 4;
 template <int P>
 __device__ __forceinline__ void sturm_counts(const double* d, const double* e2, int m, const double* x,
@@ -59,7 +74,7 @@ __device__ __forceinline__ void sturm_counts(const double* d, const double* e2, 
 #pragma unroll
     for (int p = 0; p < P; ++p) {
       if (fabs(q[p]) < pivmin) q[p] = -pivmin;
-      q[p] = (dk - x[p]) - ek / q[p];
+      q[p] = (dk - x[p]) - ek * recip_nr(q[p]);
       cnt[p] += q[p] < 0.0;
     }
   }
