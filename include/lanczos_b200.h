@@ -120,6 +120,15 @@ int lg_eigsh_plan_create(lg_eigsh_plan** plan, int n, long long nnz, const int* 
  * in-step passes to rounding, and the DGKS and breakdown tests are the same.
  * Shift-invert solves always use the in-step passes. */
 #define LG_PLAN_CGS2_INLINE 2
+/* LG_PLAN_REORDER_DEGREE renumbers the rows by descending row length (ties by
+ * the caller's index) instead, for power-law graphs (R-MAT, web and social
+ * graphs) where Cuthill-McKee finds no bandwidth: the hub vertices, which
+ * most column indices name, get the first numbers, so the entries of the
+ * vector that the sparse product gathers most often share cache sectors and
+ * stay in L2, and the rows of one length class are consecutive.  Mapped for
+ * the caller exactly like LG_PLAN_REORDER_BFS; the two flags exclude each
+ * other.  Creation sorts on the host in O(n + max row length). */
+#define LG_PLAN_REORDER_DEGREE 4
 int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const int* row_ptr,
                             const int* col_idx, const double* vals, int device_ptrs, int max_ncv,
                             int mixed, int flags);

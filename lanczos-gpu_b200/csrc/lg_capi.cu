@@ -43,8 +43,12 @@ int lg_eigsh_plan_create_ex(lg_eigsh_plan** plan, int n, long long nnz, const in
                             const double* vals, int device_ptrs, int max_ncv, int mixed, int flags) {
   if (!plan) return LG_ERR_INVALID;
   *plan = nullptr;
-  if (flags & ~(LG_PLAN_REORDER_BFS | LG_PLAN_CGS2_INLINE)) {
+  if (flags & ~(LG_PLAN_REORDER_BFS | LG_PLAN_CGS2_INLINE | LG_PLAN_REORDER_DEGREE)) {
     lg::g_last_error = "unknown plan flags";
+    return LG_ERR_INVALID;
+  }
+  if ((flags & LG_PLAN_REORDER_BFS) && (flags & LG_PLAN_REORDER_DEGREE)) {
+    lg::g_last_error = "LG_PLAN_REORDER_BFS and LG_PLAN_REORDER_DEGREE exclude each other";
     return LG_ERR_INVALID;
   }
   lg_eigsh_plan* p = new (std::nothrow) lg_eigsh_plan();

@@ -294,4 +294,24 @@ inline cudaError_t smem_attr_once(std::atomic<unsigned long long>& done, const v
   return e;
 }
 
+// Resident CTAs of `threads` threads per SM for `kernel` on the current
+// device (no dynamic shared memory), queried once per device and cached in
+// `cache` (one entry per device ordinal; 0 = not yet known).  Falls back to
+// `fallback` when the query fails.
+struct OccupancyCache {
+  std::atomic<int> blocks[64] = {};
+};
+inline int resident_blocks_once(OccupancyCache& cache, const void* kernel, int threads, int fallback) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fallback;
+  int b = cache.blocks[dev].load(std::memory_order_acquire);
+  if (b > 0) return b;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, 0) != cudaSuccess || b < 1) {
+    (void)cudaGetLastError();
+    return fallback;
+  }
+  cache.blocks[dev].store(b, std::memory_order_release);
+  return b;
+}
+
 }  // namespace lg

@@ -433,8 +433,8 @@ int Solver::create_impl(int n_, int n_cols, long long nnz_, const int* rowptr, c
     std::copy(rowptr, rowptr + n + 1, hrp.begin());
   }
   lag_steps = !(flags & LG_PLAN_CGS2_INLINE);
-  if ((flags & LG_PLAN_REORDER_BFS) && !comm) {
-    int rc = reorder_bfs(hrp);
+  if ((flags & (LG_PLAN_REORDER_BFS | LG_PLAN_REORDER_DEGREE)) && !comm) {
+    int rc = reorder_rows(hrp, (flags & LG_PLAN_REORDER_DEGREE) != 0);
     if (rc != LG_OK) return rc;
   }
   if (mixed) {
@@ -489,23 +489,41 @@ __global__ void scatter_perm_kernel(double* __restrict__ out, const double* __re
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[perm[i]] = in[i];
 }
 
-// Renumbers the rows in Cuthill-McKee order (BFS levels from a
-// pseudo-peripheral vertex, each level in the order of the vertices that
-// found it; lg_graph_cm_order on the host) so that neighbouring rows get
-// nearby numbers and the gathers of the sparse product hit L1 / L2.  The plan keeps perm (plan row -> caller row): v0 is
-// gathered through it and the Ritz vectors are written through it, so the
-// caller sees its own numbering.  hrp (host row pointer) becomes the new one.
-int Solver::reorder_bfs(std::vector<int>& hrp) {
-  // Cuthill-McKee order on the host (lg_graph_cm_order) from the column
-  // indices already on the device
-  std::vector<int> hcol((size_t)std::max<long long>(nnz, 1));
-  if (nnz > 0) {
-    LG_TRY(cudaMemcpyAsync(hcol.data(), d_col, sizeof(int) * (size_t)nnz, cudaMemcpyDeviceToHost, stream));
-    LG_TRY(cudaStreamSynchronize(stream));
-  }
+// perm[new] = old: the rows by descending length, ties by index (a counting
+// sort, O(n + longest row)).
+static void degree_order(int n, const int* hrp, int* perm) {
+  int maxlen = 0;
+  for (int i = 0; i < n; ++i) maxlen = std::max(maxlen, hrp[i + 1] - hrp[i]);
+  std::vector<long long> start((size_t)maxlen + 2, 0);
+  for (int i = 0; i < n; ++i) ++start[(size_t)(maxlen - (hrp[i + 1] - hrp[i])) + 1];
+  for (size_t d = 1; d < start.size(); ++d) start[d] += start[d - 1];
+  for (int i = 0; i < n; ++i) perm[start[(size_t)(maxlen - (hrp[i + 1] - hrp[i]))]++] = i;
+}
+
+// Renumbers the rows for locality of the sparse product's gathers.  Without
+// by_degree: Cuthill-McKee order (BFS levels from a pseudo-peripheral vertex,
+// each level in the order of the vertices that found it; lg_graph_cm_order
+// on the host), so that neighbouring rows get nearby numbers and the gathers
+// hit L1 / L2.  With by_degree: descending row length, so that the hubs of a
+// power-law graph (the entries most gathers read) are packed together at the
+// front.  The plan keeps perm (plan row -> caller row): v0 is gathered
+// through it and the Ritz vectors are written through it, so the caller sees
+// its own numbering.  hrp (host row pointer) becomes the new one.
+int Solver::reorder_rows(std::vector<int>& hrp, bool by_degree) {
   std::vector<int> perm((size_t)n), pos((size_t)n), nrp((size_t)n + 1);
-  int rc = lg_graph_cm_order(n, hrp.data(), hcol.data(), perm.data());
-  if (rc != LG_OK) return rc;
+  if (by_degree) {
+    degree_order(n, hrp.data(), perm.data());
+  } else {
+    // Cuthill-McKee order on the host from the column indices already on
+    // the device
+    std::vector<int> hcol((size_t)std::max<long long>(nnz, 1));
+    if (nnz > 0) {
+      LG_TRY(cudaMemcpyAsync(hcol.data(), d_col, sizeof(int) * (size_t)nnz, cudaMemcpyDeviceToHost, stream));
+      LG_TRY(cudaStreamSynchronize(stream));
+    }
+    int rc = lg_graph_cm_order(n, hrp.data(), hcol.data(), perm.data());
+    if (rc != LG_OK) return rc;
+  }
   for (int i = 0; i < n; ++i) pos[(size_t)perm[i]] = i;
   nrp[0] = 0;
   for (int i = 0; i < n; ++i) nrp[(size_t)i + 1] = nrp[i] + (hrp[(size_t)perm[i] + 1] - hrp[perm[i]]);

@@ -62,7 +62,7 @@ class Solver {
   int alloc_workspace();
   int create_impl(int n_rows, int n_cols, long long nnz, const int* rowptr, const int* col, const double* vals,
                   int device_ptrs, int max_ncv, int mixed, int flags);
-  int reorder_bfs(std::vector<int>& host_rowptr);
+  int reorder_rows(std::vector<int>& host_rowptr, bool by_degree);
   // Partitioned runs: sum `nrows` partial-sum rows into row `slot` of `red`
   // and all-reduce it over the ranks; *in / *nin become that single row.
   // Single GPU: *in = part, *nin = nrows.

@@ -101,13 +101,31 @@ spmv_step_kernel(int count, const int* __restrict__ list, const int* __restrict_
   int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int rowA, rowB, kA, eA, kB, eB;
   if ((long long)w * rows_per_warp * 2 < count) bounds(w, rowA, rowB, kA, eA, kB, eB);
+  // U nonzeros per lane and row are loaded before any of their gathers is
+  // issued (U * L per row per trip), so rows of hundreds of nonzeros keep
+  // 2U gathers per lane in flight; each lane still adds its nonzeros
+  // k, k + L, k + 2L, ... in that order.
+  constexpr int U = L >= 32 ? 4 : (L >= 16 ? 2 : 1);
   for (; (long long)w * rows_per_warp * 2 < count; w += warps_total) {
     double accA = 0.0, accB = 0.0;
     while (kA < eA || kB < eB) {
-      if (kA < eA) accA += (double)__ldg(val + kA) * __ldg(R + __ldg(col + kA));
-      if (kB < eB) accB += (double)__ldg(val + kB) * __ldg(R + __ldg(col + kB));
-      kA += L;
-      kB += L;
+      int cA[U], cB[U];
+      VT vA[U], vB[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int ka = kA + u * L, kb = kB + u * L;
+        cA[u] = ka < eA ? __ldg(col + ka) : -1;
+        vA[u] = ka < eA ? __ldg(val + ka) : VT(0);
+        cB[u] = kb < eB ? __ldg(col + kb) : -1;
+        vB[u] = kb < eB ? __ldg(val + kb) : VT(0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (cA[u] >= 0) accA += (double)vA[u] * __ldg(R + cA[u]);
+        if (cB[u] >= 0) accB += (double)vB[u] * __ldg(R + cB[u]);
+      }
+      kA += U * L;
+      kB += U * L;
     }
     const int curA = rowA, curB = rowB;
     const int wn = w + warps_total;
@@ -180,8 +198,22 @@ long_chunk_kernel(int nchunks, const int* __restrict__ cb, const int* __restrict
   if (state && state[ST_STATUS] != STATUS_RUNNING) return;
   const int lane = threadIdx.x & 31;
   for (int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks; c += (gridDim.x * blockDim.x) >> 5) {
+    // four nonzeros per lane are loaded before their gathers are issued; the
+    // lane adds them in index order
     double acc = 0.0;
-    for (int k = cb[c] + lane; k < ce[c]; k += 32) acc += (double)__ldg(val + k) * __ldg(x + __ldg(col + k));
+    const int e = ce[c];
+    for (int k = cb[c] + lane; k < e; k += 128) {
+      int cc[4];
+      VT vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        cc[u] = k + 32 * u < e ? __ldg(col + k + 32 * u) : -1;
+        vv[u] = k + 32 * u < e ? __ldg(val + k + 32 * u) : VT(0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (cc[u] >= 0) acc += (double)vv[u] * __ldg(x + cc[u]);
+    }
     acc = warp_sum(acc);
     if (lane == 0) csum[c] = acc;
   }
@@ -220,9 +252,15 @@ static cudaError_t launch_step(const CsrDev& A, const VT* val, cudaStream_t st, 
                                const double* R_own, double* W, double* Vj, int ldv, const double* part_in,
                                int nrows_in, int j, int beta_mode, double* alpha, double* beta, double* scal,
                                int* state) {
+  // `grid` is 8 CTAs per SM; kernels whose registers allow fewer resident
+  // CTAs get one full wave of them instead (the loop over rows is
+  // grid-strided, so CTAs that could not start at once would only add a tail)
 #define LG_STEP(LN, CNT, LIST)                                                                              \
   do {                                                                                                      \
-    cudaError_t e_ = launch_pdl(spmv_step_kernel<VT, LN>, dim3(grid), dim3(256), 0, st, CNT, LIST, A.rowptr,  \
+    static OccupancyCache occ_;                                                                             \
+    const int res_ = resident_blocks_once(occ_, (const void*)spmv_step_kernel<VT, LN>, 256, 8);             \
+    const int g_ = res_ < 8 ? grid / 8 * res_ : grid;                                                       \
+    cudaError_t e_ = launch_pdl(spmv_step_kernel<VT, LN>, dim3(g_), dim3(256), 0, st, CNT, LIST, A.rowptr,    \
                                 A.col, val, R, R_own, W, Vj, ldv, part_in, nrows_in, j, beta_mode, alpha, beta, \
                                 scal, state);                                                                \
     if (e_ != cudaSuccess) return e_;                                                                       \

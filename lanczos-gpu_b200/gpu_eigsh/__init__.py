@@ -138,21 +138,34 @@ def _default_ncv(n: int, k: int) -> int:
     return min(n, max(2 * k + 1, 20))
 
 
+def _reorder_flag(reorder) -> int:
+    if reorder is None or reorder is False:
+        return 0
+    if reorder is True or reorder in ("cm", "bfs"):
+        return _native.LG_PLAN_REORDER_BFS
+    if reorder == "degree":
+        return _native.LG_PLAN_REORDER_DEGREE
+    raise ValueError(f"reorder must be a bool, 'cm' or 'degree', got {reorder!r}")
+
+
 class EigshPlan:
     """A matrix resident on the GPU plus the solver workspace.
 
     Reusing a plan skips the CSR upload and all device allocations, which is
     what a caller solving repeatedly on one matrix wants.  ``solve`` takes the
-    same keywords as :func:`gpu_eigsh`.  ``reorder=True`` renumbers the rows
-    inside the plan by BFS level (LG_PLAN_REORDER_BFS) for locality of the
-    sparse product; v0, eigenvectors and ``matvec_device`` keep the caller's
+    same keywords as :func:`gpu_eigsh`.  ``reorder=True`` (or ``"cm"``)
+    renumbers the rows inside the plan in Cuthill-McKee order
+    (LG_PLAN_REORDER_BFS) for locality of the sparse product of mesh-like and
+    kNN graphs; ``reorder="degree"`` renumbers them by descending row length
+    (LG_PLAN_REORDER_DEGREE), which packs the hubs of a power-law graph
+    together; v0, eigenvectors and ``matvec_device`` keep the caller's
     numbering.  ``cgs2_inline=True`` keeps both Gram-Schmidt passes inside
     every Lanczos step (LG_PLAN_CGS2_INLINE) instead of delaying the second
     pass into the next step's stream of the basis (same results to rounding).
     """
 
     def __init__(self, A, max_ncv: int = 127, mixed: bool = False, device_csr=None, comm=None, n_global=None,
-                 reorder: bool = False, cgs2_inline: bool = False, callback=None):
+                 reorder=False, cgs2_inline: bool = False, callback=None):
         self._plan = None
         self._cb = None
         if callback is not None or (A is not None and device_csr is None and _operators.is_operator(A)):
@@ -168,7 +181,7 @@ class EigshPlan:
             self.n, self.nnz, self.mixed, self.max_ncv = n, 0, False, int(max_ncv)
             self.last_info = {}
             return
-        flags = (_native.LG_PLAN_REORDER_BFS if reorder else 0) | (_native.LG_PLAN_CGS2_INLINE if cgs2_inline else 0)
+        flags = _reorder_flag(reorder) | (_native.LG_PLAN_CGS2_INLINE if cgs2_inline else 0)
         if reorder and comm is not None:
             raise ValueError("reorder a partitioned matrix before splitting it (gpu_eigsh.ordering)")
         if cgs2_inline and comm is not None:
@@ -351,8 +364,10 @@ def gpu_eigsh(A, k=6, ncv=None, maxiter=None, tol=0, which="LM", sigma=None, cg_
         CG requires A - sigma I to be definite.
     v0 : starting vector (length n); None -> a seeded uniform random vector.
     mixed : fp32 matrix values with fp64 accumulation and fp64 basis.
-    reorder : renumber the rows by BFS level inside the solver for locality of
-        the sparse product (see EigshPlan); results keep the caller's order.
+    reorder : renumber the rows inside the solver for locality of the sparse
+        product: True or 'cm' (Cuthill-McKee, mesh-like and kNN graphs) or
+        'degree' (descending row length, power-law graphs); see EigshPlan.
+        Results keep the caller's order.
 
     Returns ``(w, v)`` with ``w`` ascending and ``v`` of shape (n, k), or ``w``
     alone when ``return_eigenvectors=False``.  Raises scipy's

@@ -26,6 +26,7 @@ EXCHANGE = {"auto": 0, "allgather": 1, "halo": 2}
 TRANSPORT = {"auto": 0, "nccl": 1, "peer": 2}
 LG_PLAN_REORDER_BFS = 1
 LG_PLAN_CGS2_INLINE = 2
+LG_PLAN_REORDER_DEGREE = 4
 LG_OP_DEVICE, LG_OP_HOST, LG_OP_STREAM = 0, 1, 2
 # callback types of lg_eigsh_plan_create_op (include/lanczos_b200.h)
 MATVEC_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)

@@ -186,3 +186,36 @@ def test_cm_order_is_a_bandwidth_reducing_permutation():
     B = sp.block_diag([L[:100, :100], L[:50, :50]]).tocsr()
     p2 = cm_order(torch.from_numpy(B.indptr.astype(np.int32)), torch.from_numpy(B.indices.astype(np.int32)))
     assert torch.equal(torch.sort(p2).values, torch.arange(150))
+
+
+def test_degree_order_sorts_and_deals_hubs():
+    """degree_order: descending degree, ties by index (the order
+    LG_PLAN_REORDER_DEGREE applies); with parts > 1 the sorted vertices are
+    dealt round-robin to the row blocks of partition_rows, so each block gets
+    the same share of nonzeros and starts with its hubs."""
+    import numpy as np
+
+    from gpu_eigsh import synthetic as syn
+    from gpu_eigsh.distributed import partition_rows
+    from gpu_eigsh.ordering import degree_order, permute_symmetric
+
+    n, rp, col, val, _ = syn.rmat_laplacian_device(12, device="cpu")
+    deg = (rp[1:] - rp[:-1]).long()
+    perm = degree_order(rp)
+    assert torch.equal(torch.sort(perm).values, torch.arange(n))
+    ref = sorted(range(n), key=lambda i: (-int(deg[i]), i))
+    assert perm.tolist() == ref
+    for parts in (2, 3, 4):
+        p = degree_order(rp, parts)
+        assert torch.equal(torch.sort(p).values, torch.arange(n))
+        rp2, _, _, _ = permute_symmetric(rp, col, val, p)
+        nnz_blocks = []
+        for r in range(parts):
+            r0, r1 = partition_rows(n, parts, r)
+            # block r holds sorted positions r, r + parts, ... while it has room
+            if n % parts == 0 and r1 - r0 == n // parts:   # equal blocks: a plain round-robin deal
+                assert p[r0:r1].tolist() == ref[r::parts]
+            d = deg[p[r0:r1]]
+            assert torch.all(d[:-1] >= d[1:])
+            nnz_blocks.append(int(rp2[r1] - rp2[r0]))
+        assert max(nnz_blocks) - min(nnz_blocks) <= 0.02 * max(nnz_blocks) + int(deg.max()), nnz_blocks

@@ -4,7 +4,8 @@ Two ranks (processes, one GPU each) split the rows of a kNN graph
 Laplacian (in the generator's order, and renumbered by BFS level so that the
 halos are small: run with the halo exchange and, forced, with the
 all-gather) and of an R-MAT normalised Laplacian (configuration 4's family,
-with rows longer than the row kernels' cut), through the peer-memory
+with rows longer than the row kernels' cut; in the generator's order, and
+sorted by degree with the hubs dealt to the two blocks), through the peer-memory
 transport (reductions and exchanges as kernels storing into the other rank's
 memory) and, for two cases, through NCCL.  Every rank must report the same
 eigenvalues, equal to the single-GPU plan's and to scipy ARPACK's at 1e-10, and the assembled
@@ -47,6 +48,11 @@ def _matrix(case):
     import torch
 
     n, rp, col, val, _ = syn.rmat_laplacian_device(15, device="cpu")
+    if case == "rmat_degree":
+        # hubs first, dealt round-robin to the two row blocks
+        from gpu_eigsh.ordering import degree_order, permute_symmetric
+
+        rp, col, val, _ = permute_symmetric(rp, col, val, degree_order(rp, 2))
     L = sp.csr_matrix((val.numpy(), col.numpy(), rp.numpy()), shape=(n, n))
     return L, dict(k=12, which="LA", ncv=40, tol=1e-10), False
 
@@ -100,7 +106,8 @@ def _worker(rank, world, port, case, out_w, out_y):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["knn", "knn_bfs", "knn_bfs_allgather", "rmat", "knn_bfs_nccl", "rmat_nccl"])
+@pytest.mark.parametrize("case", ["knn", "knn_bfs", "knn_bfs_allgather", "rmat", "knn_bfs_nccl", "rmat_nccl",
+                                  "rmat_degree"])
 def test_partitioned_equals_single_gpu(case):
     import torch
     import torch.multiprocessing as mp
