@@ -88,8 +88,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   extern __shared__ __align__(16) double M[];   // m x m, column-major
   __shared__ double d[kMaxCols], e[kMaxCols], e2[kMaxCols], th[kMaxCols];
   __shared__ double rz[kMaxCols], bd[kMaxCols], shifts[kMaxCols];
-  __shared__ double rot_c[32], rot_s[32];
-  __shared__ int rot_k[32];
+  __shared__ double rot_c[2][32], rot_s[2][32];
+  __shared__ int rot_k[2][32];
   __shared__ int id[kMaxCols], cl[kMaxCols];
   __shared__ double sh_bn, sh_onenrm;
   __shared__ int sh_stop, sh_done, sh_nev, sh_np, sh_nconv;
@@ -221,8 +221,11 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   // every unreduced block.  Couplings that become negligible during the
   // chases are left alone (the bulge then just passes identity rotations).
   const int np = sh_np, nev = sh_nev;
-  int tpr = 1;   // threads per row of Q in the rotation updates
-  while (tpr < 32 && 2 * tpr * m <= kRsThreads) tpr *= 2;
+  // Warp 0 computes the rotations of chase step st while the other warps
+  // apply those of step st - 1 to Q (double-buffered rotation lists), so the
+  // two halves of a step overlap; Q still receives the steps in order.
+  int tpr = 1;   // threads per row of Q in the rotation updates (warps 1..)
+  while (tpr < 32 && 2 * tpr * m <= kRsThreads - 32) tpr *= 2;
   __shared__ int blk_lo[kMaxCols], blk_hi[kMaxCols];
   __shared__ int sh_nblk;
   __syncthreads();   // M (eigenvectors) no longer needed
@@ -247,42 +250,44 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
       const int steps = (be - bs) + 3 * (nb - 1);
       double bulge = 0.0;                       // lane's bulge (warp 0)
       const double sigma = (t < 32 && lane < nb) ? shifts[b0 + lane] : 0.0;
-      for (int st = 0; st < steps; ++st) {
+      for (int st = 0; st <= steps; ++st) {
+        const int buf = st & 1;
         if (t < 32) {
-          const int k = bs + st - 3 * lane;
-          int kk = -1;
-          if (lane < nb && k >= bs && k < be) {
-            double c, s;
-            if (k == bs) {
-              givens(d[bs] - sigma, e[bs], c, s);
-            } else {
-              givens(e[k - 1], bulge, c, s);
-              e[k - 1] = c * e[k - 1] - s * bulge;
+          if (st < steps) {
+            const int k = bs + st - 3 * lane;
+            int kk = -1;
+            if (lane < nb && k >= bs && k < be) {
+              double c, s;
+              if (k == bs) {
+                givens(d[bs] - sigma, e[bs], c, s);
+              } else {
+                givens(e[k - 1], bulge, c, s);
+                e[k - 1] = c * e[k - 1] - s * bulge;
+              }
+              const double dk = d[k], dk1 = d[k + 1], ek = e[k];
+              const double cc = c * c, ss = s * s, cs = c * s;
+              d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
+              d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
+              e[k] = cs * (dk - dk1) + (cc - ss) * ek;
+              if (k + 1 < be) {
+                bulge = -s * e[k + 1];
+                e[k + 1] = c * e[k + 1];
+              }
+              rot_c[buf][lane] = c;
+              rot_s[buf][lane] = s;
+              kk = k;
             }
-            const double dk = d[k], dk1 = d[k + 1], ek = e[k];
-            const double cc = c * c, ss = s * s, cs = c * s;
-            d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
-            d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
-            e[k] = cs * (dk - dk1) + (cc - ss) * ek;
-            if (k + 1 < be) {
-              bulge = -s * e[k + 1];
-              e[k + 1] = c * e[k + 1];
-            }
-            rot_c[lane] = c;
-            rot_s[lane] = s;
-            kk = k;
+            rot_k[buf][lane] = kk;
           }
-          rot_k[lane] = kk;
-        }
-        __syncthreads();
-        // the step's rotations touch disjoint column pairs (bulges three
-        // rows apart), so the tpr threads of a row split them freely
-        if (t < tpr * m) {
-          const int row = t / tpr;
-          for (int s = t % tpr; s < nb; s += tpr) {
-            const int k = rot_k[s];
+        } else if (st > 0 && t - 32 < tpr * m) {
+          // step st - 1: its rotations touch disjoint column pairs (bulges
+          // three rows apart), so the tpr threads of a row split them freely
+          const int tq = t - 32, pb = buf ^ 1;
+          const int row = tq / tpr;
+          for (int s = tq % tpr; s < nb; s += tpr) {
+            const int k = rot_k[pb][s];
             if (k < 0) continue;
-            const double c = rot_c[s], sn = rot_s[s];
+            const double c = rot_c[pb][s], sn = rot_s[pb][s];
             const double x0 = M[row + (size_t)k * m], x1 = M[row + (size_t)(k + 1) * m];
             M[row + (size_t)k * m] = c * x0 - sn * x1;
             M[row + (size_t)(k + 1) * m] = sn * x0 + c * x1;

@@ -1044,11 +1044,15 @@ using namespace lg;
 using namespace lg::slq;
 
 // Lane layout <T, LPR, NS> of every block kernel by element type and probe
-// count (the last argument is unused).
+// count (the last argument is unused): the fewest lanes per row that cover the
+// row's 16-byte vectors, so that a block of few probes (one shard of the
+// probes on one of several GPUs) keeps every lane busy.
 #define LG_DISPATCH(DTYPE, B, CALL)                                                                   \
   ((DTYPE) == LG_F64                                                                                   \
-       ? ((B) <= 32 ? CALL(double, 16, 1, 1) : (B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
-       : ((B) <= 32 ? CALL(float, 8, 1, 1) : (B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
+       ? ((B) <= 8 ? CALL(double, 4, 1, 1) : (B) <= 16 ? CALL(double, 8, 1, 1)                         \
+          : (B) <= 32 ? CALL(double, 16, 1, 1) : (B) <= 64 ? CALL(double, 32, 1, 1) : CALL(double, 32, 2, 2)) \
+       : ((B) <= 8 ? CALL(float, 2, 1, 1) : (B) <= 16 ? CALL(float, 4, 1, 1)                            \
+          : (B) <= 32 ? CALL(float, 8, 1, 1) : (B) <= 64 ? CALL(float, 16, 1, 1) : CALL(float, 32, 1, 2)))
 extern "C" size_t lg_slq_workspace_bytes(const lg_slq_op* op, int B, int ld) {
   if (op) {
     if (check_op(op, B, ld) != LG_OK) return 0;

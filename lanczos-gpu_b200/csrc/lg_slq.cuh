@@ -170,53 +170,86 @@ struct RowLanes {
 };
 
 // y += sum_k off[k] X[col[k], :] over the row of this lane group (and yk with
-// doff when DERIV), accumulated in T.  The group loads LPR (col, value) pairs
-// at once and broadcasts them by shuffle; the loop runs to the longest row of
-// the warp so that every lane takes part in every shuffle.
+// doff when DERIV), accumulated in T.  The group loads LPR * U (col, value)
+// pairs at once (U per lane) and broadcasts them by shuffle; the loop runs to
+// the longest row of the warp so that every lane takes part in every shuffle.
+// Narrow rows (LPR < 8 lanes: blocks of few probes) take U = 8 / LPR pairs per
+// lane, so that eight neighbour rows are gathered per trip instead of LPR;
+// the neighbours are still added in index order.
 template <typename T, int LPR, int NCH, bool DERIV>
 __device__ __forceinline__ void gather_rows(const Op& op, const T* __restrict__ off, const T* __restrict__ doff,
                                             const T* __restrict__ X, int ld, int B, bool valid, long long row,
                                             const RowLanes<T, LPR>& g, T (&y)[NCH][Lanes<T>::VEC],
                                             T (&yk)[NCH][Lanes<T>::VEC]) {
   constexpr int VEC = Lanes<T>::VEC;
+  constexpr int U = LPR >= 8 ? 1 : 8 / LPR;
   const int kb = valid ? __ldg(op.rowptr + row) : 0;
   const int cnt = valid ? __ldg(op.rowptr + row + 1) - kb : 0;
   int mx = cnt;
 #pragma unroll
   for (int o = LPR; o < 32; o <<= 1) mx = max(mx, __shfl_xor_sync(kFull, mx, o));
   const int base = g.lane - g.l;
-  for (int k0 = 0; k0 < mx; k0 += LPR) {
-    const int kk = k0 + g.l;
-    int ci = 0;
-    T av = T(0), dv = T(0);
-    if (kk < cnt) {
-      ci = __ldg(op.col + kb + kk);
-      av = __ldg(off + kb + kk);
-      if (DERIV) dv = __ldg(doff + kb + kk);
-    }
-    const int nb = min(LPR, mx - k0);
-#pragma unroll 4
-    for (int s = 0; s < nb; ++s) {
-      const long long c = __shfl_sync(kFull, ci, base + s);
-      const T a = __shfl_sync(kFull, av, base + s);
-      const T d = DERIV ? __shfl_sync(kFull, dv, base + s) : T(0);
-      if (k0 + s < cnt) {
+  auto add = [&](long long c, T a, T d) {
 #pragma unroll
-        for (int ch = 0; ch < NCH; ++ch) {
-          const int c0 = g.col0(ch);
-          if (c0 < B) {
-            // padding columns (>= B) of X may hold anything: they only ever
-            // reach the padding columns of y, which are neither stored nor summed
-            T v[VEC];
-            ldvec<T, VEC>(X + c * ld + c0, VEC, v);
+    for (int ch = 0; ch < NCH; ++ch) {
+      const int c0 = g.col0(ch);
+      if (c0 < B) {
+        // padding columns (>= B) of X may hold anything: they only ever
+        // reach the padding columns of y, which are neither stored nor summed
+        T v[VEC];
+        ldvec<T, VEC>(X + c * ld + c0, VEC, v);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-              y[ch][i] += a * v[i];
-              if (DERIV) yk[ch][i] += d * v[i];
-            }
-          }
+        for (int i = 0; i < VEC; ++i) {
+          y[ch][i] += a * v[i];
+          if (DERIV) yk[ch][i] += d * v[i];
         }
       }
+    }
+  };
+  if constexpr (U == 1) {
+    for (int k0 = 0; k0 < mx; k0 += LPR) {
+      const int kk = k0 + g.l;
+      int ci = 0;
+      T av = T(0), dv = T(0);
+      if (kk < cnt) {
+        ci = __ldg(op.col + kb + kk);
+        av = __ldg(off + kb + kk);
+        if (DERIV) dv = __ldg(doff + kb + kk);
+      }
+      const int nb = min(LPR, mx - k0);
+#pragma unroll 4
+      for (int s = 0; s < nb; ++s) {
+        const long long c = __shfl_sync(kFull, ci, base + s);
+        const T a = __shfl_sync(kFull, av, base + s);
+        const T d = DERIV ? __shfl_sync(kFull, dv, base + s) : T(0);
+        if (k0 + s < cnt) add(c, a, d);
+      }
+    }
+  } else {
+    for (int k0 = 0; k0 < mx; k0 += LPR * U) {
+      int ci[U];
+      T av[U], dv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int kk = k0 + u * LPR + g.l;
+        ci[u] = 0;
+        av[u] = T(0);
+        dv[u] = T(0);
+        if (kk < cnt) {
+          ci[u] = __ldg(op.col + kb + kk);
+          av[u] = __ldg(off + kb + kk);
+          if (DERIV) dv[u] = __ldg(doff + kb + kk);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int s = 0; s < LPR; ++s) {
+          const long long c = __shfl_sync(kFull, ci[u], base + s);
+          const T a = __shfl_sync(kFull, av[u], base + s);
+          const T d = DERIV ? __shfl_sync(kFull, dv[u], base + s) : T(0);
+          if (k0 + u * LPR + s < cnt) add(c, a, d);
+        }
     }
   }
 }

@@ -176,7 +176,8 @@ def test_slq_imgp_golden(torch_cuda, golden_dir, tag, dtype_name, tol):
 
 @pytest.mark.parametrize("nu,mp,lm,dtype_name", [(3, 7, 12, "float64"), (4, 6, 10, "float64"), (2, 130, 8, "float64"),
                                                  (1, 5, 1, "float64"), (2, 4, 2, "float64"),
-                                                 (2, 64, 30, "float32")])
+                                                 (2, 64, 30, "float32"), (2, 8, 12, "float32"),
+                                                 (2, 3, 10, "float32")])
 def test_slq_imgp_matches_oracle(torch_cuda, nu, mp, lm, dtype_name):
     torch = torch_cuda
     from gpu_eigsh.funm_torch import slq_logdet
