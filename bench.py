@@ -107,12 +107,19 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
             return
         self._t = threading.Thread(target=self._read, daemon=True)
         self._t.start()
+        # nvidia-smi takes a moment to print its first sample; a timed region
+        # of a few solves can be shorter than that.  Wait for it (up to 5 s)
+        # and keep only the samples taken from here on.
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.lines = []
 
     def _read(self):
         for line in self.proc.stdout:
@@ -874,7 +881,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=600))
+                                timeout=__import__("datetime").timedelta(seconds=180))
 
     import gpu_eigsh
 
