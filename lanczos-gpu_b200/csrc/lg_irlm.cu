@@ -644,7 +644,17 @@ int Solver::setup_halo() {
   rc = comm_sendrecv(comm, 4, d_recv_pos, recv_off.data(), recv_cnt.data(), d_send_idx, send_off.data(),
                      send_cnt.data(), stream);
   if (rc != LG_OK) return rc;
-  LG_TRY(cudaStreamSynchronize(stream));   // pos goes out of scope
+  // Each send segment ascends (the readers scanned their bitmaps in order):
+  // its last entry is the highest row of this block that the peer reads.
+  // An all-gather then sends each peer only the rows up to that one (a graph
+  // numbered by descending degree keeps its never-named rows at the end).
+  ag_need.assign((size_t)nranks, 0);
+  for (int q = 0; q < nranks; ++q)
+    if (q != rank && send_cnt[q] > 0)
+      LG_TRY(cudaMemcpyAsync(&ag_need[q], d_send_idx + send_off[q] + send_cnt[q] - 1, sizeof(int),
+                             cudaMemcpyDeviceToHost, stream));
+  LG_TRY(cudaStreamSynchronize(stream));   // pos goes out of scope, ag_need has arrived
+  for (int q = 0; q < nranks; ++q) ag_need[q] = (q != rank && send_cnt[q] > 0) ? ag_need[q] - row0 + 1 : 0;
   return LG_OK;
 }
 
@@ -859,12 +869,16 @@ int Solver::apply_step(int j, int beta_mode) {
 
 int Solver::extend(int j0, int j1, int first_mode, bool lag) {
   bool last_lag = false;
+  deferred_norm_rows = 0;
   for (int j = j0; j < j1; ++j) {
     // a lag step needs a previous column and a residual whose coupling is
     // its norm (not after a fresh start, an explicit third pass or a random
     // restart, whose first step keeps the in-step passes and their checks)
     if (lag && j > 0 && (j > j0 || first_mode == BETA_RESTART)) {
-      int rc = lag_step(j);
+      // on the peer transport the norm of this step's residual is reduced
+      // by the next lag step's exchange (every step but the last)
+      const bool defer = comm && transport == LG_TRANSPORT_PEER && j + 1 < j1;
+      int rc = lag_step(j, defer);
       if (rc != LG_OK) return rc;
       last_lag = true;
       continue;
@@ -900,10 +914,19 @@ int Solver::extend(int j0, int j1, int first_mode, bool lag) {
 // j-1, then one stream of V for s = V^T u and t = V^T z, and one that
 // finishes v_j = (u - V s) / beta_j and forms the next once-orthogonalised
 // residual (lg_gs.cu, gs_lag_project / gs_lag_correct).
-int Solver::lag_step(int j) {
+int Solver::lag_step(int j, bool defer_norm) {
   const double vb = mixed ? 4.0 : 8.0;
   const double sbytes = (4.0 + vb) * (double)nnz + 4.0 * (n + 1) + 8.0 * n + 8.0 * n;
-  int rc = gather_residual();
+  int rc = LG_OK;
+  if (deferred_norm_rows > 0) {
+    // the previous step's ||R||^2 partial rows, reduced by the exchange
+    rc = peer_exchange(partC, deferred_norm_rows, 2);
+    inC = red + (size_t)2 * kPartStride;
+    nrowsC = 1;
+    deferred_norm_rows = 0;
+  } else {
+    rc = gather_residual();
+  }
   if (rc != LG_OK) return rc;
   const double* Rg = comm ? Rfull : R;
   LG_TRY(timed(LG_K_SPMV, sbytes, (A.nclasses > 0 ? A.nclasses : 1) + (A.nlong ? 2 : 0), [&] {
@@ -921,6 +944,12 @@ int Solver::lag_step(int j) {
   LG_TRY(timed(LG_K_CORRPROJ, vbytes + 32.0 * n, 1, [&] {
     return gs_lag_correct(p, stream, V, vl, j, n, R, W, inS, inT, nS, partC, scal, alpha, beta, state);
   }));
+  if (defer_norm) {
+    deferred_norm_rows = p.grid;
+    inC = partC;
+    nrowsC = p.grid;
+    return LG_OK;
+  }
   return reduce_partials_all(partC, p.grid, 2, &inC, &nrowsC);
 }
 

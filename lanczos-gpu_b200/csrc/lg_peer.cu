@@ -161,16 +161,52 @@ peer_allreduce_kernel(const double* __restrict__ partA, const double* __restrict
 // Halo mode (send_off != nullptr): entry i of the send list (global position
 // send_idx[i], peer p with send_off[p] <= i < send_off[p + 1]) goes to the
 // same position of peer p's residual buffer.  All-gather mode: this rank's
-// rows [row0, row0 + n_local) go to every peer.
+// rows [row0, row0 + P.ag_len[p]) go to peer p (the rows it reads).
+//
+// With `part` (nrows partial-sum rows of the kernel just before), the same
+// call also all-reduces them into `out`: CTA 0 first sums this rank's rows in
+// a fixed order (warp w takes rows w, w + 8, ..., then the warps in order)
+// and stores the sum into slot [rank] of every rank's mailbox (table 0); the
+// flags that announce the exchanged rows then announce that row too, and the
+// CTA that waits for them adds the ranks' rows in rank order.  One wait per
+// Lanczos step instead of two (the residual's norm and its rows).
 __global__ void __launch_bounds__(kExchangeThreads)
 peer_exchange_kernel(const double* __restrict__ Rfull, const int* __restrict__ send_idx,
                      const long long* __restrict__ send_off, long long total, int row0, int n_local, PeerPtrs P,
                      int nranks, int rank, unsigned long long seq, long long wait_cycles, unsigned* counter,
-                     int* state) {
+                     const double* __restrict__ part, int nrows, double* out, int* state) {
   griddep_wait();   // the residual rows come from the kernel just before
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   __shared__ int sh_last, sh_fail;
   const int t = threadIdx.x;
+  const int par = (int)(seq & 1ull);
+  if (part && blockIdx.x == 0) {
+    constexpr int NW = kExchangeThreads / 32;
+    constexpr int CPL = (kPartStride + 31) / 32;
+    __shared__ double wsum[NW][kPartStride];
+    const int lane = t & 31, warp = t >> 5;
+    double acc[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) acc[c] = 0.0;
+    for (int r = warp; r < nrows; r += NW) {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int col = lane + 32 * c;
+        if (col < kPartStride) acc[c] += __ldcg(part + (size_t)r * kPartStride + col);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const int col = lane + 32 * c;
+      if (col < kPartStride) wsum[warp][col] = acc[c];
+    }
+    __syncthreads();
+    if (t < kPartStride) {
+      double v = 0.0;
+      for (int w = 0; w < NW; ++w) v += wsum[w][t];
+      for (int q = 0; q < nranks; ++q) P.mail[q][mail_index(par, 0, rank, nranks) + t] = v;
+    }
+  }
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long i0 = (long long)blockIdx.x * blockDim.x + t;
   if (send_off) {
@@ -182,13 +218,14 @@ peer_exchange_kernel(const double* __restrict__ Rfull, const int* __restrict__ s
     }
   } else {
     // 16-byte stores: row0 is a multiple of 256, so pairs stay aligned
-    const long long npairs = n_local / 2;
     const double2* src = reinterpret_cast<const double2*>(Rfull + row0);
     for (int q = 0; q < nranks; ++q) {
       if (q == rank) continue;
+      const int len = min(P.ag_len[q], n_local);
+      const long long npairs = len / 2;
       double2* dst = reinterpret_cast<double2*>(P.R[q] + row0);
       for (long long i = i0; i < npairs; i += stride) dst[i] = __ldg(src + i);
-      if ((n_local & 1) && i0 == 0) P.R[q][row0 + n_local - 1] = Rfull[row0 + n_local - 1];
+      if ((len & 1) && i0 == 0) P.R[q][row0 + len - 1] = Rfull[row0 + len - 1];
     }
   }
   __threadfence_system();
@@ -196,7 +233,6 @@ peer_exchange_kernel(const double* __restrict__ Rfull, const int* __restrict__ s
   if (t == 0) sh_last = atomicAdd(counter, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!sh_last) return;
-  const int par = (int)(seq & 1ull);
   if (t == 0) {
     *counter = 0u;   // for the next call (stream-ordered)
     __threadfence_system();
@@ -210,6 +246,13 @@ peer_exchange_kernel(const double* __restrict__ Rfull, const int* __restrict__ s
       state[ST_ERRINFO] = 2;
       state[ST_STATUS] = STATUS_TIMEOUT;
     }
+    return;
+  }
+  if (part && t < kPartStride) {
+    const double* mail = P.mail[rank];
+    double v = 0.0;
+    for (int q = 0; q < nranks; ++q) v += __ldcg(mail + mail_index(par, 0, q, nranks) + t);
+    out[t] = v;
   }
 }
 
@@ -351,6 +394,7 @@ int Solver::setup_peer() {
     transport = LG_TRANSPORT_NCCL;
     return LG_OK;
   }
+  for (int q = 0; q < nranks; ++q) peer_ptrs.ag_len[q] = q < (int)ag_need.size() ? ag_need[q] : n;
   peer_ok = true;
   peer_seq = 0;
   transport = LG_TRANSPORT_PEER;
@@ -390,16 +434,19 @@ int Solver::peer_reduce(const double* partA, const double* partB, int nrows, int
   return LG_OK;
 }
 
-int Solver::peer_exchange() {
+int Solver::peer_exchange(const double* part, int nrows, int slot) {
   ++peer_seq;
   ++launches;
   const bool halo = exchange == LG_EXCHANGE_HALO;
-  const long long work = halo ? halo_send : (long long)(nranks - 1) * ((n + 1) / 2);
+  long long ag_pairs = 0;
+  for (int q = 0; q < nranks; ++q) ag_pairs += (peer_ptrs.ag_len[q] + 1) / 2;
+  const long long work = halo ? halo_send : ag_pairs;
   const int grid = (int)std::max<long long>(1, std::min<long long>((long long)num_sm * 4,
                                                                     (work + kExchangeThreads - 1) / kExchangeThreads));
   LG_PTRY(launch_pdl(peer_exchange_kernel, dim3(grid), dim3(kExchangeThreads), 0, stream, (const double*)Rfull,
                      (const int*)d_send_idx, (const long long*)(halo ? d_peer_send_off : nullptr), halo_send, row0, n,
-                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, peer_counter, state));
+                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, peer_counter, part, part ? nrows : 0,
+                     part ? red + (size_t)slot * kPartStride : nullptr, state));
   return LG_OK;
 }
 

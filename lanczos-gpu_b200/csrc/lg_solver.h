@@ -22,6 +22,9 @@ struct PeerPtrs {
   double* mail[kMaxPeerRanks];
   unsigned long long* flags[kMaxPeerRanks];
   double* R[kMaxPeerRanks];
+  // all-gather mode: rank q reads only the first ag_len[q] rows of this
+  // rank's block (the last one its columns name, plus one; 0 for none)
+  int ag_len[kMaxPeerRanks];
 };
 
 class Solver {
@@ -73,7 +76,9 @@ class Solver {
   int setup_peer();
   void release_peer();
   int peer_reduce(const double* partA, const double* partB, int nrows, int ntables, int slot);
-  int peer_exchange();
+  // The residual exchange; with `part`, also the all-reduce of its nrows
+  // partial rows into row `slot` of `red` (one wait for both).
+  int peer_exchange(const double* part = nullptr, int nrows = 0, int slot = 0);
   // reduce_partials_all of two tables of one producer (rows `slot` and
   // slot + 1 of red): one peer all-reduce, or two NCCL ones.
   int reduce_partials_all2(double* pa, double* pb, int nrows, int slot, const double** ina, const double** inb,
@@ -91,7 +96,11 @@ class Solver {
   // Gram-Schmidt pass delayed into the next step (lag_step), and the last
   // residual gets that pass at the end (finish_lag).
   int extend(int j0, int j1, int first_mode, bool lag = false);
-  int lag_step(int j);
+  // defer_norm: leave the ||R||^2 partial rows of the correction unreduced
+  // (nrowsC = their count, inC = partC); the next lag step reduces them
+  // together with its residual exchange (peer transport).
+  int lag_step(int j, bool defer_norm = false);
+  int deferred_norm_rows = 0;   // partial rows of partC awaiting the next lag step's exchange
   int finish_lag(int s);
   bool lag_steps = true;   // false: LG_PLAN_CGS2_INLINE (both passes inside every step)
   int pass3(int s);
@@ -140,6 +149,7 @@ class Solver {
   void* peer_open_R[kMaxPeerRanks] = {};
   PeerPtrs peer_ptrs{};
   int* d_send_idx = nullptr;
+  std::vector<int> ag_need;   // per peer: leading rows of this block it reads (setup_halo)
   int* d_recv_pos = nullptr;
   double* d_send_buf = nullptr;
   double* d_recv_buf = nullptr;
