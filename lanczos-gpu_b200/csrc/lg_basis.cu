@@ -21,6 +21,8 @@
 #include "lg_common.cuh"
 #include "lg_kernels.cuh"
 
+#include <algorithm>
+
 namespace lg {
 
 namespace {
@@ -60,6 +62,29 @@ template <int N>
 __device__ __forceinline__ void bs_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 }  // namespace
 
+template <int NOB>
+__global__ void basis_kernel(BasisArgs a);
+
+// CTAs of basis_kernel<NOB> resident on one SM with `smem` bytes of dynamic
+// shared memory (0 when unknown).
+static int basis_resident(int nob, size_t smem) {
+  int res = 0;
+  cudaError_t e = cudaSuccess;
+  if (nob <= 4) e = cudaFuncSetAttribute(basis_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  else if (nob <= 8) e = cudaFuncSetAttribute(basis_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  else e = cudaFuncSetAttribute(basis_kernel<kMaxOB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) {
+    if (nob <= 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, basis_kernel<4>, kBsThreads, smem);
+    else if (nob <= 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, basis_kernel<8>, kBsThreads, smem);
+    else e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, basis_kernel<kMaxOB>, kBsThreads, smem);
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return res;
+}
+
 BasisPlan basis_plan(int n, int m, int kq, int grid) {
   BasisPlan p;
   p.TR = kTR;
@@ -68,6 +93,15 @@ BasisPlan basis_plan(int n, int m, int kq, int grid) {
   const BsGeom g(m, kq);
   p.nbuf = g.smem_doubles(2) * sizeof(double) <= kBsSmemLimit ? 2 : 1;
   p.smem = g.smem_doubles(p.nbuf) * sizeof(double);
+  // one wave: the tiles are dealt to the CTAs in a grid-strided loop, every
+  // CTA the same count, so CTAs beyond the resident ones would only form a
+  // second wave as long as the first
+  int dev = 0, nsm = 0;
+  const int res = basis_resident(g.kqp / 8, p.smem);
+  if (res > 0 && cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && nsm > 0)
+    p.grid = std::max(1, std::min(p.grid, nsm * res));
+  (void)cudaGetLastError();
   return p;
 }
 
@@ -83,6 +117,7 @@ basis_kernel(BasisArgs a) {
   if (state[ST_STATUS] != STATUS_RUNNING) return;
   extern __shared__ __align__(16) double sm[];
   __shared__ double scr[32];
+  __shared__ double kvcol[kTR];   // restart: column kq - 1 of the tile's product
   const int m = a.m, kq = a.kq, n = a.n;
   const VLayout vl = a.vl;
   const BsGeom g(m, kq);
@@ -134,16 +169,69 @@ basis_kernel(BasisArgs a) {
     }
     __syncthreads();   // every thread's copies (and Qs on the first pass)
     double* Vs = Vbuf[cur];
-    double acc[NOB][2];
+    // two accumulator sets (k steps alternate between them) halve the chain
+    // of dependent MMAs; they are added once at the end
+    double acc[NOB][2], acc2[NOB][2];
 #pragma unroll
-    for (int ob = 0; ob < NOB; ++ob) acc[ob][0] = acc[ob][1] = 0.0;
+    for (int ob = 0; ob < NOB; ++ob) acc[ob][0] = acc[ob][1] = acc2[ob][0] = acc2[ob][1] = 0.0;
     const double* arow = Vs + (warp * 8 + gid) * g.sv + tig;
     const double* bcol = Qs + gid * g.sq + tig;
-    for (int k0 = 0; k0 < g.mp; k0 += 4) {
+    int k0 = 0;
+    constexpr bool kSplit = NOB <= 8;   // the widest tiles keep one set (registers)
+    for (; kSplit && k0 + 4 < g.mp; k0 += 8) {
+      const double av = arow[k0], av2 = arow[k0 + 4];
+#pragma unroll
+      for (int ob = 0; ob < NOB; ++ob)
+        if (ob < nob) {
+          dmma(acc[ob][0], acc[ob][1], av, bcol[ob * 8 * g.sq + k0]);
+          dmma(acc2[ob][0], acc2[ob][1], av2, bcol[ob * 8 * g.sq + k0 + 4]);
+        }
+    }
+    for (; k0 < g.mp; k0 += 4) {
       const double av = arow[k0];
 #pragma unroll
       for (int ob = 0; ob < NOB; ++ob)
         if (ob < nob) dmma(acc[ob][0], acc[ob][1], av, bcol[ob * 8 * g.sq + k0]);
+    }
+#pragma unroll
+    for (int ob = 0; ob < NOB; ++ob) {
+      acc[ob][0] += acc2[ob][0];
+      acc[ob][1] += acc2[ob][1];
+    }
+    if (kSplit && a.restart) {
+      // straight from the fragments into V (the tile's rows of V are all in
+      // Vs already): a thread holds columns ob*8 + 2*tig, +1 of one row, and
+      // the 32 lanes of a warp cover 8 rows x 64 contiguous bytes per panel
+      const int kv = kq - 1;
+      const int rr = warp * 8 + gid;
+      const long long row = row0 + rr;
+#pragma unroll
+      for (int ob = 0; ob < NOB; ++ob)
+        if (ob < nob) {
+          const int c = ob * 8 + 2 * tig;
+          if (row < n) {
+            double* dst = a.V + vidx(vl, row, c);
+            if (c + 1 < kv) *reinterpret_cast<double2*>(dst) = make_double2(acc[ob][0], acc[ob][1]);
+            else if (c < kv) dst[0] = acc[ob][0];
+          }
+          if (c == kv) kvcol[rr] = acc[ob][0];
+          if (c + 1 == kv) kvcol[rr] = acc[ob][1];
+        }
+      __syncthreads();   // kvcol complete; every fragment read of Vs done
+      if (t < kTR) {
+        const long long r = row0 + t;
+        if (r < n) {
+          const double rn = rcoef * a.R[r] + tau * kvcol[t];
+          a.R[r] = rn;
+          nrm += rn * rn;
+        }
+      }
+      if (a.nbuf == 1 && next < ntiles) {
+        issue(next, Vbuf[0]);
+        bs_commit();
+      }
+      cur ^= (a.nbuf - 1);
+      continue;
     }
     __syncthreads();   // all fragment reads of Vs done
 #pragma unroll
