@@ -67,7 +67,8 @@ enum {
   LG_K_BASIS = 5,    /* V*Q restart update / Ritz vectors */
   LG_K_CG = 6,       /* shift-invert CG iteration kernels */
   LG_K_OTHER = 7,
-  LG_K_CLASSES = 8
+  LG_K_COMM = 8,     /* partitioned plans: the reductions over the ranks and the residual exchanges (waits included) */
+  LG_K_CLASSES = 9
 };
 
 typedef struct lg_eigsh_info {
@@ -80,9 +81,9 @@ typedef struct lg_eigsh_info {
   int cg_failures;     /* shift-invert: solves that stopped at cg_max_iters */
   double ms;           /* device time of the solve */
   long long launches;  /* kernels launched by the solve */
-  double kernel_ms[8];          /* profile: summed device time per kernel class */
-  long long kernel_calls[8];    /* profile: launches per class */
-  double kernel_bytes[8];       /* profile: algorithmic DRAM bytes per class */
+  double kernel_ms[LG_K_CLASSES];        /* profile: summed device time per kernel class */
+  long long kernel_calls[LG_K_CLASSES];  /* profile: launches per class */
+  double kernel_bytes[LG_K_CLASSES];     /* profile: algorithmic DRAM bytes per class */
 } lg_eigsh_info;
 
 typedef struct lg_eigsh_plan lg_eigsh_plan;

@@ -428,25 +428,27 @@ int Solver::set_transport(int mode) {
 int Solver::peer_reduce(const double* partA, const double* partB, int nrows, int ntables, int slot) {
   double* out = red + (size_t)slot * kPartStride;
   ++peer_seq;
-  ++launches;
-  LG_PTRY(launch_pdl(peer_allreduce_kernel, dim3(1), dim3(kReduceThreads), 0, stream, partA, partB, nrows, ntables, out,
-                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, state));
+  LG_PTRY(timed(LG_K_COMM, 0.0, 1, [&] {
+    return launch_pdl(peer_allreduce_kernel, dim3(1), dim3(kReduceThreads), 0, stream, partA, partB, nrows, ntables,
+                      out, peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, state);
+  }));
   return LG_OK;
 }
 
 int Solver::peer_exchange(const double* part, int nrows, int slot) {
   ++peer_seq;
-  ++launches;
   const bool halo = exchange == LG_EXCHANGE_HALO;
   long long ag_pairs = 0;
   for (int q = 0; q < nranks; ++q) ag_pairs += (peer_ptrs.ag_len[q] + 1) / 2;
   const long long work = halo ? halo_send : ag_pairs;
   const int grid = (int)std::max<long long>(1, std::min<long long>((long long)num_sm * 4,
                                                                     (work + kExchangeThreads - 1) / kExchangeThreads));
-  LG_PTRY(launch_pdl(peer_exchange_kernel, dim3(grid), dim3(kExchangeThreads), 0, stream, (const double*)Rfull,
-                     (const int*)d_send_idx, (const long long*)(halo ? d_peer_send_off : nullptr), halo_send, row0, n,
-                     peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, peer_counter, part, part ? nrows : 0,
-                     part ? red + (size_t)slot * kPartStride : nullptr, state));
+  LG_PTRY(timed(LG_K_COMM, 0.0, 1, [&] {
+    return launch_pdl(peer_exchange_kernel, dim3(grid), dim3(kExchangeThreads), 0, stream, (const double*)Rfull,
+                      (const int*)d_send_idx, (const long long*)(halo ? d_peer_send_off : nullptr), halo_send, row0,
+                      n, peer_ptrs, nranks, rank, peer_seq, peer_wait_cycles, peer_counter, part, part ? nrows : 0,
+                      part ? red + (size_t)slot * kPartStride : nullptr, state);
+  }));
   return LG_OK;
 }
 

@@ -54,7 +54,7 @@ class EigshOpts(C.Structure):
     ]
 
 
-KERNEL_CLASSES = ["spmv", "gs_project", "gs_correct_project", "gs_correct", "restart", "basis", "cg", "other"]
+KERNEL_CLASSES = ["spmv", "gs_project", "gs_correct_project", "gs_correct", "restart", "basis", "cg", "other", "comm"]
 
 
 class EigshInfo(C.Structure):
@@ -68,9 +68,9 @@ class EigshInfo(C.Structure):
         ("cg_failures", C.c_int),
         ("ms", C.c_double),
         ("launches", C.c_longlong),
-        ("kernel_ms", C.c_double * 8),
-        ("kernel_calls", C.c_longlong * 8),
-        ("kernel_bytes", C.c_double * 8),
+        ("kernel_ms", C.c_double * len(KERNEL_CLASSES)),
+        ("kernel_calls", C.c_longlong * len(KERNEL_CLASSES)),
+        ("kernel_bytes", C.c_double * len(KERNEL_CLASSES)),
     ]
 
     def as_dict(self) -> dict:
