@@ -142,8 +142,13 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   // the LU factors of the inverse iterations in shared memory behind M when
   // they fit (their loads sit on the iterations' dependent chains)
   const bool f_smem = m <= kRsSmemM;
-  if (!tridiag_eigen_cta<kRsThreads>(d, e, e2, m, th, M, f_smem ? M + (size_t)m * m : a.scratch, cl, &sh_onenrm,
-                                     f_smem ? m : 0)) {
+  // Two lanes per eigenvalue (eight interior points per round, 17 rounds to
+  // full precision).  Fewer points per round take more rounds of the
+  // dependent Sturm chains; more points cost more FP64 work on this one SM.
+  // Measured at m = 60 (cycles of this phase): 1 lane 267 k, 2 lanes 183 k,
+  // 4 lanes 199 k, 8 lanes 249 k.
+  if (!tridiag_eigen_cta<kRsThreads, 2>(d, e, e2, m, th, M, f_smem ? M + (size_t)m * m : a.scratch, cl, &sh_onenrm,
+                                        f_smem ? m : 0)) {
     if (t == 0) {
       state[ST_ERRINFO] = 1;
       state[ST_STATUS] = STATUS_TRIDIAG_FAIL;
@@ -178,18 +183,24 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
         sort_ascending(0, m, rz, bd, id);
         order_wanted(a.which, m, nev, rz, bd, id);
       }
-      // shifts: unwanted values, largest Ritz estimate first
-      for (int i = 0; i < np; ++i) shifts[i] = rz[i];
-      for (int i = 1; i < np; ++i)
-        for (int k = i; k > 0 && bd[k - 1] < bd[k]; --k) {
-          double u = bd[k - 1]; bd[k - 1] = bd[k]; bd[k] = u;
-          u = shifts[k - 1]; shifts[k - 1] = shifts[k]; shifts[k] = u;
-        }
     }
     sh_done = done;
     sh_nev = nev;
     sh_np = np;
     sh_nconv = nconv;
+  }
+  __syncthreads();
+  if (!sh_done && t < sh_np) {
+    // shifts: the unwanted values rz[0, np), largest Ritz estimate first, ties
+    // in their order (a stable sort): thread t places its value by its rank
+    const int np = sh_np;
+    const double bt = bd[t];
+    int rank = 0;
+    for (int i = 0; i < np; ++i) {
+      const double bi = bd[i];
+      rank += (bi > bt) || (bi == bt && i < t);
+    }
+    shifts[rank] = rz[t];
   }
   __syncthreads();
 

@@ -173,7 +173,7 @@ __device__ inline void inverse_iteration(const double* d, const double* e, int m
 // planes of m * m); cl: kMaxCols ints of shared memory; *onenrm (shared)
 // receives ||T||_1.  Returns false (block-uniform) when T has non-finite
 // entries.  Must be called by all threads of the CTA.
-template <int NT>
+template <int NT, int GMAX = 8>
 __device__ bool tridiag_eigen_cta(const double* d, const double* e, const double* e2, int m, double* th, double* Z,
                                   double* F, int* cl, double* onenrm, int fs = 0) {
   __shared__ double sh_glo, sh_ghi, sh_pivmin;
@@ -199,13 +199,13 @@ __device__ bool tridiag_eigen_cta(const double* d, const double* e, const double
   __syncthreads();
   if (!(*onenrm >= 0.0)) return false;
   // Multisection: eigenvalue i belongs to G consecutive lanes (G a power of
-  // two, G m <= NT, at most 8), each evaluating kSturmP interior points per
+  // two, G m <= NT, at most GMAX), each evaluating kSturmP interior points per
   // round with interleaved Sturm chains (their divisions overlap), so a round
   // cuts the bracket into G kSturmP + 1 pieces.  All G lanes hold the same
   // bracket, updated from the first point whose count exceeds i.
   {
     int G = 1;
-    while (G < 8 && 2 * G * m <= NT) G *= 2;
+    while (G < GMAX && 2 * G * m <= NT) G *= 2;
     const int i = t / G, g = t % G;
     const int np = G * kSturmP;
     const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << ((t & 31) & ~(G - 1)));
