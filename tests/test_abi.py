@@ -56,3 +56,25 @@ def test_status_strings_without_gpu():
 
     assert _native.status_string(0) == "ok"
     assert "CG" in _native.status_string(_native.LG_ERR_CG_NOCONV)
+
+
+def test_info_record_matches_header():
+    """The ctypes view of lg_eigsh_info has one slot per kernel class of the
+    header's enum (LG_K_SPMV ... LG_K_COMM, LG_K_CLASSES), in the same order,
+    so the per-class device times land under the right names."""
+    from gpu_eigsh import _native
+
+    text = (HEADER_DIR / "lanczos_b200.h").read_text()
+    enum = {m.group(1): int(m.group(2)) for m in re.finditer(r"\b(LG_K_[A-Z_]+)\s*=\s*(\d+)", text)}
+    n = enum.pop("LG_K_CLASSES")
+    assert n == len(_native.KERNEL_CLASSES)
+    assert sorted(enum.values()) == list(range(n))
+    names = {"LG_K_SPMV": "spmv", "LG_K_PROJECT": "gs_project", "LG_K_CORRPROJ": "gs_correct_project",
+             "LG_K_CORRECT": "gs_correct", "LG_K_RESTART": "restart", "LG_K_BASIS": "basis", "LG_K_CG": "cg",
+             "LG_K_OTHER": "other", "LG_K_COMM": "comm"}
+    for k, v in enum.items():
+        assert _native.KERNEL_CLASSES[v] == names[k]
+    # the arrays are sized by LG_K_CLASSES in the header
+    assert "kernel_ms[LG_K_CLASSES]" in text
+    fields = dict(_native.EigshInfo._fields_)
+    assert fields["kernel_ms"]._length_ == n and fields["kernel_calls"]._length_ == n
