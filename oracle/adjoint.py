@@ -1,7 +1,7 @@
 """CPU (numpy) restatement of the reference's eigsh backward (implicit
 differentiation of the eigenpairs).
 
-TEST INFRASTRUCTURE ONLY: imported by tests/ as the checker; the product path
+TEST INFRASTRUCTURE ONLY: imported by tests/ to check results; the product path
 never imports it.  The reference's own code for this path is CUDA + LAPACK and
 cannot run here, so the restatement is pinned by known answers instead
 (tests/test_oracle_adjoint.py): eigenvalue losses against the dense

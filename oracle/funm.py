@@ -1,7 +1,7 @@
 """CPU (numpy) restatement of the reference's matrix-function primitive:
 m-step Lanczos quadrature for f(A) v and v^T f(A) v.
 
-TEST INFRASTRUCTURE ONLY: imported by tests/ as the checker; the product path
+TEST INFRASTRUCTURE ONLY: imported by tests/ to check results; the product path
 never imports it.  The reference's CUDA path links LAPACK and cannot run here;
 the restatement is pinned (tests/test_oracle_funm.py) against the dense
 ground truth U f(Lambda) U^T v that the reference's own tests use

@@ -1,7 +1,7 @@
 """Python wrapper of the CPU IRLM oracle (irlm_oracle.c).
 
-TEST INFRASTRUCTURE ONLY: used by tests/, by __graft_entry__.smoke() as the
-checker and by bench.py's cpu_baseline / --impl reference leg.  The product
+TEST INFRASTRUCTURE ONLY: used by tests/, by __graft_entry__.smoke() to check
+results and by bench.py's cpu_baseline / --impl reference leg.  The product
 path (gpu_eigsh) never imports this module.
 
 Also exposes ``arpack_eigsh`` — scipy.sparse.linalg.eigsh (ARPACK), the ground

@@ -1,7 +1,7 @@
 /*
  * irlm_oracle.c — CPU restatement of the reference's implicitly restarted
  * Lanczos eigensolver.  TEST INFRASTRUCTURE ONLY: imported by tests/, by
- * __graft_entry__.smoke() as the checker and by bench.py's cpu_baseline /
+ * __graft_entry__.smoke() to check results and by bench.py's cpu_baseline /
  * --impl reference leg.  The product path never links or calls it.
  *
  * Follows (reference file:line):

@@ -1,7 +1,7 @@
 """CPU (torch) restatement of the reference's stochastic Lanczos quadrature path.
 
-TEST INFRASTRUCTURE ONLY: imported by tests/, by __graft_entry__.smoke() as the
-checker, and by bench.py's cpu_baseline leg.  The product path never imports
+TEST INFRASTRUCTURE ONLY: imported by tests/, by __graft_entry__.smoke() to check
+results, and by bench.py's cpu_baseline leg.  The product path never imports
 it.  Pinned against golden vectors produced by the reference's own code
 (tests/golden/make_golden.py).
 
