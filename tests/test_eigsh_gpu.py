@@ -215,6 +215,40 @@ def test_bitwise_repeatable(ge):
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
 
 
+def test_profile_mode_accounts_every_launch(ge):
+    """Profile mode (CUDA events around every launch; what the bench's
+    rooflines read) changes no result, and its record is consistent: every
+    launch of the solve is in some kernel class, the single-GPU plan spends
+    nothing in the multi-GPU class, and the bytes of the sparse product are
+    its per-launch formula times its launches."""
+    from gpu_eigsh import synthetic as syn
+
+    L, _ = syn.knn_laplacian(40000, k=10, seed=8)
+    n, nnz = L.shape[0], L.nnz
+    v0 = np.random.default_rng(2).standard_normal(n)
+    plan = ge.EigshPlan(L, max_ncv=40)
+    try:
+        w0, V0 = plan.solve(k=10, which="LA", ncv=30, tol=1e-10, v0=v0)
+        plain = dict(plan.last_info)
+        w1, V1 = plan.solve(k=10, which="LA", ncv=30, tol=1e-10, v0=v0, profile=True)
+        prof = dict(plan.last_info)
+    finally:
+        plan.close()
+    assert np.array_equal(w0, w1) and np.array_equal(V0, V1)
+    assert prof["steps"] == plain["steps"] and prof["launches"] == plain["launches"]
+    calls, ms, by = prof["kernel_calls"], prof["kernel_ms"], prof["kernel_bytes"]
+    assert sum(calls.values()) <= prof["launches"]
+    for cls in ("spmv", "gs_project", "gs_correct_project", "restart", "basis"):
+        assert calls[cls] > 0 and ms[cls] > 0.0, cls
+    assert calls["comm"] == 0 and ms["comm"] == 0.0
+    # lag steps: (4 + 8) nnz + 4 (n + 1) + 8n (x) + 8n (z) per launch; the
+    # first step of each extension (in-step passes) writes v_j too (+8n)
+    lo = calls["spmv"] * ((12.0 * nnz + 4.0 * (n + 1) + 16.0 * n))
+    hi = calls["spmv"] * ((12.0 * nnz + 4.0 * (n + 1) + 24.0 * n))
+    assert lo <= by["spmv"] <= hi
+    assert sum(ms.values()) < 5.0 * prof["ms"]
+
+
 def test_device_pointer_api_with_torch(ge):
     import torch
     from gpu_eigsh import synthetic as syn
