@@ -228,6 +228,9 @@ __global__ void adj_pad_kernel(int n, int k, int ld, const double* __restrict__ 
 // B[r0+tig][b0+8tj+gid], exactly its A and B fragments; the warps of a CTA
 // are summed in warp order in shared memory.
 // ---------------------------------------------------------------------------
+// TM: the most 8-column blocks per side (ta, tb <= TM) the instantiation
+// holds in registers (a 24-column block of 20 eigenpairs needs 3).
+template <int TM>
 __global__ void __launch_bounds__(kDT)
 adj_gram_kernel(int n, int ld, const double* __restrict__ X, const double* __restrict__ B, int a0, int ta, int b0,
                 int tb, double* __restrict__ part, const int* __restrict__ active) {
@@ -236,34 +239,34 @@ adj_gram_kernel(int n, int ld, const double* __restrict__ X, const double* __res
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   for (int i = t; i < kGramChunk; i += kDT) red[i] = 0.0;
-  double acc[4][4][2];
+  double acc[TM][TM][2];
 #pragma unroll
-  for (int ti = 0; ti < 4; ++ti)
+  for (int ti = 0; ti < TM; ++ti)
 #pragma unroll
-    for (int tj = 0; tj < 4; ++tj) acc[ti][tj][0] = acc[ti][tj][1] = 0.0;
+    for (int tj = 0; tj < TM; ++tj) acc[ti][tj][0] = acc[ti][tj][1] = 0.0;
   const long long step = (long long)gridDim.x * kDW * 4;
   for (long long r0 = ((long long)blockIdx.x * kDW + warp) * 4; r0 < n; r0 += step) {
     const long long row = r0 + tig;
     const bool ok = row < n;
-    double xa[4], bb[4];
+    double xa[TM], bb[TM];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < TM; ++q) {
       xa[q] = (ok && q < ta) ? __ldg(X + row * ld + a0 + 8 * q + gid) : 0.0;
       bb[q] = (ok && q < tb) ? B[row * ld + b0 + 8 * q + gid] : 0.0;
     }
 #pragma unroll
-    for (int ti = 0; ti < 4; ++ti)
+    for (int ti = 0; ti < TM; ++ti)
 #pragma unroll
-      for (int tj = 0; tj < 4; ++tj)
+      for (int tj = 0; tj < TM; ++tj)
         if (ti < ta && tj < tb) dmma(acc[ti][tj][0], acc[ti][tj][1], xa[ti], bb[tj]);
   }
   __syncthreads();
   for (int w = 0; w < kDW; ++w) {
     if (warp == w) {
 #pragma unroll
-      for (int ti = 0; ti < 4; ++ti)
+      for (int ti = 0; ti < TM; ++ti)
 #pragma unroll
-        for (int tj = 0; tj < 4; ++tj)
+        for (int tj = 0; tj < TM; ++tj)
           if (ti < ta && tj < tb) {
             double* o = red + (8 * ti + gid) * kGramTile + 8 * tj + 2 * tig;
             o[0] += acc[ti][tj][0];
@@ -300,7 +303,10 @@ __global__ void adj_gram_reduce_kernel(const double* __restrict__ part, int npar
 //          columns still running.
 //   MODE 1: B -= X D only (deflation of a right-hand side or of the solution).
 // ---------------------------------------------------------------------------
-template <int MODE>
+// TBMAX: the most 8-column output blocks (ld / 8) the instantiation holds in
+// registers; the narrow blocks of a few eigenpairs keep few accumulators, so
+// more CTAs stay resident to stream X, B and P.
+template <int MODE, int TBMAX>
 __global__ void __launch_bounds__(kDT)
 adj_deflate_kernel(int n, int k, int ld, int it, int max_iters, const double* __restrict__ X, double* __restrict__ B,
                    double* __restrict__ P, State s) {
@@ -350,19 +356,19 @@ adj_deflate_kernel(int n, int k, int ld, int it, int max_iters, const double* __
   for (long long r0 = ((long long)blockIdx.x * kDW + warp) * 8; r0 < n; r0 += step) {
     const long long arow = r0 + gid;
     const bool aok = arow < n;
-    double acc[16][2];
+    double acc[TBMAX][2];
 #pragma unroll
-    for (int tj = 0; tj < 16; ++tj) acc[tj][0] = acc[tj][1] = 0.0;
+    for (int tj = 0; tj < TBMAX; ++tj) acc[tj][0] = acc[tj][1] = 0.0;
     for (int kk = 0; kk < KA; ++kk) {
       const double xa = aok ? __ldg(X + arow * ld + 4 * kk + tig) : 0.0;
 #pragma unroll
-      for (int tj = 0; tj < 16; ++tj)
+      for (int tj = 0; tj < TBMAX; ++tj)
         if (tj < TB) dmma(acc[tj][0], acc[tj][1], xa, sD[(4 * kk + tig) * ld + 8 * tj + gid]);
     }
     // lane holds (X D)[r0 + gid][8 tj + 2 tig + {0, 1}]
     if (!aok) continue;
 #pragma unroll
-    for (int tj = 0; tj < 16; ++tj) {
+    for (int tj = 0; tj < TBMAX; ++tj) {
       if (tj >= TB) break;
       const int c = 8 * tj + 2 * tig;
       double2* bp = reinterpret_cast<double2*>(B + arow * ld + c);
@@ -512,7 +518,7 @@ int cuda_fail(cudaError_t e) {
 }
 
 struct Work {
-  int n, k, ld, grid_rl, grid_gram, grid_defl;
+  int n, k, ld, grid_rl, grid_gram, grid_defl, sms;
   double *X, *P, *AP, *Xi, *R;
   double* part;          // max(grid_rl * kRowStride, grid_gram * kGramChunk)
   ColSum cs_pap, cs_rr, cs_nrm;
@@ -557,14 +563,22 @@ size_t carve(char* base, Work& w) {
   return off;
 }
 
-template <int MODE>
-cudaError_t launch_deflate(const Work& w, int it, int max_iters, double* B, cudaStream_t st) {
+template <int MODE, int TBMAX>
+cudaError_t launch_deflate_tb(const Work& w, int it, int max_iters, double* B, cudaStream_t st) {
   const size_t smem = sizeof(double) * (size_t)w.ld * w.ld;
   static std::atomic<unsigned long long> attr{0};
-  cudaError_t e = smem_attr_once(attr, (const void*)adj_deflate_kernel<MODE>, (int)(sizeof(double) * kMaxB * kMaxB));
+  cudaError_t e = smem_attr_once(attr, (const void*)adj_deflate_kernel<MODE, TBMAX>,
+                                 (int)(sizeof(double) * kMaxB * kMaxB));
   if (e != cudaSuccess) return e;
-  adj_deflate_kernel<MODE><<<w.grid_defl, kDT, smem, st>>>(w.n, w.k, w.ld, it, max_iters, w.X, B, w.P, w.s);
+  adj_deflate_kernel<MODE, TBMAX><<<w.grid_defl, kDT, smem, st>>>(w.n, w.k, w.ld, it, max_iters, w.X, B, w.P, w.s);
   return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_deflate(const Work& w, int it, int max_iters, double* B, cudaStream_t st) {
+  if (w.ld <= 32) return launch_deflate_tb<MODE, 4>(w, it, max_iters, B, st);
+  if (w.ld <= 64) return launch_deflate_tb<MODE, 8>(w, it, max_iters, B, st);
+  return launch_deflate_tb<MODE, 16>(w, it, max_iters, B, st);
 }
 
 // D = X^T B over every 32 x 32 chunk of (ld x ld).
@@ -573,10 +587,24 @@ cudaError_t gram(const Work& w, const double* B, const int* active, cudaStream_t
     const int ta = std::min(4, (w.ld - a0) / 8);
     for (int b0 = 0; b0 < w.ld; b0 += kGramTile) {
       const int tb = std::min(4, (w.ld - b0) / 8);
-      adj_gram_kernel<<<w.grid_gram, kDT, 0, st>>>(w.n, w.ld, w.X, B, a0, ta, b0, tb, w.part, active);
+      // one wave of resident CTAs (at most grid_gram, the partial rows' capacity)
+      int g = w.grid_gram;
+      if (std::max(ta, tb) <= 2) {
+        static OccupancyCache occ;
+        g = std::min(g, w.sms * resident_blocks_once(occ, (const void*)adj_gram_kernel<2>, kDT, 2));
+        adj_gram_kernel<2><<<g, kDT, 0, st>>>(w.n, w.ld, w.X, B, a0, ta, b0, tb, w.part, active);
+      } else if (std::max(ta, tb) == 3) {
+        static OccupancyCache occ;
+        g = std::min(g, w.sms * resident_blocks_once(occ, (const void*)adj_gram_kernel<3>, kDT, 2));
+        adj_gram_kernel<3><<<g, kDT, 0, st>>>(w.n, w.ld, w.X, B, a0, ta, b0, tb, w.part, active);
+      } else {
+        static OccupancyCache occ;
+        g = std::min(g, w.sms * resident_blocks_once(occ, (const void*)adj_gram_kernel<4>, kDT, 2));
+        adj_gram_kernel<4><<<g, kDT, 0, st>>>(w.n, w.ld, w.X, B, a0, ta, b0, tb, w.part, active);
+      }
       const int entries = ta * 8 * tb * 8;
-      adj_gram_reduce_kernel<<<(entries * 32 + 255) / 256, 256, 0, st>>>(w.part, w.grid_gram, a0, ta * 8, b0,
-                                                                         tb * 8, w.s.D, active);
+      adj_gram_reduce_kernel<<<(entries * 32 + 255) / 256, 256, 0, st>>>(w.part, g, a0, ta * 8, b0, tb * 8, w.s.D,
+                                                                         active);
     }
   }
   return cudaGetLastError();
@@ -672,7 +700,8 @@ extern "C" int lg_eigsh_adjoint(int n, long long nnz, const int* rowptr, const i
   w.k = k;
   w.ld = (k + 7) / 8 * 8;
   w.grid_rl = 2 * sms;   // the row kernels are built for 2 CTAs of 512 threads per SM
-  w.grid_gram = 2 * sms;
+  w.grid_gram = 4 * sms;   // capacity: up to four resident CTAs of the narrow Gram tiles per SM
+  w.sms = sms;
   w.grid_defl = 4 * sms;
   void* base = nullptr;
   cudaMemPool_t pool = nullptr;
