@@ -29,7 +29,6 @@ namespace {
 constexpr int kBsThreads = 256;
 constexpr int kTR = 64;                      // basis rows per tile (8 warps x 8 rows)
 constexpr int kMaxOB = kMaxCols / 8;         // output blocks of 8 columns
-constexpr size_t kBsSmemLimit = 227 * 1024;  // dynamic shared memory of one CTA
 
 __host__ __device__ inline int pad_stride(int x) {   // x multiple of 4 -> stride = 4 or 12 (mod 16)
   return (x % 16 == 0 || x % 16 == 8) ? x + 4 : x;
@@ -91,7 +90,13 @@ BasisPlan basis_plan(int n, int m, int kq, int grid) {
   const int ntiles = (n + kTR - 1) / kTR;
   p.grid = grid < ntiles ? grid : ntiles;
   const BsGeom g(m, kq);
-  p.nbuf = g.smem_doubles(2) * sizeof(double) <= kBsSmemLimit ? 2 : 1;
+  // One tile buffer per CTA: the copies of one CTA then overlap the MMAs of
+  // the other CTAs on the SM, and half the shared memory doubles the resident
+  // CTAs.  Measured against two buffers per CTA: V*Q per configuration-1 solve
+  // (m = 60) 2.03 -> 1.96 ms, per R-MAT solve (m = 96, one CTA per SM with two
+  // buffers, two with one) 212 -> 133 ms.
+  // (at m = 127: Q 128 x 132 and one 64 x 132 tile, 203 KB)
+  p.nbuf = 1;
   p.smem = g.smem_doubles(p.nbuf) * sizeof(double);
   // one wave: the tiles are dealt to the CTAs in a grid-strided loop, every
   // CTA the same count, so CTAs beyond the resident ones would only form a
