@@ -88,8 +88,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   extern __shared__ __align__(16) double M[];   // m x m, column-major
   __shared__ double d[kMaxCols], e[kMaxCols], e2[kMaxCols], th[kMaxCols];
   __shared__ double rz[kMaxCols], bd[kMaxCols], shifts[kMaxCols];
-  __shared__ double rot_c[2][32], rot_s[2][32];
-  __shared__ int rot_k[2][32];
+  __shared__ double rot_c[2][2][32], rot_s[2][2][32];
+  __shared__ int rot_k[2][2][32];
   __shared__ int id[kMaxCols], cl[kMaxCols];
   __shared__ double sh_bn, sh_onenrm;
   __shared__ int sh_stop, sh_done, sh_nev, sh_np, sh_nconv;
@@ -232,9 +232,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
   // every unreduced block.  Couplings that become negligible during the
   // chases are left alone (the bulge then just passes identity rotations).
   const int np = sh_np, nev = sh_nev;
-  // Warp 0 computes the rotations of chase step st while the other warps
-  // apply those of step st - 1 to Q (double-buffered rotation lists), so the
-  // two halves of a step overlap; Q still receives the steps in order.
+  // Warp 0 computes the rotations of the chase while the other warps apply
+  // the rotations computed before to Q (double-buffered rotation lists).
   int tpr = 1;   // threads per row of Q in the rotation updates (warps 1..)
   while (tpr < 32 && 2 * tpr * m <= kRsThreads - 32) tpr *= 2;
   __shared__ int blk_lo[kMaxCols], blk_hi[kMaxCols];
@@ -261,48 +260,61 @@ __global__ void __launch_bounds__(kRsThreads, 1) restart_kernel(RestartArgs a) {
       const int steps = (be - bs) + 3 * (nb - 1);
       double bulge = 0.0;                       // lane's bulge (warp 0)
       const double sigma = (t < 32 && lane < nb) ? shifts[b0 + lane] : 0.0;
-      for (int st = 0; st <= steps; ++st) {
-        const int buf = st & 1;
+      // Steps run in pairs.  Warp 0 computes the rotations of steps 2p and
+      // 2p + 1 (a __syncwarp between them: a bulge's next rotation reads the
+      // coupling its upper neighbour's rotation has just written) while the
+      // other warps apply the previous pair to Q.  Within a pair a bulge's
+      // two rotations touch columns k .. k+2 and the next bulge's k-3 .. k-1,
+      // so each thread applies both rotations of its bulges in order, and
+      // every column of Q receives its rotations in the same order as one
+      // step at a time (bitwise the same Q), with half the barriers.
+      const int npairs = (steps + 1) / 2;
+      for (int pr = 0; pr <= npairs; ++pr) {
+        const int buf = pr & 1;
         if (t < 32) {
-          if (st < steps) {
-            const int k = bs + st - 3 * lane;
-            int kk = -1;
-            if (lane < nb && k >= bs && k < be) {
-              double c, s;
-              if (k == bs) {
-                givens(d[bs] - sigma, e[bs], c, s);
-              } else {
-                givens(e[k - 1], bulge, c, s);
-                e[k - 1] = c * e[k - 1] - s * bulge;
+          if (pr < npairs) {
+            for (int q = 0; q < 2; ++q) {
+              const int st = 2 * pr + q;
+              const int k = bs + st - 3 * lane;
+              int kk = -1;
+              if (st < steps && lane < nb && k >= bs && k < be) {
+                double c, s;
+                if (k == bs) {
+                  givens(d[bs] - sigma, e[bs], c, s);
+                } else {
+                  givens(e[k - 1], bulge, c, s);
+                  e[k - 1] = c * e[k - 1] - s * bulge;
+                }
+                const double dk = d[k], dk1 = d[k + 1], ek = e[k];
+                const double cc = c * c, ss = s * s, cs = c * s;
+                d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
+                d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
+                e[k] = cs * (dk - dk1) + (cc - ss) * ek;
+                if (k + 1 < be) {
+                  bulge = -s * e[k + 1];
+                  e[k + 1] = c * e[k + 1];
+                }
+                rot_c[buf][q][lane] = c;
+                rot_s[buf][q][lane] = s;
+                kk = k;
               }
-              const double dk = d[k], dk1 = d[k + 1], ek = e[k];
-              const double cc = c * c, ss = s * s, cs = c * s;
-              d[k] = cc * dk - 2.0 * cs * ek + ss * dk1;
-              d[k + 1] = ss * dk + 2.0 * cs * ek + cc * dk1;
-              e[k] = cs * (dk - dk1) + (cc - ss) * ek;
-              if (k + 1 < be) {
-                bulge = -s * e[k + 1];
-                e[k + 1] = c * e[k + 1];
-              }
-              rot_c[buf][lane] = c;
-              rot_s[buf][lane] = s;
-              kk = k;
+              rot_k[buf][q][lane] = kk;
+              __syncwarp();
             }
-            rot_k[buf][lane] = kk;
           }
-        } else if (st > 0 && t - 32 < tpr * m) {
-          // step st - 1: its rotations touch disjoint column pairs (bulges
-          // three rows apart), so the tpr threads of a row split them freely
+        } else if (pr > 0 && t - 32 < tpr * m) {
+          // the previous pair: the tpr threads of a row split the bulges
           const int tq = t - 32, pb = buf ^ 1;
           const int row = tq / tpr;
-          for (int s = tq % tpr; s < nb; s += tpr) {
-            const int k = rot_k[pb][s];
-            if (k < 0) continue;
-            const double c = rot_c[pb][s], sn = rot_s[pb][s];
-            const double x0 = M[row + (size_t)k * m], x1 = M[row + (size_t)(k + 1) * m];
-            M[row + (size_t)k * m] = c * x0 - sn * x1;
-            M[row + (size_t)(k + 1) * m] = sn * x0 + c * x1;
-          }
+          for (int s = tq % tpr; s < nb; s += tpr)
+            for (int q = 0; q < 2; ++q) {
+              const int k = rot_k[pb][q][s];
+              if (k < 0) continue;
+              const double c = rot_c[pb][q][s], sn = rot_s[pb][q][s];
+              const double x0 = M[row + (size_t)k * m], x1 = M[row + (size_t)(k + 1) * m];
+              M[row + (size_t)k * m] = c * x0 - sn * x1;
+              M[row + (size_t)(k + 1) * m] = sn * x0 + c * x1;
+            }
         }
         __syncthreads();
       }
