@@ -42,7 +42,7 @@ struct BsGeom {
     sv = pad_stride(mp > kqp ? mp : kqp);
     sq = pad_stride(mp);
   }
-  __host__ __device__ size_t smem_doubles(int nbuf) const { return (size_t)kqp * sq + (size_t)nbuf * kTR * sv; }
+  __host__ __device__ size_t smem_doubles() const { return (size_t)kqp * sq + (size_t)kTR * sv; }
 };
 
 __device__ __forceinline__ void dmma(double& c0, double& c1, double a, double b) {
@@ -90,14 +90,13 @@ BasisPlan basis_plan(int n, int m, int kq, int grid) {
   const int ntiles = (n + kTR - 1) / kTR;
   p.grid = grid < ntiles ? grid : ntiles;
   const BsGeom g(m, kq);
-  // One tile buffer per CTA: the copies of one CTA then overlap the MMAs of
-  // the other CTAs on the SM, and half the shared memory doubles the resident
-  // CTAs.  Measured against two buffers per CTA: V*Q per configuration-1 solve
-  // (m = 60) 2.03 -> 1.96 ms, per R-MAT solve (m = 96, one CTA per SM with two
-  // buffers, two with one) 212 -> 133 ms.
-  // (at m = 127: Q 128 x 132 and one 64 x 132 tile, 203 KB)
-  p.nbuf = 1;
-  p.smem = g.smem_doubles(p.nbuf) * sizeof(double);
+  // One tile buffer per CTA: the copies of one CTA overlap the MMAs of the
+  // other CTAs on the SM, and the shared memory of a second buffer would halve
+  // the resident CTAs.  Measured against two buffers per CTA: V*Q per
+  // configuration-1 solve (m = 60) 2.03 -> 1.96 ms, per R-MAT solve (m = 96,
+  // one CTA per SM with two buffers, two with one) 212 -> 133 ms.
+  // At m = 127: Q 128 x 132 and one 64 x 132 tile, 203 KB.
+  p.smem = g.smem_doubles() * sizeof(double);
   // one wave: the tiles are dealt to the CTAs in a grid-strided loop, every
   // CTA the same count, so CTAs beyond the resident ones would only form a
   // second wave as long as the first
@@ -113,10 +112,13 @@ BasisPlan basis_plan(int n, int m, int kq, int grid) {
 // One tile of kTR basis rows: out = V[rows, 0:m] Q[0:m, 0:kq] on the FP64
 // tensor cores.  The tile's rows of V arrive in shared memory by asynchronous
 // 16-byte copies, two columns at a time (in the solver's panel layout the 64
-// rows of a panel are 4 KB of contiguous memory); with two buffers the copies
-// of the next tile are in flight while this one is contracted and written.
+// rows of a panel are 4 KB of contiguous memory); the next tile's copies start
+// once this one is contracted and written, and the other CTAs of the SM keep
+// the memory busy meanwhile.
+// Register caps: four CTAs of 256 threads per SM for the narrow instantiation
+// (up to 32 outputs: the restart of ncv <= 64), two for the wider ones.
 template <int NOB>
-__global__ void __launch_bounds__(kBsThreads)
+__global__ void __launch_bounds__(kBsThreads, NOB <= 4 ? 4 : 2)
 basis_kernel(BasisArgs a) {
   int* state = a.state;
   if (state[ST_STATUS] != STATUS_RUNNING) return;
@@ -127,7 +129,7 @@ basis_kernel(BasisArgs a) {
   const VLayout vl = a.vl;
   const BsGeom g(m, kq);
   double* Qs = sm;                              // kqp columns x sq (column-major, zero padded)
-  double* Vbuf[2] = {sm + (size_t)g.kqp * g.sq, sm + (size_t)g.kqp * g.sq + (size_t)(a.nbuf - 1) * kTR * g.sv};
+  double* Vs = sm + (size_t)g.kqp * g.sq;       // one tile of kTR rows x sv
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int gid = lane >> 2, tig = lane & 3;
 
@@ -159,21 +161,13 @@ basis_kernel(BasisArgs a) {
     }
   };
 
-  int cur = 0;
-  if ((int)blockIdx.x < ntiles) issue(blockIdx.x, Vbuf[0]);
+  if ((int)blockIdx.x < ntiles) issue(blockIdx.x, Vs);
   bs_commit();
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const long long row0 = (long long)tile * kTR;
     const int next = tile + gridDim.x;
-    if (a.nbuf == 2) {
-      if (next < ntiles) issue(next, Vbuf[cur ^ 1]);
-      bs_commit();
-      bs_wait<1>();    // this thread's copies of the current tile have landed
-    } else {
-      bs_wait<0>();
-    }
+    bs_wait<0>();
     __syncthreads();   // every thread's copies (and Qs on the first pass)
-    double* Vs = Vbuf[cur];
     // two accumulator sets (k steps alternate between them) halve the chain
     // of dependent MMAs; they are added once at the end
     double acc[NOB][2], acc2[NOB][2];
@@ -231,11 +225,10 @@ basis_kernel(BasisArgs a) {
           nrm += rn * rn;
         }
       }
-      if (a.nbuf == 1 && next < ntiles) {
-        issue(next, Vbuf[0]);
+      if (next < ntiles) {
+        issue(next, Vs);
         bs_commit();
       }
-      cur ^= (a.nbuf - 1);
       continue;
     }
     __syncthreads();   // all fragment reads of Vs done
@@ -278,11 +271,10 @@ basis_kernel(BasisArgs a) {
       }
     }
     __syncthreads();   // the outputs are read out of Vs before Vs receives copies again
-    if (a.nbuf == 1 && next < ntiles) {
-      issue(next, Vbuf[0]);
+    if (next < ntiles) {
+      issue(next, Vs);
       bs_commit();
     }
-    cur ^= (a.nbuf - 1);
   }
   bs_wait<0>();
   if (a.restart) {
@@ -293,7 +285,6 @@ basis_kernel(BasisArgs a) {
 
 cudaError_t basis_update(const BasisPlan& p, const BasisArgs& a_in, cudaStream_t st) {
   BasisArgs a = a_in;
-  a.nbuf = p.nbuf;
   const int nob = ((a.kq + 7) & ~7) / 8;
 #define LG_BS(N)                                                                                     \
   do {                                                                                               \

@@ -162,11 +162,9 @@ struct BasisArgs {
   int rowmajor = 0;
   const int* ymap = nullptr;   // ritz mode: row r of out goes to row ymap[r] of Y (null: r)
   int* state = nullptr;
-  int nbuf = 1;                // set by basis_update from the plan
 };
 struct BasisPlan {
   int TR = 32, grid = 0;
-  int nbuf = 1;   // tile buffers: 2 = the next tile's copies overlap this tile's contraction
   size_t smem = 0;
 };
 BasisPlan basis_plan(int n, int m, int kq, int grid);
